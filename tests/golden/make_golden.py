@@ -1,0 +1,253 @@
+"""Generate the golden fixtures under tests/golden/ by running the reference (zzf1955/StreamVoxel) itself.
+
+Run in a container where the reference checkout exists (read-only is fine):
+
+    python tests/golden/make_golden.py --reference <path to the StreamVoxel checkout>
+
+It writes small .npz files (inputs, the reference's outputs, and the RNG draws the reference made) that the CPU
+tests compare the oracle and the product's host logic against. Nothing here runs on the GPU box.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _save(name, **arrays):
+    path = os.path.join(HERE, name)
+    np.savez_compressed(path, **arrays)
+    print(f'wrote {path} ({os.path.getsize(path)} bytes)')
+
+
+# ---------------------------------------------------------------------------------------------- sampler
+
+def quota_cases():
+    """Inputs/outputs of `block_quota_select`, following the reference test generator
+    (`tests/stream/test_live_fast_ops.py:32-49`) plus full-size columns."""
+    from streamvoxel.sampling.block_quota import block_quota_select, block_view
+    out = {}
+    cases = [((16, 8, 8), s) for s in range(25)] + [((256, 16, 16), 100 + s) for s in range(6)]
+    for index, (shape, seed) in enumerate(cases):
+        b = 4
+        g = torch.Generator().manual_seed(seed)
+        last = torch.zeros(shape, dtype=torch.bool)
+        tops = torch.randint(4, shape[0], shape[1:], generator=g)
+        for z in range(shape[1]):
+            for x in range(shape[2]):
+                last[tops[z, x]:, z, x] = True
+        non_last = ~last
+        committed_mask = non_last & (torch.rand(shape, generator=g) < torch.rand((), generator=g))
+        selectable = non_last & ~committed_mask
+        k = int(torch.randint(1, max(2, int(selectable.sum())), (), generator=g))
+        if index % 3 == 2:   # quota-sized steps as the live sampler takes them
+            k = max(1, min(int(selectable.sum()), int(selectable.sum()) // 7))
+        committed = int(committed_mask.sum())
+        frac = (committed + k) / int(non_last.sum())
+        blocks = int(np.prod(shape)) // b ** 3
+        order = torch.randperm(blocks, generator=g)
+        n_total = block_view(non_last.contiguous(), b).sum(1)
+        score = (torch.randn(shape, generator=g) * 2).round() / 2
+        if index % 2:
+            score = torch.randn(shape, generator=g)
+        chosen = block_quota_select(score, selectable, k, b, order, frac, n_total)
+        pre = f'c{index}_'
+        out.update({pre + 'score': score.numpy(), pre + 'selectable': selectable.numpy(), pre + 'k': np.int64(k),
+                    pre + 'order': order.numpy(), pre + 'frac': np.float64(frac), pre + 'n_total': n_total.numpy(),
+                    pre + 'committed': np.int64(committed), pre + 'chosen': chosen.numpy()})
+    out['count'] = np.int64(len(cases))
+    _save('quota_select.npz', **out)
+
+
+def top_mask_cases():
+    from streamvoxel.sampling.block_quota import top_mask
+    out = {}
+    g = torch.Generator().manual_seed(1)
+    for i, count in enumerate((0, 1, 7, 40, 500)):
+        scores = torch.randint(-4, 1, (8, 8, 8), generator=g).float()
+        eligible = torch.rand((8, 8, 8), generator=g) < .3
+        out.update({f't{i}_scores': scores.numpy(), f't{i}_eligible': eligible.numpy(), f't{i}_count': np.int64(count),
+                    f't{i}_mask': top_mask(scores, eligible, count).numpy()})
+    out['count'] = np.int64(5)
+    _save('top_mask.npz', **out)
+
+
+def schedule_cases():
+    from streamvoxel.sampling.low_entropy_last import low_entropy_last_quotas
+    from streamvoxel.sampling.schedule import counts, actual_time
+    rows = []
+    for total, steps, n_last in [(65536, 32, 0), (65536, 32, 4096), (65536, 32, 30000), (65536, 32, 65536),
+                                 (1024, 8, 0), (1024, 8, 300), (1024, 9, 1000), (65536, 16, 123), (65536, 64, 777)]:
+        q = low_entropy_last_quotas(total, steps, n_last)
+        rows.append((total, steps, n_last, q, counts(total, dict(steps=steps, schedule='quartercos', rounding='positive'))))
+    flat = {}
+    for i, (total, steps, n_last, q, c) in enumerate(rows):
+        flat[f's{i}_args'] = np.asarray([total, steps, n_last], np.int64)
+        flat[f's{i}_quotas'] = np.asarray(q, np.int64)
+        flat[f's{i}_counts'] = np.asarray(c, np.int64)
+    fractions = np.linspace(0, 1, 41)
+    flat['time_in'] = fractions
+    flat['time_out'] = np.asarray([actual_time(f) for f in fractions])
+    flat['count'] = np.int64(len(rows))
+    _save('schedule.npz', **flat)
+
+
+def score_cases():
+    """`entropy_scores`, the air probability and the per-column last mask on seeded logits."""
+    from streamvoxel.sampling.entropy import entropy_scores
+    from streamvoxel.sampling.low_entropy_last import low_entropy_last_update
+    g = torch.Generator().manual_seed(7)
+    out = {}
+    for i, (classes, shape, eps) in enumerate([(6, (16, 8, 8), 1e-3), (256, (16, 4, 4), 1e-4), (33, (32, 4, 4), 0.05)]):
+        logits = torch.randn((classes, *shape), generator=g) * 2
+        logits[0, shape[0] // 2:] += 30.  # certain air above the middle
+        logits[0, shape[0] // 2 - 2:shape[0] // 2] += 9.
+        air = logits.float().softmax(0)[torch.tensor([0])].sum(0)
+        mask = torch.ones(shape, dtype=torch.bool)
+        last = low_entropy_last_update(torch.zeros(shape, dtype=torch.bool), mask, air, torch.zeros(shape, dtype=torch.bool),
+                                       eps, False, True)
+        out.update({f'e{i}_logits': logits.numpy(), f'e{i}_eps': np.float64(eps), f'e{i}_entropy': entropy_scores(logits).numpy(),
+                    f'e{i}_air': air.numpy(), f'e{i}_last': last.numpy()})
+    out['count'] = np.int64(3)
+    _save('scores.npz', **out)
+
+
+def _fixture_logits(step, ground=8, classes=6, shape=(16, 8, 8)):
+    """`tests/stream/test_live_fast_ops.py:63-67`."""
+    generator = torch.Generator().manual_seed(step + 1)
+    logits = torch.randn((classes, *shape), generator=generator)
+    logits[0, ground:] += 30.
+    return logits
+
+
+def slot_cases():
+    """Whole windows of the reference `LowEntropyLastSlot` (`streamvoxel/stream/slot.py:50-176`) on the fixture logits
+    of `tests/stream/test_live_fast_ops.py:70-91`, with the block order and every categorical draw's exponential
+    noise recorded (cloned generator state, same call `torch.multinomial` makes)."""
+    from streamvoxel.stream.slot import LowEntropyLastSlot
+    shape, classes = (16, 8, 8), 6
+    out = {}
+    for i, seed in enumerate([3, 11, 12345]):
+        slot = LowEntropyLastSlot(shape, classes, air_ids=(0,), air_token=0, last_eps=1e-3, block_size=4, device='cpu')
+        tokens = torch.full(shape, classes, dtype=torch.long)
+        cap = 8 + i
+        slot.arm(seed, cap, (i, 0))
+        out[f'w{i}_order'] = slot.order.numpy()
+        out[f'w{i}_args'] = np.asarray([seed, cap, 6 + i], np.int64)
+        step, draws = 0, []
+        while not slot.idle:
+            logits = _fixture_logits(step + 31 * i, ground=6 + i)
+            noise = None
+            if slot.phase == 'solid' and slot.solid_calls < len(slot.quotas):
+                k = slot.quotas[slot.solid_calls]
+                clone = torch.Generator().set_state(slot.generator.get_state())
+                noise = torch.empty((k, classes)).exponential_(generator=clone)
+            record, commit = slot.consume(logits, tokens)
+            if commit is not None:
+                p = logits.permute(1, 2, 3, 0).reshape(-1, classes)[torch.as_tensor(commit['positions']).long()].softmax(-1)
+                assert torch.equal((p / noise).argmax(-1).to(torch.int16), torch.as_tensor(commit['values'])), 'multinomial != argmax(p/q)'
+                out[f'w{i}_s{step}_positions'] = commit['positions']
+                out[f'w{i}_s{step}_values'] = commit['values']
+                out[f'w{i}_s{step}_noise'] = noise.numpy()
+            step += 1
+        out[f'w{i}_steps'] = np.int64(step)
+        out[f'w{i}_tokens'] = tokens.numpy()
+        out[f'w{i}_step_map'] = record['step_map'].numpy()
+        out[f'w{i}_values'] = record['values'].numpy()
+        out[f'w{i}_record'] = np.asarray([record['nfe'], record['actual'], record['last_count']], np.int64)
+    out['count'] = np.int64(3)
+    _save('slot_windows.npz', **out)
+
+
+# ------------------------------------------------------------------------------------------------ models
+
+def _reinit(model, std, seed):
+    torch.manual_seed(seed)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.normal_(std=std)
+    return model.eval().requires_grad_(False)
+
+
+def _state(model):
+    return {k: v.detach().numpy() for k, v in model.state_dict().items()}
+
+
+def model_cases():
+    """Tiny time-free DiT and compact ControlNet forwards with every parameter re-drawn (the reference's own init
+    zeroes the head, which would make every logit 0). fp32 on the CPU, the reference's CPU numerics."""
+    from streamvoxel.models.unconditional_md4_timefree import UnconditionalMD4DiT
+    from streamvoxel.models.compact_controlnet import CompactStreamingControlNet
+    from streamvoxel.stream.condition import ModelSpec, Item
+    from streamvoxel.stream.engine import unpadded_logits, encode_item
+    from streamvoxel.stream.fast_ops import FastSlotForward
+
+    cfg = dict(num_classes=5, voxel_shape=(16, 16, 16), hidden_dim=48, depth=3, num_heads=4, time_free=True)
+    base = _reinit(UnconditionalMD4DiT(**cfg), 0.05, 11)
+    tokens = torch.randint(6, (2, 16, 16, 16), generator=torch.Generator().manual_seed(12))
+    logits = base(tokens, timestep=torch.ones(2))
+    _save('dit_tiny.npz', tokens=tokens.numpy(), logits=logits.numpy(),
+          **{'sd.' + k: v for k, v in _state(base).items()})
+    with torch.autocast('cpu', dtype=torch.bfloat16):
+        cpu_bf16 = base(tokens, timestep=torch.ones(2)).float()
+    _save('dit_tiny_cpu_autocast.npz', logits=cpu_bf16.numpy())
+
+    torch.manual_seed(5)
+    base = UnconditionalMD4DiT(num_classes=3, voxel_shape=(16, 16, 16), hidden_dim=48, depth=5, num_heads=4, time_free=True)
+    model = CompactStreamingControlNet(base, control_depth=3, control_hidden_dim=24, checkpointing=False,
+                                       biome_halo=4, biome_patch=2, struct_classes=0)
+    _reinit(model, 0.05, 13)
+    spec = ModelSpec(height=16, tile=16, num_classes=3, biome_classes=66, biome_halo=4, y_origin=-64.)
+    rng = np.random.default_rng(1)
+    items = []
+    for n1, n2, seed in ((1, 2, 1), (3, 3, 2), (0, 2, 3)):
+        l1 = rng.integers(0, 3, (n1, 16, 16, 16)).astype(np.int16)
+        l2 = rng.integers(0, 3, (n2, 16, 16, 16)).astype(np.int16)
+        xz1 = np.asarray([[-16, 0], [16, 0], [0, 16]][:n1], np.int64).reshape(-1, 2)
+        xz2 = np.asarray([[-32, 0], [32, 16], [0, -32]][:n2], np.int64).reshape(-1, 2)
+        biomes = np.zeros((4, 12, 12), np.int64)
+        biomes[:, 3:9, 3:9] = rng.integers(0, 66, (4, 6, 6))
+        items.append(Item(f'i{seed}', seed, 8, 1.0, l1, xz1, l2, xz2, biomes, None))
+    tokens = torch.randint(4, (3, 16, 16, 16), generator=torch.Generator().manual_seed(14))
+    out = {'sd.' + k: v for k, v in _state(model).items()}
+    engine = FastSlotForward(model, spec, 'cpu', 3, 3, 3, patchify='gather', attention='sdpa', capture=False)
+    for i, item in enumerate(items):
+        want = unpadded_logits(model, item, spec, tokens[i:i + 1], torch.ones(1))[0]
+        layers = engine.encode(item)
+        out[f'i{i}_logits'] = want.numpy()
+        out[f'i{i}_l1'], out[f'i{i}_l1_xz'] = item.l1_blocks, item.l1_xz
+        out[f'i{i}_l2'], out[f'i{i}_l2_xz'] = item.l2_blocks, item.l2_xz
+        out[f'i{i}_biomes'] = item.biomes
+        out[f'i{i}_k0'], out[f'i{i}_v0'] = layers[0][0][0].numpy(), layers[0][1][0].numpy()
+        out[f'i{i}_k2'], out[f'i{i}_v2'] = layers[2][0][0].numpy(), layers[2][1][0].numpy()
+        engine.load_slot(i, item)
+    engine.tokens.copy_(tokens)
+    packed = engine.eager(torch.ones(3))
+    out['packed_logits'] = packed.numpy()
+    out['lengths'] = engine.packed.lengths.numpy()
+    out['tokens'] = tokens.numpy()
+    out['layer_indices'] = np.asarray(model.layer_indices, np.int64)
+    _save('control_tiny.npz', **out)
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument('--reference', required=True)
+    args = parser.parse_args()
+    sys.path.insert(0, os.path.abspath(args.reference))
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    quota_cases()
+    top_mask_cases()
+    schedule_cases()
+    score_cases()
+    slot_cases()
+    model_cases()
+
+
+if __name__ == '__main__':
+    main()
