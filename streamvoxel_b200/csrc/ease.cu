@@ -1,0 +1,755 @@
+// EASE sampler kernels: entropy scores, low-entropy-last marking, 4^3 block-quota selection, categorical draw.
+//
+// Logits are class-major per slot, [classes][voxels] (the reference's [V,Y,Z,X], `streamvoxel/stream/fast_ops.py:307`),
+// so a warp reading one class for 32 x VPT consecutive voxels issues fully coalesced 16-byte loads.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace svx {
+namespace {
+
+constexpr int kScoreThreads = 256;
+constexpr int kSelectThreads = 1024;
+
+// ----------------------------------------------------------------------------------------------- scores
+
+template <typename T, int VPT> struct Vec;
+template <> struct Vec<uint16_t, 8> {
+  static __device__ __forceinline__ void load(const uint16_t* p, float (&x)[8]) {
+    uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __uint_as_float(w[i] << 16);
+      x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+};
+template <> struct Vec<float, 4> {
+  static __device__ __forceinline__ void load(const float* p, float (&x)[4]) {
+    float4 raw = *reinterpret_cast<const float4*>(p);
+    x[0] = raw.x; x[1] = raw.y; x[2] = raw.z; x[3] = raw.w;
+  }
+};
+
+// Online softmax statistics over the class axis: m = running max, s = sum e^(x-m), t = sum e^(x-m) (x-m).
+// Rescaling to a new max m': t' = e^d (t + d s), s' = e^d s with d = m - m' (exact identity).
+struct Stats {
+  float m, s, t;
+  __device__ __forceinline__ void init() { m = -INFINITY; s = 0.f; t = 0.f; }
+  __device__ __forceinline__ void rescale(float new_max) {
+    if (new_max > m) {
+      float d = (m == -INFINITY) ? 0.f : m - new_max;
+      float scale = expf(d);
+      t = scale * (t + d * s);
+      s = scale * s;
+      m = new_max;
+    }
+  }
+  __device__ __forceinline__ void add(float x) {
+    float z = x - m;
+    float e = expf(z);
+    s += e;
+    t = fmaf(e, z, t);
+  }
+};
+
+// Negative entropy sum_c p log p = t/s - log s  (== `(logp.exp()*logp).sum(0)`, `sampling/entropy.py:3-4`).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kScoreThreads) ease_scores_kernel(const T* __restrict__ logits, int classes,
+                                                                    int voxels, int64_t slot_stride,
+                                                                    float* __restrict__ scores,
+                                                                    uint32_t* __restrict__ status) {
+  const int slot = blockIdx.y;
+  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * VPT;
+  if (n0 >= voxels) return;
+  const T* base = logits + slot * slot_stride + n0;
+  Stats st[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) st[v].init();
+  constexpr int CH = 4;
+  int c = 0;
+  for (; c + CH <= classes; c += CH) {
+    float x[CH][VPT];
+#pragma unroll
+    for (int j = 0; j < CH; ++j) Vec<T, VPT>::load(base + (int64_t)(c + j) * voxels, x[j]);
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      float cm = fmaxf(fmaxf(x[0][v], x[1][v]), fmaxf(x[2][v], x[3][v]));
+      st[v].rescale(cm);
+#pragma unroll
+      for (int j = 0; j < CH; ++j) st[v].add(x[j][v]);
+    }
+  }
+  for (; c < classes; ++c) {
+    float x[VPT];
+    Vec<T, VPT>::load(base + (int64_t)c * voxels, x);
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      st[v].rescale(x[v]);
+      st[v].add(x[v]);
+    }
+  }
+  bool nan = false;
+  float out[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    out[v] = st[v].t / st[v].s - logf(st[v].s);
+    nan |= isnan(out[v]);
+  }
+  float* dst = scores + (int64_t)slot * voxels + n0;
+#pragma unroll
+  for (int v = 0; v < VPT; v += 4)
+    *reinterpret_cast<float4*>(dst + v) = make_float4(out[v], out[v + 1], out[v + 2], out[v + 3]);
+  if (nan && status) atomicOr(status + slot, SVX_STATUS_NAN_LOGITS);
+}
+
+// ----------------------------------------------------------------------------------------------- marking
+
+// good[n] = !(air(n) <= threshold), air = sum over air ids of softmax(logits)[a] (`stream/slot.py:126`).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kScoreThreads) ease_air_kernel(const T* __restrict__ logits, int classes, int voxels,
+                                                                 int64_t slot_stride, const int32_t* __restrict__ air_ids,
+                                                                 int n_air, float threshold, uint8_t* __restrict__ good) {
+  const int slot = blockIdx.y;
+  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * VPT;
+  if (n0 >= voxels) return;
+  const T* base = logits + slot * slot_stride + n0;
+  float m[VPT], s[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) { m[v] = -INFINITY; s[v] = 0.f; }
+  for (int c = 0; c < classes; ++c) {
+    float x[VPT];
+    Vec<T, VPT>::load(base + (int64_t)c * voxels, x);
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      if (x[v] > m[v]) {
+        s[v] = (m[v] == -INFINITY) ? 0.f : s[v] * expf(m[v] - x[v]);
+        m[v] = x[v];
+      }
+      s[v] += expf(x[v] - m[v]);
+    }
+  }
+  float air[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) air[v] = 0.f;
+  for (int a = 0; a < n_air; ++a) {
+    float x[VPT];
+    Vec<T, VPT>::load(base + (int64_t)air_ids[a] * voxels, x);
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) air[v] += expf(x[v] - m[v]) / s[v];
+  }
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) good[(int64_t)slot * voxels + n0 + v] = !(air[v] <= threshold);
+}
+
+// last[y,z,x] = good[y'..] for all y' >= y: the per-column top run (`low_entropy_last.py:11-13`, col=True).
+__global__ void ease_column_run_kernel(uint8_t* __restrict__ last, int height, int columns, int32_t* last_count) {
+  const int slot = blockIdx.x;
+  uint8_t* col = last + (int64_t)slot * height * columns;
+  int count = 0;
+  for (int c = threadIdx.x; c < columns; c += blockDim.x) {
+    bool run = true;
+    for (int y = height - 1; y >= 0; --y) {
+      run = run && col[(int64_t)y * columns + c];
+      col[(int64_t)y * columns + c] = run;
+      count += run;
+    }
+  }
+  __shared__ int total;
+  if (threadIdx.x == 0) total = 0;
+  __syncthreads();
+  atomicAdd(&total, count);
+  __syncthreads();
+  if (threadIdx.x == 0) last_count[slot] = total;
+}
+
+// ----------------------------------------------------------------------------------------------- selection
+
+struct BlockGeom {
+  int height, depth, width, nbz, nbx, blocks;
+  __device__ __forceinline__ int voxel(int j, int i) const {  // block j (YZX), in-block offset i (YZX, b = 4)
+    int by = j / (nbz * nbx), bz = (j / nbx) % nbz, bx = j % nbx;
+    int dy = i >> 4, dz = (i >> 2) & 3, dx = i & 3;
+    return ((by * 4 + dy) * depth + bz * 4 + dz) * width + bx * 4 + dx;
+  }
+};
+
+// Per-block quota (`block_quota.py:24-30` / `fast_ops.py:451-463`): float64 apportioning of the step goal over
+// blocks, the remainder to the blocks with the largest fractional part (seeded order `pos` breaks ties).
+__global__ void __launch_bounds__(kSelectThreads) ease_quota_kernel(const int16_t* __restrict__ tokens,
+                                                                    const uint8_t* __restrict__ last,
+                                                                    const int32_t* __restrict__ pos,
+                                                                    const svx_step_params* __restrict__ params,
+                                                                    BlockGeom g, int mask_id, int32_t* __restrict__ quota,
+                                                                    int32_t* __restrict__ got) {
+  const int slot = blockIdx.x;
+  const int j = threadIdx.x;
+  const int voxels = g.height * g.depth * g.width;
+  const svx_step_params p = params[slot];
+  __shared__ double keys[kSelectThreads];
+  __shared__ int ids[kSelectThreads];
+  __shared__ unsigned long long base_sum;
+  if (j == 0) { base_sum = 0; got[slot] = 0; }
+  __syncthreads();
+  long long base = 0;
+  double key = INFINITY;
+  const int16_t* tok = tokens + (int64_t)slot * voxels;
+  const uint8_t* lst = last + (int64_t)slot * voxels;
+  if (j < g.blocks && p.k > 0) {
+    int ntot = 0;
+    for (int i = 0; i < 64; ++i) ntot += !lst[g.voxel(j, i)];
+    double ideal = p.frac * (double)ntot;
+    base = (long long)floor(ideal + 1e-9);
+    key = -(ideal - (double)base) * 1e6 + (double)pos[(int64_t)slot * g.blocks + j];
+  }
+  atomicAdd(&base_sum, (unsigned long long)base);
+  keys[j] = key;
+  ids[j] = j;
+  __syncthreads();
+  // Bitonic sort of (key, id) ascending over the power-of-two padded block count.
+  int size = 1;
+  while (size < g.blocks) size <<= 1;
+  for (int k = 2; k <= size; k <<= 1) {
+    for (int stride = k >> 1; stride > 0; stride >>= 1) {
+      int partner = j ^ stride;
+      if (j < size && partner > j && partner < size) {
+        bool up = (j & k) == 0;
+        double ka = keys[j], kb = keys[partner];
+        int ia = ids[j], ib = ids[partner];
+        bool greater = ka > kb || (ka == kb && ia > ib);
+        if (greater == up) {
+          keys[j] = kb; keys[partner] = ka;
+          ids[j] = ib; ids[partner] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  long long extra = (long long)p.committed + p.k - (long long)base_sum;
+  if (extra < 0) extra = 0;
+  // ids[r] is the block of rank r; blocks with rank < extra get one more voxel.
+  if (j < g.blocks && p.k > 0) {
+    const int block = ids[j];
+    int lg = 0, nt = 0;
+    for (int i = 0; i < 64; ++i) {
+      int n = g.voxel(block, i);
+      bool nl = !lst[n];
+      nt += nl;
+      lg += nl && tok[n] == mask_id;
+    }
+    long long b = (long long)floor(p.frac * (double)nt + 1e-9);
+    long long target = b + (j < extra ? 1 : 0);
+    long long q = target - (nt - lg);
+    q = q < 0 ? 0 : q;
+    q = q > lg ? lg : q;
+    quota[(int64_t)slot * g.blocks + block] = (int32_t)q;
+  } else if (j < g.blocks) {
+    quota[(int64_t)slot * g.blocks + j] = 0;
+  }
+}
+
+// In-block ranking (`block_quota.py:31-33`): a warp per 4^3 block; voxel i is chosen when fewer than quota selectable
+// voxels of its block beat it (higher score, or equal score and lower in-block index: a stable descending sort).
+__global__ void ease_block_select_kernel(const float* __restrict__ scores, const int16_t* __restrict__ tokens,
+                                         const uint8_t* __restrict__ last, const int32_t* __restrict__ quota,
+                                         const svx_step_params* __restrict__ params, BlockGeom g, int mask_id,
+                                         uint8_t* __restrict__ chosen, int32_t* __restrict__ got) {
+  const int slot = blockIdx.y;
+  const int j = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (j >= g.blocks) return;
+  const int lane = lane_id();
+  const int voxels = g.height * g.depth * g.width;
+  const int64_t off = (int64_t)slot * voxels;
+  const int q = params[slot].k > 0 ? quota[(int64_t)slot * g.blocks + j] : 0;
+  int n[2];
+  float sm[2];
+  bool sel[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    n[h] = g.voxel(j, lane + 32 * h);
+    sel[h] = !last[off + n[h]] && tokens[off + n[h]] == mask_id;
+    sm[h] = sel[h] ? scores[off + n[h]] : -INFINITY;
+  }
+  int rank[2] = {0, 0};
+#pragma unroll 4
+  for (int l = 0; l < 64; ++l) {
+    float other = __shfl_sync(0xffffffffu, l < 32 ? sm[0] : sm[1], l & 31);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int i = lane + 32 * h;
+      rank[h] += (other > sm[h]) || (other == sm[h] && l < i);
+    }
+  }
+  int count = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    bool c = sel[h] && rank[h] < q;
+    chosen[off + n[h]] = c;
+    count += c;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) count += __shfl_xor_sync(0xffffffffu, count, o);
+  if (lane == 0 && count) atomicAdd(got + slot, count);
+}
+
+__device__ __forceinline__ uint64_t order_key(float score, int n) {
+  uint32_t u = __float_as_uint(score);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (uint64_t(u) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(n));
+}
+
+// Global trim / top-up (`block_quota.py:34-37`, `top_mask` `:4-12`) when the clamped block quotas miss k, then the
+// ascending compaction of the chosen voxels (`nonzero_static`, `fast_ops.py:548`) and the quota check (`:540`).
+// The fix-up is a radix select over the 64-bit key (score order, then lower voxel index first).
+__global__ void __launch_bounds__(kSelectThreads) ease_fixup_compact_kernel(
+    const float* __restrict__ scores, const int16_t* __restrict__ tokens, const uint8_t* __restrict__ last,
+    const svx_step_params* __restrict__ params, int voxels, int mask_id, uint8_t* __restrict__ chosen,
+    int32_t* __restrict__ got, int32_t* __restrict__ index_out, int index_capacity, int32_t* __restrict__ chosen_count,
+    uint32_t* __restrict__ status) {
+  const int slot = blockIdx.x;
+  const int t = threadIdx.x;
+  const int64_t off = (int64_t)slot * voxels;
+  const int k = params[slot].k;
+  const int have = got[slot];
+  __shared__ uint32_t hist[256];
+  __shared__ unsigned long long prefix, prefix_mask;
+  __shared__ int remaining, candidates;
+  __shared__ int scan[kSelectThreads];
+  if (k > 0 && have != k) {
+    const bool trim = have > k;  // trim: keep the best k of the chosen; top-up: add the best k-have of the rest
+    if (t == 0) { prefix = 0; prefix_mask = 0; remaining = trim ? k : k - have; candidates = 0; }
+    __syncthreads();
+    int mine = 0;
+    for (int n = t; n < voxels; n += blockDim.x) {
+      bool sel = !last[off + n] && tokens[off + n] == mask_id;
+      bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
+      mine += cand;
+    }
+    atomicAdd(&candidates, mine);
+    __syncthreads();
+    const bool take_all = remaining >= candidates;
+    if (!take_all && remaining > 0) {
+      for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int i = t; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int n = t; n < voxels; n += blockDim.x) {
+          bool sel = !last[off + n] && tokens[off + n] == mask_id;
+          bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
+          if (!cand) continue;
+          uint64_t key = order_key(scores[off + n], n);
+          if ((key & prefix_mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (t == 0) {
+          int acc = 0;
+          for (int d = 255; d >= 0; --d) {
+            int c = (int)hist[d];
+            if (acc + c >= remaining) {
+              remaining -= acc;
+              prefix |= (unsigned long long)d << shift;
+              prefix_mask |= 255ull << shift;
+              break;
+            }
+            acc += c;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    // prefix is now the key of the remaining-th best candidate; candidates at or above it are taken.
+    for (int n = t; n < voxels; n += blockDim.x) {
+      bool sel = !last[off + n] && tokens[off + n] == mask_id;
+      bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
+      bool take = cand && (take_all || (remaining > 0 && order_key(scores[off + n], n) >= prefix));
+      if (trim && cand && !take) chosen[off + n] = 0;
+      if (!trim && take) chosen[off + n] = 1;
+    }
+    __syncthreads();
+  }
+  // Ascending compaction: thread t owns voxels [t*per, (t+1)*per).
+  const int per = (voxels + blockDim.x - 1) / blockDim.x;
+  const int lo = min(voxels, t * per), hi = min(voxels, lo + per);
+  int count = 0;
+  bool bad = false;
+  for (int n = lo; n < hi; ++n) {
+    if (chosen[off + n]) {
+      ++count;
+      bad |= last[off + n] || tokens[off + n] != mask_id;
+    }
+  }
+  scan[t] = count;
+  __syncthreads();
+  for (int s = 1; s < (int)blockDim.x; s <<= 1) {  // Hillis-Steele inclusive scan
+    int v = t >= s ? scan[t - s] : 0;
+    __syncthreads();
+    scan[t] += v;
+    __syncthreads();
+  }
+  int w = scan[t] - count;
+  for (int n = lo; n < hi; ++n)
+    if (chosen[off + n]) {
+      if (w < index_capacity) index_out[(int64_t)slot * index_capacity + w] = n;
+      ++w;
+    }
+  const int total = scan[blockDim.x - 1];
+  for (int i = total + t; i < index_capacity; i += blockDim.x) index_out[(int64_t)slot * index_capacity + i] = -1;
+  bad = __syncthreads_or(bad);
+  if (t == 0) {
+    chosen_count[slot] = total;
+    got[slot] = total;
+    if ((bad || total != k) && status) atomicOr(status + slot, SVX_STATUS_QUOTA_MISSED);
+  }
+}
+
+// ----------------------------------------------------------------------------------------------- sampling
+
+// Row softmax in torch's CUDA order (persistent warp softmax for rows of <= 1024 fp32 elements): W = min(npot, 32)
+// lanes, element it*W + lane in register it, per-lane max then butterfly max, per-lane sum of expf(x - max) in
+// register order then butterfly sum, p = e / sum.
+template <int ITER>
+__device__ __forceinline__ void torch_softmax_lane(const float (&x)[ITER], int width, float (&p)[ITER]) {
+  float m = x[0];
+#pragma unroll
+  for (int it = 1; it < ITER; ++it) m = (m > x[it]) ? m : x[it];
+  for (int o = width >> 1; o > 0; o >>= 1) {
+    float b = __shfl_xor_sync(0xffffffffu, m, o, width);
+    m = (m < b) ? b : m;
+  }
+  float s = 0.f;
+  float e[ITER];
+#pragma unroll
+  for (int it = 0; it < ITER; ++it) {
+    e[it] = expf(x[it] - m);
+    s += e[it];
+  }
+  for (int o = width >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o, width);
+#pragma unroll
+  for (int it = 0; it < ITER; ++it) p[it] = e[it] / s;
+}
+
+__device__ __forceinline__ void argmax_merge(float& val, int& idx, float v2, int i2) {
+  bool better = (v2 > val) || (v2 == val && i2 < idx) || (isnan(v2) && !isnan(val));
+  if (better) { val = v2; idx = i2; }
+}
+
+template <typename T, int ITER>
+__global__ void ease_sample_parity_kernel(const T* __restrict__ logits, int classes, int voxels, int64_t slot_stride,
+                                          const int32_t* __restrict__ index, const svx_step_params* __restrict__ params,
+                                          const float* __restrict__ noise, int64_t noise_slot_stride, int index_capacity,
+                                          int width, int16_t* __restrict__ tokens, int16_t* __restrict__ values_out,
+                                          uint32_t* __restrict__ status) {
+  const int slot = blockIdx.y;
+  const int warps = blockDim.x >> 5;
+  const int i = blockIdx.x * warps + warp_id();
+  const int k = params[slot].k;
+  if (i >= k || i >= index_capacity) return;
+  const int lane = lane_id();
+  const int n = index[(int64_t)slot * index_capacity + i];
+  if (n < 0) return;
+  const T* col = logits + slot * slot_stride + n;
+  const float* q = noise + slot * noise_slot_stride + (int64_t)i * classes;
+  float x[ITER], p[ITER];
+#pragma unroll
+  for (int it = 0; it < ITER; ++it) {
+    int c = it * width + lane;
+    x[it] = (lane < width && c < classes) ? load_as_f32(col + (int64_t)c * voxels) : -INFINITY;
+  }
+  torch_softmax_lane<ITER>(x, width, p);
+  float best = -INFINITY;
+  int arg = 0x7fffffff;
+  bool nan = false;
+#pragma unroll
+  for (int it = 0; it < ITER; ++it) {
+    int c = it * width + lane;
+    if (lane < width && c < classes) {
+      float r = p[it] / q[c];
+      nan |= isnan(p[it]);
+      argmax_merge(best, arg, r, c);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float b = __shfl_xor_sync(0xffffffffu, best, o);
+    int a = __shfl_xor_sync(0xffffffffu, arg, o);
+    argmax_merge(best, arg, b, a);
+  }
+  nan = __any_sync(0xffffffffu, nan);
+  if (lane == 0) {
+    tokens[(int64_t)slot * voxels + n] = (int16_t)arg;
+    values_out[(int64_t)slot * index_capacity + i] = (int16_t)arg;
+    if (nan && status) atomicOr(status + slot, SVX_STATUS_NAN_LOGITS);
+  }
+}
+
+// Philox4x32-10 (Salmon et al., SC 2011): ten rounds, key bumped by the Weyl constants between rounds.
+__device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    if (r) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
+    uint32_t hi0 = __umulhi(0xD2511F53u, c[0]), lo0 = 0xD2511F53u * c[0];
+    uint32_t hi1 = __umulhi(0xCD9E8D57u, c[2]), lo1 = 0xCD9E8D57u * c[2];
+    uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+  }
+}
+
+constexpr uint32_t kNativeStream = 0x53564F58u;
+
+// Native draw: argmax_v e^(x_v - max) / E_v, E_v = -log(u_v), u from Philox keyed by (seed, step, voxel, class).
+// Lane L owns class groups g = L, L+32, ... of 4 consecutive classes, so each Philox call feeds 4 classes.
+template <typename T>
+__global__ void ease_sample_native_kernel(const T* __restrict__ logits, int classes, int voxels, int64_t slot_stride,
+                                          const int32_t* __restrict__ index, const svx_step_params* __restrict__ params,
+                                          int index_capacity, int16_t* __restrict__ tokens,
+                                          int16_t* __restrict__ values_out, uint32_t* __restrict__ status) {
+  const int slot = blockIdx.y;
+  const int warps = blockDim.x >> 5;
+  const int i = blockIdx.x * warps + warp_id();
+  const svx_step_params p = params[slot];
+  if (i >= p.k || i >= index_capacity) return;
+  const int lane = lane_id();
+  const int n = index[(int64_t)slot * index_capacity + i];
+  if (n < 0) return;
+  const T* col = logits + slot * slot_stride + n;
+  const int groups = (classes + 3) >> 2;
+  float m = -INFINITY;
+  for (int c = lane; c < classes; c += 32) m = fmaxf(m, load_as_f32(col + (int64_t)c * voxels));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float best = -INFINITY;
+  int arg = 0x7fffffff;
+  bool nan = isnan(m);
+  for (int g = lane; g < groups; g += 32) {
+    uint32_t w[4] = {(uint32_t)g, (uint32_t)n, (uint32_t)p.step, kNativeStream};
+    philox4x32_10(w, (uint32_t)p.seed, (uint32_t)(p.seed >> 32));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int c = g * 4 + j;
+      if (c >= classes) break;
+      float u = ((float)(w[j] >> 8) + 0.5f) * 5.9604644775390625e-08f;  // 2^-24
+      float race = -logf(u);
+      float e = expf(load_as_f32(col + (int64_t)c * voxels) - m);
+      argmax_merge(best, arg, e / race, c);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float b = __shfl_xor_sync(0xffffffffu, best, o);
+    int a = __shfl_xor_sync(0xffffffffu, arg, o);
+    argmax_merge(best, arg, b, a);
+  }
+  if (lane == 0) {
+    tokens[(int64_t)slot * voxels + n] = (int16_t)arg;
+    values_out[(int64_t)slot * index_capacity + i] = (int16_t)arg;
+    if (nan && status) atomicOr(status + slot, SVX_STATUS_NAN_LOGITS);
+  }
+}
+
+template <int ITER>
+__global__ void softmax_rows_kernel(const float* __restrict__ x, int rows, int classes, int width,
+                                    float* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (row >= rows) return;
+  const int lane = lane_id();
+  float v[ITER], p[ITER];
+#pragma unroll
+  for (int it = 0; it < ITER; ++it) {
+    int c = it * width + lane;
+    v[it] = (lane < width && c < classes) ? x[(int64_t)row * classes + c] : -INFINITY;
+  }
+  torch_softmax_lane<ITER>(v, width, p);
+#pragma unroll
+  for (int it = 0; it < ITER; ++it) {
+    int c = it * width + lane;
+    if (lane < width && c < classes) out[(int64_t)row * classes + c] = p[it];
+  }
+}
+
+__global__ void ease_finish_kernel(int16_t* __restrict__ tokens, const uint8_t* __restrict__ last,
+                                   const uint8_t* __restrict__ finish, int voxels, int air_token) {
+  const int slot = blockIdx.y;
+  if (!finish[slot]) return;
+  const int64_t off = (int64_t)slot * voxels;
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < voxels; n += gridDim.x * blockDim.x)
+    if (last[off + n]) tokens[off + n] = (int16_t)air_token;
+}
+
+// Torch's persistent softmax geometry for a row of `classes` elements: lanes and registers per lane.
+void softmax_geometry(int classes, int& width, int& iters) {
+  int npot = 1;
+  while (npot < classes) npot <<= 1;
+  width = npot < 32 ? npot : 32;
+  iters = npot / width;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace svx
+
+using namespace svx;
+
+extern "C" int svx_ease_scores(const void* logits, int dtype, int slots, int classes, int voxels,
+                               int64_t logit_slot_stride, float* scores, uint32_t* status, void* stream) {
+  SVX_REQUIRE(logits && scores && slots > 0 && classes > 0 && voxels > 0, "svx_ease_scores: bad arguments");
+  SVX_REQUIRE(aligned16(logits) && aligned16(scores), "svx_ease_scores: logits and scores must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == SVX_BF16) {
+    SVX_REQUIRE(voxels % 8 == 0 && logit_slot_stride % 8 == 0, "svx_ease_scores: voxels must be a multiple of 8");
+    dim3 grid((voxels / 8 + kScoreThreads - 1) / kScoreThreads, slots);
+    ease_scores_kernel<uint16_t, 8><<<grid, kScoreThreads, 0, s>>>(static_cast<const uint16_t*>(logits), classes,
+                                                                 voxels, logit_slot_stride, scores, status);
+  } else if (dtype == SVX_F32) {
+    SVX_REQUIRE(voxels % 4 == 0 && logit_slot_stride % 4 == 0, "svx_ease_scores: voxels must be a multiple of 4");
+    dim3 grid((voxels / 4 + kScoreThreads - 1) / kScoreThreads, slots);
+    ease_scores_kernel<float, 4><<<grid, kScoreThreads, 0, s>>>(static_cast<const float*>(logits), classes, voxels,
+                                                              logit_slot_stride, scores, status);
+  } else {
+    return fail(SVX_ERR_INVALID, "svx_ease_scores: dtype must be SVX_F32 or SVX_BF16");
+  }
+  return launch_status("ease_scores_kernel");
+}
+
+extern "C" int svx_ease_mark(const void* logits, int dtype, int slots, int classes, int height, int depth, int width,
+                             int64_t logit_slot_stride, const int32_t* air_ids, int n_air, double last_eps,
+                             uint8_t* last, int32_t* last_count, void* stream) {
+  const int voxels = height * depth * width;
+  SVX_REQUIRE(logits && last && last_count && air_ids && n_air > 0 && slots > 0 && voxels > 0,
+              "svx_ease_mark: bad arguments");
+  SVX_REQUIRE(aligned16(logits), "svx_ease_mark: logits must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  const float threshold = (float)(1.0 - last_eps);  // torch compares the fp32 tensor with the scalar cast to fp32
+  if (dtype == SVX_BF16) {
+    SVX_REQUIRE(voxels % 8 == 0 && logit_slot_stride % 8 == 0, "svx_ease_mark: voxels must be a multiple of 8");
+    dim3 grid((voxels / 8 + kScoreThreads - 1) / kScoreThreads, slots);
+    ease_air_kernel<uint16_t, 8><<<grid, kScoreThreads, 0, s>>>(static_cast<const uint16_t*>(logits), classes, voxels,
+                                                              logit_slot_stride, air_ids, n_air, threshold, last);
+  } else if (dtype == SVX_F32) {
+    SVX_REQUIRE(voxels % 4 == 0 && logit_slot_stride % 4 == 0, "svx_ease_mark: voxels must be a multiple of 4");
+    dim3 grid((voxels / 4 + kScoreThreads - 1) / kScoreThreads, slots);
+    ease_air_kernel<float, 4><<<grid, kScoreThreads, 0, s>>>(static_cast<const float*>(logits), classes, voxels,
+                                                           logit_slot_stride, air_ids, n_air, threshold, last);
+  } else {
+    return fail(SVX_ERR_INVALID, "svx_ease_mark: dtype must be SVX_F32 or SVX_BF16");
+  }
+  int rc = launch_status("ease_air_kernel");
+  if (rc) return rc;
+  ease_column_run_kernel<<<slots, 256, 0, s>>>(last, height, depth * width, last_count);
+  return launch_status("ease_column_run_kernel");
+}
+
+extern "C" size_t svx_ease_select_workspace_bytes(int slots, int voxels) {
+  return (size_t)slots * (voxels / 64 + 1) * sizeof(int32_t);
+}
+
+extern "C" int svx_ease_select(const float* scores, const int16_t* tokens, const uint8_t* last, const int32_t* pos,
+                               const svx_step_params* params, int slots, int height, int depth, int width, int block,
+                               int mask_id, uint8_t* chosen, int32_t* index_out, int index_capacity,
+                               int32_t* chosen_count, uint32_t* status, void* workspace, void* stream) {
+  SVX_REQUIRE(block == 4, "svx_ease_select: only 4^3 blocks are implemented");
+  SVX_REQUIRE(height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 && height > 0 && depth > 0 && width > 0,
+              "svx_ease_select: shape must be a positive multiple of 4");
+  const int voxels = height * depth * width;
+  BlockGeom g{height, depth, width, depth / 4, width / 4, voxels / 64};
+  SVX_REQUIRE(g.blocks <= kSelectThreads, "svx_ease_select: at most 1024 blocks per column");
+  SVX_REQUIRE(scores && tokens && last && pos && params && chosen && index_out && chosen_count && workspace &&
+                  slots > 0 && index_capacity > 0,
+              "svx_ease_select: bad arguments");
+  cudaStream_t s = as_stream(stream);
+  int32_t* quota = static_cast<int32_t*>(workspace);
+  int32_t* got = quota + (size_t)slots * g.blocks;
+  ease_quota_kernel<<<slots, kSelectThreads, 0, s>>>(tokens, last, pos, params, g, mask_id, quota, got);
+  int rc = launch_status("ease_quota_kernel");
+  if (rc) return rc;
+  const int warps = 8;
+  dim3 grid((g.blocks + warps - 1) / warps, slots);
+  ease_block_select_kernel<<<grid, warps * 32, 0, s>>>(scores, tokens, last, quota, params, g, mask_id, chosen, got);
+  rc = launch_status("ease_block_select_kernel");
+  if (rc) return rc;
+  ease_fixup_compact_kernel<<<slots, kSelectThreads, 0, s>>>(scores, tokens, last, params, voxels, mask_id, chosen, got,
+                                                            index_out, index_capacity, chosen_count, status);
+  return launch_status("ease_fixup_compact_kernel");
+}
+
+template <typename T>
+static int launch_parity(const T* logits, int classes, int voxels, int64_t stride, const int32_t* index,
+                         const svx_step_params* params, const float* noise, int64_t noise_stride, int cap, int slots,
+                         int16_t* tokens, int16_t* values, uint32_t* status, cudaStream_t s) {
+  int width, iters;
+  softmax_geometry(classes, width, iters);
+  const int warps = 8;
+  dim3 grid((cap + warps - 1) / warps, slots);
+#define SVX_PARITY(I)                                                                                            \
+  case I:                                                                                                        \
+    ease_sample_parity_kernel<T, I><<<grid, warps * 32, 0, s>>>(logits, classes, voxels, stride, index, params,  \
+                                                                noise, noise_stride, cap, width, tokens, values, \
+                                                                status);                                         \
+    break;
+  switch (iters) {
+    SVX_PARITY(1) SVX_PARITY(2) SVX_PARITY(4) SVX_PARITY(8) SVX_PARITY(16) SVX_PARITY(32)
+    default: return fail(SVX_ERR_INVALID, "svx_ease_sample: at most 1024 classes");
+  }
+#undef SVX_PARITY
+  return launch_status("ease_sample_parity_kernel");
+}
+
+extern "C" int svx_ease_sample(const void* logits, int dtype, int slots, int classes, int voxels,
+                               int64_t logit_slot_stride, const int32_t* index, const svx_step_params* params,
+                               const float* noise, int64_t noise_slot_stride, int index_capacity, int16_t* tokens,
+                               int16_t* values_out, uint32_t* status, void* stream) {
+  SVX_REQUIRE(logits && index && params && tokens && values_out && slots > 0 && classes > 0 && classes <= 1024 &&
+                  index_capacity > 0,
+              "svx_ease_sample: bad arguments");
+  cudaStream_t s = as_stream(stream);
+  if (noise) {
+    if (dtype == SVX_BF16)
+      return launch_parity(static_cast<const uint16_t*>(logits), classes, voxels, logit_slot_stride, index, params,
+                           noise, noise_slot_stride, index_capacity, slots, tokens, values_out, status, s);
+    if (dtype == SVX_F32)
+      return launch_parity(static_cast<const float*>(logits), classes, voxels, logit_slot_stride, index, params, noise,
+                           noise_slot_stride, index_capacity, slots, tokens, values_out, status, s);
+    return fail(SVX_ERR_INVALID, "svx_ease_sample: dtype must be SVX_F32 or SVX_BF16");
+  }
+  const int warps = 8;
+  dim3 grid((index_capacity + warps - 1) / warps, slots);
+  if (dtype == SVX_BF16)
+    ease_sample_native_kernel<uint16_t><<<grid, warps * 32, 0, s>>>(static_cast<const uint16_t*>(logits), classes,
+                                                                   voxels, logit_slot_stride, index, params,
+                                                                   index_capacity, tokens, values_out, status);
+  else if (dtype == SVX_F32)
+    ease_sample_native_kernel<float><<<grid, warps * 32, 0, s>>>(static_cast<const float*>(logits), classes, voxels,
+                                                                logit_slot_stride, index, params, index_capacity,
+                                                                tokens, values_out, status);
+  else
+    return fail(SVX_ERR_INVALID, "svx_ease_sample: dtype must be SVX_F32 or SVX_BF16");
+  return launch_status("ease_sample_native_kernel");
+}
+
+extern "C" int svx_softmax_rows(const float* x, int rows, int classes, float* out, void* stream) {
+  SVX_REQUIRE(x && out && rows > 0 && classes > 0 && classes <= 1024, "svx_softmax_rows: bad arguments");
+  int width, iters;
+  softmax_geometry(classes, width, iters);
+  const int warps = 8;
+  const int grid = (rows + warps - 1) / warps;
+  cudaStream_t s = as_stream(stream);
+  switch (iters) {
+    case 1: softmax_rows_kernel<1><<<grid, warps * 32, 0, s>>>(x, rows, classes, width, out); break;
+    case 2: softmax_rows_kernel<2><<<grid, warps * 32, 0, s>>>(x, rows, classes, width, out); break;
+    case 4: softmax_rows_kernel<4><<<grid, warps * 32, 0, s>>>(x, rows, classes, width, out); break;
+    case 8: softmax_rows_kernel<8><<<grid, warps * 32, 0, s>>>(x, rows, classes, width, out); break;
+    case 16: softmax_rows_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, classes, width, out); break;
+    case 32: softmax_rows_kernel<32><<<grid, warps * 32, 0, s>>>(x, rows, classes, width, out); break;
+    default: return fail(SVX_ERR_INVALID, "svx_softmax_rows: at most 1024 classes");
+  }
+  return launch_status("softmax_rows_kernel");
+}
+
+extern "C" int svx_ease_finish(int16_t* tokens, const uint8_t* last, const uint8_t* finish, int slots, int voxels,
+                               int air_token, void* stream) {
+  SVX_REQUIRE(tokens && last && finish && slots > 0 && voxels > 0, "svx_ease_finish: bad arguments");
+  dim3 grid(64, slots);
+  ease_finish_kernel<<<grid, 256, 0, as_stream(stream)>>>(tokens, last, finish, voxels, air_token);
+  return launch_status("ease_finish_kernel");
+}

@@ -1,0 +1,186 @@
+// Patch-4 token embed (both branches in one pass) and LayerNorm + AdaLN modulate.
+#include <math.h>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace svx {
+namespace {
+
+__device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 raw) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    acc[2 * j] += __uint_as_float(w[j] << 16);
+    acc[2 * j + 1] += __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ void unpack_bf16x8(uint4 raw, float (&v)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = __uint_as_float(w[j] << 16);
+    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w[j] = (uint32_t)f32_to_bf16(v[2 * j]) | ((uint32_t)f32_to_bf16(v[2 * j + 1]) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// out[p] = bf16(bf16(bf16(sum_o T[t_o * 64 + o]) + bias) + add[p]): the gather form of the one-hot Conv3d
+// (`streamvoxel/stream/fast_ops.py:69-75`: fp32 accumulation over the 64 patch offsets, the conv bias added in bf16),
+// then the per-position y-embedding (`fast_ops.py:282-283`). One CTA per patch, 8 channels per thread.
+__global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int height, int depth, int width, int classes,
+                                   int d, const uint16_t* __restrict__ table_b, const uint16_t* __restrict__ bias_b,
+                                   const uint16_t* __restrict__ add_b, uint16_t* __restrict__ out_b,
+                                   const uint16_t* __restrict__ table_c, const uint16_t* __restrict__ bias_c,
+                                   const uint16_t* __restrict__ add_c, uint16_t* __restrict__ out_c) {
+  constexpr int P = 4, P3 = 64;
+  const int gz = depth / P, gx = width / P;
+  const int patches = (height / P) * gz * gx;
+  const int row = blockIdx.x;  // slot * patches + p
+  const int slot = row / patches, p = row % patches;
+  const int py = p / (gz * gx), pz = (p / gx) % gz, px = p % gx;
+  __shared__ int rows[P3];
+  if (threadIdx.x < P3) {
+    const int o = threadIdx.x, oy = o >> 4, oz = (o >> 2) & 3, ox = o & 3;
+    const int64_t voxel = (((int64_t)slot * height + py * P + oy) * depth + pz * P + oz) * width + px * P + ox;
+    int t = tokens[voxel];
+    t = t < 0 ? 0 : (t > classes ? classes : t);  // out-of-vocabulary ids clamp instead of reading out of bounds
+    rows[o] = t * P3 + o;
+  }
+  __syncthreads();
+  const int c0 = threadIdx.x * 8;
+  if (c0 >= d) return;
+  for (int branch = 0; branch < 2; ++branch) {
+    const uint16_t* table = branch ? table_c : table_b;
+    if (!table) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int o = 0; o < P3; ++o) add_bf16x8(acc, *reinterpret_cast<const uint4*>(table + (int64_t)rows[o] * d + c0));
+    float bias[8], add[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>((branch ? bias_c : bias_b) + c0), bias);
+    unpack_bf16x8(*reinterpret_cast<const uint4*>((branch ? add_c : add_b) + (int64_t)p * d + c0), add);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = round_bf16(round_bf16(round_bf16(acc[j]) + bias[j]) + add[j]);
+    *reinterpret_cast<uint4*>((branch ? out_c : out_b) + (int64_t)row * d + c0) = pack_bf16x8(acc);
+  }
+}
+
+// LayerNorm (no affine; fp32 statistics, `unconditional_md4_timefree.py:53-54`) and the AdaLN modulate
+// x * (1 + scale) + shift in fp32 (`:12-13`), rounded to bf16 where the next linear casts its input.
+// One warp per row; lane L holds the 8-channel chunks L, L+32, ... (d % 8 == 0, at most 32*PER chunks).
+template <int PER>
+__global__ void layernorm_modulate_kernel(const uint16_t* __restrict__ x, int rows, int d, float eps,
+                                          const uint16_t* __restrict__ ops, const uint16_t* __restrict__ shift,
+                                          uint16_t* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (row >= rows) return;
+  const int lane = lane_id();
+  const int chunks = d >> 3;
+  const uint16_t* src = x + (int64_t)row * d;
+  float v[PER][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = i * 32 + lane;
+    if (c < chunks) {
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(src + c * 8), v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[i][j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / d;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    if (i * 32 + lane < chunks) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float c = v[i][j] - mean;
+        var += c * c;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float rstd = rsqrtf(var / d + eps);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = i * 32 + lane;
+    if (c >= chunks) continue;
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = (v[i][j] - mean) * rstd;
+    if (ops) {
+      float s[8], b[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(ops + c * 8), s);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(shift + c * 8), b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = __fadd_rn(__fmul_rn(y[j], s[j]), b[j]);
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)row * d + c * 8) = pack_bf16x8(y);
+  }
+}
+
+}  // namespace
+
+int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int width, int classes, int d,
+                    const uint16_t* table_b, const uint16_t* bias_b, const uint16_t* add_b, uint16_t* out_b,
+                    const uint16_t* table_c, const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c,
+                    cudaStream_t stream) {
+  const int patches = (height / 4) * (depth / 4) * (width / 4);
+  int threads = ((d / 8 + 31) / 32) * 32;
+  if (threads < 64) threads = 64;
+  patch_embed_kernel<<<slots * patches, threads, 0, stream>>>(tokens, height, depth, width, classes, d, table_b,
+                                                              bias_b, add_b, out_b, table_c, bias_c, add_c, out_c);
+  return launch_status("patch_embed_kernel");
+}
+
+int layernorm_run(const uint16_t* x, int rows, int d, float eps, const uint16_t* ops, const uint16_t* shift,
+                  uint16_t* out, cudaStream_t stream) {
+  const int warps = 8;
+  const int grid = (rows + warps - 1) / warps;
+  switch ((d / 8 + 31) / 32) {
+    case 1: layernorm_modulate_kernel<1><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
+    case 2: layernorm_modulate_kernel<2><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
+    case 3: layernorm_modulate_kernel<3><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
+    case 4: layernorm_modulate_kernel<4><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
+    case 5: layernorm_modulate_kernel<5><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
+    case 6: layernorm_modulate_kernel<6><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
+    default: return fail(SVX_ERR_INVALID, "layernorm: d must be at most 1536");
+  }
+  return launch_status("layernorm_modulate_kernel");
+}
+
+}  // namespace svx
+
+using namespace svx;
+
+extern "C" int svx_patch_embed(const int16_t* tokens, int slots, int height, int depth, int width, int patch,
+                               int classes, int d, const uint16_t* table_b, const uint16_t* bias_b,
+                               const uint16_t* add_b, uint16_t* out_b, const uint16_t* table_c,
+                               const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c, void* stream) {
+  SVX_REQUIRE(patch == 4, "svx_patch_embed: only patch 4 is implemented");
+  SVX_REQUIRE(height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 && slots > 0, "svx_patch_embed: bad shape");
+  SVX_REQUIRE(d % 8 == 0 && d <= 8192, "svx_patch_embed: d must be a multiple of 8");
+  SVX_REQUIRE(tokens && table_b && bias_b && add_b && out_b, "svx_patch_embed: null backbone operand");
+  SVX_REQUIRE(!table_c || (bias_c && add_c && out_c), "svx_patch_embed: incomplete control operands");
+  return patch_embed_run(tokens, slots, height, depth, width, classes, d, table_b, bias_b, add_b, out_b, table_c,
+                         bias_c, add_c, out_c, as_stream(stream));
+}
+
+extern "C" int svx_layernorm_modulate(const uint16_t* x, int rows, int d, float eps, const uint16_t* one_plus_scale,
+                                      const uint16_t* shift, uint16_t* out, void* stream) {
+  SVX_REQUIRE(x && out && rows > 0, "svx_layernorm_modulate: bad arguments");
+  SVX_REQUIRE((one_plus_scale == nullptr) == (shift == nullptr), "svx_layernorm_modulate: scale and shift go together");
+  SVX_REQUIRE(d % 8 == 0 && d <= 1536, "svx_layernorm_modulate: d must be a multiple of 8, at most 1536");
+  return layernorm_run(x, rows, d, eps, one_plus_scale, shift, out, as_stream(stream));
+}

@@ -1,0 +1,205 @@
+// The slot-batched forward of the time-free DiT backbone + compact ControlNet as one host-driven launch sequence.
+//
+// Replaces `FastSlotForward.forward` (`streamvoxel/stream/fast_ops.py:274-308`), i.e.
+// `CompactStreamingControlNet.forward` (`streamvoxel/models/compact_controlnet.py:100-159`) over cached packed K/V:
+//   b, c = embed(tokens) + y_embed
+//   for i in layers: if i feeds control layer j: c = block_c(c); c = c + cross_j(c); b = block_b(b) + zero_j(c)
+//                    else:                      b = block_b(b)
+//   logits = head(modulate(LN(b)))  in class-major [slot][V][Y][Z][X]
+// Every TMA descriptor is built once in svx_engine_create; svx_engine_forward only enqueues kernels, so it can be
+// captured in a CUDA graph per slot bucket.
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+struct svx_engine {
+  svx_engine_config cfg;
+  std::vector<int> layer_map;  // backbone layer -> control layer or -1
+  svx_engine_weights w;
+  std::vector<svx_block_weights> backbone, control;
+  std::vector<svx_cross_weights> cross;
+  svx_engine_workspace ws;
+  int patches, rows_max;
+  // GEMM plans: per backbone layer [qkv, proj, fc1, fc2]; per control layer [qkv, proj, fc1, fc2, query, cproj, zero].
+  std::vector<svx::GemmPlan> bplan, cplan;
+  svx::GemmPlan head;
+};
+
+namespace svx {
+namespace {
+
+constexpr int HD = 96;
+
+int plan_block(std::vector<GemmPlan>& plans, const svx_block_weights& bw, const svx_engine_workspace& ws, int rows,
+               int d, int mlp) {
+  GemmPlan p;
+  int rc;
+  if ((rc = gemm_plan(&p, ws.h, bw.qkv_w, rows, 3 * d, d, 0))) return rc;
+  plans.push_back(p);
+  if ((rc = gemm_plan(&p, ws.attn, bw.proj_w, rows, d, d, 0))) return rc;
+  plans.push_back(p);
+  if ((rc = gemm_plan(&p, ws.h, bw.fc1_w, rows, mlp, d, 0))) return rc;
+  plans.push_back(p);
+  if ((rc = gemm_plan(&p, ws.mlp, bw.fc2_w, rows, d, mlp, 0))) return rc;
+  plans.push_back(p);
+  return SVX_OK;
+}
+
+EpiParams epi(int kind, const uint16_t* bias) {
+  EpiParams e{};
+  e.epilogue = kind;
+  e.bias = bias;
+  return e;
+}
+
+// One time-free AdaLN block on x (`UnconditionalBlock.forward`, `unconditional_md4_timefree.py:60-63`).
+int run_block(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
+              cudaStream_t s) {
+  const int d = E.cfg.d, rows = n * E.patches;
+  const svx_engine_workspace& ws = E.ws;
+  int rc;
+  if ((rc = layernorm_run(x, rows, d, 1e-6f, bw.one_plus_scale1, bw.shift1, ws.h, s))) return rc;
+  EpiParams e = epi(SVX_EPI_ROPE, bw.qkv_b);
+  e.rope_sin = E.w.rope_sin; e.rope_cos = E.w.rope_cos;
+  e.rope_cols = 2 * d; e.rows_per_slot = E.patches; e.head_dim = HD;
+  if ((rc = gemm_run(plans[0], rows, ws.qkv, e, s))) return rc;
+  const int64_t ld = 3 * d;
+  if ((rc = attention_run(ws.qkv, ld, ws.qkv + d, ws.qkv + 2 * d, (int64_t)E.patches * ld, HD, ld, nullptr, n,
+                          E.cfg.heads, E.patches, E.patches, ws.attn, s)))
+    return rc;
+  e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);
+  e.gate = bw.gate1; e.residual = x;
+  if ((rc = gemm_run(plans[1], rows, x, e, s))) return rc;
+  if ((rc = layernorm_run(x, rows, d, 1e-6f, bw.one_plus_scale2, bw.shift2, ws.h, s))) return rc;
+  if ((rc = gemm_run(plans[2], rows, ws.mlp, epi(SVX_EPI_BIAS_GELU, bw.fc1_b), s))) return rc;
+  e = epi(SVX_EPI_GATE_RESIDUAL, bw.fc2_b);
+  e.gate = bw.gate2; e.residual = x;
+  return gemm_run(plans[3], rows, x, e, s);
+}
+
+// c = c + cross_j(c): LN -> query -> RoPE -> attention over the slot's packed keys -> proj
+// (`RotaryCrossAttention.forward`, `streaming_controlnet.py:37-61`, as `cross_flex` `fast_ops.py:104-108`).
+int run_cross(const svx_engine& E, const svx_cross_weights& cw, const GemmPlan* plans, int n, cudaStream_t s) {
+  const int d = E.cfg.d, rows = n * E.patches;
+  const svx_engine_workspace& ws = E.ws;
+  int rc;
+  if ((rc = layernorm_run(ws.xc, rows, d, 1e-6f, nullptr, nullptr, ws.h, s))) return rc;
+  EpiParams e = epi(SVX_EPI_ROPE, cw.query_b);
+  e.rope_sin = E.w.cross_sin; e.rope_cos = E.w.cross_cos;
+  e.rope_cols = d; e.rows_per_slot = E.patches; e.head_dim = HD;
+  if ((rc = gemm_run(plans[0], rows, ws.qkv, e, s))) return rc;
+  const int64_t cap = E.cfg.key_capacity;
+  if ((rc = attention_run(ws.qkv, d, cw.k, cw.v, (int64_t)E.cfg.heads * cap * HD, cap * HD, HD, E.w.lengths, n,
+                          E.cfg.heads, E.patches, E.cfg.key_capacity, ws.attn, s)))
+    return rc;
+  e = epi(SVX_EPI_RESIDUAL, cw.proj_b);
+  e.residual = ws.xc;
+  return gemm_run(plans[1], rows, ws.xc, e, s);
+}
+
+}  // namespace
+}  // namespace svx
+
+using namespace svx;
+
+extern "C" int svx_engine_create(const svx_engine_config* config, const svx_engine_weights* weights,
+                                 const svx_engine_workspace* workspace, svx_engine** out) {
+  SVX_REQUIRE(config && weights && workspace && out, "svx_engine_create: null argument");
+  const svx_engine_config& c = *config;
+  SVX_REQUIRE(c.patch == 4, "svx_engine_create: patch must be 4");
+  SVX_REQUIRE(c.height % 4 == 0 && c.depth % 4 == 0 && c.width % 4 == 0, "svx_engine_create: bad voxel shape");
+  SVX_REQUIRE(c.heads > 0 && c.d == c.heads * HD, "svx_engine_create: head_dim must be 96 (d = heads * 96)");
+  SVX_REQUIRE(c.slots > 0 && c.depth_layers > 0 && c.n_control >= 0 && c.n_control <= c.depth_layers,
+              "svx_engine_create: bad layer counts");
+  SVX_REQUIRE(c.n_control == 0 || (c.layer_index && c.key_capacity > 0 && c.key_capacity % 64 == 0),
+              "svx_engine_create: control layers need layer indexes and a key capacity (multiple of 64)");
+  auto* e = new svx_engine();
+  e->cfg = c;
+  e->w = *weights;
+  e->ws = *workspace;
+  e->patches = (c.height / 4) * (c.depth / 4) * (c.width / 4);
+  e->rows_max = c.slots * e->patches;
+  e->layer_map.assign(c.depth_layers, -1);
+  for (int j = 0; j < c.n_control; ++j) {
+    const int i = c.layer_index[j];
+    if (i < 0 || i >= c.depth_layers || (j > 0 && i <= c.layer_index[j - 1])) {
+      delete e;
+      return fail(SVX_ERR_INVALID, "svx_engine_create: layer indexes must be increasing and within the backbone");
+    }
+    e->layer_map[i] = j;
+  }
+  e->cfg.layer_index = nullptr;
+  e->backbone.assign(weights->backbone, weights->backbone + c.depth_layers);
+  if (c.n_control) {
+    e->control.assign(weights->control, weights->control + c.n_control);
+    e->cross.assign(weights->cross, weights->cross + c.n_control);
+  }
+  e->w.backbone = nullptr; e->w.control = nullptr; e->w.cross = nullptr;
+  int rc = SVX_OK;
+  for (int i = 0; i < c.depth_layers && !rc; ++i)
+    rc = plan_block(e->bplan, e->backbone[i], e->ws, e->rows_max, c.d, c.mlp);
+  for (int j = 0; j < c.n_control && !rc; ++j) {
+    rc = plan_block(e->cplan, e->control[j], e->ws, e->rows_max, c.d, c.mlp);
+    GemmPlan p;
+    if (!rc) rc = gemm_plan(&p, e->ws.h, e->cross[j].query_w, e->rows_max, c.d, c.d, 0);
+    if (!rc) e->cplan.push_back(p);
+    if (!rc) rc = gemm_plan(&p, e->ws.attn, e->cross[j].proj_w, e->rows_max, c.d, c.d, 0);
+    if (!rc) e->cplan.push_back(p);
+    if (!rc) rc = gemm_plan(&p, e->ws.xc, e->cross[j].zero_w, e->rows_max, c.d, c.d, 0);
+    if (!rc) e->cplan.push_back(p);
+  }
+  if (!rc) rc = gemm_plan(&e->head, e->ws.h, weights->head_w, e->rows_max, c.classes * 64, c.d, 0);
+  if (rc) {
+    delete e;
+    return rc;
+  }
+  *out = e;
+  return SVX_OK;
+}
+
+extern "C" int svx_engine_forward(svx_engine* E, int n, const int16_t* tokens, uint16_t* logits, void* stream) {
+  SVX_REQUIRE(E && tokens && logits, "svx_engine_forward: null argument");
+  SVX_REQUIRE(n >= 1 && n <= E->cfg.slots, "svx_engine_forward: n must be in 1..slots");
+  cudaStream_t s = as_stream(stream);
+  const svx_engine_config& c = E->cfg;
+  const svx_engine_workspace& ws = E->ws;
+  const int rows = n * E->patches;
+  int rc = patch_embed_run(tokens, n, c.height, c.depth, c.width, c.classes, c.d, E->w.table_b, E->w.bias_b,
+                           E->w.yadd_b, ws.xb, c.n_control ? E->w.table_c : nullptr, E->w.bias_c, E->w.yadd_c, ws.xc,
+                           s);
+  if (rc) return rc;
+  for (int i = 0; i < c.depth_layers; ++i) {
+    const int j = E->layer_map[i];
+    if (j >= 0) {
+      const GemmPlan* cp = &E->cplan[(size_t)j * 7];
+      if ((rc = run_block(*E, E->control[j], cp, ws.xc, n, s))) return rc;
+      if ((rc = run_cross(*E, E->cross[j], cp + 4, n, s))) return rc;
+    }
+    if ((rc = run_block(*E, E->backbone[i], &E->bplan[(size_t)i * 4], ws.xb, n, s))) return rc;
+    if (j >= 0) {
+      EpiParams e{};
+      e.epilogue = SVX_EPI_RESIDUAL;
+      e.bias = E->cross[j].zero_b;
+      e.residual = ws.xb;
+      if ((rc = gemm_run(E->cplan[(size_t)j * 7 + 6], rows, ws.xb, e, s))) return rc;
+    }
+  }
+  if ((rc = layernorm_run(ws.xb, rows, c.d, 1e-6f, E->w.final_one_plus_scale, E->w.final_shift, ws.h, s))) return rc;
+  EpiParams e{};
+  e.epilogue = SVX_EPI_CLASS_MAJOR;
+  e.bias = E->w.head_b;
+  e.rows_per_slot = E->patches;
+  e.classes = c.classes;
+  e.height = c.height; e.depth = c.depth; e.width = c.width; e.patch = 4;
+  return gemm_run(E->head, rows, logits, e, s);
+}
+
+extern "C" int svx_engine_launches(const svx_engine* E, int n) {
+  if (!E || n < 1) return 0;
+  const int per_block = 7;   // LN, qkv, attention, proj, LN, fc1, fc2
+  const int per_cross = 5;   // LN, query, attention, proj, zero
+  return 1 + E->cfg.depth_layers * per_block + E->cfg.n_control * (per_block + per_cross) + 2;
+}
+
+extern "C" void svx_engine_destroy(svx_engine* E) { delete E; }

@@ -1,0 +1,38 @@
+// Host-side entry points shared by the C-ABI wrappers and the engine (TMA descriptors are built once per operand).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace svx {
+
+struct EpiParams {
+  int epilogue;
+  const uint16_t* bias;
+  const uint16_t* gate;
+  const uint16_t* residual;
+  const uint16_t* rope_sin;
+  const uint16_t* rope_cos;
+  int rope_cols, rows_per_slot, head_dim, classes, height, depth, width, patch;
+};
+
+struct GemmPlan {
+  CUtensorMap a, b;
+  int M, N, K, bn;
+};
+
+int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N, int K, int bn);
+int gemm_run(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream);
+int epi_from_args(const svx_epilogue_args* e, EpiParams* ep, int N);
+int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
+                  int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride, const int32_t* lengths,
+                  int slots, int heads, int queries, int keys, uint16_t* out, cudaStream_t stream);
+int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int width, int classes, int d,
+                    const uint16_t* table_b, const uint16_t* bias_b, const uint16_t* add_b, uint16_t* out_b,
+                    const uint16_t* table_c, const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c,
+                    cudaStream_t stream);
+int layernorm_run(const uint16_t* x, int rows, int d, float eps, const uint16_t* ops, const uint16_t* shift,
+                  uint16_t* out, cudaStream_t stream);
+
+}  // namespace svx
