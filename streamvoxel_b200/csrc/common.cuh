@@ -41,8 +41,15 @@ template <typename T> __device__ __forceinline__ float load_as_f32(const T* p);
 template <> __device__ __forceinline__ float load_as_f32<float>(const float* p) { return *p; }
 template <> __device__ __forceinline__ float load_as_f32<uint16_t>(const uint16_t* p) { return bf16_to_f32(*p); }
 
-// Bounded spin: at most this many polls of an mbarrier before the kernel reports SVX_STATUS_WAIT_TIMEOUT.
-constexpr uint32_t kWaitLimit = 1u << 26;
+// Bounded spin: an mbarrier wait gives up after this many nanoseconds of %globaltimer and the kernel reports
+// SVX_STATUS_WAIT_TIMEOUT (try_wait may suspend for a system-dependent time per poll, so polls are not counted).
+constexpr uint64_t kWaitNanoseconds = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -68,11 +75,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Wait for the phase with the given parity; false after kWaitLimit polls (the caller records the timeout).
+// Wait for the phase with the given parity; false after kWaitNanoseconds (the caller records the timeout).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_timer_ns() - start > kWaitNanoseconds) return false;
+  return true;
 }
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }

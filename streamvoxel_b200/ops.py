@@ -1,0 +1,181 @@
+"""Torch-tensor wrappers over the libsvx entry points (device tensors in, device tensors out, current stream).
+
+Each wrapper validates dtypes/shapes on the host and calls exactly one C-ABI function; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from streamvoxel_b200 import _lib
+from streamvoxel_b200._lib import check, ptr, stream_ptr
+
+STEP_DTYPE = np.dtype([('k', '<i4'), ('step', '<i4'), ('committed', '<i8'), ('frac', '<f8'), ('seed', '<u8')])
+assert STEP_DTYPE.itemsize == ctypes.sizeof(_lib.StepParams)
+
+
+def _dtype_code(t):
+    if t.dtype == torch.bfloat16:
+        return _lib.BF16
+    if t.dtype == torch.float32:
+        return _lib.F32
+    raise ValueError(f'logits must be bf16 or fp32, got {t.dtype}')
+
+
+def step_params(rows, device=None, out=None):
+    """Pack per-slot step scalars [(k, step, committed, frac, seed)] into an `svx_step_params` array.
+
+    Returns a uint8 tensor on `device` (or copies into `out`, a pinned/device uint8 tensor of the right size)."""
+    arr = np.zeros(len(rows), STEP_DTYPE)
+    for i, (k, step, committed, frac, seed) in enumerate(rows):
+        arr[i] = (int(k), int(step), int(committed), float(frac), int(seed) & 0xFFFFFFFFFFFFFFFF)
+    host = torch.from_numpy(arr.view(np.uint8).copy())
+    if out is not None:
+        out.copy_(host, non_blocking=False)
+        return out
+    return host.to(device)
+
+
+def _slots_view(logits):
+    """[S, C, ...] contiguous -> (S, C, voxels, slot stride)."""
+    if not logits.is_contiguous():
+        raise ValueError('logits must be contiguous [slots, classes, Y, Z, X]')
+    s, c = logits.shape[0], logits.shape[1]
+    voxels = logits[0, 0].numel()
+    return s, c, voxels, c * voxels
+
+
+def ease_scores(logits, status=None):
+    """Negative entropy per voxel of class-major logits [S, C, Y, Z, X] -> fp32 [S, Y, Z, X]."""
+    s, c, voxels, stride = _slots_view(logits)
+    scores = torch.empty((s, *logits.shape[2:]), device=logits.device, dtype=torch.float32)
+    check(_lib.load().svx_ease_scores(ptr(logits), _dtype_code(logits), s, c, voxels, stride, ptr(scores), ptr(status),
+                                      stream_ptr()), 'svx_ease_scores')
+    return scores
+
+
+def ease_mark(logits, air_ids, last_eps, last=None, last_count=None):
+    """Marking forward: per-column top run of voxels with P(air) > 1 - eps. Returns (last uint8, last_count int32)."""
+    s, c, voxels, stride = _slots_view(logits)
+    height, depth, width = logits.shape[2:]
+    dev = logits.device
+    if last is None:
+        last = torch.empty((s, height, depth, width), device=dev, dtype=torch.uint8)
+    if last_count is None:
+        last_count = torch.empty(s, device=dev, dtype=torch.int32)
+    air = torch.as_tensor(list(air_ids), dtype=torch.int32, device=dev)
+    check(_lib.load().svx_ease_mark(ptr(logits), _dtype_code(logits), s, c, height, depth, width, stride, ptr(air),
+                                    len(air_ids), float(last_eps), ptr(last), ptr(last_count), stream_ptr()),
+          'svx_ease_mark')
+    return last, last_count
+
+
+def select_workspace(slots, voxels, device):
+    n = _lib.load().svx_ease_select_workspace_bytes(slots, voxels)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def ease_select(scores, tokens, last, pos, params, mask_id, index_capacity, *, chosen=None, index=None, count=None,
+                status=None, workspace=None, block=4):
+    """Block-quota selection. Returns (chosen uint8 [S,Y,Z,X], index int32 [S, capacity], count int32 [S])."""
+    s, height, depth, width = tokens.shape
+    dev = tokens.device
+    assert tokens.dtype == torch.int16 and last.dtype == torch.uint8 and scores.dtype == torch.float32
+    assert pos.dtype == torch.int32 and params.dtype == torch.uint8
+    if chosen is None:
+        chosen = torch.empty((s, height, depth, width), device=dev, dtype=torch.uint8)
+    if index is None:
+        index = torch.empty((s, index_capacity), device=dev, dtype=torch.int32)
+    if count is None:
+        count = torch.empty(s, device=dev, dtype=torch.int32)
+    if workspace is None:
+        workspace = select_workspace(s, height * depth * width, dev)
+    check(_lib.load().svx_ease_select(ptr(scores), ptr(tokens), ptr(last), ptr(pos), ptr(params), s, height, depth,
+                                      width, block, mask_id, ptr(chosen), ptr(index), index_capacity, ptr(count),
+                                      ptr(status), ptr(workspace), stream_ptr()), 'svx_ease_select')
+    return chosen, index, count
+
+
+def ease_sample(logits, index, params, tokens, noise=None, values=None, status=None):
+    """Categorical draw for the chosen voxels; writes tokens in place. noise [S, capacity, C] fp32 or None (native)."""
+    s, c, voxels, stride = _slots_view(logits)
+    capacity = index.shape[1]
+    if values is None:
+        values = torch.empty((s, capacity), device=logits.device, dtype=torch.int16)
+    noise_stride = 0
+    if noise is not None:
+        assert noise.dtype == torch.float32 and noise.is_contiguous() and noise.shape[-1] == c
+        noise_stride = noise[0].numel() if noise.dim() == 3 else 0
+    check(_lib.load().svx_ease_sample(ptr(logits), _dtype_code(logits), s, c, voxels, stride, ptr(index), ptr(params),
+                                      ptr(noise), noise_stride, capacity, ptr(tokens), ptr(values), ptr(status),
+                                      stream_ptr()), 'svx_ease_sample')
+    return values
+
+
+def softmax_rows(x):
+    out = torch.empty_like(x)
+    check(_lib.load().svx_softmax_rows(ptr(x), x.shape[0], x.shape[1], ptr(out), stream_ptr()), 'svx_softmax_rows')
+    return out
+
+
+def ease_finish(tokens, last, finish, air_token):
+    s = tokens.shape[0]
+    check(_lib.load().svx_ease_finish(ptr(tokens), ptr(last), ptr(finish), s, tokens[0].numel(), int(air_token),
+                                      stream_ptr()), 'svx_ease_finish')
+
+
+def patch_embed(tokens, classes, table_b, bias_b, add_b, table_c=None, bias_c=None, add_c=None, out_b=None,
+                out_c=None):
+    s, height, depth, width = tokens.shape
+    d = table_b.shape[1]
+    patches = (height // 4) * (depth // 4) * (width // 4)
+    if out_b is None:
+        out_b = torch.empty((s * patches, d), device=tokens.device, dtype=torch.bfloat16)
+    if table_c is not None and out_c is None:
+        out_c = torch.empty((s * patches, d), device=tokens.device, dtype=torch.bfloat16)
+    check(_lib.load().svx_patch_embed(ptr(tokens), s, height, depth, width, 4, classes, d, ptr(table_b), ptr(bias_b),
+                                      ptr(add_b), ptr(out_b), ptr(table_c), ptr(bias_c), ptr(add_c), ptr(out_c),
+                                      stream_ptr()), 'svx_patch_embed')
+    return out_b, out_c
+
+
+def layernorm_modulate(x, eps=1e-6, one_plus_scale=None, shift=None, out=None):
+    rows, d = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    check(_lib.load().svx_layernorm_modulate(ptr(x), rows, d, float(eps), ptr(one_plus_scale), ptr(shift), ptr(out),
+                                             stream_ptr()), 'svx_layernorm_modulate')
+    return out
+
+
+def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None, rope=None, rope_cols=0,
+         rows_per_slot=0, head_dim=96, classes=0, geometry=(0, 0, 0)):
+    """out = epilogue(a @ w.T + bias) on the tcgen05 GEMM. a [M,K], w [N,K], bias [N] bf16."""
+    m, k = a.shape
+    n = w.shape[0]
+    for t in (a, w, bias):
+        assert t.dtype == torch.bfloat16 and t.is_contiguous()
+    if out is None:
+        if epilogue == _lib.EPI_CLASS_MAJOR:
+            out = torch.empty((m // rows_per_slot, classes, *geometry), device=a.device, dtype=torch.bfloat16)
+        else:
+            out = torch.empty((m, n), device=a.device, dtype=torch.bfloat16)
+    args = _lib.EpilogueArgs(epilogue=epilogue, bias=bias.data_ptr(), gate=ptr(gate).value, residual=ptr(residual).value,
+                             rope_sin=ptr(rope[0] if rope else None).value, rope_cos=ptr(rope[1] if rope else None).value,
+                             rope_cols=rope_cols, rows_per_slot=rows_per_slot, head_dim=head_dim, classes=classes,
+                             height=geometry[0], depth=geometry[1], width=geometry[2], patch=4)
+    check(_lib.load().svx_gemm(ptr(a), ptr(w), ptr(out), m, n, k, ctypes.byref(args), stream_ptr()), 'svx_gemm')
+    return out
+
+
+def attention(q, k, v, slots, heads, queries, keys, *, q_row_stride, kv_slot_stride, kv_head_stride, kv_row_stride,
+              lengths=None, out=None):
+    """Non-causal head_dim-96 attention over per-slot key lengths; out [slots*queries, heads*96] bf16."""
+    if out is None:
+        out = torch.empty((slots * queries, heads * 96), device=q.device, dtype=torch.bfloat16)
+    check(_lib.load().svx_attention(ptr(q), q_row_stride, ptr(k), ptr(v), kv_slot_stride, kv_head_stride,
+                                    kv_row_stride, ptr(lengths), slots, heads, queries, keys, ptr(out), stream_ptr()),
+          'svx_attention')
+    return out

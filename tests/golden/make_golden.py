@@ -59,7 +59,8 @@ def quota_cases():
         pre = f'c{index}_'
         out.update({pre + 'score': score.numpy(), pre + 'selectable': selectable.numpy(), pre + 'k': np.int64(k),
                     pre + 'order': order.numpy(), pre + 'frac': np.float64(frac), pre + 'n_total': n_total.numpy(),
-                    pre + 'committed': np.int64(committed), pre + 'chosen': chosen.numpy()})
+                    pre + 'committed': np.int64(committed), pre + 'chosen': chosen.numpy(),
+                    pre + 'last': last.numpy()})
     out['count'] = np.int64(len(cases))
     _save('quota_select.npz', **out)
 

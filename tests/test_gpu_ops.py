@@ -1,0 +1,302 @@
+"""Per-kernel parity of libsvx on the GPU, through the C-ABI (streamvoxel_b200.ops), against the CPU oracle.
+
+Tolerances: integer/index results (selection, marking, sampling given identical inputs) are exact; entropy within
+1e-5 abs (the contract of the EASE scores); bf16 GEMM/attention outputs within 1e-2 abs + 1e-2 rel of an fp32
+reference rounded at the same points (one bf16 ulp at the magnitudes used).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sampler as osm
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
+
+
+@pytest.fixture(scope='module')
+def ops():
+    from streamvoxel_b200 import _lib, ops
+    _lib.require_device()
+    return ops
+
+
+def _bf16(x):
+    return x.bfloat16().float()
+
+
+# ---------------------------------------------------------------------------------------------- EASE
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_entropy_scores_match_oracle(ops, dtype):
+    g = torch.Generator().manual_seed(0)
+    logits = (torch.randn((3, 256, 64, 16, 16), generator=g) * 2).to(dtype)
+    logits[:, 7] += 6.0
+    got = ops.ease_scores(logits.cuda().contiguous()).cpu()
+    want = np.stack([osm.entropy_scores(logits[i].float().numpy()) for i in range(3)])
+    np.testing.assert_allclose(got.numpy(), want, atol=1e-5, rtol=0)
+
+
+def test_marking_matches_oracle(ops):
+    g = np.load(os.path.join(GOLDEN, 'scores.npz'))
+    for i in range(int(g['count'])):
+        logits = torch.from_numpy(g[f'e{i}_logits'])[None].contiguous()
+        if logits[0, 0].numel() % 4:
+            continue
+        last, count = ops.ease_mark(logits.cuda(), (0,), float(g[f'e{i}_eps']))
+        assert np.array_equal(last[0].cpu().numpy().astype(bool), g[f'e{i}_last']), i
+        assert int(count[0]) == int(g[f'e{i}_last'].sum())
+
+
+def _select_inputs(score, selectable, last, mask_id=256):
+    tokens = np.where(selectable | last, mask_id, 0).astype(np.int16)
+    return tokens
+
+
+def test_selection_matches_reference_fixtures(ops):
+    """The kernel fed the reference's scores selects exactly the reference's voxels (`block_quota_select`)."""
+    g = np.load(os.path.join(GOLDEN, 'quota_select.npz'))
+    for i in range(int(g['count'])):
+        p = f'c{i}_'
+        score, selectable, last = g[p + 'score'], g[p + 'selectable'], g[p + 'last']
+        k, committed, frac = int(g[p + 'k']), int(g[p + 'committed']), float(g[p + 'frac'])
+        order = g[p + 'order']
+        pos = np.empty_like(order)
+        pos[order] = np.arange(len(order))
+        tokens = _select_inputs(score, selectable, last)
+        params = ops.step_params([(k, 1, committed, frac, 0)], 'cuda')
+        status = torch.zeros(1, dtype=torch.int32, device='cuda')
+        chosen, index, count = ops.ease_select(
+            torch.from_numpy(score)[None].cuda(), torch.from_numpy(tokens)[None].cuda(),
+            torch.from_numpy(last.astype(np.uint8))[None].cuda(), torch.from_numpy(pos.astype(np.int32))[None].cuda(),
+            params, 256, max(k, 1), status=status)
+        want = g[p + 'chosen']
+        assert np.array_equal(chosen[0].cpu().numpy().astype(bool), want), i
+        assert int(count[0]) == k and int(status[0]) == 0
+        assert np.array_equal(index[0, :k].cpu().numpy(), np.flatnonzero(want)), i
+
+
+@pytest.mark.parametrize('seed', range(4))
+def test_selection_full_size_batch_matches_oracle(ops, seed):
+    """8 slots of full-size columns in one launch, including steps that need the global trim / top-up."""
+    rng = np.random.default_rng(seed)
+    shape, slots = (256, 16, 16), 8
+    scores, tokens, lasts, poss, rows, wants = [], [], [], [], [], []
+    for s in range(slots):
+        tops = rng.integers(40, 256, (16, 16))
+        last = np.arange(256)[:, None, None] >= tops[None]
+        committed_mask = ~last & (rng.random(shape) < rng.random())
+        selectable = ~last & ~committed_mask
+        k = int(rng.integers(1, max(2, int(selectable.sum()))))
+        committed = int(committed_mask.sum())
+        frac = (committed + k) / int((~last).sum())
+        if s % 3 == 1:   # break the invariant so the clamped quotas miss k and the fix-up runs
+            frac = min(1.0, frac * 1.3)
+        order = rng.permutation(1024)
+        score = rng.standard_normal(shape).astype(np.float32)
+        if s % 2:
+            score = np.round(score * 2) / 2   # ties inside blocks
+        n_total = osm.block_view(~last, 4).sum(1)
+        pos = np.empty_like(order)
+        pos[order] = np.arange(1024)
+        want = osm.block_quota_select(score, selectable, k, 4, order, frac, n_total)
+        scores.append(score); tokens.append(_select_inputs(score, selectable, last)); lasts.append(last)
+        poss.append(pos); rows.append((k, 1, committed, frac, seed)); wants.append(want)
+    params = ops.step_params(rows, 'cuda')
+    cap = max(r[0] for r in rows)
+    status = torch.zeros(slots, dtype=torch.int32, device='cuda')
+    chosen, index, count = ops.ease_select(
+        torch.from_numpy(np.stack(scores)).cuda(), torch.from_numpy(np.stack(tokens)).cuda(),
+        torch.from_numpy(np.stack(lasts).astype(np.uint8)).cuda(), torch.from_numpy(np.stack(poss).astype(np.int32)).cuda(),
+        params, 256, cap, status=status)
+    chosen = chosen.cpu().numpy().astype(bool)
+    for s in range(slots):
+        assert np.array_equal(chosen[s], wants[s]), s
+        assert int(count[s]) == rows[s][0]
+    assert int(status.sum()) == 0
+
+
+def test_softmax_rows_bitwise_equal_torch(ops):
+    """The parity-mode softmax reproduces torch's CUDA `softmax(-1)` bit for bit (the multinomial's input)."""
+    g = torch.Generator(device='cuda').manual_seed(3)
+    for classes in (256, 6, 33, 1000, 1):
+        x = torch.randn((4099, classes), device='cuda', generator=g) * 3
+        assert torch.equal(ops.softmax_rows(x), x.softmax(-1)), classes
+
+
+@pytest.mark.parametrize('classes', [256, 6])
+def test_parity_sampling_equals_torch_multinomial(ops, classes):
+    """Given the slot generator, the kernel's draw equals `torch.multinomial(softmax(x), 1, generator)`."""
+    torch.manual_seed(0)
+    voxels, k = 4096, 777
+    logits = (torch.randn((1, classes, voxels), device='cuda') * 2).contiguous()
+    idx = torch.sort(torch.randperm(voxels, device='cuda')[:k]).values.int()
+    gen = torch.Generator(device='cuda').manual_seed(1234)
+    clone = torch.Generator(device='cuda').set_state(gen.get_state())
+    probs = logits[0][:, idx.long()].t().contiguous().float().softmax(-1)
+    want = torch.multinomial(probs, 1, generator=clone).squeeze(-1)
+    noise = torch.empty((k, classes), device='cuda').exponential_(generator=gen)
+    assert torch.equal(gen.get_state(), clone.get_state())
+    tokens = torch.full((1, voxels), classes, dtype=torch.int16, device='cuda')
+    params = ops.step_params([(k, 1, 0, 0.0, 0)], 'cuda')
+    values = ops.ease_sample(logits, idx[None].contiguous(), params, tokens, noise=noise[None].contiguous())
+    assert torch.equal(values[0].long(), want)
+    assert torch.equal(tokens[0, idx.long()].long(), want)
+
+
+def test_native_sampling_matches_oracle_rule(ops):
+    torch.manual_seed(1)
+    classes, voxels, k = 256, 65536, 2048
+    logits = (torch.randn((1, classes, voxels), device='cuda') * 2).to(torch.bfloat16).contiguous()
+    idx = torch.sort(torch.randperm(voxels, device='cuda')[:k]).values.int()
+    tokens = torch.full((1, voxels), classes, dtype=torch.int16, device='cuda')
+    seed, step = 0x1234567890ABCDEF, 7
+    params = ops.step_params([(k, step, 0, 0.0, seed)], 'cuda')
+    values = ops.ease_sample(logits, idx[None].contiguous(), params, tokens)[0].cpu().numpy()
+    cols = logits[0].float().cpu().numpy()[:, idx.cpu().numpy()]
+    want = osm.native_sample(cols, idx.cpu().numpy(), seed, step)
+    agree = float((values == want).mean())
+    assert agree >= 0.999, agree
+
+
+# ---------------------------------------------------------------------------------------------- forward ops
+
+def _linear_ref(a, w, b):
+    return _bf16(a.float() @ w.float().t() + b.float())
+
+
+@pytest.mark.parametrize('m,n,k', [(256, 576, 192), (1024, 768, 768), (8192, 2304, 768), (2048, 768, 3072),
+                                   (1024, 3072, 768)])
+def test_gemm_bias_matches_fp32(ops, m, n, k):
+    torch.manual_seed(m + n + k)
+    a = (torch.randn((m, k), device='cuda') * 0.5).bfloat16()
+    w = (torch.randn((n, k), device='cuda') * 0.05).bfloat16()
+    b = (torch.randn(n, device='cuda') * 0.1).bfloat16()
+    got = ops.gemm(a, w, b).float()
+    want = _linear_ref(a, w, b)
+    torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)
+    assert (got - want).abs().mean() < 1e-3
+
+
+def test_gemm_fused_epilogues(ops):
+    from streamvoxel_b200 import _lib
+    torch.manual_seed(0)
+    m, n, k = 512, 768, 384
+    a = (torch.randn((m, k), device='cuda') * 0.5).bfloat16()
+    w = (torch.randn((n, k), device='cuda') * 0.05).bfloat16()
+    b = (torch.randn(n, device='cuda') * 0.1).bfloat16()
+    gate = (torch.randn(n, device='cuda') * 0.5).bfloat16()
+    res = torch.randn((m, n), device='cuda').bfloat16()
+    y = _linear_ref(a, w, b)
+    got = ops.gemm(a, w, b, _lib.EPI_BIAS_GELU).float()
+    torch.testing.assert_close(got, _bf16(torch.nn.functional.gelu(y)), atol=1e-2, rtol=1e-2)
+    got = ops.gemm(a, w, b, _lib.EPI_GATE_RESIDUAL, gate=gate, residual=res.clone()).float()
+    torch.testing.assert_close(got, _bf16(res.float() + _bf16(gate.float() * y)), atol=2e-2, rtol=1e-2)
+    got = ops.gemm(a, w, b, _lib.EPI_RESIDUAL, residual=res.clone()).float()
+    torch.testing.assert_close(got, _bf16(res.float() + y), atol=2e-2, rtol=1e-2)
+    inplace = res.clone()
+    ops.gemm(a, w, b, _lib.EPI_RESIDUAL, residual=inplace, out=inplace)
+    torch.testing.assert_close(inplace.float(), _bf16(res.float() + y), atol=2e-2, rtol=1e-2)
+
+
+def test_gemm_rope_epilogue_matches_oracle_rope(ops):
+    from oracle import model as om
+    from oracle.model import Precision
+    from streamvoxel_b200 import _lib
+    torch.manual_seed(2)
+    heads, patches, slots = 2, 256, 2
+    d = heads * 96
+    m, k = slots * patches, 192
+    a = (torch.randn((m, k), device='cuda') * 0.5).bfloat16()
+    w = (torch.randn((3 * d, k), device='cuda') * 0.05).bfloat16()
+    b = (torch.randn(3 * d, device='cuda') * 0.1).bfloat16()
+    positions = om.patch_centers_xyz((64, 16, 16), 4) / 4
+    phase = positions[:, :, None] * om.rope_frequencies(96)
+    sin, cos = phase.sin().reshape(patches, 48).bfloat16().cuda(), phase.cos().reshape(patches, 48).bfloat16().cuda()
+    got = ops.gemm(a, w, b, _lib.EPI_ROPE, rope=(sin, cos), rope_cols=2 * d, rows_per_slot=patches).float().cpu()
+    y = _linear_ref(a, w, b).cpu().reshape(slots, patches, 3, heads, 96)
+    p = Precision(True)
+    want = []
+    for part in range(3):
+        t = y[:, :, part].transpose(1, 2)
+        if part < 2:
+            t = om.rope(t, positions[None].expand(slots, -1, -1), om.rope_frequencies(96), p)
+        want.append(t.transpose(1, 2))
+    want = torch.stack(want, 2).reshape(m, 3 * d)
+    torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)
+
+
+def test_gemm_class_major_head_layout(ops):
+    from streamvoxel_b200 import _lib
+    torch.manual_seed(3)
+    shape, classes, slots = (64, 16, 16), 32, 2
+    patches = 16 * 4 * 4
+    m, k = slots * patches, 192
+    a = (torch.randn((m, k), device='cuda') * 0.5).bfloat16()
+    w = (torch.randn((64 * classes, k), device='cuda') * 0.05).bfloat16()   # reference order n = o * V + v
+    b = (torch.randn(64 * classes, device='cuda') * 0.1).bfloat16()
+    # kernel order n' = v * 64 + o
+    w2 = w.reshape(64, classes, k).transpose(0, 1).reshape(64 * classes, k).contiguous()
+    b2 = b.reshape(64, classes).t().reshape(-1).contiguous()
+    got = ops.gemm(a, w2, b2, _lib.EPI_CLASS_MAJOR, rows_per_slot=patches, classes=classes, geometry=shape).float()
+    y = _linear_ref(a, w, b)
+    want = y.reshape(slots, 16, 4, 4, 4, 4, 4, classes).permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(slots, classes, *shape)
+    torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)
+
+
+def test_attention_self_and_varlen_cross(ops):
+    torch.manual_seed(4)
+    slots, heads, n, d = 3, 2, 256, 192
+    qkv = (torch.randn((slots * n, 3 * d), device='cuda')).bfloat16()
+    got = ops.attention(qkv, qkv[:, d:], qkv[:, 2 * d:], slots, heads, n, n, q_row_stride=3 * d,
+                        kv_slot_stride=n * 3 * d, kv_head_stride=96, kv_row_stride=3 * d).float()
+    q, k_, v = qkv.float().reshape(slots, n, 3, heads, 96).unbind(2)
+    want = torch.nn.functional.scaled_dot_product_attention(q.transpose(1, 2), k_.transpose(1, 2), v.transpose(1, 2))
+    want = want.transpose(1, 2).reshape(slots * n, d)
+    torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)
+    cap = 1280
+    kc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    vc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    lengths = torch.tensor([84, 1280, 577], dtype=torch.int32, device='cuda')
+    qx = torch.randn((slots * n, d), device='cuda').bfloat16()
+    got = ops.attention(qx, kc, vc, slots, heads, n, cap, q_row_stride=d, kv_slot_stride=heads * cap * 96,
+                        kv_head_stride=cap * 96, kv_row_stride=96, lengths=lengths).float()
+    for s in range(slots):
+        L = int(lengths[s])
+        qs = qx[s * n:(s + 1) * n].float().reshape(n, heads, 96).transpose(0, 1)
+        want = torch.nn.functional.scaled_dot_product_attention(qs, kc[s, :, :L].float(), vc[s, :, :L].float())
+        torch.testing.assert_close(got[s * n:(s + 1) * n], want.transpose(0, 1).reshape(n, d), atol=1e-2, rtol=1e-2)
+
+
+def test_layernorm_modulate(ops):
+    torch.manual_seed(5)
+    for d in (192, 768):
+        x = torch.randn((1000, d), device='cuda').bfloat16()
+        ops_ = (1 + torch.randn(d, device='cuda') * 0.1).bfloat16()
+        shift = (torch.randn(d, device='cuda') * 0.1).bfloat16()
+        got = ops.layernorm_modulate(x, 1e-6, ops_, shift).float()
+        ln = torch.nn.functional.layer_norm(x.float(), (d,), eps=1e-6)
+        torch.testing.assert_close(got, _bf16(ln * ops_.float() + shift.float()), atol=1e-2, rtol=1e-2)
+        got = ops.layernorm_modulate(x, 1e-6).float()
+        torch.testing.assert_close(got, _bf16(ln), atol=1e-2, rtol=1e-2)
+
+
+def test_patch_embed_matches_gather(ops):
+    from oracle import model as om
+    from oracle.model import Precision
+    torch.manual_seed(6)
+    classes, d, shape = 31, 192, (64, 16, 16)
+    sd = {'t.weight': torch.randn((d, classes + 1, 4, 4, 4)) * 0.05, 't.bias': torch.randn(d) * 0.1}
+    tokens = torch.randint(0, classes + 1, (2, *shape))
+    p = Precision(True)
+    want = om.patchify(sd, 't', tokens, classes, p)
+    add = (torch.randn((256, d)) * 0.1).bfloat16()
+    want = _bf16(want + add.float()[None])
+    table = sd['t.weight'].permute(1, 2, 3, 4, 0).reshape(-1, d).bfloat16().cuda()
+    out_b, out_c = ops.patch_embed(tokens.to(torch.int16).cuda(), classes, table, sd['t.bias'].bfloat16().cuda(),
+                                   add.cuda(), table, sd['t.bias'].bfloat16().cuda(), add.cuda())
+    torch.testing.assert_close(out_b.float().cpu().reshape(2, 256, d), want, atol=1e-2, rtol=1e-2)
+    assert torch.equal(out_b, out_c)
