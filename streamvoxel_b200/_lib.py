@@ -137,6 +137,17 @@ def require_device(device=None):
 
 
 def ptr(tensor):
+    """Raw device pointer of a contiguous tensor (None -> NULL). Non-contiguous views would be read with the wrong
+    strides by the kernels, so they are rejected."""
+    if tensor is None:
+        return ctypes.c_void_p(0)
+    if not tensor.is_contiguous():
+        raise ValueError('libsvx operands must be contiguous tensors')
+    return ctypes.c_void_p(tensor.data_ptr())
+
+
+def raw_ptr(tensor):
+    """Device pointer of a strided view whose strides the callee takes as explicit arguments."""
     return ctypes.c_void_p(0 if tensor is None else tensor.data_ptr())
 
 

@@ -294,8 +294,10 @@ __global__ void ease_block_select_kernel(const float* __restrict__ scores, const
   if (lane == 0 && count) atomicAdd(got + slot, count);
 }
 
+// Total order of (score descending, voxel index ascending) as one unsigned key. -0.0 and +0.0 compare equal in the
+// reference's sort, so both map to the key of +0.0 and tie-break on the index.
 __device__ __forceinline__ uint64_t order_key(float score, int n) {
-  uint32_t u = __float_as_uint(score);
+  uint32_t u = score == 0.0f ? 0u : __float_as_uint(score);
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   return (uint64_t(u) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(n));
 }

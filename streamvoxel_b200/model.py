@@ -1,0 +1,416 @@
+"""Model configuration, seeded weights, device weight preparation and the per-window condition encoder.
+
+The network is the reference's live model: a time-free AdaLN DiT backbone (`streamvoxel/models/
+unconditional_md4_timefree.py`) plus a CompactStreamingControlNet with full width (`streamvoxel/models/
+compact_controlnet.py`). Weights use the reference's state-dict names, so a reference checkpoint's state dict loads
+unchanged. Everything a time-free model holds constant is precomputed here once, on the device, with the same torch
+operations and bf16 autocast rounding the reference applies every forward:
+
+* AdaLN vectors `ada(constant_time)` per block and the final `final_ada` (`timefree.py:58,120-121,171`);
+* the per-position y-embedding `y_embed(y)` (`timefree.py:166-168`) and both RoPE sin/cos tables (`:24-30`);
+* the patch-embed gather tables `GatherPatch.table` (`streamvoxel/stream/fast_ops.py:61-67`);
+* the class head reordered so its output columns are class-major (n = v*64 + o).
+
+The per-step forward then runs entirely in libsvx (`svx_engine_forward`).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field, replace
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from streamvoxel_b200 import _lib, ops
+from streamvoxel_b200._lib import check
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    classes: int = 256                  # V; the mask token id is V
+    voxel_shape: tuple = (256, 16, 16)  # Y, Z, X
+    patch: int = 4
+    d: int = 768
+    heads: int = 8                      # head_dim 96 (= d / heads), the only width the axial RoPE allows at d=768
+    depth: int = 12
+    mlp: int = 3072
+    layer_indices: tuple = tuple(range(12))  # backbone layer fed by each control layer
+    biome_halo: int = 4
+    biome_patch: int = 4
+    biome_classes: int = 16
+    y_range: tuple = (-64., 192.)
+
+    @property
+    def patches(self):
+        y, z, x = self.voxel_shape
+        return (y // 4) * (z // 4) * (x // 4)
+
+    @property
+    def head_dim(self):
+        return self.d // self.heads
+
+    def condition_widths(self):
+        """`streamvoxel/stream/engine.py:60-72`: tokens of one L1 tile, one L2 tile and the biome window."""
+        height, tile = self.voxel_shape[0], self.voxel_shape[1]
+        l1 = (height // 4) * (tile // 4) * (tile // 4)
+        l2 = (height // 16) * (tile // 16) * (tile // 16)
+        if self.biome_halo == 16 and self.biome_patch == 1:
+            biome = (height // 4) * 12 * 12
+        else:
+            side = 6 if self.biome_halo == 4 else 12
+            side += (-side) % self.biome_patch
+            biome = (height // 4 // self.biome_patch) * (side // self.biome_patch) ** 2
+        return l1, l2, biome
+
+
+def dit_b4_control():
+    """DiT-B/4 (d=768, 8 heads x 96, MLP 3072, 12 layers, V=256) + 12-layer ControlNet."""
+    return ModelConfig()
+
+
+def dit_b4_unconditional():
+    """the time-free DiT-B/4 alone (no ControlNet)."""
+    return ModelConfig(layer_indices=())
+
+
+def small_test_config(**overrides):
+    """A small model with the same kernels (head_dim 96) for parity tests: d=192, 2 heads, 3 layers, V=32."""
+    base = ModelConfig(classes=32, voxel_shape=(64, 16, 16), d=192, heads=2, depth=3, mlp=768, layer_indices=(0, 2),
+                       biome_classes=16)
+    return replace(base, **overrides)
+
+
+def state_dict_shapes(cfg):
+    """Every parameter the live path reads, with the reference's names and shapes (no buffers, no time MLP)."""
+    d, v, m = cfg.d, cfg.classes, cfg.mlp
+    shapes = {}
+
+    def backbone_like(prefix, blocks):
+        shapes[f'{prefix}.target_patch.weight'] = (d, v + 1, 4, 4, 4)
+        shapes[f'{prefix}.target_patch.bias'] = (d,)
+        shapes[f'{prefix}.y_embed.0.weight'] = (d, 1)
+        shapes[f'{prefix}.y_embed.0.bias'] = (d,)
+        shapes[f'{prefix}.y_embed.2.weight'] = (d, d)
+        shapes[f'{prefix}.y_embed.2.bias'] = (d,)
+        shapes[f'{prefix}.constant_time'] = (d,)
+        for i in blocks:
+            b = f'{prefix}.blocks.{i}'
+            shapes.update({f'{b}.attn.qkv.weight': (3 * d, d), f'{b}.attn.qkv.bias': (3 * d,),
+                           f'{b}.attn.proj.weight': (d, d), f'{b}.attn.proj.bias': (d,),
+                           f'{b}.mlp.0.weight': (m, d), f'{b}.mlp.0.bias': (m,),
+                           f'{b}.mlp.2.weight': (d, m), f'{b}.mlp.2.bias': (d,),
+                           f'{b}.ada.1.weight': (6 * d, d), f'{b}.ada.1.bias': (6 * d,)})
+
+    backbone_like('backbone', range(cfg.depth))
+    shapes['backbone.final_ada.1.weight'] = (2 * d, d)
+    shapes['backbone.final_ada.1.bias'] = (2 * d,)
+    shapes['backbone.class_head.weight'] = (64 * v, d)
+    shapes['backbone.class_head.bias'] = (64 * v,)
+    if not cfg.layer_indices:
+        return shapes
+    backbone_like('control', range(len(cfg.layer_indices)))
+    for j in range(len(cfg.layer_indices)):
+        shapes.update({f'cross.{j}.query.weight': (d, d), f'cross.{j}.query.bias': (d,),
+                       f'cross.{j}.key_value.weight': (2 * d, d), f'cross.{j}.key_value.bias': (2 * d,),
+                       f'cross.{j}.proj.weight': (d, d), f'cross.{j}.proj.bias': (d,),
+                       f'zero.{j}.weight': (d, d), f'zero.{j}.bias': (d,)})
+    for name in ('l1_patch', 'l2_patch'):
+        shapes[f'{name}.weight'] = (d, v + 1, 4, 4, 4)
+        shapes[f'{name}.bias'] = (d,)
+    shapes.update({'l2_norm.weight': (d,), 'l2_norm.bias': (d,), 'l2_down.weight': (d, d, 4, 4, 4),
+                   'l2_down.bias': (d,), 'biome_embed.weight': (cfg.biome_classes, d),
+                   'type_embed.weight': (3, d), 'size_embed.weight': (2, d)})
+    if cfg.biome_patch > 1:
+        p = cfg.biome_patch
+        shapes['biome_down.weight'] = (d, d, p, p, p)
+        shapes['biome_down.bias'] = (d,)
+    if cfg.biome_patch == 2:
+        shapes['biome_size8'] = (d,)
+    return shapes
+
+
+def synthetic_state_dict(cfg, seed=0, std=0.02):
+    """Seeded random weights with the reference's names: every parameter re-drawn N(0, std^2) (the reference's own
+    init zeroes the head and AdaLN outputs, which makes every logit 0). fp32 on the CPU."""
+    g = torch.Generator().manual_seed(seed)
+    sd = {}
+    for name, shape in state_dict_shapes(cfg).items():
+        sd[name] = torch.empty(shape).normal_(0.0, std, generator=g)
+    return sd
+
+
+def _bf16(t, device):
+    return t.detach().to(device=device, dtype=torch.float32).to(torch.bfloat16).contiguous()
+
+
+def patch_centers_xyz(voxel_shape, patch):
+    """`unconditional_md4_timefree.py:84-86`: patch centres (x, y, z) in voxels, patch grid in YZX order."""
+    grid = torch.stack(torch.meshgrid(*(torch.arange(v // patch).float() for v in voxel_shape), indexing='ij'), -1)
+    return grid.reshape(-1, 3)[:, [2, 0, 1]] * patch + patch / 2
+
+
+def rope_frequencies(head_dim, base=10000.):
+    """`unconditional_md4_timefree.py:19-22`."""
+    axis = head_dim // 3
+    return base ** (-torch.arange(0, axis, 2).float() / axis)
+
+
+def rope_tables(positions, head_dim):
+    """sin/cos of `AxialRoPE.forward` (`timefree.py:26-27`): fp32 phases, rounded to bf16; [N, 3*16] axis-major."""
+    phase = positions.float()[..., None] * rope_frequencies(head_dim).to(positions.device)
+    n = positions.shape[0]
+    return (phase.sin().to(torch.bfloat16).reshape(n, -1).contiguous(),
+            phase.cos().to(torch.bfloat16).reshape(n, -1).contiguous())
+
+
+class PreparedModel:
+    """Device-resident bf16 weights and precomputed constants of one model (one per GPU)."""
+
+    def __init__(self, cfg, state_dict, device):
+        if cfg.patch != 4 or cfg.head_dim != 96:
+            raise ValueError('the kernels implement patch 4 and head_dim 96')
+        self.cfg = cfg
+        self.device = torch.device(device)
+        dev = self.device
+        sd = {k: v.detach().to(dev, torch.float32) for k, v in state_dict.items()}
+        self.sd = sd
+        origin = torch.tensor([0., float(cfg.y_range[0]), 0.], device=dev)
+        self.origin = origin
+        local = patch_centers_xyz(cfg.voxel_shape, 4).to(dev)
+        centers = local + origin
+        y = 2 * (centers[:, 1:2] - cfg.y_range[0]) / (cfg.y_range[1] - cfg.y_range[0]) - 1
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            self.backbone = [self._block(f'backbone.blocks.{i}', 'backbone.constant_time') for i in range(cfg.depth)]
+            self.control = [self._block(f'control.blocks.{j}', 'control.constant_time')
+                            for j in range(len(cfg.layer_indices))]
+            shift, gain = self._ada('backbone.final_ada', 'backbone.constant_time', 2)
+            self.final_shift, self.final_ops = shift, (1 + gain).contiguous()
+            self.yadd_b = self._y_embed('backbone.y_embed', y)
+            self.yadd_c = self._y_embed('control.y_embed', y) if cfg.layer_indices else self.yadd_b
+        # Self-attention positions are the local patch centres / 4; cross-attention queries use the group-relative
+        # centres (`compact_controlnet.py:104-108`), identical here because every slot shares the group origin.
+        self.rope_sin, self.rope_cos = rope_tables(local / 4, 96)
+        self.cross_sin, self.cross_cos = rope_tables((centers - origin) / 4, 96)
+        self.table_b, self.bias_b = self._table('backbone.target_patch')
+        self.table_c, self.bias_c = (self._table('control.target_patch') if cfg.layer_indices
+                                     else (self.table_b, self.bias_b))
+        v = cfg.classes
+        head_w = sd['backbone.class_head.weight'].reshape(64, v, cfg.d).transpose(0, 1).reshape(64 * v, cfg.d)
+        self.head_w = head_w.to(torch.bfloat16).contiguous()
+        self.head_b = sd['backbone.class_head.bias'].reshape(64, v).t().reshape(-1).to(torch.bfloat16).contiguous()
+        self.cross = []
+        for j in range(len(cfg.layer_indices)):
+            self.cross.append({n: _bf16(sd[f'cross.{j}.{n}'], dev) for n in
+                               ('query.weight', 'query.bias', 'proj.weight', 'proj.bias')} |
+                              {'zero.weight': _bf16(sd[f'zero.{j}.weight'], dev),
+                               'zero.bias': _bf16(sd[f'zero.{j}.bias'], dev)})
+        self.zero_yadd = torch.zeros((cfg.patches, cfg.d), device=dev, dtype=torch.bfloat16)
+        if cfg.layer_indices:
+            self.table_l1, self.bias_l1 = self._table('l1_patch')
+            self.table_l2, self.bias_l2 = self._table('l2_patch')
+
+    # -- constants
+    def _ada(self, prefix, time_key, count):
+        time = self.sd[time_key][None]
+        out = F.linear(F.silu(time), self.sd[prefix + '.1.weight'], self.sd[prefix + '.1.bias'])[0]
+        return [c.contiguous() for c in out.chunk(count)]
+
+    def _block(self, prefix, time_key):
+        s1, c1, g1, s2, c2, g2 = self._ada(prefix + '.ada', time_key, 6)
+        w = {n: _bf16(self.sd[f'{prefix}.{n}'], self.device) for n in
+             ('attn.qkv.weight', 'attn.qkv.bias', 'attn.proj.weight', 'attn.proj.bias', 'mlp.0.weight', 'mlp.0.bias',
+              'mlp.2.weight', 'mlp.2.bias')}
+        w.update(shift1=s1, ops1=(1 + c1).contiguous(), gate1=g1, shift2=s2, ops2=(1 + c2).contiguous(), gate2=g2)
+        return w
+
+    def _y_embed(self, prefix, y):
+        h = F.silu(F.linear(y, self.sd[prefix + '.0.weight'], self.sd[prefix + '.0.bias']))
+        return F.linear(h, self.sd[prefix + '.2.weight'], self.sd[prefix + '.2.bias']).contiguous()
+
+    def _table(self, prefix):
+        w = self.sd[prefix + '.weight']
+        table = w.permute(1, 2, 3, 4, 0).reshape(-1, w.shape[0]).to(torch.bfloat16).contiguous()
+        return table, self.sd[prefix + '.bias'].to(torch.bfloat16).contiguous()
+
+    # -- per-window condition encoder (runs once per window, on the caller's stream)
+    @torch.no_grad()
+    def encode_item(self, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes):
+        """Packed per-layer cross K/V of one window: `FastSlotForward.encode` (`streamvoxel/stream/fast_ops.py:228-239`)
+        = `encode_item` (`streamvoxel/stream/engine.py:75-84`) -> `encode_group` / `prefix_kv` / `local_condition`
+        (`streamvoxel/models/streaming_controlnet.py:160-219`) -> `local_kv` (`fast_ops.py:90-95`).
+        Returns [(k, v)] per control layer, each [heads, L, 96] bf16 (RoPE on k), prefix keys first."""
+        cfg, dev, sd = self.cfg, self.device, self.sd
+        height, tile = cfg.voxel_shape[0], cfg.voxel_shape[1]
+        pos1, pos2, bio_pos = _group_positions(l1_xz, l2_xz, height, tile, dev)
+        with torch.autocast('cuda', dtype=torch.bfloat16):
+            l2 = self._encode_columns(np.asarray(l2_blocks), 1).flatten(0, 1)
+            prefix = F.layer_norm(l2.float(), (cfg.d,), eps=1e-6)
+            l1 = F.layer_norm(self._encode_columns(np.asarray(l1_blocks), 0).float(), (cfg.d,), eps=1e-6)
+            bio, bio_positions = self._biome(torch.as_tensor(np.asarray(biomes), device=dev).long(), bio_pos)
+            local = torch.cat((l1.flatten(0, 1), bio), 0)
+            local_positions = torch.cat((pos1.reshape(-1, 3), bio_positions), 0)
+            layers = []
+            freq = rope_frequencies(96).to(dev)
+            for j in range(len(cfg.layer_indices)):
+                w, b = sd[f'cross.{j}.key_value.weight'], sd[f'cross.{j}.key_value.bias']
+                ks, vs = [], []
+                for value, positions in ((prefix, pos2), (local, local_positions)):
+                    k, v = F.linear(value, w, b).reshape(len(value), 2, cfg.heads, 96).unbind(1)
+                    k, v = k.transpose(0, 1), v.transpose(0, 1)
+                    ks.append(_rope(k, positions, freq))
+                    vs.append(v)
+                layers.append((torch.cat(ks, 1).to(torch.bfloat16), torch.cat(vs, 1).to(torch.bfloat16)))
+        return layers
+
+    def _encode_columns(self, tokens, level):
+        """`_encode_columns` (`streaming_controlnet.py:142-158`): one-hot conv patchify (the gather kernel), for L2 then
+        LayerNorm (affine) -> GELU -> 4^3 down-conv; plus the type and size embeddings (fp32 parameters)."""
+        cfg, dev, sd = self.cfg, self.device, self.sd
+        if len(tokens) == 0:
+            count = (tokens.shape[1] // (16 if level else 4)) * (1 if level else 16) if tokens.ndim == 4 else 0
+            return torch.zeros((0, count, cfg.d), device=dev)
+        t = torch.as_tensor(tokens, device=dev).to(torch.int16).contiguous()
+        table, bias = (self.table_l1, self.bias_l1) if level == 0 else (self.table_l2, self.bias_l2)
+        x, _ = ops.patch_embed(t, cfg.classes, table, bias, self.zero_yadd)
+        n = len(t)
+        x = x.reshape(n, cfg.patches, cfg.d)
+        if level:
+            x = F.gelu(F.layer_norm(x.float(), (cfg.d,), sd['l2_norm.weight'], sd['l2_norm.bias'], 1e-5))
+            h, w = cfg.voxel_shape[0] // 4, cfg.voxel_shape[1] // 4
+            grid = x.reshape(n, h, w, w, cfg.d).permute(0, 4, 1, 2, 3)
+            x = F.conv3d(grid, sd['l2_down.weight'], None, stride=4)
+            x = (x + sd['l2_down.bias'].to(x.dtype)[:, None, None, None]).flatten(2).transpose(1, 2)
+        return x + sd['type_embed.weight'][level] + sd['size_embed.weight'][level]
+
+    def _biome(self, biomes, bio_positions):
+        """`_biome_condition` (`streaming_controlnet.py:196-219`)."""
+        cfg, sd = self.cfg, self.sd
+        height = cfg.voxel_shape[0]
+        if cfg.biome_halo == 16 and cfg.biome_patch == 1:
+            values = F.embedding(biomes.reshape(-1), sd['biome_embed.weight'])
+            positions = bio_positions
+        else:
+            labels = biomes.reshape(1, height // 4, 12, 12)
+            positions = bio_positions.reshape(1, height // 4, 12, 12, 3)
+            if cfg.biome_halo == 4:
+                labels, positions = labels[:, :, 3:9, 3:9], positions[:, :, 3:9, 3:9]
+            values = F.embedding(labels, sd['biome_embed.weight']).permute(0, 4, 1, 2, 3)
+            p = cfg.biome_patch
+            if p > 1:
+                pad = (-labels.shape[-1]) % p
+                mask = values.new_ones((1, 1, height // 4, labels.shape[-2], labels.shape[-1]))
+                fraction = F.avg_pool3d(F.pad(mask, (0, pad, 0, pad)), p, p)
+                down = F.conv3d(F.pad(values, (0, pad, 0, pad)), sd['biome_down.weight'], None, stride=p)
+                down = down + sd['biome_down.bias'].to(down.dtype)[:, None, None, None]
+                values = down / fraction
+                coords = F.avg_pool3d(F.pad(positions.permute(0, 4, 1, 2, 3), (0, pad, 0, pad)), p, p) / fraction
+                positions = coords.flatten(2).transpose(1, 2)[0]
+            else:
+                positions = positions.reshape(-1, 3)
+            values = values.flatten(2).transpose(1, 2)[0]
+        size = sd['biome_size8'] if cfg.biome_patch == 2 else sd['size_embed.weight'][int(cfg.biome_patch == 4)]
+        values = values + sd['type_embed.weight'][2] + size
+        return F.layer_norm(values.float(), (cfg.d,), eps=1e-6), positions
+
+
+def _rope(x, positions, freq):
+    """`AxialRoPE.forward` on [H, N, D] bf16 (`timefree.py:24-30`): bf16 element-wise ops, fp32 phases."""
+    phase = positions.float()[..., None] * freq
+    sin, cos = phase.sin()[None].to(x.dtype), phase.cos()[None].to(x.dtype)
+    pairs = x.reshape(*x.shape[:-1], 3, x.shape[-1] // 6, 2)
+    a, b = pairs.unbind(-1)
+    return torch.stack((a * cos - b * sin, a * sin + b * cos), -1).flatten(-3)
+
+
+def _centers(shape, size):
+    """`streamvoxel/stream/condition.py:201-204`."""
+    grid = np.stack(np.meshgrid(*(np.arange(s) for s in shape), indexing='ij'), -1)
+    return (grid[..., [2, 0, 1]] * size + size / 2).reshape(-1, 3).astype(np.float32)
+
+
+def _group_positions(l1_xz, l2_xz, height, tile, device):
+    """Key positions of `build_group` (`streamvoxel/stream/condition.py:207-223`) in the target's frame."""
+    offsets = lambda xz: np.stack((xz[:, 0], np.zeros(len(xz)), xz[:, 1]), -1).astype(np.float32)
+    l1_xz, l2_xz = np.asarray(l1_xz).reshape(-1, 2), np.asarray(l2_xz).reshape(-1, 2)
+    pos1 = (_centers((height // 4, tile // 4, tile // 4), 4)[None] + offsets(l1_xz)[:, None]) / 4
+    pos2 = ((_centers((height // 16, 1, 1), 16)[None] + offsets(l2_xz)[:, None]) / 4).reshape(-1, 3)
+    bio = (_centers((height // 4, 12, 12), 4) + np.asarray([-tile, 0, -tile], np.float32)) / 4
+    return (torch.from_numpy(pos1).to(device), torch.from_numpy(pos2).to(device), torch.from_numpy(bio).to(device))
+
+
+class Engine:
+    """Owner of one `svx_engine` handle: packed K/V buffers, per-slot key lengths and the activation workspace."""
+
+    def __init__(self, model, slots, key_capacity):
+        cfg, dev = model.cfg, model.device
+        self.model, self.cfg, self.slots = model, cfg, int(slots)
+        self.key_capacity = int(key_capacity)
+        rows = self.slots * cfg.patches
+        bf = dict(device=dev, dtype=torch.bfloat16)
+        n_control = len(cfg.layer_indices)
+        self.kv = [(torch.zeros((self.slots, cfg.heads, self.key_capacity, 96), **bf),
+                    torch.zeros((self.slots, cfg.heads, self.key_capacity, 96), **bf)) for _ in range(n_control)]
+        self.lengths = torch.zeros(self.slots, dtype=torch.int32, device=dev)
+        self.ws = {n: torch.zeros((rows, w), **bf) for n, w in
+                   (('xb', cfg.d), ('xc', cfg.d), ('h', cfg.d), ('qkv', 3 * cfg.d), ('attn', cfg.d), ('mlp', cfg.mlp))}
+        p = lambda t: t.data_ptr()
+
+        def block(w):
+            return _lib.BlockWeights(p(w['attn.qkv.weight']), p(w['attn.qkv.bias']), p(w['attn.proj.weight']),
+                                     p(w['attn.proj.bias']), p(w['mlp.0.weight']), p(w['mlp.0.bias']),
+                                     p(w['mlp.2.weight']), p(w['mlp.2.bias']), p(w['shift1']), p(w['ops1']),
+                                     p(w['gate1']), p(w['shift2']), p(w['ops2']), p(w['gate2']))
+        self._backbone = (_lib.BlockWeights * cfg.depth)(*[block(w) for w in model.backbone])
+        self._control = (_lib.BlockWeights * max(1, n_control))(*[block(w) for w in model.control])
+        self._cross = (_lib.CrossWeights * max(1, n_control))(*[
+            _lib.CrossWeights(p(c['query.weight']), p(c['query.bias']), p(c['proj.weight']), p(c['proj.bias']),
+                              p(c['zero.weight']), p(c['zero.bias']), p(k), p(v))
+            for c, (k, v) in zip(model.cross, self.kv)])
+        self._layer_index = (ctypes.c_int32 * max(1, n_control))(*cfg.layer_indices)
+        y, z, x = cfg.voxel_shape
+        self._config = _lib.EngineConfig(self.slots, y, z, x, 4, cfg.classes, cfg.d, cfg.heads, cfg.mlp, cfg.depth,
+                                         self.key_capacity, n_control, self._layer_index)
+        self._weights = _lib.EngineWeights(
+            p(model.table_b), p(model.bias_b), p(model.yadd_b), p(model.table_c), p(model.bias_c), p(model.yadd_c),
+            self._backbone, self._control, self._cross, p(model.final_shift), p(model.final_ops), p(model.head_w),
+            p(model.head_b), p(model.rope_sin), p(model.rope_cos), p(model.cross_sin), p(model.cross_cos),
+            p(self.lengths))
+        self._workspace = _lib.EngineWorkspace(*[p(self.ws[n]) for n in ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp')])
+        handle = ctypes.c_void_p()
+        check(_lib.load().svx_engine_create(ctypes.byref(self._config), ctypes.byref(self._weights),
+                                            ctypes.byref(self._workspace), ctypes.byref(handle)), 'svx_engine_create')
+        self.handle = handle
+
+    def write_slot(self, index, layers):
+        """Copy one window's packed K/V into slot `index` (`FastSlotForward._write`, `fast_ops.py:241-250`)."""
+        length = layers[0][0].shape[1]
+        if length > self.key_capacity:
+            raise ValueError('Condition exceeds the captured capacity')
+        for (sk, sv), (k, v) in zip(self.kv, layers):
+            sk[index, :, :length].copy_(k)
+            sv[index, :, :length].copy_(v)
+            sk[index, :, length:].zero_()
+            sv[index, :, length:].zero_()
+        self.lengths[index] = length
+
+    def forward(self, n, tokens, logits, stream=None):
+        """Logits of the first n slots into `logits` [>= n, V, Y, Z, X] bf16 from int16 tokens."""
+        assert tokens.dtype == torch.int16 and tokens.is_contiguous() and logits.dtype == torch.bfloat16
+        check(_lib.load().svx_engine_forward(self.handle, int(n), _lib.ptr(tokens), _lib.ptr(logits),
+                                             _lib.stream_ptr(stream)), 'svx_engine_forward')
+        return logits
+
+    def launches(self, n):
+        return _lib.load().svx_engine_launches(self.handle, int(n))
+
+    def close(self):
+        if getattr(self, 'handle', None):
+            _lib.load().svx_engine_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -47,10 +47,10 @@ def _slots_view(logits):
     return s, c, voxels, c * voxels
 
 
-def ease_scores(logits, status=None):
+def ease_scores(logits, status=None, out=None):
     """Negative entropy per voxel of class-major logits [S, C, Y, Z, X] -> fp32 [S, Y, Z, X]."""
     s, c, voxels, stride = _slots_view(logits)
-    scores = torch.empty((s, *logits.shape[2:]), device=logits.device, dtype=torch.float32)
+    scores = out if out is not None else torch.empty((s, *logits.shape[2:]), device=logits.device, dtype=torch.float32)
     check(_lib.load().svx_ease_scores(ptr(logits), _dtype_code(logits), s, c, voxels, stride, ptr(scores), ptr(status),
                                       stream_ptr()), 'svx_ease_scores')
     return scores
@@ -175,7 +175,8 @@ def attention(q, k, v, slots, heads, queries, keys, *, q_row_stride, kv_slot_str
     """Non-causal head_dim-96 attention over per-slot key lengths; out [slots*queries, heads*96] bf16."""
     if out is None:
         out = torch.empty((slots * queries, heads * 96), device=q.device, dtype=torch.bfloat16)
-    check(_lib.load().svx_attention(ptr(q), q_row_stride, ptr(k), ptr(v), kv_slot_stride, kv_head_stride,
+    raw = _lib.raw_ptr
+    check(_lib.load().svx_attention(raw(q), q_row_stride, raw(k), raw(v), kv_slot_stride, kv_head_stride,
                                     kv_row_stride, ptr(lengths), slots, heads, queries, keys, ptr(out), stream_ptr()),
           'svx_attention')
     return out

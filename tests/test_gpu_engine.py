@@ -1,0 +1,129 @@
+"""The slot-batched forward (svx_engine_forward through FastSlotForward) against the CPU oracle's bf16 forward.
+
+Tolerance (BASELINE contract): logits within 2e-2 abs + 1e-2 rel of the reference bf16 forward on the same
+random-init weights and inputs. The oracle runs the reference's forward in fp32 arithmetic with the bf16 rounding points
+of CUDA autocast (`oracle/model.py`); it is fed the same packed K/V the engine holds, so this isolates the forward.
+The encoder is checked separately against the oracle encoder.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def _cfg_dict(cfg):
+    return dict(num_classes=cfg.classes, voxel_shape=cfg.voxel_shape, patch_size=4, depth=cfg.depth,
+                num_heads=cfg.heads, y_range=cfg.y_range, layer_indices=list(cfg.layer_indices),
+                biome_halo=cfg.biome_halo, biome_patch=cfg.biome_patch)
+
+
+def _engine(cfg, slots, seed=0, std=0.02, l1_cap=3, l2_cap=80):
+    from streamvoxel_b200 import model as sm
+    from streamvoxel_b200.stream.condition import ModelSpec
+    from streamvoxel_b200.stream.fast_ops import FastSlotForward
+    sd = sm.synthetic_state_dict(cfg, seed=seed, std=std)
+    spec = ModelSpec.of(cfg)
+    engine = FastSlotForward((cfg, sd), spec, 'cuda', slots, l1_cap, l2_cap)
+    return engine, sd, spec
+
+
+def _kv_of_slot(engine, slot):
+    length = int(engine.packed.lengths[slot])
+    return [(k[slot:slot + 1, :, :length].float().cpu(), v[slot:slot + 1, :, :length].float().cpu())
+            for k, v in engine.packed.kv]
+
+
+def _assert_logits(got, want):
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=RTOL)
+    agree = float((got.argmax(0) == want.argmax(0)).float().mean())
+    assert agree >= 0.99, agree
+
+
+def test_small_forward_matches_oracle_per_slot():
+    from streamvoxel_b200 import model as sm, synth
+    cfg = sm.small_test_config()
+    engine, sd, spec = _engine(cfg, 3, std=0.05, l1_cap=3, l2_cap=8)
+    tokens = []
+    for i, k in enumerate((0, 2, 3)):
+        engine.load_slot(i, synth.item(100 + i, spec, k=k, far=8))
+        t, _ = synth.target_tokens(200 + i, spec)
+        tokens.append(t)
+    engine.wait_loads()
+    engine.tokens.copy_(torch.from_numpy(np.stack(tokens)).cuda())
+    got = engine.eager(torch.ones(3)).float().cpu()
+    for i in range(3):
+        want = om.control_forward(sd, torch.from_numpy(tokens[i][None]).long(), _kv_of_slot(engine, i),
+                                  _cfg_dict(cfg), bf16=True)[0]
+        _assert_logits(got[i], want)
+
+
+def test_graph_replay_equals_eager_and_buckets_agree():
+    from streamvoxel_b200 import model as sm, synth
+    cfg = sm.small_test_config()
+    engine, sd, spec = _engine(cfg, 4, std=0.05, l1_cap=2, l2_cap=8)
+    for i in range(4):
+        engine.load_slot(i, synth.item(300 + i, spec, k=i % 3, far=8))
+    engine.wait_loads()
+    engine.tokens.copy_(torch.from_numpy(np.stack([synth.target_tokens(400 + i, spec)[0] for i in range(4)])).cuda())
+    assert sorted(engine.graphs) == [1, 2, 4]
+    eager = engine.eager(torch.ones(4)).clone()
+    replayed = engine.replay(torch.ones(4)).clone()
+    assert torch.equal(eager, replayed)
+    small = engine.replay(torch.ones(4), 2)[:2].clone()
+    assert torch.equal(small, eager[:2])   # row-independent kernels: the bucket does not change slot results
+    report = engine.numerical_gate(synth.item(500, spec, k=1, far=8), synth.item(501, spec, k=2, far=8))
+    assert report['graph_equal'] and report['padded_close'] and report['bucket_close']
+
+
+def test_encoder_matches_oracle_encoder():
+    from streamvoxel_b200 import model as sm, synth
+    cfg = sm.small_test_config()
+    engine, sd, spec = _engine(cfg, 1, std=0.05, l1_cap=3, l2_cap=8)
+    item = synth.item(600, spec, k=3, far=8)
+    got = engine.encode(item)
+    want = om.encode_kv(sd, item.l1_blocks, item.l1_xz, item.l2_blocks, item.l2_xz, item.biomes, _cfg_dict(cfg),
+                        bf16=True)
+    assert got[0][0].shape[1] == want[0][0].shape[2] == 8 * 16 + 3 * 256 + 16
+    for (gk, gv), (wk, wv) in zip(got, want):
+        torch.testing.assert_close(gk.float().cpu(), wk[0], atol=3e-2, rtol=2e-2)
+        torch.testing.assert_close(gv.float().cpu(), wv[0], atol=3e-2, rtol=2e-2)
+
+
+@pytest.mark.slow
+def test_full_size_control_forward_matches_oracle():
+    """DiT-B/4 + 12-layer ControlNet (BASELINE config 2 model), slot 1 of a 2-slot batch, k=2 L1 + 80 L2 + biome."""
+    from streamvoxel_b200 import model as sm, synth
+    cfg = sm.dit_b4_control()
+    engine, sd, spec = _engine(cfg, 2, l1_cap=8, l2_cap=81)
+    engine.load_slot(0, synth.item(700, spec, k=5))
+    engine.load_slot(1, synth.item(701, spec, k=2))
+    engine.wait_loads()
+    tokens = np.stack([synth.target_tokens(800 + i, spec)[0] for i in range(2)])
+    engine.tokens.copy_(torch.from_numpy(tokens).cuda())
+    got = engine.replay(torch.ones(2))[1].float().cpu()
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    want = om.control_forward(sd, torch.from_numpy(tokens[1:2]).long(), _kv_of_slot(engine, 1), _cfg_dict(cfg),
+                              bf16=True)[0]
+    _assert_logits(got, want)
+
+
+@pytest.mark.slow
+def test_full_size_unconditional_forward_matches_oracle():
+    """BASELINE config 1 model: the time-free DiT-B/4 alone, batch 1, a partially masked column."""
+    from streamvoxel_b200 import model as sm, synth
+    from streamvoxel_b200.model import Engine, PreparedModel
+    cfg = sm.dit_b4_unconditional()
+    sd = sm.synthetic_state_dict(cfg, seed=3)
+    model = PreparedModel(cfg, sd, 'cuda')
+    engine = Engine(model, 1, 0)
+    from streamvoxel_b200.stream.condition import ModelSpec
+    tokens, _ = synth.target_tokens(900, ModelSpec.of(cfg))
+    t = torch.from_numpy(tokens[None]).cuda()
+    logits = torch.empty((1, cfg.classes, *cfg.voxel_shape), dtype=torch.bfloat16, device='cuda')
+    got = engine.forward(1, t, logits)[0].float().cpu()
+    want = om.unconditional_forward(sd, torch.from_numpy(tokens[None]).long(), _cfg_dict(cfg), bf16=True)[0]
+    _assert_logits(got, want)

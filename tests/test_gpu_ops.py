@@ -295,7 +295,7 @@ def test_patch_embed_matches_gather(ops):
     want = om.patchify(sd, 't', tokens, classes, p)
     add = (torch.randn((256, d)) * 0.1).bfloat16()
     want = _bf16(want + add.float()[None])
-    table = sd['t.weight'].permute(1, 2, 3, 4, 0).reshape(-1, d).bfloat16().cuda()
+    table = sd['t.weight'].permute(1, 2, 3, 4, 0).reshape(-1, d).bfloat16().contiguous().cuda()
     out_b, out_c = ops.patch_embed(tokens.to(torch.int16).cuda(), classes, table, sd['t.bias'].bfloat16().cuda(),
                                    add.cuda(), table, sd['t.bias'].bfloat16().cuda(), add.cuda())
     torch.testing.assert_close(out_b.float().cpu().reshape(2, 256, d), want, atol=1e-2, rtol=1e-2)
