@@ -51,8 +51,14 @@ class Precision:
         return self.r(a * b)
 
     def sdpa(self, q, k, v):
-        """`F.scaled_dot_product_attention` (non-causal, scale 1/sqrt(D)); bf16 output under autocast."""
-        return self.r(F.scaled_dot_product_attention(q, k, v))
+        """`F.scaled_dot_product_attention` (non-causal, scale 1/sqrt(D)). Under CUDA autocast SDPA runs a flash-style
+        bf16 kernel: fp32 scores and row sums, the unnormalised probabilities rounded to bf16 for the P.V product,
+        the output normalised in fp32 and rounded to bf16. The bf16 emulation follows those rounding points."""
+        if not self.bf16:
+            return F.scaled_dot_product_attention(q, k, v)
+        s = (q @ k.transpose(-1, -2)) * (1.0 / q.shape[-1] ** 0.5)
+        p = torch.exp(s - s.amax(-1, keepdim=True))
+        return self.r((self.r(p) @ v) / p.sum(-1, keepdim=True))
 
 
 # ------------------------------------------------------------------------------------------------- RoPE

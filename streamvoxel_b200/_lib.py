@@ -131,7 +131,11 @@ def require_device(device=None):
     if not torch.cuda.is_available():
         raise RuntimeError('streamvoxel_b200 needs a CUDA device (B200, sm_100a); no CPU fallback exists')
     if device is not None:
-        torch.cuda.set_device(device)
+        device = torch.device(device)
+        if device.type != 'cuda':
+            raise RuntimeError(f'streamvoxel_b200 runs on CUDA devices only, got {device}')
+        if device.index is not None:
+            torch.cuda.set_device(device)
     if not load().svx_device_supported():
         raise RuntimeError('streamvoxel_b200 kernels are built for sm_100a (B200) only')
 
