@@ -1,0 +1,395 @@
+"""Committed voxels/s of StreamVoxel's column-generation step on B200 (BASELINE.json `metric`, config 2 workload).
+
+One step = one slot-batched bf16 forward of DiT-B/4 + 12-layer ControlNet over 8 slots with cached packed K/V,
+followed by the EASE step of every slot (entropy, 4^3 block-quota selection, low-entropy-last deferral, counter-based
+categorical draw, token commit), all in one CUDA graph. Windows run their whole schedule (1 marking + up to 32 solid
+forwards, cap 32, quartercos) and are re-armed when they finish; committed voxels count every voxel a window commits,
+the deferred ones at its finish (`streamvoxel/stream/slot.py:166-176`).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1: one process per GPU (torchrun), each with its own 8 slots and no collective on the data path (windows shard
+by dependency-safe admission); rank 0 prints the whole-job line with the time = max over ranks. `--impl reference`
+times the reference algorithm's CPU path (the oracle port: fp32 torch forward + numpy EASE step) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = 'committed voxels/s per B200 (8 slots)'
+UNIT = 'voxels/s'
+SLOTS, L1_CAP, L2_CAP, CAP = 8, 8, 81, 32
+WORKLOAD = 'config2: DiT-B/4 (d=768, 8x96 heads, 12 layers, V=256) + 12-layer ControlNet, 8 slots, bf16, cached K/V'
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=66)
+    p.add_argument('--warmup', type=int, default=5)
+    p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    p.add_argument('--cpu-sample', type=int, default=1, help='slot-forwards in the CPU baseline sample')
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    return rank, world, local
+
+
+# ------------------------------------------------------------------------------------------------- clocks
+
+class Clocks:
+    """nvidia-smi samples of SM clocks and throttle reasons during the timed region."""
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+             'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+             'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.QUERY}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([v.strip() for v in line.split(',')])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=['nvidia-smi unavailable'], samples=0)
+        sm = [float(r[1]) for r in self.rows if r[1].replace('.', '').isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace('.', '').isdigit()]
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.strip().lower() == 'active'})
+        return dict(sm_mhz=float(np.median(sm)) if sm else None, sm_max_mhz=max(mx) if mx else None,
+                    reasons=reasons, samples=len(self.rows))
+
+
+# ------------------------------------------------------------------------------------------------ ours
+
+def build(device, seed=0):
+    from streamvoxel_b200 import model as sm, synth
+    from streamvoxel_b200.stream.batch import SlotBatch
+    from streamvoxel_b200.stream.condition import ModelSpec
+    from streamvoxel_b200.stream.fast_ops import FastSlotForward
+    cfg = sm.dit_b4_control()
+    sd = sm.synthetic_state_dict(cfg, seed=seed)
+    spec = ModelSpec.of(cfg)
+    forward = FastSlotForward((cfg, sd), spec, device, SLOTS, L1_CAP, L2_CAP)
+    rng = np.random.default_rng(seed)
+    lengths = []
+    for i in range(SLOTS):
+        forward.load_slot(i, synth.item(int(rng.integers(1 << 30)), spec))
+    forward.wait_loads()
+    lengths = forward.packed.lengths.tolist()
+    batch = SlotBatch(forward)
+    return cfg, sd, forward, batch, lengths
+
+
+def run_device_steps(batch, steps, seeds):
+    """Exactly `steps` forwards, device-resident inside each window (see `SlotBatch.run_cycles`). Returns
+    (committed voxels, kernel launches, marking forwards)."""
+    from streamvoxel_b200.stream.batch import EASE_LAUNCHES
+    committed = launches = markings = 0
+    per_step = batch.launches()
+    done = 0
+    it = iter(seeds)
+    while done < steps:
+        for i in range(batch.slots):
+            batch.arm(i, next(it), CAP)
+        batch.params.zero_()
+        batch.graph.replay()
+        batch._mark(range(batch.slots))
+        counts = batch.last_count.tolist()
+        batch._after_mark(range(batch.slots), counts)
+        launches += per_step + 2 * batch.slots
+        markings += 1
+        done += 1
+        staged, ks = [], []
+        while done + len(staged) < steps and any(st['solid_calls'] < len(st['quotas']) for st in batch.state):
+            rows = batch._rows()
+            staged.append(batch._pack(rows))
+            ks.append(sum(r[0] for r in rows))
+            for st in batch.state:
+                if st['solid_calls'] < len(st['quotas']):
+                    st['solid_calls'] += 1
+                    st['nfe'] += 1
+        if staged:
+            table = torch.stack(staged).to(batch.device)
+            for s in range(len(staged)):
+                batch.params.copy_(table[s])
+                batch.graph.replay()
+            launches += len(staged) * per_step
+            done += len(staged)
+            committed += sum(ks)
+        if all(st['solid_calls'] >= len(st['quotas']) for st in batch.state):
+            for i in range(batch.slots):
+                batch._finish(i)
+                committed += counts[i]   # deferred voxels are committed at finish
+    return committed, launches, markings
+
+
+def run_api_steps(batch, steps, seeds):
+    """Exactly `steps` forwards through `SlotBatch.step` (per-step H2D scalars, D2H commits, host bookkeeping)."""
+    committed = h2d = d2h = 0
+    it = iter(seeds)
+    for i in range(batch.slots):
+        if batch.state[i]['phase'] == 'idle':
+            batch.arm(i, next(it), CAP)
+    for _ in range(steps):
+        rows = batch._rows()
+        kmax = max([r[0] for r in rows] + [0])
+        h2d += batch.params_host.numel()
+        d2h += (2 * batch.slots) * 4 + (batch.slots * kmax * (4 + 2) if kmax else 0)
+        results = batch.step()
+        for i, (record, commit) in results.items():
+            if commit is not None:
+                committed += len(commit['positions'])
+            if record is not None:
+                committed += record['last_count']
+                batch.arm(i, next(it), CAP)
+    return committed, h2d, d2h
+
+
+def time_kernels(cfg, forward, batch, lengths):
+    """Average launch duration of each kernel class of the step at the step's shapes (CUDA events, 20 launches)."""
+    from streamvoxel_b200 import ops, _lib
+    dev = forward.device
+    rows, d, heads = SLOTS * cfg.patches, cfg.d, cfg.heads
+    ws = forward.engine.ws
+    m = forward.model
+    bw, cw = m.backbone[0], m.cross[0]
+    k0, v0 = forward.engine.kv[0]
+    tables = m.rope_sin, m.rope_cos
+
+    def clock(fn, reps=20):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps * 1e-3
+
+    mean_len = float(np.mean(lengths))
+    kernels = {
+        'gemm_qkv_rope': (lambda: ops.gemm(ws['h'], bw['attn.qkv.weight'], bw['attn.qkv.bias'], _lib.EPI_ROPE,
+                                           out=ws['qkv'], rope=tables, rope_cols=2 * d, rows_per_slot=cfg.patches),
+                          2.0 * rows * d * 3 * d, 24),
+        'gemm_fc1_gelu': (lambda: ops.gemm(ws['h'], bw['mlp.0.weight'], bw['mlp.0.bias'], _lib.EPI_BIAS_GELU,
+                                           out=ws['mlp']), 2.0 * rows * d * cfg.mlp, 24),
+        'gemm_fc2_gate': (lambda: ops.gemm(ws['mlp'], bw['mlp.2.weight'], bw['mlp.2.bias'], _lib.EPI_GATE_RESIDUAL,
+                                           out=ws['xb'], gate=bw['gate2'], residual=ws['xb']),
+                          2.0 * rows * cfg.mlp * d, 24),
+        'gemm_dxd': (lambda: ops.gemm(ws['attn'], bw['attn.proj.weight'], bw['attn.proj.bias'],
+                                      _lib.EPI_GATE_RESIDUAL, out=ws['xb'], gate=bw['gate1'], residual=ws['xb']),
+                     2.0 * rows * d * d, 24 + 4 * 12),
+        'gemm_head': (lambda: ops.gemm(ws['h'], m.head_w, m.head_b, _lib.EPI_CLASS_MAJOR, out=forward.logits,
+                                       rows_per_slot=cfg.patches, classes=cfg.classes, geometry=cfg.voxel_shape),
+                      2.0 * rows * d * 64 * cfg.classes, 1),
+        'attention_self': (lambda: ops.attention(ws['qkv'], ws['qkv'][:, d:], ws['qkv'][:, 2 * d:], SLOTS, heads,
+                                                 cfg.patches, cfg.patches, q_row_stride=3 * d,
+                                                 kv_slot_stride=cfg.patches * 3 * d, kv_head_stride=96,
+                                                 kv_row_stride=3 * d, out=ws['attn']),
+                           4.0 * SLOTS * heads * cfg.patches * cfg.patches * 96, 24),
+        'attention_cross': (lambda: ops.attention(ws['qkv'], k0, v0, SLOTS, heads, cfg.patches, k0.shape[2],
+                                                  q_row_stride=d, kv_slot_stride=heads * k0.shape[2] * 96,
+                                                  kv_head_stride=k0.shape[2] * 96, kv_row_stride=96,
+                                                  lengths=forward.engine.lengths, out=ws['attn']),
+                            4.0 * SLOTS * heads * cfg.patches * mean_len * 96, 12),
+        'ease_scores': (lambda: ops.ease_scores(forward.logits, batch.status, out=batch.scores),
+                        float(forward.logits.numel() * 2 + batch.scores.numel() * 4), 1),
+    }
+    out = {}
+    for name, (fn, work, count) in kernels.items():
+        t = clock(fn)
+        out[name] = dict(seconds=t, work=work, per_step=count, share_seconds=t * count)
+    return out
+
+
+def cpu_baseline(cfg, sd, lengths, sample=1):
+    """The reference's CPU path (oracle port: fp32 torch forward + numpy EASE step) on the host cores for `sample`
+    slot-forwards of the same workload (one slot, its own packed K/V length), in committed voxels/s."""
+    from oracle import model as om
+    from oracle import sampler as osm
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfgd = dict(num_classes=cfg.classes, voxel_shape=cfg.voxel_shape, patch_size=4, depth=cfg.depth,
+                num_heads=cfg.heads, y_range=cfg.y_range, layer_indices=list(cfg.layer_indices))
+    rng = np.random.default_rng(1)
+    length = int(np.median(lengths))
+    kv = [(torch.randn(1, cfg.heads, length, 96), torch.randn(1, cfg.heads, length, 96)) for _ in cfg.layer_indices]
+    tokens = torch.full((1, *cfg.voxel_shape), cfg.classes, dtype=torch.long)
+    total = int(np.prod(cfg.voxel_shape))
+    quotas = osm.low_entropy_last_quotas(total, CAP, 0)
+    began = time.perf_counter()
+    with torch.no_grad():
+        for s in range(sample):
+            logits = om.control_forward(sd, tokens, kv, cfgd)[0].numpy()
+            slot = osm.Slot(cfg.voxel_shape, cfg.classes, (0,), 0, 1e-4, 4)
+            slot.arm(s, CAP, (), rng.permutation(total // 64))
+            slot.phase, slot.quotas, slot.last = 'solid', quotas, np.zeros(cfg.voxel_shape, bool)
+            slot.solid_calls = 0
+            slot.consume(logits, tokens[0].numpy().copy(), native=True)
+    seconds = (time.perf_counter() - began) / sample
+    per_forward = total / (1 + len(quotas))   # voxels a slot commits per forward, averaged over its window
+    return dict(value=per_forward / seconds, unit=UNIT, cores=threads, kind='port',
+                sample=f'{sample} slot-forward(s) of the config-2 model (fp32, K/V length {length}) + one EASE solid '
+                       f'step on [256, 65536]; {seconds:.2f} s each; voxels/s = 65536/33 per slot-forward')
+
+
+def main_ours(args):
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300))
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    from streamvoxel_b200 import _lib
+    _lib.require_device(device)
+    cfg, sd, forward, batch, lengths = build(device, seed=rank)
+    seeds = list(range(rank * 1_000_000, rank * 1_000_000 + 100_000))
+    # warm-up: W forwards through the public step path
+    run_api_steps(batch, max(3, args.warmup), iter(seeds[50_000:]))
+    for i in range(batch.slots):
+        batch.state[i] = dict(phase='idle')
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        barrier()
+        start.record()
+        committed, launches, markings = run_device_steps(batch, args.steps, iter(seeds))
+        stop.record()
+        barrier()
+    seconds = max_over_ranks(start.elapsed_time(stop) * 1e-3)
+    total_committed = committed * world if world > 1 else committed
+    value = total_committed / seconds
+    # end to end through the public step API (host scalars in, commits out, host bookkeeping), same step count
+    for i in range(batch.slots):
+        batch.state[i] = dict(phase='idle')
+    barrier()
+    start.record()
+    e2e_committed, h2d, d2h = run_api_steps(batch, args.steps, iter(seeds[10_000:]))
+    stop.record()
+    barrier()
+    e2e_seconds = max_over_ranks(start.elapsed_time(stop) * 1e-3)
+    e2e_value = e2e_committed * world / e2e_seconds
+    kernels = time_kernels(cfg, forward, batch, lengths)
+    if rank != 0:
+        return
+    peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json'))) if os.path.exists(
+        os.path.join(ROOT, 'MEASURED_PEAKS.json')) else {}
+    dominant = max(kernels, key=lambda k: kernels[k]['share_seconds'])
+    kd = kernels[dominant]
+    if dominant.startswith('ease'):
+        peak, unit, bound, src = peaks.get('hbm_gbs', 6650.0), 'GB/s', 'hbm', 'measured' if peaks else 'fallback'
+        achieved = kd['work'] / kd['seconds'] / 1e9
+    else:
+        peak, unit, bound = peaks.get('bf16_tflops', 1590.0), 'TFLOP/s', 'tensor'
+        src = 'measured (burst; kernel timed alone)' if peaks else 'fallback'
+        achieved = kd['work'] / kd['seconds'] / 1e12
+    step_flops = sum(k['work'] * k['per_step'] for n, k in kernels.items() if not n.startswith('ease'))
+    cpu = cpu_baseline(cfg, sd, lengths, args.cpu_sample)
+    steps_per_s = args.steps / seconds
+    line = dict(
+        metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+        ms_per_step=seconds / args.steps * 1e3, higher_is_better=True, scaling='weak', vs_baseline=None,
+        dtype='bf16', data='synthetic (seeded world generator, random-init N(0,0.02) weights)',
+        config=dict(workload=WORKLOAD, slots_per_gpu=SLOTS, cap=CAP, l1_cap=L1_CAP, l2_cap=L2_CAP,
+                    mean_packed_keys=float(np.mean(lengths)), sampler='EASE native Philox draw',
+                    l2_policy='inputs larger than L2 (268 MB logits + 0.86 GB weights per step)',
+                    parallelism=f'{world} independent engines, no collective'),
+        forwards_per_s=steps_per_s * world, marking_forwards=markings,
+        e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d / args.steps, d2h_bytes_per_step=d2h / args.steps),
+        gpu_launches=launches,
+        roofline=dict(kernel=dominant, bound=bound, achieved=achieved, peak=peak, unit=unit, frac=achieved / peak,
+                      peak_source=src, traffic=None,
+                      algorithmic=f"{kd['work']:.4g} {'bytes' if bound == 'hbm' else 'FLOP'} per launch"),
+        step_tflops=step_flops / (seconds / args.steps) / 1e12,
+        kernels={k: dict(us=v['seconds'] * 1e6, per_step=v['per_step'],
+                         rate=(v['work'] / v['seconds'] / (1e9 if k.startswith('ease') else 1e12)))
+                 for k, v in kernels.items()},
+        cpu_baseline=cpu, clocks=clocks.summary())
+    print(json.dumps(line), flush=True)
+
+
+def main_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from streamvoxel_b200 import model as sm
+    cfg = sm.dit_b4_control()
+    sd = sm.synthetic_state_dict(cfg, seed=0)
+    lengths = [1280 + 1024 * 4 + 64]   # k = 4 L1 tiles + 80 L2 columns + 64 biome tokens (mean of k ~ U{0..8})
+    began = time.perf_counter()
+    result = cpu_baseline(cfg, sd, lengths, min(max(1, args.steps), 3))
+    seconds = time.perf_counter() - began
+    line = dict(metric=METRIC, value=result['value'], unit=UNIT, n_gpus=world, steps=args.steps,
+                warmup=args.warmup, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
+                data='synthetic', impl='reference',
+                config=dict(workload=WORKLOAD, sample=result['sample']),
+                cpu_baseline=result, e2e=dict(value=result['value'], unit=UNIT, h2d_bytes_per_step=0,
+                                              d2h_bytes_per_step=0), seconds=seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        main_reference(args)
+    else:
+        main_ours(args)
+
+
+if __name__ == '__main__':
+    main()

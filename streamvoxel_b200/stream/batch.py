@@ -1,0 +1,216 @@
+"""All slots of one engine stepping together: the worker's engine step (`streamvoxel/stream/worker.py:378-399`) as one
+CUDA graph per step -- the slot-batched forward, then entropy, block-quota selection, the categorical draw and the
+token commit for every slot in the same graph, with no host read inside.
+
+Per-window work stays outside the graph, as in the reference: the block order (`torch.randperm` on the device with the
+window seed + 9173, `streamvoxel/stream/slot.py:97-99`), the marking forward's last mask and its count (one host read,
+`slot.py:130`) and the quartercos quota list. Slots that are marking, finished or idle take k = 0 in the step graph.
+
+Two drivers:
+* `step()` -- one forward for every armed slot with the host bookkeeping of `consume_batch`: per-step scalars copied
+  H2D from pinned memory, commits copied D2H and returned (the worker-facing path, one host wait per forward);
+* `run_cycles(n)` -- n whole windows per slot back to back on the device: the scalars of every step are staged once per
+  window, so the host never waits inside a window (device-resident throughput).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from streamvoxel_b200 import ops
+from streamvoxel_b200.sampling import low_entropy_last_quotas
+
+EASE_LAUNCHES = 5   # scores, quota, block select, fix-up/compaction, sample
+
+
+class SlotBatch:
+    def __init__(self, forward, *, air_ids=(0,), air_token=0, last_eps=1e-4, block_size=4, sampling='native'):
+        if sampling != 'native':
+            raise ValueError('the whole-step graph draws with the native counter-based sampler')
+        if block_size != 4:
+            raise ValueError('the selection kernel implements 4^3 blocks')
+        self.forward = forward
+        self.device = forward.device
+        self.slots = forward.batch
+        self.shape = forward.shape
+        self.total = int(np.prod(self.shape))
+        self.classes = forward.classes
+        self.air_ids, self.air_token, self.last_eps = tuple(air_ids), int(air_token), float(last_eps)
+        dev, b = self.device, self.slots
+        self.blocks = self.total // 64
+        self.params = torch.zeros(b * ops.STEP_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+        self.params_host = torch.zeros(b * ops.STEP_DTYPE.itemsize, dtype=torch.uint8, pin_memory=True)
+        self.pos = torch.zeros((b, self.blocks), dtype=torch.int32, device=dev)
+        self.last = torch.zeros((b, *self.shape), dtype=torch.uint8, device=dev)
+        self.last_count = torch.zeros(b, dtype=torch.int32, device=dev)
+        self.scores = torch.zeros((b, *self.shape), dtype=torch.float32, device=dev)
+        self.chosen = torch.zeros((b, *self.shape), dtype=torch.uint8, device=dev)
+        self.index = torch.zeros((b, self.total), dtype=torch.int32, device=dev)
+        self.count = torch.zeros(b, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(b, dtype=torch.int32, device=dev)
+        self.values = torch.zeros((b, self.total), dtype=torch.int16, device=dev)
+        self.workspace = ops.select_workspace(b, self.total, dev)
+        self.host_index = torch.zeros((b, self.total), dtype=torch.int32, pin_memory=True)
+        self.host_values = torch.zeros((b, self.total), dtype=torch.int16, pin_memory=True)
+        self.host_small = torch.zeros(2 * b, dtype=torch.int32, pin_memory=True)
+        self.state = [dict(phase='idle') for _ in range(b)]
+        self.graph = None
+        self._capture()
+
+    # -- device work of one step
+    def _ease(self):
+        logits = self.forward.logits
+        ops.ease_scores(logits, self.status, out=self.scores)
+        ops.ease_select(self.scores, self.forward.tokens, self.last, self.pos, self.params, self.classes, self.total,
+                        chosen=self.chosen, index=self.index, count=self.count, status=self.status,
+                        workspace=self.workspace)
+        ops.ease_sample(logits, self.index, self.params, self.forward.tokens, values=self.values, status=self.status)
+
+    def _device_step(self):
+        self.forward._call(self.slots)
+        self._ease()
+
+    def _capture(self):
+        self.params.zero_()
+        current = torch.cuda.current_stream(self.device)
+        warm = torch.cuda.Stream(device=self.device)
+        warm.wait_stream(current)
+        with torch.cuda.stream(warm):
+            for _ in range(3):
+                self._device_step()
+        current.wait_stream(warm)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=self.device), capture_error_mode='thread_local'):
+            self._device_step()
+        self.graph = graph
+
+    def launches(self):
+        """Kernel launches in one step graph."""
+        return self.forward.engine.launches(self.slots) + EASE_LAUNCHES
+
+    # -- windows
+    def arm(self, slot, seed, cap, item=None, target=()):
+        """Start a window in `slot` (`LowEntropyLastSlot.arm`, `slot.py:86-103`); `item` loads its conditions."""
+        if item is not None:
+            self.forward.load_slot(slot, item)
+            self.forward.wait_loads()
+        else:
+            self.forward.tokens[slot].fill_(self.classes)
+        g = torch.Generator(device=self.device).manual_seed(int(seed) + 9173)
+        order = torch.randperm(self.blocks, device=self.device, generator=g)
+        self.pos[slot, order] = torch.arange(self.blocks, device=self.device, dtype=torch.int32)
+        self.last[slot].zero_()
+        self.state[slot] = dict(phase='marking', seed=int(seed), cap=int(cap), target=tuple(target), nfe=0,
+                                solid_calls=0, quotas=None, last_count=0)
+
+    def _rows(self):
+        rows = []
+        for st in self.state:
+            if st['phase'] == 'solid' and st['solid_calls'] < len(st['quotas']):
+                k = st['quotas'][st['solid_calls']]
+                committed = sum(st['quotas'][:st['solid_calls']])
+                frac = (committed + k) / (self.total - st['last_count'])
+                rows.append((k, st['nfe'] + 1, committed, frac, st['seed']))
+            else:
+                rows.append((0, 0, 0, 0.0, 0))
+        return rows
+
+    def _pack(self, rows):
+        arr = np.zeros(len(rows), ops.STEP_DTYPE)
+        for i, row in enumerate(rows):
+            arr[i] = (row[0], row[1], row[2], row[3], row[4] & 0xFFFFFFFFFFFFFFFF)
+        return torch.from_numpy(arr.view(np.uint8))
+
+    def _mark(self, marking):
+        logits = self.forward.logits
+        for i in marking:
+            ops.ease_mark(logits[i:i + 1], self.air_ids, self.last_eps, last=self.last[i:i + 1],
+                          last_count=self.last_count[i:i + 1])
+
+    def _after_mark(self, marking, counts):
+        finished = []
+        for i in marking:
+            st = self.state[i]
+            st['nfe'] += 1
+            st['last_count'] = int(counts[i])
+            st['quotas'] = low_entropy_last_quotas(self.total, st['cap'], st['last_count'], 'quartercos')
+            st['phase'] = 'solid'
+            if not st['quotas']:
+                finished.append(i)
+        return finished
+
+    def _finish(self, i):
+        """`_finish` (`slot.py:166-176`): deferred voxels take air_token; returns the window record."""
+        st = self.state[i]
+        self.forward.tokens[i].masked_fill_(self.last[i].bool(), self.air_token)
+        st['phase'] = 'idle'
+        return dict(target=st['target'], seed=st['seed'], cap=st['cap'], nfe=st['nfe'], actual=st['solid_calls'],
+                    last_count=st['last_count'], last_frac=st['last_count'] / self.total)
+
+    def step(self):
+        """One forward for every armed slot with its EASE step; returns {slot: (record|None, commit|None)}."""
+        marking = [i for i, st in enumerate(self.state) if st['phase'] == 'marking']
+        rows = self._rows()
+        solid = [i for i, r in enumerate(rows) if r[0] > 0]
+        self.params_host.copy_(self._pack(rows))
+        self.params.copy_(self.params_host, non_blocking=True)
+        self.status.zero_()
+        self.graph.replay()
+        self._mark(marking)
+        kmax = max([r[0] for r in rows] + [0])
+        if kmax:
+            self.host_index[:, :kmax].copy_(self.index[:, :kmax], non_blocking=True)
+            self.host_values[:, :kmax].copy_(self.values[:, :kmax], non_blocking=True)
+        self.host_small[:self.slots].copy_(self.status, non_blocking=True)
+        self.host_small[self.slots:].copy_(self.last_count, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        results = {}
+        for i in self._after_mark(marking, self.host_small[self.slots:].tolist()):
+            results[i] = (self._finish(i), None)
+        for i in marking:
+            results.setdefault(i, (None, None))
+        for i in solid:
+            if int(self.host_small[i]) & 1:
+                raise AssertionError('low-entropy-last solid step did not meet its quota')
+            st = self.state[i]
+            k = rows[i][0]
+            st['solid_calls'] += 1
+            st['nfe'] += 1
+            commit = dict(positions=self.host_index[i, :k].numpy().copy(), values=self.host_values[i, :k].numpy().copy(),
+                          step=st['nfe'])
+            record = self._finish(i) if st['solid_calls'] >= len(st['quotas']) else None
+            results[i] = (record, commit)
+        return dict(sorted(results.items()))
+
+    def run_cycles(self, cycles, seeds):
+        """`cycles` whole windows in every slot, device-resident: per window one marking forward, one host read of the
+        last counts, then every solid step's scalars staged in one H2D copy and replayed back to back. Returns the
+        committed voxel count (every window commits all its voxels, the deferred ones at finish)."""
+        committed = 0
+        dev = self.device
+        for c in range(cycles):
+            for i in range(self.slots):
+                self.arm(i, seeds[c * self.slots + i], 32)
+            # marking forward for every slot (params all k = 0)
+            self.params.zero_()
+            self.graph.replay()
+            self._mark(range(self.slots))
+            counts = self.last_count.tolist()
+            self._after_mark(range(self.slots), counts)
+            steps = max(len(st['quotas']) for st in self.state)
+            staged = []
+            for s in range(steps):
+                staged.append(self._pack(self._rows()))
+                for st in self.state:
+                    if st['solid_calls'] < len(st['quotas']):
+                        st['solid_calls'] += 1
+                        st['nfe'] += 1
+            table = torch.stack(staged).to(dev, non_blocking=False)
+            for s in range(steps):
+                self.params.copy_(table[s])
+                self.graph.replay()
+            for i in range(self.slots):
+                self._finish(i)
+            committed += self.slots * self.total
+        return committed
