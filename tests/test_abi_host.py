@@ -1,0 +1,88 @@
+"""CPU checks of the boundary and the host logic: libsvx.so loads and exports every function include/svx.h declares,
+the ctypes structs match the C layout, and the host-side schedule and weight naming match the reference."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
+
+
+@pytest.fixture(scope='module')
+def lib():
+    from streamvoxel_b200 import _lib, build
+    build.build()
+    return _lib.load()
+
+
+def test_library_exports_every_header_symbol(lib):
+    from streamvoxel_b200 import _lib
+    names = _lib.header_symbols()
+    assert len(names) >= 19
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) == set(_lib._SIGNATURES), set(names) ^ set(_lib._SIGNATURES)
+
+
+def test_library_answers_without_a_device(lib):
+    assert lib.svx_version() == 1
+    if not torch.cuda.is_available():
+        assert lib.svx_device_supported() == 0
+    assert isinstance(lib.svx_last_error(), bytes)
+
+
+def test_invalid_arguments_are_rejected_before_any_launch(lib):
+    from streamvoxel_b200 import _lib
+    status = lib.svx_ease_select(None, None, None, None, None, 1, 256, 16, 16, 3, 256, None, None, 1, None, None,
+                                 None, None)
+    assert status == _lib.SVX_ERR_INVALID and b'4^3' in lib.svx_last_error()
+    with pytest.raises(ValueError):
+        _lib.check(status)
+
+
+def test_ctypes_structs_match_the_c_layout():
+    from streamvoxel_b200 import _lib, ops
+    assert ctypes.sizeof(_lib.StepParams) == 32 == ops.STEP_DTYPE.itemsize
+    assert _lib.EpilogueArgs.bias.offset == 8 and ctypes.sizeof(_lib.EpilogueArgs) == 8 + 5 * 8 + 8 * 4
+    assert ctypes.sizeof(_lib.BlockWeights) == 14 * 8 and ctypes.sizeof(_lib.CrossWeights) == 8 * 8
+    assert _lib.EngineConfig.layer_index.offset == 48
+
+
+def test_host_schedule_matches_reference_fixtures():
+    from streamvoxel_b200 import sampling
+    g = np.load(os.path.join(GOLDEN, 'schedule.npz'))
+    for i in range(int(g['count'])):
+        total, steps, n_last = (int(v) for v in g[f's{i}_args'])
+        assert sampling.low_entropy_last_quotas(total, steps, n_last) == g[f's{i}_quotas'].tolist()
+        assert sampling.counts(total, steps) == g[f's{i}_counts'].tolist()
+    assert [sampling.actual_time(f) for f in g['time_in']] == g['time_out'].tolist()
+
+
+def test_weight_names_and_shapes_match_the_reference_state_dict():
+    from streamvoxel_b200 import model as sm
+    g = np.load(os.path.join(GOLDEN, 'dit_tiny.npz'))
+    ref = {'backbone.' + k[3:]: tuple(g[k].shape) for k in g.files if k.startswith('sd.')}
+    cfg = sm.ModelConfig(classes=5, voxel_shape=(16, 16, 16), d=48, heads=4, depth=3, mlp=192, layer_indices=())
+    ours = sm.state_dict_shapes(cfg)
+    for name, shape in ours.items():
+        assert ref.get(name) == shape, name
+    unused = {k for k in ref if k not in ours}
+    assert all('time_' in k or 'rope' in k or 'patch_centers' in k for k in unused), unused
+
+
+def test_synthetic_data_follows_the_benchmark_distribution():
+    from streamvoxel_b200 import synth
+    from streamvoxel_b200.stream.condition import ModelSpec
+    spec = ModelSpec(height=256, tile=16, num_classes=256, biome_classes=16, biome_halo=4, y_origin=-64.)
+    cells = synth.world(3, 2, 2)
+    col = cells[(0, 0)]
+    top = (col > 0).sum(0)
+    assert top.min() >= 40 - 9 and top.max() <= 120 + 9
+    assert set(np.unique(col[:30])) <= set(range(1, 256))
+    item = synth.item(5, spec, k=4)
+    assert item.l1_blocks.shape == (4, 256, 16, 16) and item.l2_blocks.shape == (80, 256, 16, 16)
+    assert item.biomes.shape == (64, 12, 12) and item.biomes[:, :3].sum() == 0
+    logits, truth = synth.ease_logits(0, 2, classes=8, voxels=1000)
+    assert logits.shape == (2, 8, 1000) and truth.shape == (2, 1000)
