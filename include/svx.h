@@ -87,6 +87,20 @@ SVX_API int svx_ease_select(const float* scores, const int16_t* tokens, const ui
                             int mask_id, uint8_t* chosen, int32_t* index_out, int index_capacity,
                             int32_t* chosen_count, uint32_t* status, void* workspace, void* stream);
 
+/* svx_ease_select for callers that cannot allocate device memory (this entry point has no counterpart in the
+ * reference). A host whose device memory belongs entirely to another framework's pool, or that must not allocate
+ * while it is running, cannot hand svx_ease_select a workspace; this variant takes none. Its scratch is a fixed
+ * array compiled into the library (262,400 bytes, held on every GPU that loads the library until the process exits),
+ * so it accepts at most 64 slots and 1024 4^3 blocks per column and returns SVX_ERR_INVALID beyond that. The first call
+ * on each device looks the array's device address up (cudaGetSymbolAddress); make that first call before any stream
+ * capture. Every call uses the same array: calls whose kernels overlap on the GPU (other streams, other host threads)
+ * race and must be serialised by the caller. The kernels overwrite all scratch they read on every call. Outputs,
+ * inputs and errors are those of svx_ease_select. */
+SVX_API int svx_ease_select_noalloc(const float* scores, const int16_t* tokens, const uint8_t* last, const int32_t* pos,
+                                    const svx_step_params* params, int slots, int height, int depth, int width,
+                                    int block, int mask_id, uint8_t* chosen, int32_t* index_out, int index_capacity,
+                                    int32_t* chosen_count, uint32_t* status, void* stream);
+
 /* Categorical draw + token commit for the chosen voxels (`streamvoxel/stream/fast_ops.py:549-551`,
  * `streamvoxel/stream/slot.py:149-151`): p = softmax over classes in fp32, value = argmax(p / q).
  * noise != NULL (parity mode): q = noise[slot][i][classes] fp32, the exponential draws torch.multinomial takes from

@@ -75,6 +75,8 @@ _SIGNATURES = {
     'svx_ease_select_workspace_bytes': (ctypes.c_size_t, [c_int, c_int]),
     'svx_ease_select': (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, c_int, c_int, c_int, c_ptr,
                                 c_ptr, c_int, c_ptr, c_ptr, c_ptr, c_ptr]),
+    'svx_ease_select_noalloc': (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, c_int, c_int, c_int,
+                                        c_ptr, c_ptr, c_int, c_ptr, c_ptr, c_ptr]),
     'svx_ease_sample': (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_int, c_ptr,
                                 c_ptr, c_ptr, c_ptr]),
     'svx_softmax_rows': (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),

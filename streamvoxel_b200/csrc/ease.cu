@@ -755,3 +755,67 @@ extern "C" int svx_ease_finish(int16_t* tokens, const uint8_t* last, const uint8
   ease_finish_kernel<<<grid, 256, 0, as_stream(stream)>>>(tokens, last, finish, voxels, air_token);
   return launch_status("ease_finish_kernel");
 }
+
+// ------------------------------------------------------------------------------------- selection without allocation
+//
+// Some hosts cannot give this library device memory for its selection scratch: a plugin whose process leaves all
+// device memory to another framework's pool, or a caller inside a region where allocating would synchronise the
+// device. For them svx_ease_select_noalloc runs the same three selection kernels on a fixed scratch array that lives
+// in the library's own device image. Every GPU that loads the library holds this array until the process exits.
+#include <mutex>
+
+namespace svx {
+namespace {
+constexpr int kNoAllocMaxSlots = 64;
+constexpr int kNoAllocMaxBlocks = kSelectThreads;  // 4^3 blocks per column, as svx_ease_select allows
+constexpr int kNoAllocMaxDevices = 64;
+}  // namespace
+}  // namespace svx
+
+// Per-call scratch of the selection: block quotas [slots][blocks] and per-slot counters [slots] (int32).
+// 64 * (1024 + 1) * 4 = 262,400 bytes on each device.
+static __device__ __align__(256) int32_t g_select_scratch[svx::kNoAllocMaxSlots * (svx::kNoAllocMaxBlocks + 1)];
+
+namespace svx {
+namespace {
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kNoAllocMaxDevices] = {};
+
+// Device address of g_select_scratch on the current device, looked up once per device. In host code the array's name
+// only stands in for the symbol; a kernel must be given the address cudaGetSymbolAddress returns.
+int scratch_address(void** out) {
+  int device = 0;
+  SVX_CHECK_CUDA(cudaGetDevice(&device));
+  if (device < 0 || device >= kNoAllocMaxDevices) return fail(SVX_ERR_INVALID, "svx_ease_select_noalloc: device index");
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[device]) {
+    void* address = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&address, g_select_scratch);
+    if (e != cudaSuccess)
+      return fail(SVX_ERR_CUDA, std::string("svx_ease_select_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    g_scratch_address[device] = address;
+  }
+  *out = g_scratch_address[device];
+  return SVX_OK;
+}
+}  // namespace
+}  // namespace svx
+
+extern "C" int svx_ease_select_noalloc(const float* scores, const int16_t* tokens, const uint8_t* last,
+                                       const int32_t* pos, const svx_step_params* params, int slots, int height,
+                                       int depth, int width, int block, int mask_id, uint8_t* chosen,
+                                       int32_t* index_out, int index_capacity, int32_t* chosen_count,
+                                       uint32_t* status, void* stream) {
+  SVX_REQUIRE(slots > 0 && slots <= kNoAllocMaxSlots,
+              "svx_ease_select_noalloc: at most 64 slots per call (the fixed scratch holds 64 x 1025 int32)");
+  SVX_REQUIRE(height > 0 && depth > 0 && width > 0 && height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 &&
+                  (height / 4) * (depth / 4) * (width / 4) <= kNoAllocMaxBlocks,
+              "svx_ease_select_noalloc: at most 1024 4^3 blocks per column");
+  void* scratch = nullptr;
+  int rc = scratch_address(&scratch);
+  if (rc) return rc;
+  // The first selection kernel zeroes the per-slot counters and writes every block quota before the later kernels
+  // read them, so nothing left in the array by an earlier call is ever read.
+  return svx_ease_select(scores, tokens, last, pos, params, slots, height, depth, width, block, mask_id, chosen,
+                         index_out, index_capacity, chosen_count, status, scratch, stream);
+}
