@@ -1,0 +1,98 @@
+"""Run one hot kernel at the config-2 step shapes, for a focused profiler capture.
+
+    python -m streamvoxel_b200.profile_case <case> [--launches N]
+
+Cases: attention_cross, attention_self, gemm_fc1, gemm_qkv, gemm_dxd, gemm_head, ease_scores, ease_select,
+ease_sample. Inputs are seeded random tensors with the bench's shapes (8 slots, d=768, 8 heads x 96, V=256,
+65536 voxels, packed keys of k = 0..7 L1 tiles); every case's working set is larger than the 126 MB L2 except the
+selection. Prints the mean launch time measured with CUDA events.
+"""
+from __future__ import annotations
+
+import argparse
+
+import numpy as np
+import torch
+
+from streamvoxel_b200 import _lib, ops
+
+SLOTS, PATCHES, D, HEADS, V, MLP, VOXELS = 8, 1024, 768, 8, 256, 3072, 65536
+CAPACITY = 9600
+
+
+def cases():
+    g = torch.Generator(device='cuda').manual_seed(0)
+    bf = dict(device='cuda', dtype=torch.bfloat16)
+    rows = SLOTS * PATCHES
+    rnd = lambda *shape, s=1.0: (torch.randn(shape, device='cuda', generator=g) * s).to(torch.bfloat16)
+    h = rnd(rows, D)
+    qkv = rnd(rows, 3 * D)
+    out = torch.empty((rows, D), **bf)
+    mlp = torch.empty((rows, MLP), **bf)
+    k = rnd(SLOTS, HEADS, CAPACITY, 96)
+    v = rnd(SLOTS, HEADS, CAPACITY, 96)
+    lengths = torch.tensor([1344 + 1024 * i for i in range(SLOTS)], dtype=torch.int32, device='cuda')
+    w = {n: rnd(*shape, s=0.02) for n, shape in
+         (('qkv', (3 * D, D)), ('fc1', (MLP, D)), ('dxd', (D, D)), ('head', (64 * V, D)))}
+    b = {n: rnd(t.shape[0], s=0.02) for n, t in w.items()}
+    gate = rnd(D, s=0.1)
+    logits = rnd(SLOTS, V, 256, 16, 16, s=2.0)
+    sin = rnd(PATCHES, 48)
+    cos = rnd(PATCHES, 48)
+    scores = torch.empty((SLOTS, 256, 16, 16), device='cuda', dtype=torch.float32)
+    tokens = torch.full((SLOTS, 256, 16, 16), V, dtype=torch.int16, device='cuda')
+    last = torch.zeros((SLOTS, 256, 16, 16), dtype=torch.uint8, device='cuda')
+    rng = np.random.default_rng(0)
+    pos = torch.from_numpy(np.stack([rng.permutation(1024) for _ in range(SLOTS)]).astype(np.int32)).cuda()
+    params = ops.step_params([(2048, 5, 2048 * 4, 2048 * 5 / VOXELS, i) for i in range(SLOTS)], 'cuda')
+    ops.ease_scores(logits, out=scores)
+    chosen, index, count = ops.ease_select(scores, tokens, last, pos, params, V, VOXELS)
+    return {
+        'attention_cross': (lambda: ops.attention(qkv, k, v, SLOTS, HEADS, PATCHES, CAPACITY, q_row_stride=3 * D,
+                                                  kv_slot_stride=HEADS * CAPACITY * 96, kv_head_stride=CAPACITY * 96,
+                                                  kv_row_stride=96, lengths=lengths, out=out),
+                            4.0 * HEADS * PATCHES * 96 * float(lengths.sum())),
+        'attention_self': (lambda: ops.attention(qkv, qkv[:, D:], qkv[:, 2 * D:], SLOTS, HEADS, PATCHES, PATCHES,
+                                                 q_row_stride=3 * D, kv_slot_stride=PATCHES * 3 * D, kv_head_stride=96,
+                                                 kv_row_stride=3 * D, out=out),
+                           4.0 * SLOTS * HEADS * PATCHES * PATCHES * 96),
+        'gemm_fc1': (lambda: ops.gemm(h, w['fc1'], b['fc1'], _lib.EPI_BIAS_GELU, out=mlp), 2.0 * rows * D * MLP),
+        'gemm_qkv': (lambda: ops.gemm(h, w['qkv'], b['qkv'], _lib.EPI_ROPE, out=qkv, rope=(sin, cos),
+                                      rope_cols=2 * D, rows_per_slot=PATCHES), 2.0 * rows * D * 3 * D),
+        'gemm_dxd': (lambda: ops.gemm(h, w['dxd'], b['dxd'], _lib.EPI_GATE_RESIDUAL, out=out, gate=gate,
+                                      residual=out), 2.0 * rows * D * D),
+        'gemm_head': (lambda: ops.gemm(h, w['head'], b['head'], _lib.EPI_CLASS_MAJOR, out=logits,
+                                       rows_per_slot=PATCHES, classes=V, geometry=(256, 16, 16)),
+                      2.0 * rows * D * 64 * V),
+        'ease_scores': (lambda: ops.ease_scores(logits, out=scores), float(logits.numel() * 2 + scores.numel() * 4)),
+        'ease_select': (lambda: ops.ease_select(scores, tokens, last, pos, params, V, VOXELS, chosen=chosen,
+                                                index=index, count=count), float(SLOTS * VOXELS * 8)),
+        'ease_sample': (lambda: ops.ease_sample(logits, index, params, tokens.clone()),
+                        float(SLOTS * 2048 * V * 2)),
+    }
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument('case')
+    parser.add_argument('--launches', type=int, default=3)
+    args = parser.parse_args()
+    _lib.require_device()
+    table = cases()
+    fn, work = table[args.case]
+    fn()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.launches):
+        fn()
+    stop.record()
+    stop.synchronize()
+    seconds = start.elapsed_time(stop) * 1e-3 / args.launches
+    unit = 'GB/s' if args.case.startswith('ease') else 'TFLOP/s'
+    rate = work / seconds / (1e9 if unit == 'GB/s' else 1e12)
+    print(f'{args.case}: {seconds * 1e6:.1f} us per launch, {rate:.1f} {unit} (work {work:.4g})')
+
+
+if __name__ == '__main__':
+    main()
