@@ -1,222 +1,323 @@
-// Non-causal attention with head_dim 96 over per-slot variable-length keys (FlashAttention-2 style online softmax).
+// Non-causal attention, head_dim 96, over per-slot variable-length keys, on the 5th-generation tensor cores.
 //
-// One CTA = 128 queries of one (slot, head); 8 warps x 16 query rows. K/V tiles of 64 keys are double-buffered in
-// shared memory with cp.async (rows past the slot length are zero-filled and masked to -inf), so a slot pays only for
-// ceil(length / 64) key tiles: the packed-key FlexAttention block mask of `streamvoxel/stream/fast_ops.py:149-159`.
-// S = Q K^T and O = P V run on mma.sync m16n8k16 (bf16 in, fp32 accumulate); P is rounded to bf16 for the second
-// product like SDPA's flash kernel; O is normalised in fp32 and written as bf16.
+// One CTA = 128 queries of one (slot, head). Key tiles of 128 are streamed by TMA (two 64-dim 128B-swizzled boxes per
+// operand; the tensor maps' inner extent is 96, so dims 96..127 of a box read as zero and cost no DRAM traffic) into a
+// two-stage ring, and only the ceil(length / 128) tiles of a slot are loaded: the packed-key block mask of
+// `streamvoxel/stream/fast_ops.py:149-159`.
+//
+// Warp roles (256 threads): warp 0 loads Q and the K ring, warp 2 the V ring (TMA); warp 1 owns TMEM and one thread
+// issues tcgen05.mma:
+//   S(t) = Q K(t)^T    M=128, N=128, K=96  -> TMEM columns [128 (t%2), +128)   (double buffered)
+//   O   += P(t) V(t)   M=128, N=96,  K=128 -> TMEM columns [256, 352)           (V read MN-major)
+// Warps 4-7 are the softmax warps, one query row per thread (TMEM lane): each reads its row of S(t) once with
+// tcgen05.ld, frees the S buffer, and writes P(t) = 2^(S*scale - m) as bf16 into a 128B-swizzled K-major tile in shared
+// memory (the A operand of the P.V product). The exponent base m is raised lazily: only when a row's max grows by more
+// than 8 (a factor 256, so P <= 256 stays exact in the fp32 sums), and then the warp rescales its O rows and running
+// sums in TMEM/registers after the previous P.V has completed -- exact, since P, O and the sum always share one m.
+// S(t+1) runs on the tensor core while the softmax of S(t) runs. P is rounded to bf16 before P.V and the row sums stay
+// fp32, as in SDPA's flash kernels; the output is normalised in fp32 and written as bf16.
+// Every mbarrier wait is bounded (tc::wait); a timeout raises a CTA-wide abort, sets SVX_STATUS_WAIT_TIMEOUT in the
+// library's timeout word and skips the rest of the CTA's work.
 #include <math.h>
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "tc.cuh"
 
 namespace svx {
+
+__device__ uint32_t g_svx_attention_timeouts = 0;
+
 namespace {
 
-constexpr int HD = 96;             // head dim
-constexpr int LDS = HD + 8;        // padded smem row (208 B): conflict-free ldmatrix
-constexpr int BQ = 128, BKEY = 64;
-constexpr int kWarps = 8, kThreads = kWarps * 32;
+constexpr int TQ = 128, TK = 128, HD = 96;
+constexpr uint32_t ATOM = 128 * 128;  // one 128-row x 128 B swizzle atom column block (16 KB)
+constexpr uint32_t TILE = 2 * ATOM;   // a 128 x 128 bf16 operand tile (dims or keys 0-63, 64-127)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int kThreads = 256;
+constexpr size_t kSmem = 1024 + TILE + 2 * TILE + 2 * TILE + 2 * TILE + 18 * 8 + 16;
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_addr(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_addr(p)));
-}
-
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
+struct AttnParams {
+  int heads, queries, keys, kv_mode;  // kv_mode 0: K/V groups = heads, rows = slot*keys + key; 1: groups = slot*heads + head
+  const int32_t* lengths;
+  uint16_t* out;
+  float scale_log2;
+};
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
 }
 
-// Load rows [row0, row0+ROWS) x 96 dims of a row-major operand into smem (zero-fill rows >= valid).
-template <int ROWS>
-__device__ __forceinline__ void load_tile(uint16_t* dst, const uint16_t* src, int64_t row_stride, int row0, int valid) {
-  constexpr int CHUNKS = ROWS * (HD / 8);
-  for (int c = threadIdx.x; c < CHUNKS; c += kThreads) {
-    const int r = c / (HD / 8), k = (c % (HD / 8)) * 8;
-    const bool ok = row0 + r < valid;
-    const uint16_t* s = src + (int64_t)(ok ? row0 + r : 0) * row_stride + k;
-    cp_async16(dst + r * LDS + k, s, ok);
-  }
-}
+__global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_constant__ CUtensorMap mq,
+                                                                   const __grid_constant__ CUtensorMap mk,
+                                                                   const __grid_constant__ CUtensorMap mv,
+                                                                   const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* sk = sq + TILE;                 // K ring (2 tiles)
+  uint8_t* sv = sk + 2 * TILE;             // V ring (2 tiles)
+  uint8_t* sp = sv + 2 * TILE;             // P buffers (2 tiles)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * TILE);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_free = bars + 11;
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_full = bars + 15;   // P.V of the tile in P buffer b has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
 
-__global__ void __launch_bounds__(kThreads) attention_kernel(const uint16_t* __restrict__ q, int64_t q_row_stride,
-                                                              const uint16_t* __restrict__ k,
-                                                              const uint16_t* __restrict__ v, int64_t kv_slot_stride,
-                                                              int64_t kv_head_stride, int64_t kv_row_stride,
-                                                              const int32_t* __restrict__ lengths, int heads,
-                                                              int queries, int keys, uint16_t* __restrict__ out,
-                                                              float scale_log2) {
-  extern __shared__ __align__(16) uint16_t sm[];
-  uint16_t* sq = sm;                       // [BQ][LDS]
-  uint16_t* sk = sq + BQ * LDS;            // [2][BKEY][LDS]
-  uint16_t* sv = sk + 2 * BKEY * LDS;      // [2][BKEY][LDS]
-  const int slot = blockIdx.z, head = blockIdx.y, q0 = blockIdx.x * BQ;
   const int warp = warp_id(), lane = lane_id();
-  const int length = lengths ? min(lengths[slot], keys) : keys;
+  const int slot = blockIdx.z, head = blockIdx.y, q0 = blockIdx.x * TQ;
+  const int length = p.lengths ? min(p.lengths[slot], p.keys) : p.keys;
+  const int tiles = (length + TK - 1) / TK;
 
-  const uint16_t* qbase = q + ((int64_t)slot * queries) * q_row_stride + head * HD;
-  const uint16_t* kbase = k + slot * kv_slot_stride + head * kv_head_stride;
-  const uint16_t* vbase = v + slot * kv_slot_stride + head * kv_head_stride;
-  const int tiles = (length + BKEY - 1) / BKEY;
-
-  load_tile<BQ>(sq, qbase, q_row_stride, q0, queries);
-  if (tiles > 0) {
-    load_tile<BKEY>(sk, kbase, kv_row_stride, 0, length);
-    load_tile<BKEY>(sv, vbase, kv_row_stride, 0, length);
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(k_full + i, 1); mbar_init(k_empty + i, 1);
+      mbar_init(v_full + i, 1); mbar_init(v_empty + i, 1);
+      mbar_init(s_full + i, 1); mbar_init(s_free + i, 128);
+      mbar_init(p_full + i, 128); mbar_init(o_full + i, 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tc::prefetch_map(&mq); tc::prefetch_map(&mk); tc::prefetch_map(&mv);
   }
-  cp_commit();
+  if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem + 256;
+  const int kg = p.kv_mode == 0 ? head : slot * p.heads + head;
+  const int kr0 = p.kv_mode == 0 ? slot * p.keys : 0;
 
-  float o[HD / 8][4];
-#pragma unroll
-  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  uint32_t qa[HD / 16][4];
-
-  for (int t = 0; t < tiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < tiles) {
-      load_tile<BKEY>(sk + (buf ^ 1) * BKEY * LDS, kbase, kv_row_stride, (t + 1) * BKEY, length);
-      load_tile<BKEY>(sv + (buf ^ 1) * BKEY * LDS, vbase, kv_row_stride, (t + 1) * BKEY, length);
-    }
-    cp_commit();
-    cp_wait<1>();
-    __syncthreads();
-    if (t == 0) {
-#pragma unroll
-      for (int kk = 0; kk < HD / 16; ++kk)
-        ldsm_x4(qa[kk], sq + (warp * 16 + (lane & 15)) * LDS + kk * 16 + (lane >> 4) * 8);
-    }
-    const uint16_t* kt = sk + buf * BKEY * LDS;
-    const uint16_t* vt = sv + buf * BKEY * LDS;
-    // S = Q K^T for this warp's 16 rows x 64 keys.
-    float s[BKEY / 8][4];
-#pragma unroll
-    for (int j = 0; j < BKEY / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < HD / 16; ++kk) {
-#pragma unroll
-      for (int j = 0; j < BKEY / 8; j += 2) {
-        uint32_t b[4];
-        const int mi = lane >> 3;
-        ldsm_x4(b, kt + (j * 8 + (mi >> 1) * 8 + (lane & 7)) * LDS + kk * 16 + (mi & 1) * 8);
-        mma_bf16(s[j], qa[kk], b[0], b[1]);
-        mma_bf16(s[j + 1], qa[kk], b[2], b[3]);
+  if (warp == 0) {
+    if (lane == 0 && tiles > 0) {
+      const int qr = slot * p.queries + q0;
+      mbar_expect_tx(q_full, TILE);
+      tc::tma_load_3d(sq, &mq, 0, head, qr, q_full);
+      tc::tma_load_3d(sq + ATOM, &mq, 64, head, qr, q_full);
+      for (int t = 0; t < tiles; ++t) {
+        const int s = t & 1;
+        if (t >= 2 && !tc::wait(k_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
+        mbar_expect_tx(k_full + s, TILE);
+        tc::tma_load_3d(sk + s * TILE, &mk, 0, kg, kr0 + t * TK, k_full + s);
+        tc::tma_load_3d(sk + s * TILE + ATOM, &mk, 64, kg, kr0 + t * TK, k_full + s);
       }
     }
-    // Mask keys past the slot length, then the online softmax update (log2 domain).
-    const int key0 = t * BKEY;
-#pragma unroll
-    for (int j = 0; j < BKEY / 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = key0 + j * 8 + (lane & 3) * 2 + (e & 1);
-        s[j][e] = key < length ? s[j][e] * scale_log2 : -INFINITY;
+  } else if (warp == 2) {
+    if (lane == 0 && tiles > 0) {
+      for (int t = 0; t < tiles; ++t) {
+        const int s = t & 1;
+        if (t >= 2 && !tc::wait(v_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
+        mbar_expect_tx(v_full + s, TILE);
+        tc::tma_load_3d(sv + s * TILE, &mv, 0, kg, kr0 + t * TK, v_full + s);
+        tc::tma_load_3d(sv + s * TILE + ATOM, &mv, 64, kg, kr0 + t * TK, v_full + s);
       }
     }
-    float mx[2] = {m[0], m[1]};
+  } else if (warp == 1) {
+    if (lane == 0 && tiles > 0) {
+      constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
+      constexpr uint32_t idesc_o = tc::instr_desc(TQ, HD, true);
+      bool ok = tc::wait(q_full, 0, abort_flag);
+      const uint32_t qa = smem_addr(sq);
+      for (int t = 0; ok && t <= tiles; ++t) {
+        if (t < tiles) {
+          const int s = t & 1;
+          ok = tc::wait(k_full + s, (t >> 1) & 1, abort_flag);
+          if (ok && t >= 2) ok = tc::wait(s_free + s, ((t - 2) >> 1) & 1, abort_flag);
+          if (!ok) break;
+          tc::fence_after();
+          const uint32_t kb = smem_addr(sk + s * TILE);
 #pragma unroll
-    for (int j = 0; j < BKEY / 8; ++j) {
-      mx[0] = fmaxf(mx[0], fmaxf(s[j][0], s[j][1]));
-      mx[1] = fmaxf(mx[1], fmaxf(s[j][2], s[j][3]));
-    }
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
+            tc::umma(tmem + s * 128, tc::sw128_desc(qa + off), tc::sw128_desc(kb + off), idesc_s, kk > 0);
+          }
+          tc::commit(s_full + s);
+          tc::commit(k_empty + s);
+        }
+        if (t >= 1) {
+          const int u = t - 1, su = u & 1;
+          ok = tc::wait(v_full + su, (u >> 1) & 1, abort_flag);
+          if (ok) ok = tc::wait(p_full + su, (u >> 1) & 1, abort_flag);
+          if (!ok) break;
+          tc::fence_after();
+          const uint32_t pa = smem_addr(sp + su * TILE), vb = smem_addr(sv + su * TILE);
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-    }
-    float alpha[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      alpha[r] = exp2f(m[r] - mx[r]);  // m = -inf on the first tile: alpha = 0
-      m[r] = mx[r];
-    }
-    uint32_t pa[BKEY / 16][4];
-#pragma unroll
-    for (int j = 0; j < BKEY / 8; ++j) {
-      const float p0 = exp2f(s[j][0] - m[0]), p1 = exp2f(s[j][1] - m[0]);
-      const float p2 = exp2f(s[j][2] - m[1]), p3 = exp2f(s[j][3] - m[1]);
-      rs[0] += p0 + p1;
-      rs[1] += p2 + p3;
-      pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16(p0, p1);
-      pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16(p2, p3);
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-      l[r] = l[r] * alpha[r] + rs[r];
-    }
-#pragma unroll
-    for (int i = 0; i < HD / 8; ++i) {
-      o[i][0] *= alpha[0]; o[i][1] *= alpha[0];
-      o[i][2] *= alpha[1]; o[i][3] *= alpha[1];
-    }
-    // O += P V: the A fragments of P are the S accumulators of key columns 16c..16c+15.
-#pragma unroll
-    for (int c = 0; c < BKEY / 16; ++c) {
-#pragma unroll
-      for (int i = 0; i < HD / 8; i += 2) {
-        uint32_t b[4];
-        const int mi = lane >> 3;
-        ldsm_x4_t(b, vt + (c * 16 + (mi & 1) * 8 + (lane & 7)) * LDS + i * 8 + (mi >> 1) * 8);
-        mma_bf16(o[i], pa[c], b[0], b[1]);
-        mma_bf16(o[i + 1], pa[c], b[2], b[3]);
+          for (int kk = 0; kk < TK / 16; ++kk) {
+            const uint32_t aoff = (kk >> 2) * ATOM + (kk & 3) * 32;
+            tc::umma(tmem_o, tc::sw128_desc(pa + aoff), tc::sw128_desc(vb + kk * 2048, ATOM, 1024), idesc_o,
+                     (u > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::commit(o_full + su);
+          tc::commit(v_empty + su);
+        }
       }
     }
-    __syncthreads();
+  } else if (warp >= 4) {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = p.scale_log2;
+    float m_used = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int t = 0; t < tiles; ++t) {
+      const int s = t & 1;
+      if (!tc::wait(s_full + s, (t >> 1) & 1, abort_flag)) { ok = false; break; }
+      tc::fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::ld32(tmem + lanes + s * 128 + c * 32, r[c]);
+      tc::wait_ld();
+      tc::fence_before();
+      tc::mbar_arrive(s_free + s);
+      const int key0 = t * TK;
+      const bool full = key0 + TK <= length;
+      if (!full) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (key0 + c * 32 + j >= length) r[c][j] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[c][j]));
+      mx *= sl2;
+      // Raise the exponent base only when the row max outgrows it by more than 8 (warp-uniform rescale of O).
+      const bool raise = mx > m_used + 8.f;
+      if (__any_sync(0xffffffffu, raise)) {
+        const float m_new = raise ? mx : m_used;
+        const float alpha = tc::ex2(m_used - m_new);   // m_used = -inf on the first tile: alpha = 0
+        l_run *= alpha;
+        m_used = m_new;
+        if (t >= 1) {
+          // O holds the P.V products of tiles < t; the last one (t-1) must have completed.
+          const int u = t - 1;
+          if (!tc::wait(o_full + (u & 1), (u >> 1) & 1, abort_flag)) { ok = false; break; }
+          tc::fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tc::ld32(tmem_o + lanes + c * 32, o);
+            tc::wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+            tc::st32(tmem_o + lanes + c * 32, o);
+          }
+          tc::wait_st();
+        }
+      }
+      // P buffer s was last read by the P.V of tile t-2.
+      if (t >= 2 && !tc::wait(o_full + s, ((t - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
+      const float base = m_used;
+      float sum = 0.f;
+      uint8_t* pb = sp + s * TILE;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float p0 = tc::ex2(__uint_as_float(r[c][j]) * sl2 - base);
+          const float p1 = tc::ex2(__uint_as_float(r[c][j + 1]) * sl2 - base);
+          sum += p0 + p1;
+          packed[j >> 1] = pack_bf16(p0, p1);
+        }
+        // keys c*32 .. c*32+31: swizzle atom c/2, 16-byte chunks (c%2)*4 .. +3, chunk index XOR (row % 8)
+        uint8_t* rowp = pb + (c >> 1) * ATOM + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = ((c & 1) * 4 + q) ^ (row & 7);
+          *reinterpret_cast<uint4*>(rowp + chunk * 16) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        }
+      }
+      l_run += sum;
+      tc::fence_before();
+      tc::fence_async_smem();
+      tc::mbar_arrive(p_full + s);
+    }
+    const int qrow = q0 + row;
+    if (ok && tiles > 0) {
+      const int u = tiles - 1;
+      ok = tc::wait(o_full + (u & 1), (u >> 1) & 1, abort_flag);
+      if (ok) {
+        tc::fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)slot * p.queries + qrow) * (p.heads * HD) + head * HD);
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tc::ld32(tmem_o + lanes + c * 32, o);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float* f = reinterpret_cast<const float*>(o) + 8 * i;
+            dst[c * 4 + i] = make_uint4(pack_bf16(f[0] * inv, f[1] * inv), pack_bf16(f[2] * inv, f[3] * inv),
+                                        pack_bf16(f[4] * inv, f[5] * inv), pack_bf16(f[6] * inv, f[7] * inv));
+          }
+        }
+      }
+    } else if (ok && qrow < p.queries) {
+      uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)slot * p.queries + qrow) * (p.heads * HD) + head * HD);
+      for (int i = 0; i < HD / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+    }
+    if (!ok && lane == 0) atomicOr(&g_svx_attention_timeouts, SVX_STATUS_WAIT_TIMEOUT);
   }
-  cp_wait<0>();
-  // Normalise and store: rows g and g+8 of the warp, dims i*8 + 2*(lane&3) + {0,1}.
-  const int g = lane >> 2;
-  const float inv0 = l[0] > 0.f ? 1.f / l[0] : 0.f, inv1 = l[1] > 0.f ? 1.f / l[1] : 0.f;
-  const int row0 = q0 + warp * 16 + g;
-  uint16_t* out0 = out + ((int64_t)slot * queries + row0) * (heads * HD) + head * HD;
-  uint16_t* out1 = out0 + 8 * (int64_t)(heads * HD);
-#pragma unroll
-  for (int i = 0; i < HD / 8; ++i) {
-    const int d = i * 8 + (lane & 3) * 2;
-    if (row0 < queries) *reinterpret_cast<uint32_t*>(out0 + d) = pack_bf16(o[i][0] * inv0, o[i][1] * inv0);
-    if (row0 + 8 < queries) *reinterpret_cast<uint32_t*>(out1 + d) = pack_bf16(o[i][2] * inv1, o[i][3] * inv1);
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
   }
 }
-
-constexpr size_t kSmem = (size_t)(BQ + 4 * BKEY) * LDS * sizeof(uint16_t);
 
 }  // namespace
 
 int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
                   int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride, const int32_t* lengths,
                   int slots, int heads, int queries, int keys, uint16_t* out, cudaStream_t stream) {
+  SVX_REQUIRE(queries % TQ == 0, "attention: queries must be a multiple of 128");
+  int kv_mode;
+  uint64_t groups, rows, group_stride, row_stride;
+  if (kv_slot_stride == (int64_t)keys * kv_row_stride) {          // [slot*keys + key][.. head*stride ..]
+    kv_mode = 0; groups = heads; rows = (uint64_t)slots * keys;
+    group_stride = kv_head_stride * 2; row_stride = kv_row_stride * 2;
+  } else if (kv_slot_stride == (int64_t)heads * kv_head_stride) {  // [slot][head][key][dim]
+    kv_mode = 1; groups = (uint64_t)slots * heads; rows = keys;
+    group_stride = kv_head_stride * 2; row_stride = kv_row_stride * 2;
+  } else {
+    return fail(SVX_ERR_INVALID, "attention: K/V strides must be [slot*keys][head] or [slot][head][key] layouts");
+  }
+  CUtensorMap mq, mk, mv;
+  int rc = make_map_3d(&mq, q, HD, heads, (uint64_t)slots * queries, HD * 2, q_row_stride * 2, 64, TQ);
+  if (!rc) rc = make_map_3d(&mk, k, HD, groups, rows, group_stride, row_stride, 64, TK);
+  if (!rc) rc = make_map_3d(&mv, v, HD, groups, rows, group_stride, row_stride, 64, TK);
+  if (rc) return rc;
   static bool configured = false;
   if (!configured) {
-    SVX_CHECK_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+    SVX_CHECK_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
     configured = true;
   }
-  dim3 grid((queries + BQ - 1) / BQ, heads, slots);
-  const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
-  attention_kernel<<<grid, kThreads, kSmem, stream>>>(q, q_row_stride, k, v, kv_slot_stride, kv_head_stride,
-                                                      kv_row_stride, lengths, heads, queries, keys, out, scale_log2);
-  return launch_status("attention_kernel");
+  AttnParams prm{heads, queries, keys, kv_mode, lengths, out, (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
+  dim3 grid(queries / TQ, heads, slots);
+  attention_tc_kernel<<<grid, kThreads, kSmem, stream>>>(mq, mk, mv, prm);
+  return launch_status("attention_tc_kernel");
+}
+
+uint32_t attention_timeouts() {
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_svx_attention_timeouts, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  return v;
 }
 
 }  // namespace svx

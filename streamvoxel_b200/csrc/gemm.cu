@@ -322,6 +322,23 @@ static int make_kmajor_map(CUtensorMap* map, const void* ptr, int rows, int cols
   return SVX_OK;
 }
 
+int make_map_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t groups, uint64_t rows,
+                uint64_t group_stride_bytes, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+  EncodeTiled encode = encode_fn();
+  if (!encode) return fail(SVX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  SVX_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0, "TMA operand must be 16-byte aligned");
+  SVX_REQUIRE(group_stride_bytes % 16 == 0 && row_stride_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)groups, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)group_stride_bytes, (cuuint64_t)row_stride_bytes};
+  cuuint32_t box[3] = {box_inner, 1, box_rows};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, elem,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SVX_ERR_CUDA, "cuTensorMapEncodeTiled (3d) failed: " + std::to_string((int)r));
+  return SVX_OK;
+}
+
 static int pick_bn(int M, int N) {
   if (N % 256 == 0 && (long)(N / 256) * (M / BM) >= 148) return 256;
   if (N % 128 == 0) return 128;
@@ -402,5 +419,5 @@ extern "C" int svx_gemm(const uint16_t* A, const uint16_t* W, uint16_t* out, int
 extern "C" uint32_t svx_wait_timeouts(void) {
   uint32_t v = 0;
   if (cudaMemcpyFromSymbol(&v, g_svx_timeouts, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
-  return v;
+  return v | attention_timeouts();
 }
