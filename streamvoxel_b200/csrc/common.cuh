@@ -6,7 +6,7 @@
 #include <stdint.h>
 #include <string>
 
-#include "../../include/svx.h"
+#include "svx.h"
 
 namespace svx {
 

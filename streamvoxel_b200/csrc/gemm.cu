@@ -1,16 +1,19 @@
 // Dense bf16 GEMM with fused epilogues on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA.
 //
 // D[M,N] = A[M,K] . W[N,K]^T, both operands K-major (activations row-major, nn.Linear weights as stored).
-// One 128 x BN output tile per CTA. Warp roles: warp 0 issues TMA loads into a STAGES-deep shared-memory ring
-// (128B-swizzled tiles), warp 1 allocates TMEM and one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into an
-// fp32 TMEM accumulator, committing each stage back to the producer; warps 2-5 wait for the final commit, read the
-// accumulator with tcgen05.ld (each warp owns its 32-lane TMEM quarter = 32 output rows) and run the epilogue.
+// Persistent: one CTA per SM walks the 128 x BN output tiles round-robin. Warp 0 streams A/W k-blocks through a
+// STAGES-deep ring of 128B-swizzled shared-memory tiles that runs continuously across tiles; warp 1 owns TMEM and one
+// elected thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators (2 x BN fp32 columns),
+// committing each stage back to the producer and each finished tile to the epilogue; warps 4-11 are the epilogue:
+// two warps per 32-lane TMEM quarter (one per column half) read the accumulator with tcgen05.ld, run the fused
+// epilogue and release the accumulator, so the epilogue of tile i overlaps the main loop of tile i+1.
 // Every mbarrier wait is bounded; a timeout sets SVX_STATUS_WAIT_TIMEOUT in g_svx_timeouts and skips the work.
 #include <cuda.h>
 #include <math.h>
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "tc.cuh"
 
 namespace svx {
 
@@ -19,76 +22,11 @@ __device__ uint32_t g_svx_timeouts = 0;
 namespace {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 384;  // warps 0-1 producer/MMA, 2-3 idle, 4-11 epilogue
+constexpr int kEpilogueWarps = 8;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
 __device__ __forceinline__ void record_timeout() { atomicOr(&g_svx_timeouts, SVX_STATUS_WAIT_TIMEOUT); }
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// UMMA shared-memory descriptor of a K-major tile in the canonical 128B-swizzle layout (8-row atoms of 128 B,
-// 1024 B apart): start address >> 4, LBO = 1 (unused for swizzled K-major), SBO = 1024 B, version 1, SWIZZLE_128B.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;
-  d |= (uint64_t)(1024 >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t instr_desc(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void load_bf16x32(const uint16_t* p, float (&v)[32]) {
-  const uint4* q = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 raw = q[i];
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
-      v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
-    }
-  }
-}
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
@@ -105,23 +43,72 @@ __device__ __forceinline__ void store_bf16x32(uint16_t* p, const float (&v)[32])
 // GELU (erf form), in the operation order of ATen's GeluCUDAKernelImpl: x * 0.5 * (1 + erf(x * sqrt(1/2))).
 __device__ __forceinline__ float gelu_erf(float x) { return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f)); }
 
+__device__ __forceinline__ void unpack8(uint4 raw, float* v) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = __uint_as_float(w[j] << 16);
+    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+
+// Operands an epilogue chunk reads from global memory, fetched before the accumulator is ready (bf16, packed).
+struct Operands {
+  uint4 bias[4];
+  uint4 extra[4];   // gate (GATE_RESIDUAL) | sin, cos (ROPE: 2 + 2)
+  uint4 res[4];     // residual row slice (GATE_RESIDUAL, RESIDUAL)
+};
+
+template <int EPI>
+__device__ __forceinline__ void prefetch32(const EpiParams& ep, int N, int row, int n, Operands& o) {
+  const uint4* b = reinterpret_cast<const uint4*>(ep.bias + n);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o.bias[i] = b[i];
+  if constexpr (EPI == SVX_EPI_GATE_RESIDUAL) {
+    const uint4* g = reinterpret_cast<const uint4*>(ep.gate + n);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o.extra[i] = g[i];
+  }
+  if constexpr (EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL) {
+    const uint4* r = reinterpret_cast<const uint4*>(ep.residual + (int64_t)row * N + n);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o.res[i] = r[i];
+  }
+  if constexpr (EPI == SVX_EPI_ROPE) {
+    if (n < ep.rope_cols) {
+      const int p = row % ep.rows_per_slot;
+      const int half = ep.head_dim >> 1;
+      const int64_t t = (int64_t)p * half + ((n % ep.head_dim) >> 1);   // 16 consecutive table entries, 16-byte aligned
+      const uint4* sn = reinterpret_cast<const uint4*>(ep.rope_sin + t);
+      const uint4* cs = reinterpret_cast<const uint4*>(ep.rope_cos + t);
+      o.extra[0] = sn[0]; o.extra[1] = sn[1]; o.extra[2] = cs[0]; o.extra[3] = cs[1];
+    }
+  }
+}
+
 // Epilogue of one row x 32 columns [n, n+32) of the tile; acc holds fp32 accumulators.
 template <int EPI>
 __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, int N, int row, int n,
-                                           const uint32_t (&acc)[32]) {
-  float bias[32], y[32];
-  load_bf16x32(ep.bias + n, bias);
+                                           const uint32_t (&acc)[32], const Operands& o) {
+  float y[32];
+  {
+    float bias[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) y[j] = round_bf16(__uint_as_float(acc[j]) + bias[j]);
+    for (int i = 0; i < 4; ++i) unpack8(o.bias[i], bias + 8 * i);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = round_bf16(__uint_as_float(acc[j]) + bias[j]);
+  }
   if constexpr (EPI == SVX_EPI_BIAS_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) y[j] = gelu_erf(y[j]);
   } else if constexpr (EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL) {
     float res[32];
-    load_bf16x32(ep.residual + (int64_t)row * N + n, res);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) unpack8(o.res[i], res + 8 * i);
     if constexpr (EPI == SVX_EPI_GATE_RESIDUAL) {
       float gate[32];
-      load_bf16x32(ep.gate + n, gate);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) unpack8(o.extra[i], gate + 8 * i);
 #pragma unroll
       for (int j = 0; j < 32; ++j) y[j] = round_bf16(gate[j] * y[j]);
     }
@@ -131,17 +118,15 @@ __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, i
     if (n < ep.rope_cols) {
       // Axial RoPE (`unconditional_md4_timefree.py:24-30`): pair (2f, 2f+1) of a head rotates by table entry f;
       // a*cos, b*sin, ... are bf16 ops, so every product and sum rounds to bf16.
-      const int p = row % ep.rows_per_slot;
-      const int half = ep.head_dim >> 1;
-      const int dim0 = n % ep.head_dim;
-      const uint16_t* sn = ep.rope_sin + (int64_t)p * half + (dim0 >> 1);
-      const uint16_t* cs = ep.rope_cos + (int64_t)p * half + (dim0 >> 1);
+      float sn[16], cs[16];
+      unpack8(o.extra[0], sn); unpack8(o.extra[1], sn + 8);
+      unpack8(o.extra[2], cs); unpack8(o.extra[3], cs + 8);
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
-        float s = bf16_to_f32(sn[j >> 1]), c = bf16_to_f32(cs[j >> 1]);
-        float a = y[j], b = y[j + 1];
-        y[j] = round_bf16(round_bf16(a * c) - round_bf16(b * s));
-        y[j + 1] = round_bf16(round_bf16(a * s) + round_bf16(b * c));
+        const float sv = sn[j >> 1], cv = cs[j >> 1];
+        const float a = y[j], b = y[j + 1];
+        y[j] = round_bf16(round_bf16(a * cv) - round_bf16(b * sv));
+        y[j + 1] = round_bf16(round_bf16(a * sv) + round_bf16(b * cv));
       }
     }
   }
@@ -155,8 +140,8 @@ __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, i
     uint16_t* base = out + ((int64_t)slot * ep.classes + v) * ((int64_t)ep.height * ep.depth * ep.width);
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {  // four consecutive x voxels per 8-byte store
-      const int o = o0 + j;
-      const int oy = o >> 4, oz = (o >> 2) & 3;
+      const int oo = o0 + j;
+      const int oy = oo >> 4, oz = (oo >> 2) & 3;
       const int64_t idx = ((int64_t)(py * P + oy) * ep.depth + (pz * P + oz)) * ep.width + px * P;
       *reinterpret_cast<uint2*>(base + idx) = make_uint2(pack2(y[j], y[j + 1]), pack2(y[j + 2], y[j + 3]));
     }
@@ -171,93 +156,118 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                                                            uint16_t* __restrict__ out, int M, int N, int K,
                                                            const EpiParams ep) {
   constexpr uint32_t B_BYTES = BN * BK * 2;
-  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_s = smem;
   uint8_t* b_s = smem + STAGES * A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(b_s + STAGES * B_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = warp_id(), lane = lane_id();
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int kblocks = K / BK;
+  const int n_tiles = N / BN;
+  const int tiles = (M / BM) * n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, kEpilogueWarps); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    tc::prefetch_map(&tmA);
+    tc::prefetch_map(&tmB);
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  fence_before();
+  if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
+  tc::fence_before();
   __syncthreads();
-  fence_after();
+  tc::fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
-        if (round > 0 && !mbar_wait(empty + s, (round - 1) & 1)) { *abort_flag = 1; record_timeout(); break; }
-        if (*abort_flag) break;
-        mbar_expect_tx(full + s, A_BYTES + B_BYTES);
-        tma_load_2d(a_s + s * A_BYTES, &tmA, kb * BK, m0, full + s);
-        tma_load_2d(b_s + s * B_BYTES, &tmB, kb * BK, n0, full + s);
+      int it = 0;  // ring position across all tiles of this CTA
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES, round = it / STAGES;
+          if (round > 0 && !tc::wait(empty + s, (round - 1) & 1, abort_flag)) { record_timeout(); goto done; }
+          mbar_expect_tx(full + s, A_BYTES + B_BYTES);
+          tc::tma_load_2d(a_s + s * A_BYTES, &tmA, kb * BK, m0, full + s);
+          tc::tma_load_2d(b_s + s * B_BYTES, &tmB, kb * BK, n0, full + s);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(BN);
-      bool ok = true;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
-        if (!mbar_wait(full + s, round & 1)) { *abort_flag = 1; record_timeout(); ok = false; break; }
-        fence_after();
-        const uint32_t a0 = smem_addr(a_s + s * A_BYTES), b0 = smem_addr(b_s + s * B_BYTES);
+      constexpr uint32_t idesc = tc::instr_desc(BM, BN);
+      int it = 0, local = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+        const int buf = local & 1, use = local >> 1;
+        if (use > 0 && !tc::wait(acc_empty + buf, (use - 1) & 1, abort_flag)) { record_timeout(); goto done; }
+        tc::fence_after();
+        const uint32_t acc = tmem + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES, round = it / STAGES;
+          if (!tc::wait(full + s, round & 1, abort_flag)) { record_timeout(); goto done; }
+          tc::fence_after();
+          const uint32_t a0 = smem_addr(a_s + s * A_BYTES), b0 = smem_addr(b_s + s * B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          umma(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (kb | kk) != 0);
-        umma_commit(empty + s);
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc::umma(acc, tc::sw128_desc(a0 + kk * 32), tc::sw128_desc(b0 + kk * 32), idesc, (kb | kk) != 0);
+          tc::commit(empty + s);
+        }
+        tc::commit(acc_full + buf);
       }
-      if (ok) umma_commit(accum);
     }
-  } else {
-    // Epilogue warps 2..5: TMEM lane quarter (warp % 4) holds rows 32*(warp%4) .. +31 of the tile.
-    const int quarter = warp & 3;
-    const int row = m0 + quarter * 32 + lane;
-    if (mbar_wait(accum, 0)) {
-      fence_after();
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t acc[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), acc);
-        if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + c * 32, acc);
+  } else if (warp >= 4) {
+    // Epilogue warps 4..11: TMEM lane quarter (warp % 4) = rows 32*(warp%4) .. +31; column half (warp - 4) / 4.
+    const int quarter = warp & 3, half = (warp - 4) >> 2;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+      const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+      const int buf = local & 1, use = local >> 1;
+      const int row = m0 + quarter * 32 + lane;
+      constexpr int CHUNKS = BN / 64;   // 32-column chunks of this warp's column half
+      const int col0 = half * (BN / 2);
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + col0);
+      // Chunk 0's operands are fetched while the main loop still runs; then chunk c's math overlaps chunk c+1's loads.
+      Operands ops[2];
+      uint32_t acc[2][32];
+      prefetch32<EPI>(ep, N, row, n0 + col0, ops[0]);
+      if (!tc::wait(acc_full + buf, use & 1, abort_flag)) { record_timeout(); break; }
+      tc::fence_after();
+      tc::ld32(taddr, acc[0]);
+      tc::wait_ld();
+#pragma unroll
+      for (int c = 0; c < CHUNKS; ++c) {
+        if (c + 1 < CHUNKS) {
+          prefetch32<EPI>(ep, N, row, n0 + col0 + (c + 1) * 32, ops[(c + 1) & 1]);
+          tc::ld32(taddr + (c + 1) * 32, acc[(c + 1) & 1]);
+        }
+        if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + col0 + c * 32, acc[c & 1], ops[c & 1]);
+        if (c + 1 < CHUNKS) tc::wait_ld();
       }
-    } else {
-      record_timeout();
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(acc_empty + buf);
     }
   }
-  fence_before();
+done:
+  tc::fence_before();
   __syncthreads();
   if (warp == 1) {
-    fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
 template <int BN, int STAGES>
 constexpr size_t smem_bytes() {
-  return 1024 + STAGES * (A_BYTES + (size_t)BN * BK * 2) + (2 * STAGES + 1) * 8 + 16;
+  return 1024 + STAGES * (A_BYTES + (size_t)BN * BK * 2) + (2 * STAGES + 4) * 8 + 16;
 }
 
 template <int BN, int STAGES, int EPI>
@@ -270,8 +280,11 @@ int launch_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, int M
                                         (int)bytes));
     configured = true;
   }
-  dim3 grid(N / BN, M / BM);
-  gemm_kernel<BN, STAGES, EPI><<<grid, kThreads, bytes, stream>>>(a, b, out, M, N, K, ep);
+  int device = 0, sms = 0;
+  SVX_CHECK_CUDA(cudaGetDevice(&device));
+  SVX_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  const int tiles = (N / BN) * (M / BM);
+  gemm_kernel<BN, STAGES, EPI><<<tiles < sms ? tiles : sms, kThreads, bytes, stream>>>(a, b, out, M, N, K, ep);
   return launch_status("gemm_kernel");
 }
 
@@ -339,10 +352,22 @@ int make_map_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t grou
   return SVX_OK;
 }
 
+// Tile width for the persistent grid. A CTA streams the 128-row A slice and the BN-row W slice of every tile it owns,
+// so a tile costs about (128 + BN) operand rows of traffic: pick the smallest (tiles per SM, rounded up) x (128 + BN),
+// the wider tile on ties (measured on B200 at M = 8192: BN 64 reaches ~420 TFLOP/s, BN 256 ~800-980).
 static int pick_bn(int M, int N) {
-  if (N % 256 == 0 && (long)(N / 256) * (M / BM) >= 148) return 256;
-  if (N % 128 == 0) return 128;
-  return 64;
+  int sms = 148;
+  int device = 0;
+  if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  int best = 0;
+  long best_cost = 0;
+  for (int bn : {256, 128, 64}) {
+    if (N % bn) continue;
+    const long tiles = (long)(N / bn) * (M / BM);
+    const long cost = ((tiles + sms - 1) / sms) * (BM + bn);
+    if (!best || cost < best_cost) { best = bn; best_cost = cost; }
+  }
+  return best;
 }
 
 int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N, int K, int bn) {
