@@ -1,21 +1,24 @@
 // Non-causal attention, head_dim 96, over per-slot variable-length keys, on the 5th-generation tensor cores.
 //
-// One CTA = 128 queries of one (slot, head). Key tiles of 128 are streamed by TMA (two 64-dim 128B-swizzled boxes per
-// operand; the tensor maps' inner extent is 96, so dims 96..127 of a box read as zero and cost no DRAM traffic) into a
-// two-stage ring, and only the ceil(length / 128) tiles of a slot are loaded: the packed-key block mask of
-// `streamvoxel/stream/fast_ops.py:149-159`.
+// One CTA = two 128-query tiles of one (slot, head) sharing every K/V tile. Key tiles of 128 are streamed by TMA into
+// two-stage K and V rings, and only the ceil(length / 128) tiles of a slot are loaded: the packed-key block mask of
+// `streamvoxel/stream/fast_ops.py:149-159`. Every operand tile (Q, K, V) is exactly 96 dims wide: dims 0-63 as a
+// 128B-swizzled part (128-byte rows) and dims 64-95 as a 64B-swizzled part (64-byte rows), two TMA boxes per tile.
 //
-// Warp roles (256 threads): warp 0 loads Q and the K ring, warp 2 the V ring (TMA); warp 1 owns TMEM and one thread
-// issues tcgen05.mma:
-//   S(t) = Q K(t)^T    M=128, N=128, K=96  -> TMEM columns [128 (t%2), +128)   (double buffered)
-//   O   += P(t) V(t)   M=128, N=96,  K=128 -> TMEM columns [256, 352)           (V read MN-major)
-// Warps 4-7 are the softmax warps, one query row per thread (TMEM lane): each reads its row of S(t) once with
-// tcgen05.ld, frees the S buffer, and writes P(t) = 2^(S*scale - m) as bf16 into a 128B-swizzled K-major tile in shared
-// memory (the A operand of the P.V product). The exponent base m is raised lazily: only when a row's max grows by more
-// than 8 (a factor 256, so P <= 256 stays exact in the fp32 sums), and then the warp rescales its O rows and running
-// sums in TMEM/registers after the previous P.V has completed -- exact, since P, O and the sum always share one m.
-// S(t+1) runs on the tensor core while the softmax of S(t) runs. P is rounded to bf16 before P.V and the row sums stay
-// fp32, as in SDPA's flash kernels; the output is normalised in fp32 and written as bf16.
+// Warp roles (384 threads): warp 0 loads Q and the K ring, warp 2 the V ring; warp 1 owns TMEM and one thread issues
+// tcgen05.mma for both query tiles i = 0, 1:
+//   S_i = Q_i K(t)^T   M=128, N=128, K=96  -> TMEM columns [128 i, +128)
+//   O_i += P_i V(t)    M=128, N=64 + N=32, K=128 -> TMEM columns [256 + 128 i, +96)   (V read MN-major)
+// Warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1, one query row per thread (TMEM lane): each
+// reads its row of S_i once with tcgen05.ld, frees S_i (so S_i(t+1) is computed during the softmax of t), and writes
+// P_i = 2^(S*scale - m) as bf16 into a 128B-swizzled K-major tile in shared memory (the A operand of P.V). While one
+// warpgroup computes exponentials the tensor core works for the other. The exponent base m is raised lazily: only
+// when a row's max grows by more than 8 (a factor 256, so P <= 256 stays exact in the fp32 sums), and then the warp
+// rescales its O rows in TMEM after the previous P.V has completed -- exact, since P, O and the sum share one m.
+// P is rounded to bf16 before P.V and the row sums stay fp32, as in SDPA's flash kernels; the output is normalised
+// in fp32 and written as bf16.
+// CTAs are numbered longest slot first (the hardware starts them in index order), so the long cross-attention
+// slots do not trail the grid.
 // Every mbarrier wait is bounded (tc::wait); a timeout raises a CTA-wide abort, sets SVX_STATUS_WAIT_TIMEOUT in the
 // library's timeout word and skips the rest of the CTA's work.
 #include <math.h>
@@ -31,50 +34,56 @@ __device__ uint32_t g_svx_attention_timeouts = 0;
 namespace {
 
 constexpr int TQ = 128, TK = 128, HD = 96;
-constexpr uint32_t ATOM = 128 * 128;  // one 128-row x 128 B swizzle atom column block (16 KB)
-constexpr uint32_t TILE = 2 * ATOM;   // a 128 x 128 bf16 operand tile (dims or keys 0-63, 64-127)
+constexpr uint32_t WIDE = 128 * 128;       // 128 rows x 128 B: dims 0-63 of an operand tile (128B swizzle)
+constexpr uint32_t NARROW = 128 * 64;      // 128 rows x 64 B: dims 64-95 (64B swizzle)
+constexpr uint32_t OPER = WIDE + NARROW;   // one Q, K or V tile (24 KB)
+constexpr uint32_t PTILE = 2 * WIDE;       // one P tile: 128 queries x 128 keys bf16, two 64-key swizzle atoms
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int kThreads = 256;
-constexpr size_t kSmem = 1024 + TILE + 2 * TILE + 2 * TILE + 2 * TILE + 18 * 8 + 16;
+constexpr int kThreads = 384;
+constexpr int kBars = 17;
+constexpr size_t kSmem = 1024 + 6 * OPER + 2 * PTILE + kBars * 8 + 16;
 
 struct AttnParams {
-  int heads, queries, keys, kv_mode;  // kv_mode 0: K/V groups = heads, rows = slot*keys + key; 1: groups = slot*heads + head
+  int slots, heads, queries, keys, pairs;
+  int kv_mode;  // 0: K/V groups = heads, rows = slot*keys + key; 1: groups = slot*heads + head, rows = key
   const int32_t* lengths;
   uint16_t* out;
   float scale_log2;
 };
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  return (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
-}
-
-__global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_constant__ CUtensorMap mq,
-                                                                   const __grid_constant__ CUtensorMap mk,
-                                                                   const __grid_constant__ CUtensorMap mv,
+__global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_constant__ CUtensorMap mq_wide,
+                                                                   const __grid_constant__ CUtensorMap mq_narrow,
+                                                                   const __grid_constant__ CUtensorMap mk_wide,
+                                                                   const __grid_constant__ CUtensorMap mk_narrow,
+                                                                   const __grid_constant__ CUtensorMap mv_wide,
+                                                                   const __grid_constant__ CUtensorMap mv_narrow,
                                                                    const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem;
-  uint8_t* sk = sq + TILE;                 // K ring (2 tiles)
-  uint8_t* sv = sk + 2 * TILE;             // V ring (2 tiles)
-  uint8_t* sp = sv + 2 * TILE;             // P buffers (2 tiles)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * TILE);
+  uint8_t* sq = smem;                      // Q tiles 0, 1
+  uint8_t* sk = sq + 2 * OPER;             // K ring
+  uint8_t* sv = sk + 2 * OPER;             // V ring
+  uint8_t* sp = sv + 2 * OPER;             // P tiles 0, 1
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * PTILE);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 3;
   uint64_t* v_full = bars + 5;
   uint64_t* v_empty = bars + 7;
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_free = bars + 11;
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_full = bars + 15;   // P.V of the tile in P buffer b has completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile uint32_t* abort_flag = tmem_slot + 1;
+  uint64_t* s_full = bars + 9;    // per query tile
+  uint64_t* s_free = bars + 11;   // per query tile, 128 arrivals
+  uint64_t* p_full = bars + 13;   // per query tile, 128 arrivals
+  uint64_t* pv_done = bars + 15;  // per query tile: P_i V has completed (P_i free, O_i current)
+  uint32_t* misc = reinterpret_cast<uint32_t*>(bars + kBars);
+  uint32_t* tmem_slot = misc;
+  volatile uint32_t* abort_flag = misc + 1;
+  volatile int* slot_of = reinterpret_cast<volatile int*>(misc + 2);
 
   const int warp = warp_id(), lane = lane_id();
-  const int slot = blockIdx.z, head = blockIdx.y, q0 = blockIdx.x * TQ;
-  const int length = p.lengths ? min(p.lengths[slot], p.keys) : p.keys;
-  const int tiles = (length + TK - 1) / TK;
+  const int per_slot = p.heads * p.pairs;
+  const int rank = blockIdx.x / per_slot, rem = blockIdx.x % per_slot;
+  const int head = rem / p.pairs, q0 = (rem % p.pairs) * 2 * TQ;
+  const int nq = min(2, (p.queries - q0) / TQ);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -82,202 +91,254 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       mbar_init(k_full + i, 1); mbar_init(k_empty + i, 1);
       mbar_init(v_full + i, 1); mbar_init(v_empty + i, 1);
       mbar_init(s_full + i, 1); mbar_init(s_free + i, 128);
-      mbar_init(p_full + i, 128); mbar_init(o_full + i, 1);
+      mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    tc::prefetch_map(&mq); tc::prefetch_map(&mk); tc::prefetch_map(&mv);
+    tc::prefetch_map(&mq_wide); tc::prefetch_map(&mq_narrow);
+    tc::prefetch_map(&mk_wide); tc::prefetch_map(&mk_narrow);
+    tc::prefetch_map(&mv_wide); tc::prefetch_map(&mv_narrow);
+  }
+  if (warp == 3) {
+    // The slot of this rank in descending key-length order (ties by slot index): a permutation, one lane matches.
+    if (p.lengths) {
+      for (int s = lane; s < p.slots; s += 32) {
+        const int ls = max(0, min(p.lengths[s], p.keys));
+        int r = 0;
+        for (int u = 0; u < p.slots; ++u) {
+          const int lu = max(0, min(p.lengths[u], p.keys));
+          r += (lu > ls) || (lu == ls && u < s);
+        }
+        if (r == rank) *slot_of = s;
+      }
+    } else if (lane == 0) {
+      *slot_of = rank;
+    }
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;
+  const int slot = *slot_of;
+  const int length = p.lengths ? max(0, min(p.lengths[slot], p.keys)) : p.keys;
+  const int tiles = (length + TK - 1) / TK;
   const int kg = p.kv_mode == 0 ? head : slot * p.heads + head;
   const int kr0 = p.kv_mode == 0 ? slot * p.keys : 0;
 
-  if (warp == 0) {
-    if (lane == 0 && tiles > 0) {
-      const int qr = slot * p.queries + q0;
-      mbar_expect_tx(q_full, TILE);
-      tc::tma_load_3d(sq, &mq, 0, head, qr, q_full);
-      tc::tma_load_3d(sq + ATOM, &mq, 64, head, qr, q_full);
-      for (int t = 0; t < tiles; ++t) {
-        const int s = t & 1;
-        if (t >= 2 && !tc::wait(k_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
-        mbar_expect_tx(k_full + s, TILE);
-        tc::tma_load_3d(sk + s * TILE, &mk, 0, kg, kr0 + t * TK, k_full + s);
-        tc::tma_load_3d(sk + s * TILE + ATOM, &mk, 64, kg, kr0 + t * TK, k_full + s);
-      }
-    }
-  } else if (warp == 2) {
-    if (lane == 0 && tiles > 0) {
-      for (int t = 0; t < tiles; ++t) {
-        const int s = t & 1;
-        if (t >= 2 && !tc::wait(v_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
-        mbar_expect_tx(v_full + s, TILE);
-        tc::tma_load_3d(sv + s * TILE, &mv, 0, kg, kr0 + t * TK, v_full + s);
-        tc::tma_load_3d(sv + s * TILE + ATOM, &mv, 64, kg, kr0 + t * TK, v_full + s);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && tiles > 0) {
-      constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
-      constexpr uint32_t idesc_o = tc::instr_desc(TQ, HD, true);
-      bool ok = tc::wait(q_full, 0, abort_flag);
-      const uint32_t qa = smem_addr(sq);
-      for (int t = 0; ok && t <= tiles; ++t) {
-        if (t < tiles) {
+  // Register split: the load/MMA warpgroup keeps 40 per thread, the two softmax warpgroups take 232
+  // (128 x 40 + 256 x 232 = 384 x 168, the launch's allocation).
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
+    if (warp == 0) {
+      if (lane == 0 && tiles > 0) {
+        mbar_expect_tx(q_full, nq * OPER);
+        for (int i = 0; i < nq; ++i) {
+          const int qr = slot * p.queries + q0 + i * TQ;
+          tc::tma_load_3d(sq + i * OPER, &mq_wide, 0, head, qr, q_full);
+          tc::tma_load_3d(sq + i * OPER + WIDE, &mq_narrow, 64, head, qr, q_full);
+        }
+        for (int t = 0; t < tiles; ++t) {
           const int s = t & 1;
-          ok = tc::wait(k_full + s, (t >> 1) & 1, abort_flag);
-          if (ok && t >= 2) ok = tc::wait(s_free + s, ((t - 2) >> 1) & 1, abort_flag);
-          if (!ok) break;
-          tc::fence_after();
-          const uint32_t kb = smem_addr(sk + s * TILE);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
-            tc::umma(tmem + s * 128, tc::sw128_desc(qa + off), tc::sw128_desc(kb + off), idesc_s, kk > 0);
-          }
-          tc::commit(s_full + s);
-          tc::commit(k_empty + s);
+          if (t >= 2 && !tc::wait(k_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
+          mbar_expect_tx(k_full + s, OPER);
+          tc::tma_load_3d(sk + s * OPER, &mk_wide, 0, kg, kr0 + t * TK, k_full + s);
+          tc::tma_load_3d(sk + s * OPER + WIDE, &mk_narrow, 64, kg, kr0 + t * TK, k_full + s);
         }
-        if (t >= 1) {
-          const int u = t - 1, su = u & 1;
-          ok = tc::wait(v_full + su, (u >> 1) & 1, abort_flag);
-          if (ok) ok = tc::wait(p_full + su, (u >> 1) & 1, abort_flag);
-          if (!ok) break;
-          tc::fence_after();
-          const uint32_t pa = smem_addr(sp + su * TILE), vb = smem_addr(sv + su * TILE);
-#pragma unroll
-          for (int kk = 0; kk < TK / 16; ++kk) {
-            const uint32_t aoff = (kk >> 2) * ATOM + (kk & 3) * 32;
-            tc::umma(tmem_o, tc::sw128_desc(pa + aoff), tc::sw128_desc(vb + kk * 2048, ATOM, 1024), idesc_o,
-                     (u > 0 || kk > 0) ? 1u : 0u);
+      }
+    } else if (warp == 2) {
+      if (lane == 0 && tiles > 0) {
+        for (int t = 0; t < tiles; ++t) {
+          const int s = t & 1;
+          if (t >= 2 && !tc::wait(v_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
+          mbar_expect_tx(v_full + s, OPER);
+          tc::tma_load_3d(sv + s * OPER, &mv_wide, 0, kg, kr0 + t * TK, v_full + s);
+          tc::tma_load_3d(sv + s * OPER + WIDE, &mv_narrow, 64, kg, kr0 + t * TK, v_full + s);
+        }
+      }
+    } else if (warp == 1) {
+      if (lane == 0 && tiles > 0) {
+        constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
+        constexpr uint32_t idesc_wide = tc::instr_desc(TQ, 64, true);
+        constexpr uint32_t idesc_narrow = tc::instr_desc(TQ, 32, true);
+        bool ok = tc::wait(q_full, 0, abort_flag);
+        for (int t = 0; ok && t <= tiles; ++t) {
+          if (t < tiles) {
+            const int s = t & 1;
+            ok = tc::wait(k_full + s, (t >> 1) & 1, abort_flag);
+            const uint32_t kb = smem_addr(sk + s * OPER);
+            for (int i = 0; ok && i < nq; ++i) {
+              if (t >= 1) ok = tc::wait(s_free + i, (t - 1) & 1, abort_flag);
+              if (!ok) break;
+              tc::fence_after();
+              const uint32_t qa = smem_addr(sq + i * OPER);
+  #pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                tc::umma(tmem + i * 128, tc::sw128_desc(qa + kk * 32), tc::sw128_desc(kb + kk * 32), idesc_s, kk > 0);
+  #pragma unroll
+              for (int kk = 0; kk < 2; ++kk)
+                tc::umma(tmem + i * 128, tc::sw64_desc(qa + WIDE + kk * 32), tc::sw64_desc(kb + WIDE + kk * 32),
+                         idesc_s, 1u);
+              tc::commit(s_full + i);
+            }
+            if (!ok) break;
+            tc::commit(k_empty + s);
           }
-          tc::commit(o_full + su);
-          tc::commit(v_empty + su);
+          if (t >= 1) {
+            const int u = t - 1, su = u & 1;
+            ok = tc::wait(v_full + su, (u >> 1) & 1, abort_flag);
+            const uint32_t vb = smem_addr(sv + su * OPER);
+            for (int i = 0; ok && i < nq; ++i) {
+              ok = tc::wait(p_full + i, u & 1, abort_flag);
+              if (!ok) break;
+              tc::fence_after();
+              const uint32_t pa = smem_addr(sp + i * PTILE);
+              const uint32_t o = tmem + 256 + i * 128;
+  #pragma unroll
+              for (int kk = 0; kk < TK / 16; ++kk) {
+                const uint64_t a = tc::sw128_desc(pa + (kk >> 2) * WIDE + (kk & 3) * 32);
+                const uint32_t acc = (u > 0 || kk > 0) ? 1u : 0u;
+                tc::umma(o, a, tc::sw128_desc(vb + kk * 2048, WIDE, 1024), idesc_wide, acc);
+                tc::umma(o + 64, a, tc::sw64_desc(vb + WIDE + kk * 1024, NARROW, 512), idesc_narrow, acc);
+              }
+              tc::commit(pv_done + i);
+            }
+            if (!ok) break;
+            tc::commit(v_empty + su);
+          }
         }
       }
     }
-  } else if (warp >= 4) {
+    tc::fence_before();
+    __syncwarp();
+    asm volatile("barrier.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (warp == 1) {
+      tc::fence_after();
+      tc::tmem_dealloc(*tmem_slot, TMEM_COLS);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+    const int i = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    const uint32_t ts = tmem + lanes + i * 128, to = tmem + lanes + 256 + i * 128;
+    const int qrow = q0 + i * TQ + row;
+    uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)slot * p.queries + qrow) * (p.heads * HD) + head * HD);
     const float sl2 = p.scale_log2;
     float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int t = 0; t < tiles; ++t) {
-      const int s = t & 1;
-      if (!tc::wait(s_full + s, (t >> 1) & 1, abort_flag)) { ok = false; break; }
+    uint8_t* rowp = sp + i * PTILE + row * 128;
+    for (int t = 0; i < nq && t < tiles; ++t) {
+      if (!tc::wait(s_full + i, t & 1, abort_flag)) { ok = false; break; }
       tc::fence_after();
       uint32_t r[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tc::ld32(tmem + lanes + s * 128 + c * 32, r[c]);
+      for (int c = 0; c < 4; ++c) tc::ld32(ts + c * 32, r[c]);
       tc::wait_ld();
       tc::fence_before();
-      tc::mbar_arrive(s_free + s);
+      tc::mbar_arrive(s_free + i);
       const int key0 = t * TK;
-      const bool full = key0 + TK <= length;
-      if (!full) {
+      if (key0 + TK > length) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (key0 + c * 32 + j >= length) r[c][j] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      float mc[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float a = __uint_as_float(r[c][0]), b = __uint_as_float(r[c][1]);
+#pragma unroll
+        for (int j = 2; j < 32; j += 4) {
+          a = tc::fmax3(a, __uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1]));
+          b = tc::fmax3(b, __uint_as_float(r[c][j + 2]), __uint_as_float(r[c][j + 3]));
+        }
+        mc[c] = fmaxf(a, b);
+      }
+      const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])) * sl2;
+      // Raise the exponent base only when the row max outgrows it by more than 8 (warp-uniform rescale of O).
+      const bool raise = mx > m_used + 8.f;
+      const bool any_raise = __any_sync(0xffffffffu, raise);
+      float alpha = 1.f;
+      if (any_raise) {
+        const float m_new = raise ? mx : m_used;
+        alpha = tc::ex2(m_used - m_new);   // m_used = -inf on the first tile: alpha = 0
+        m_used = m_new;
+      }
+      const float2 scale2 = make_float2(sl2, sl2), nbase2 = make_float2(-m_used, -m_used);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      uint32_t packed[64];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[c][j]));
-      mx *= sl2;
-      // Raise the exponent base only when the row max outgrows it by more than 8 (warp-uniform rescale of O).
-      const bool raise = mx > m_used + 8.f;
-      if (__any_sync(0xffffffffu, raise)) {
-        const float m_new = raise ? mx : m_used;
-        const float alpha = tc::ex2(m_used - m_new);   // m_used = -inf on the first tile: alpha = 0
-        l_run *= alpha;
-        m_used = m_new;
-        if (t >= 1) {
-          // O holds the P.V products of tiles < t; the last one (t-1) must have completed.
-          const int u = t - 1;
-          if (!tc::wait(o_full + (u & 1), (u >> 1) & 1, abort_flag)) { ok = false; break; }
-          tc::fence_after();
+        for (int j = 0; j < 32; j += 2) {
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1])), scale2,
+                                      nbase2);
+          const float2 e = make_float2(tc::ex2(x.x), tc::ex2(x.y));
+          acc[(j >> 1) & 3] = __fadd2_rn(acc[(j >> 1) & 3], e);
+          packed[c * 16 + (j >> 1)] = tc::pack_bf16x2(e.x, e.y);
+        }
+      // P_i and O_i are free once the P.V of tile t-1 has completed.
+      if (t >= 1) {
+        if (!tc::wait(pv_done + i, (t - 1) & 1, abort_flag)) { ok = false; break; }
+        tc::fence_after();
+        if (any_raise) {
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t o[32];
-            tc::ld32(tmem_o + lanes + c * 32, o);
+            tc::ld32(to + c * 32, o);
             tc::wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-            tc::st32(tmem_o + lanes + c * 32, o);
+            tc::st32(to + c * 32, o);
           }
           tc::wait_st();
         }
       }
-      // P buffer s was last read by the P.V of tile t-2.
-      if (t >= 2 && !tc::wait(o_full + s, ((t - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
-      const float base = m_used;
-      float sum = 0.f;
-      uint8_t* pb = sp + s * TILE;
+      // keys 8q .. 8q+7: swizzle atom q/8, 16-byte chunk q%8 XOR (row % 8)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float p0 = tc::ex2(__uint_as_float(r[c][j]) * sl2 - base);
-          const float p1 = tc::ex2(__uint_as_float(r[c][j + 1]) * sl2 - base);
-          sum += p0 + p1;
-          packed[j >> 1] = pack_bf16(p0, p1);
-        }
-        // keys c*32 .. c*32+31: swizzle atom c/2, 16-byte chunks (c%2)*4 .. +3, chunk index XOR (row % 8)
-        uint8_t* rowp = pb + (c >> 1) * ATOM + row * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = ((c & 1) * 4 + q) ^ (row & 7);
-          *reinterpret_cast<uint4*>(rowp + chunk * 16) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-        }
+      for (int q = 0; q < 16; ++q) {
+        const int chunk = (q & 7) ^ (row & 7);
+        *reinterpret_cast<uint4*>(rowp + (q >> 3) * WIDE + chunk * 16) =
+            make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
       }
-      l_run += sum;
+      const float2 s01 = __fadd2_rn(acc[0], acc[1]), s23 = __fadd2_rn(acc[2], acc[3]);
+      l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
       tc::fence_before();
       tc::fence_async_smem();
-      tc::mbar_arrive(p_full + s);
+      tc::mbar_arrive(p_full + i);
     }
-    const int qrow = q0 + row;
-    if (ok && tiles > 0) {
-      const int u = tiles - 1;
-      ok = tc::wait(o_full + (u & 1), (u >> 1) & 1, abort_flag);
-      if (ok) {
-        tc::fence_after();
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)slot * p.queries + qrow) * (p.heads * HD) + head * HD);
+    if (i < nq) {
+      if (ok && tiles > 0) {
+        const int u = tiles - 1;
+        ok = tc::wait(pv_done + i, u & 1, abort_flag);
+        if (ok) {
+          tc::fence_after();
+          const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t o[32];
-          tc::ld32(tmem_o + lanes + c * 32, o);
-          tc::wait_ld();
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tc::ld32(to + c * 32, o);
+            tc::wait_ld();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float* f = reinterpret_cast<const float*>(o) + 8 * i;
-            dst[c * 4 + i] = make_uint4(pack_bf16(f[0] * inv, f[1] * inv), pack_bf16(f[2] * inv, f[3] * inv),
-                                        pack_bf16(f[4] * inv, f[5] * inv), pack_bf16(f[6] * inv, f[7] * inv));
+            for (int k = 0; k < 4; ++k) {
+              const float* f = reinterpret_cast<const float*>(o) + 8 * k;
+              dst[c * 4 + k] = make_uint4(tc::pack_bf16x2(f[0] * inv, f[1] * inv), tc::pack_bf16x2(f[2] * inv, f[3] * inv),
+                                          tc::pack_bf16x2(f[4] * inv, f[5] * inv), tc::pack_bf16x2(f[6] * inv, f[7] * inv));
+            }
           }
         }
+      } else if (ok) {
+        for (int k = 0; k < HD / 8; ++k) dst[k] = make_uint4(0, 0, 0, 0);
       }
-    } else if (ok && qrow < p.queries) {
-      uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)slot * p.queries + qrow) * (p.heads * HD) + head * HD);
-      for (int i = 0; i < HD / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+      if (!ok && lane == 0) atomicOr(&g_svx_attention_timeouts, SVX_STATUS_WAIT_TIMEOUT);
     }
-    if (!ok && lane == 0) atomicOr(&g_svx_attention_timeouts, SVX_STATUS_WAIT_TIMEOUT);
-  }
-  tc::fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc::fence_after();
-    tc::tmem_dealloc(tmem, TMEM_COLS);
+    // Teardown: every TMEM access of this warpgroup is done; the TMEM owner frees the columns after all 12 warps.
+    tc::fence_before();
+    __syncwarp();
+    asm volatile("barrier.arrive 1, %0;" ::"n"(kThreads) : "memory");
   }
 }
 
@@ -298,19 +359,25 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
   } else {
     return fail(SVX_ERR_INVALID, "attention: K/V strides must be [slot*keys][head] or [slot][head][key] layouts");
   }
-  CUtensorMap mq, mk, mv;
-  int rc = make_map_3d(&mq, q, HD, heads, (uint64_t)slots * queries, HD * 2, q_row_stride * 2, 64, TQ);
-  if (!rc) rc = make_map_3d(&mk, k, HD, groups, rows, group_stride, row_stride, 64, TK);
-  if (!rc) rc = make_map_3d(&mv, v, HD, groups, rows, group_stride, row_stride, 64, TK);
+  CUtensorMap m[6];
+  const uint64_t qrows = (uint64_t)slots * queries;
+  constexpr CUtensorMapSwizzle SW64 = CU_TENSOR_MAP_SWIZZLE_64B;
+  int rc = make_map_3d(&m[0], q, HD, heads, qrows, HD * 2, q_row_stride * 2, 64, TQ);
+  if (!rc) rc = make_map_3d(&m[1], q, HD, heads, qrows, HD * 2, q_row_stride * 2, 32, TQ, SW64);
+  if (!rc) rc = make_map_3d(&m[2], k, HD, groups, rows, group_stride, row_stride, 64, TK);
+  if (!rc) rc = make_map_3d(&m[3], k, HD, groups, rows, group_stride, row_stride, 32, TK, SW64);
+  if (!rc) rc = make_map_3d(&m[4], v, HD, groups, rows, group_stride, row_stride, 64, TK);
+  if (!rc) rc = make_map_3d(&m[5], v, HD, groups, rows, group_stride, row_stride, 32, TK, SW64);
   if (rc) return rc;
   static bool configured = false;
   if (!configured) {
     SVX_CHECK_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
     configured = true;
   }
-  AttnParams prm{heads, queries, keys, kv_mode, lengths, out, (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
-  dim3 grid(queries / TQ, heads, slots);
-  attention_tc_kernel<<<grid, kThreads, kSmem, stream>>>(mq, mk, mv, prm);
+  const int pairs = (queries / TQ + 1) / 2;
+  AttnParams prm{slots, heads, queries, keys, pairs, kv_mode, lengths, out,
+                 (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
+  attention_tc_kernel<<<slots * heads * pairs, kThreads, kSmem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], prm);
   return launch_status("attention_tc_kernel");
 }
 

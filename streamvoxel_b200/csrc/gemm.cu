@@ -336,7 +336,8 @@ static int make_kmajor_map(CUtensorMap* map, const void* ptr, int rows, int cols
 }
 
 int make_map_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t groups, uint64_t rows,
-                uint64_t group_stride_bytes, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+                uint64_t group_stride_bytes, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                CUtensorMapSwizzle swizzle) {
   EncodeTiled encode = encode_fn();
   if (!encode) return fail(SVX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   SVX_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0, "TMA operand must be 16-byte aligned");
@@ -346,7 +347,7 @@ int make_map_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t grou
   cuuint32_t box[3] = {box_inner, 1, box_rows};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, elem,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SVX_ERR_CUDA, "cuTensorMapEncodeTiled (3d) failed: " + std::to_string((int)r));
   return SVX_OK;

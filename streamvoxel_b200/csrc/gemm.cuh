@@ -24,9 +24,11 @@ struct GemmPlan {
 
 int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N, int K, int bn);
 int gemm_run(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream);
-// 3-D bf16 tensor map (inner, groups, rows), 128B swizzle, box (box_inner, 1, box_rows); elements past `inner` read 0.
+// 3-D bf16 tensor map (inner, groups, rows), box (box_inner, 1, box_rows), 128B swizzle (box_inner 64) or 64B swizzle
+// (box_inner 32); elements past `inner` read 0.
 int make_map_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t groups, uint64_t rows,
-                uint64_t group_stride_bytes, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows);
+                uint64_t group_stride_bytes, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 uint32_t attention_timeouts();
 int epi_from_args(const svx_epilogue_args* e, EpiParams* ep, int N);
 int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,

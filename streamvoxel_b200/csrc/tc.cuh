@@ -26,16 +26,22 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// UMMA shared-memory descriptor, 128B swizzle, sm_100 version bit. K-major tiles: 8-row atoms of 128 B, 1024 B apart
-// (SBO), LBO unused (1). MN-major tiles: 64-element (128 B) rows along MN, 8 K-rows per atom 1024 B apart (SBO),
-// atoms along MN `lbo` bytes apart (LBO).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes = 16, uint32_t sbo_bytes = 1024) {
+// UMMA shared-memory descriptor (sm_100 version bit), swizzled canonical layouts. K-major: 8-row atoms whose rows are
+// the swizzle width (128 or 64 B), atoms `sbo` bytes apart, LBO unused. MN-major: rows of one swizzle width along MN,
+// 8 K-rows per atom `sbo` bytes apart, atoms along MN `lbo` bytes apart. Layout field: 2 = 128B swizzle, 4 = 64B.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;
   return d;
+}
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes = 16, uint32_t sbo_bytes = 1024) {
+  return smem_desc(saddr, lbo_bytes, sbo_bytes, 2);
+}
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr, uint32_t lbo_bytes = 16, uint32_t sbo_bytes = 512) {
+  return smem_desc(saddr, lbo_bytes, sbo_bytes, 4);
 }
 
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, A K-major, B K-major (b_mn = false) or MN-major.
@@ -88,6 +94,20 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two fp32 values rounded to nearest-even bf16 and packed (lo in bits 0-15).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(d) : "f"(lo), "f"(hi));
+  return d;
 }
 
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

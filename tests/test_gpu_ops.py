@@ -271,6 +271,34 @@ def test_attention_self_and_varlen_cross(ops):
         torch.testing.assert_close(got[s * n:(s + 1) * n], want.transpose(0, 1).reshape(n, d), atol=1e-2, rtol=1e-2)
 
 
+def test_attention_odd_query_tiles_ties_and_empty_slots(ops):
+    """384 queries (a CTA with one query tile), tied and zero key lengths, and logits large enough to raise the
+    exponent base several times within a row."""
+    torch.manual_seed(14)
+    slots, heads, n, d = 4, 2, 384, 192
+    qkv = (torch.randn((slots * n, 3 * d), device='cuda') * 2.5).bfloat16()
+    got = ops.attention(qkv, qkv[:, d:], qkv[:, 2 * d:], slots, heads, n, n, q_row_stride=3 * d,
+                        kv_slot_stride=n * 3 * d, kv_head_stride=96, kv_row_stride=3 * d).float()
+    q, k_, v = qkv.float().reshape(slots, n, 3, heads, 96).unbind(2)
+    want = torch.nn.functional.scaled_dot_product_attention(q.transpose(1, 2), k_.transpose(1, 2), v.transpose(1, 2))
+    torch.testing.assert_close(got, want.transpose(1, 2).reshape(slots * n, d), atol=2e-2, rtol=2e-2)
+    cap = 1280
+    kc = (torch.randn((slots, heads, cap, 96), device='cuda') * 2.0).bfloat16()
+    vc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    lengths = torch.tensor([577, 0, 577, 1280], dtype=torch.int32, device='cuda')
+    qx = (torch.randn((slots * n, d), device='cuda') * 2.0).bfloat16()
+    got = ops.attention(qx, kc, vc, slots, heads, n, cap, q_row_stride=d, kv_slot_stride=heads * cap * 96,
+                        kv_head_stride=cap * 96, kv_row_stride=96, lengths=lengths).float()
+    for s in range(slots):
+        L = int(lengths[s])
+        if L == 0:
+            assert torch.count_nonzero(got[s * n:(s + 1) * n]) == 0
+            continue
+        qs = qx[s * n:(s + 1) * n].float().reshape(n, heads, 96).transpose(0, 1)
+        want = torch.nn.functional.scaled_dot_product_attention(qs, kc[s, :, :L].float(), vc[s, :, :L].float())
+        torch.testing.assert_close(got[s * n:(s + 1) * n], want.transpose(0, 1).reshape(n, d), atol=2e-2, rtol=2e-2)
+
+
 def test_layernorm_modulate(ops):
     torch.manual_seed(5)
     for d in (192, 768):
