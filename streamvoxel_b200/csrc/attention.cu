@@ -1,22 +1,25 @@
 // Non-causal attention, head_dim 96, over per-slot variable-length keys, on the 5th-generation tensor cores.
 //
 // One CTA = two 128-query tiles of one (slot, head) sharing every K/V tile. Key tiles of 128 are streamed by TMA into
-// two-stage K and V rings, and only the ceil(length / 128) tiles of a slot are loaded: the packed-key block mask of
+// three-stage K and V rings, and only the ceil(length / 128) tiles of a slot are loaded: the packed-key block mask of
 // `streamvoxel/stream/fast_ops.py:149-159`. Every operand tile (Q, K, V) is exactly 96 dims wide: dims 0-63 as a
 // 128B-swizzled part (128-byte rows) and dims 64-95 as a 64B-swizzled part (64-byte rows), two TMA boxes per tile.
 //
-// Warp roles (384 threads): warp 0 loads Q and the K ring, warp 2 the V ring; warp 1 owns TMEM and one thread issues
-// tcgen05.mma for both query tiles i = 0, 1:
-//   S_i = Q_i K(t)^T   M=128, N=128, K=96  -> TMEM columns [128 i, +128)
-//   O_i += P_i V(t)    M=128, N=64 + N=32, K=128 -> TMEM columns [256 + 128 i, +96)   (V read MN-major)
-// Warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1, one query row per thread (TMEM lane): each
-// reads its row of S_i once with tcgen05.ld, frees S_i (so S_i(t+1) is computed during the softmax of t), and writes
-// P_i = 2^(S*scale - m) as bf16 into a 128B-swizzled K-major tile in shared memory (the A operand of P.V). While one
+// Tensor memory per query tile i (512 columns): S_i fp32 at [128 i, +128), O_i fp32 at [256 + 128 i, +96). The
+// softmax writes P_i as bf16 pairs over the first 64 columns of S_i, and P_i V takes its A operand from there, so
+// P never touches shared memory (whose bandwidth bounds the small-N products when both operands come from it).
+//
+// Warp roles (384 threads): warp 0 loads Q and the K ring, warp 2 the V ring; warp 1 owns TMEM and issues the
+// products (each loop warp-converged, one elected lane issuing), per query tile i in turn:
+//   O_i += P_i(t) V(t)   M=128, N=64 + N=32, K=128   (A = P_i in TMEM, V read MN-major)
+//   S_i  = Q_i K(t+1)^T  M=128, N=128, K=96          (issued once P_i(t) V(t) has completed: S_i overwrites P_i)
+// Warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1, one query row per thread (TMEM lane): read the
+// row of S_i with tcgen05.ld, write P_i = 2^(S*scale - m) with tcgen05.st, signal the MMA warp. While one
 // warpgroup computes exponentials the tensor core works for the other. The exponent base m is raised lazily: only
 // when a row's max grows by more than 8 (a factor 256, so P <= 256 stays exact in the fp32 sums), and then the warp
-// rescales its O rows in TMEM after the previous P.V has completed -- exact, since P, O and the sum share one m.
-// P is rounded to bf16 before P.V and the row sums stay fp32, as in SDPA's flash kernels; the output is normalised
-// in fp32 and written as bf16.
+// rescales its O rows in TMEM (P_i V of the previous tile has completed before S_i was issued) -- exact, since P, O
+// and the sum share one m. P is rounded to bf16 before P.V and the row sums stay fp32, as in SDPA's flash kernels;
+// the output is normalised in fp32 and written as bf16.
 // CTAs are numbered longest slot first (the hardware starts them in index order), so the long cross-attention
 // slots do not trail the grid.
 // Every mbarrier wait is bounded (tc::wait); a timeout raises a CTA-wide abort, sets SVX_STATUS_WAIT_TIMEOUT in the
@@ -34,14 +37,14 @@ __device__ uint32_t g_svx_attention_timeouts = 0;
 namespace {
 
 constexpr int TQ = 128, TK = 128, HD = 96;
+constexpr int STAGES = 3;                  // K and V ring depth
 constexpr uint32_t WIDE = 128 * 128;       // 128 rows x 128 B: dims 0-63 of an operand tile (128B swizzle)
 constexpr uint32_t NARROW = 128 * 64;      // 128 rows x 64 B: dims 64-95 (64B swizzle)
 constexpr uint32_t OPER = WIDE + NARROW;   // one Q, K or V tile (24 KB)
-constexpr uint32_t PTILE = 2 * WIDE;       // one P tile: 128 queries x 128 keys bf16, two 64-key swizzle atoms
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int kThreads = 384;
-constexpr int kBars = 17;
-constexpr size_t kSmem = 1024 + 6 * OPER + 2 * PTILE + kBars * 8 + 16;
+constexpr int kBars = 1 + 4 * STAGES + 6;
+constexpr size_t kSmem = 1024 + (2 + 2 * STAGES) * OPER + kBars * 8 + 16;
 
 struct AttnParams {
   int slots, heads, queries, keys, pairs;
@@ -62,18 +65,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;                      // Q tiles 0, 1
   uint8_t* sk = sq + 2 * OPER;             // K ring
-  uint8_t* sv = sk + 2 * OPER;             // V ring
-  uint8_t* sp = sv + 2 * OPER;             // P tiles 0, 1
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * PTILE);
+  uint8_t* sv = sk + STAGES * OPER;        // V ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + STAGES * OPER);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 3;
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 7;
-  uint64_t* s_full = bars + 9;    // per query tile
-  uint64_t* s_free = bars + 11;   // per query tile, 128 arrivals
-  uint64_t* p_full = bars + 13;   // per query tile, 128 arrivals
-  uint64_t* pv_done = bars + 15;  // per query tile: P_i V has completed (P_i free, O_i current)
+  uint64_t* k_empty = k_full + STAGES;
+  uint64_t* v_full = k_empty + STAGES;
+  uint64_t* v_empty = v_full + STAGES;
+  uint64_t* s_full = v_empty + STAGES;   // per query tile: S_i computed
+  uint64_t* p_full = s_full + 2;         // per query tile, 128 arrivals: P_i written (and O_i rescaled)
+  uint64_t* pv_done = p_full + 2;        // per query tile: P_i V completed
   uint32_t* misc = reinterpret_cast<uint32_t*>(bars + kBars);
   uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
@@ -87,11 +88,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < STAGES; ++i) {
       mbar_init(k_full + i, 1); mbar_init(k_empty + i, 1);
       mbar_init(v_full + i, 1); mbar_init(v_empty + i, 1);
-      mbar_init(s_full + i, 1); mbar_init(s_free + i, 128);
-      mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full + i, 1); mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -126,89 +128,80 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   const int kg = p.kv_mode == 0 ? head : slot * p.heads + head;
   const int kr0 = p.kv_mode == 0 ? slot * p.keys : 0;
 
-  // Register split: the load/MMA warpgroup keeps 40 per thread, the two softmax warpgroups take 232
-  // (128 x 40 + 256 x 232 = 384 x 168, the launch's allocation).
+  // Register split: the load/MMA warpgroup keeps 64 per thread, the two softmax warpgroups take 216
+  // (128 x 64 + 256 x 216 <= 384 x 168, the launch's allocation).
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
-    if (warp == 0) {
-      if (lane == 0 && tiles > 0) {
-        mbar_expect_tx(q_full, nq * OPER);
-        for (int i = 0; i < nq; ++i) {
-          const int qr = slot * p.queries + q0 + i * TQ;
-          tc::tma_load_3d(sq + i * OPER, &mq_wide, 0, head, qr, q_full);
-          tc::tma_load_3d(sq + i * OPER + WIDE, &mq_narrow, 64, head, qr, q_full);
-        }
-        for (int t = 0; t < tiles; ++t) {
-          const int s = t & 1;
-          if (t >= 2 && !tc::wait(k_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
-          mbar_expect_tx(k_full + s, OPER);
-          tc::tma_load_3d(sk + s * OPER, &mk_wide, 0, kg, kr0 + t * TK, k_full + s);
-          tc::tma_load_3d(sk + s * OPER + WIDE, &mk_narrow, 64, kg, kr0 + t * TK, k_full + s);
-        }
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+    if (warp == 0 && tiles > 0) {
+      tc::expect_tx_w(q_full, nq * OPER);
+      for (int i = 0; i < nq; ++i) {
+        const int qr = slot * p.queries + q0 + i * TQ;
+        tc::tma_load_3d_w(sq + i * OPER, &mq_wide, 0, head, qr, q_full);
+        tc::tma_load_3d_w(sq + i * OPER + WIDE, &mq_narrow, 64, head, qr, q_full);
       }
-    } else if (warp == 2) {
-      if (lane == 0 && tiles > 0) {
-        for (int t = 0; t < tiles; ++t) {
-          const int s = t & 1;
-          if (t >= 2 && !tc::wait(v_empty + s, ((t - 2) >> 1) & 1, abort_flag)) break;
-          mbar_expect_tx(v_full + s, OPER);
-          tc::tma_load_3d(sv + s * OPER, &mv_wide, 0, kg, kr0 + t * TK, v_full + s);
-          tc::tma_load_3d(sv + s * OPER + WIDE, &mv_narrow, 64, kg, kr0 + t * TK, v_full + s);
-        }
+      for (int t = 0; t < tiles; ++t) {
+        const int s = t % STAGES;
+        if (t >= STAGES && !tc::wait_w(k_empty + s, (t / STAGES - 1) & 1, abort_flag)) break;
+        tc::expect_tx_w(k_full + s, OPER);
+        tc::tma_load_3d_w(sk + s * OPER, &mk_wide, 0, kg, kr0 + t * TK, k_full + s);
+        tc::tma_load_3d_w(sk + s * OPER + WIDE, &mk_narrow, 64, kg, kr0 + t * TK, k_full + s);
       }
-    } else if (warp == 1) {
-      if (lane == 0 && tiles > 0) {
-        constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
-        constexpr uint32_t idesc_wide = tc::instr_desc(TQ, 64, true);
-        constexpr uint32_t idesc_narrow = tc::instr_desc(TQ, 32, true);
-        bool ok = tc::wait(q_full, 0, abort_flag);
-        for (int t = 0; ok && t <= tiles; ++t) {
-          if (t < tiles) {
-            const int s = t & 1;
-            ok = tc::wait(k_full + s, (t >> 1) & 1, abort_flag);
-            const uint32_t kb = smem_addr(sk + s * OPER);
-            for (int i = 0; ok && i < nq; ++i) {
-              if (t >= 1) ok = tc::wait(s_free + i, (t - 1) & 1, abort_flag);
-              if (!ok) break;
-              tc::fence_after();
-              const uint32_t qa = smem_addr(sq + i * OPER);
-  #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                tc::umma(tmem + i * 128, tc::sw128_desc(qa + kk * 32), tc::sw128_desc(kb + kk * 32), idesc_s, kk > 0);
-  #pragma unroll
-              for (int kk = 0; kk < 2; ++kk)
-                tc::umma(tmem + i * 128, tc::sw64_desc(qa + WIDE + kk * 32), tc::sw64_desc(kb + WIDE + kk * 32),
-                         idesc_s, 1u);
-              tc::commit(s_full + i);
-            }
-            if (!ok) break;
-            tc::commit(k_empty + s);
-          }
+    } else if (warp == 2 && tiles > 0) {
+      for (int t = 0; t < tiles; ++t) {
+        const int s = t % STAGES;
+        if (t >= STAGES && !tc::wait_w(v_empty + s, (t / STAGES - 1) & 1, abort_flag)) break;
+        tc::expect_tx_w(v_full + s, OPER);
+        tc::tma_load_3d_w(sv + s * OPER, &mv_wide, 0, kg, kr0 + t * TK, v_full + s);
+        tc::tma_load_3d_w(sv + s * OPER + WIDE, &mv_narrow, 64, kg, kr0 + t * TK, v_full + s);
+      }
+    } else if (warp == 1 && tiles > 0) {
+      constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
+      constexpr uint32_t idesc_wide = tc::instr_desc(TQ, 64, true);
+      constexpr uint32_t idesc_narrow = tc::instr_desc(TQ, 32, true);
+      bool ok = tc::wait_w(q_full, 0, abort_flag) && tc::wait_w(k_full, 0, abort_flag);
+      // Each query tile runs its own chain  S_i(t) -> softmax_i(t) -> P_i(t) V(t) -> S_i(t+1) -> ...; the two chains
+      // interleave on the tensor core.
+      for (int t = 0; ok && t <= tiles; ++t) {
+        const int ks = t % STAGES, vs = (t - 1 + STAGES) % STAGES;
+        const uint32_t kb = smem_addr(sk + ks * OPER), vb = smem_addr(sv + vs * OPER);
+        for (int i = 0; ok && i < nq; ++i) {
           if (t >= 1) {
-            const int u = t - 1, su = u & 1;
-            ok = tc::wait(v_full + su, (u >> 1) & 1, abort_flag);
-            const uint32_t vb = smem_addr(sv + su * OPER);
-            for (int i = 0; ok && i < nq; ++i) {
-              ok = tc::wait(p_full + i, u & 1, abort_flag);
-              if (!ok) break;
-              tc::fence_after();
-              const uint32_t pa = smem_addr(sp + i * PTILE);
-              const uint32_t o = tmem + 256 + i * 128;
-  #pragma unroll
-              for (int kk = 0; kk < TK / 16; ++kk) {
-                const uint64_t a = tc::sw128_desc(pa + (kk >> 2) * WIDE + (kk & 3) * 32);
-                const uint32_t acc = (u > 0 || kk > 0) ? 1u : 0u;
-                tc::umma(o, a, tc::sw128_desc(vb + kk * 2048, WIDE, 1024), idesc_wide, acc);
-                tc::umma(o + 64, a, tc::sw64_desc(vb + WIDE + kk * 1024, NARROW, 512), idesc_narrow, acc);
-              }
-              tc::commit(pv_done + i);
-            }
+            const int u = t - 1;
+            if (i == 0) ok = tc::wait_w(v_full + vs, (u / STAGES) & 1, abort_flag);
+            if (ok) ok = tc::wait_w(p_full + i, u & 1, abort_flag);
             if (!ok) break;
-            tc::commit(v_empty + su);
+            tc::fence_after();
+            const uint32_t o = tmem + 256 + i * 128;
+#pragma unroll
+            for (int kk = 0; kk < TK / 16; ++kk) {
+              const uint32_t a = tmem + i * 128 + kk * 8;
+              const uint32_t acc = (u > 0 || kk > 0) ? 1u : 0u;
+              tc::umma_ts_w(o, a, tc::sw128_desc(vb + kk * 2048, WIDE, 1024), idesc_wide, acc);
+              tc::umma_ts_w(o + 64, a, tc::sw64_desc(vb + WIDE + kk * 1024, NARROW, 512), idesc_narrow, acc);
+            }
+            tc::commit_w(pv_done + i);
+            if (i == nq - 1) tc::commit_w(v_empty + vs);
+          }
+          if (t < tiles) {
+            if (i == 0 && t >= 1) ok = tc::wait_w(k_full + ks, (t / STAGES) & 1, abort_flag);
+            if (ok && t >= 1) ok = tc::wait_w(pv_done + i, (t - 1) & 1, abort_flag);   // P_i(t-1) consumed
+            if (!ok) break;
+            tc::fence_after();
+            const uint32_t qa = smem_addr(sq + i * OPER);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc::umma_w(tmem + i * 128, tc::sw128_desc(qa + kk * 32), tc::sw128_desc(kb + kk * 32), idesc_s, kk > 0);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+              tc::umma_w(tmem + i * 128, tc::sw64_desc(qa + WIDE + kk * 32), tc::sw64_desc(kb + WIDE + kk * 32),
+                         idesc_s, 1u);
+            tc::commit_w(s_full + i);
+            if (i == nq - 1) tc::commit_w(k_empty + ks);
           }
         }
       }
     }
+    // Teardown: the TMEM owner frees the columns once all 12 warps are past their last TMEM access.
     tc::fence_before();
     __syncwarp();
     asm volatile("barrier.sync 1, %0;" ::"n"(kThreads) : "memory");
@@ -217,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       tc::tmem_dealloc(*tmem_slot, TMEM_COLS);
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");
     const int i = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
@@ -228,7 +221,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     const float sl2 = p.scale_log2;
     float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
-    uint8_t* rowp = sp + i * PTILE + row * 128;
     for (int t = 0; i < nq && t < tiles; ++t) {
       if (!tc::wait(s_full + i, t & 1, abort_flag)) { ok = false; break; }
       tc::fence_after();
@@ -236,8 +228,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
 #pragma unroll
       for (int c = 0; c < 4; ++c) tc::ld32(ts + c * 32, r[c]);
       tc::wait_ld();
-      tc::fence_before();
-      tc::mbar_arrive(s_free + i);
       const int key0 = t * TK;
       if (key0 + TK > length) {
 #pragma unroll
@@ -267,47 +257,39 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
         alpha = tc::ex2(m_used - m_new);   // m_used = -inf on the first tile: alpha = 0
         m_used = m_new;
       }
+      // P = 2^(S*scale - m) as bf16 pairs: keys 64h .. 64h+63 -> TMEM columns [32h, +32) of S_i.
       const float2 scale2 = make_float2(sl2, sl2), nbase2 = make_float2(-m_used, -m_used);
       float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      uint32_t packed[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int h = 0; h < 2; ++h) {
+        uint32_t packed[32];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1])), scale2,
+        for (int j = 0; j < 64; j += 2) {
+          const int c = 2 * h + (j >> 5), jj = j & 31;
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[c][jj]), __uint_as_float(r[c][jj + 1])), scale2,
                                       nbase2);
           const float2 e = make_float2(tc::ex2(x.x), tc::ex2(x.y));
           acc[(j >> 1) & 3] = __fadd2_rn(acc[(j >> 1) & 3], e);
-          packed[c * 16 + (j >> 1)] = tc::pack_bf16x2(e.x, e.y);
+          packed[j >> 1] = tc::pack_bf16x2(e.x, e.y);
         }
-      // P_i and O_i are free once the P.V of tile t-1 has completed.
-      if (t >= 1) {
-        if (!tc::wait(pv_done + i, (t - 1) & 1, abort_flag)) { ok = false; break; }
-        tc::fence_after();
-        if (any_raise) {
+        tc::st32(ts + h * 32, packed);
+      }
+      // O_i holds the products of tiles < t (the P_i V of tile t-1 completed before S_i(t) was issued).
+      if (any_raise && t >= 1) {
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tc::ld32(to + c * 32, o);
-            tc::wait_ld();
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tc::ld32(to + c * 32, o);
+          tc::wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-            tc::st32(to + c * 32, o);
-          }
-          tc::wait_st();
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+          tc::st32(to + c * 32, o);
         }
       }
-      // keys 8q .. 8q+7: swizzle atom q/8, 16-byte chunk q%8 XOR (row % 8)
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const int chunk = (q & 7) ^ (row & 7);
-        *reinterpret_cast<uint4*>(rowp + (q >> 3) * WIDE + chunk * 16) =
-            make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-      }
+      tc::wait_st();
       const float2 s01 = __fadd2_rn(acc[0], acc[1]), s23 = __fadd2_rn(acc[2], acc[3]);
       l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
       tc::fence_before();
-      tc::fence_async_smem();
       tc::mbar_arrive(p_full + i);
     }
     if (i < nq) {

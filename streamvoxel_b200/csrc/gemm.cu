@@ -4,9 +4,11 @@
 // Persistent: one CTA per SM walks the 128 x BN output tiles round-robin. Warp 0 streams A/W k-blocks through a
 // STAGES-deep ring of 128B-swizzled shared-memory tiles that runs continuously across tiles; warp 1 owns TMEM and one
 // elected thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators (2 x BN fp32 columns),
-// committing each stage back to the producer and each finished tile to the epilogue; warps 4-11 are the epilogue:
-// two warps per 32-lane TMEM quarter (one per column half) read the accumulator with tcgen05.ld, run the fused
-// epilogue and release the accumulator, so the epilogue of tile i overlaps the main loop of tile i+1.
+// committing each stage back to the producer and each finished tile to the epilogue; warps 4-19 are the epilogue:
+// four warps per 32-lane TMEM quarter (32-column chunks dealt round-robin) read the accumulator with tcgen05.ld, run
+// the fused epilogue (paired fp32 arithmetic, one bf16x2 conversion per pair) and release the accumulator, so the
+// epilogue of tile i overlaps the main loop of tile i+1. The producer/MMA warpgroup runs on 48 registers a thread so
+// the 512 epilogue threads can hold 104 (setmaxnreg; 128 x 48 + 512 x 104 <= 640 x 96 at launch).
 // Every mbarrier wait is bounded; a timeout sets SVX_STATUS_WAIT_TIMEOUT in g_svx_timeouts and skips the work.
 #include <cuda.h>
 #include <math.h>
@@ -22,33 +24,41 @@ __device__ uint32_t g_svx_timeouts = 0;
 namespace {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kThreads = 384;  // warps 0-1 producer/MMA, 2-3 idle, 4-11 epilogue
-constexpr int kEpilogueWarps = 8;
+constexpr int kThreads = 640;  // warps 0-1 producer/MMA, 2-3 idle, 4-19 epilogue
+constexpr int kEpilogueWarps = 16;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
 __device__ __forceinline__ void record_timeout() { atomicOr(&g_svx_timeouts, SVX_STATUS_WAIT_TIMEOUT); }
 
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  return (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
+
+// Round a pair to bf16 (nearest-even) and back to fp32.
+__device__ __forceinline__ float2 round2(float2 v) { return unpack2(tc::pack_bf16x2(v.x, v.y)); }
 
 __device__ __forceinline__ void store_bf16x32(uint16_t* p, const float (&v)[32]) {
   uint4* q = reinterpret_cast<uint4*>(p);
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    q[i] = make_uint4(pack2(v[8 * i], v[8 * i + 1]), pack2(v[8 * i + 2], v[8 * i + 3]),
-                      pack2(v[8 * i + 4], v[8 * i + 5]), pack2(v[8 * i + 6], v[8 * i + 7]));
+    q[i] = make_uint4(tc::pack_bf16x2(v[8 * i], v[8 * i + 1]), tc::pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                      tc::pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), tc::pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
 }
 
-// GELU (erf form), in the operation order of ATen's GeluCUDAKernelImpl: x * 0.5 * (1 + erf(x * sqrt(1/2))).
-__device__ __forceinline__ float gelu_erf(float x) { return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f)); }
+// GELU (erf form) of a pair, in the operation order of ATen's GeluCUDAKernelImpl: x * 0.5 * (1 + erf(x * sqrt(1/2))).
+__device__ __forceinline__ float2 gelu_erf2(float2 x) {
+  const float2 u = __fmul2_rn(x, make_float2(0.70710678118654752440f, 0.70710678118654752440f));
+  const float2 h = __fmul2_rn(x, make_float2(0.5f, 0.5f));
+  return __fmul2_rn(h, __fadd2_rn(make_float2(1.f, 1.f), make_float2(erff(u.x), erff(u.y))));
+}
 
 __device__ __forceinline__ void unpack8(uint4 raw, float* v) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    v[2 * j] = __uint_as_float(w[j] << 16);
-    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    const float2 f = unpack2(w[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
   }
 }
 
@@ -91,29 +101,32 @@ template <int EPI>
 __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, int N, int row, int n,
                                            const uint32_t (&acc)[32], const Operands& o) {
   float y[32];
-  {
-    float bias[32];
+  const uint32_t* bw = reinterpret_cast<const uint32_t*>(o.bias);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) unpack8(o.bias[i], bias + 8 * i);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = round_bf16(__uint_as_float(acc[j]) + bias[j]);
+  for (int j = 0; j < 16; ++j) {
+    const float2 v = round2(__fadd2_rn(make_float2(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1])),
+                                       unpack2(bw[j])));
+    y[2 * j] = v.x;
+    y[2 * j + 1] = v.y;
   }
   if constexpr (EPI == SVX_EPI_BIAS_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = gelu_erf(y[j]);
-  } else if constexpr (EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL) {
-    float res[32];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) unpack8(o.res[i], res + 8 * i);
-    if constexpr (EPI == SVX_EPI_GATE_RESIDUAL) {
-      float gate[32];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) unpack8(o.extra[i], gate + 8 * i);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) y[j] = round_bf16(gate[j] * y[j]);
+    for (int j = 0; j < 16; ++j) {
+      const float2 g = gelu_erf2(make_float2(y[2 * j], y[2 * j + 1]));
+      y[2 * j] = g.x;
+      y[2 * j + 1] = g.y;
     }
+  } else if constexpr (EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL) {
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(o.res);
+    const uint32_t* gw = reinterpret_cast<const uint32_t*>(o.extra);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = res[j] + y[j];
+    for (int j = 0; j < 16; ++j) {
+      float2 v = make_float2(y[2 * j], y[2 * j + 1]);
+      if constexpr (EPI == SVX_EPI_GATE_RESIDUAL) v = round2(__fmul2_rn(unpack2(gw[j]), v));
+      v = __fadd2_rn(unpack2(rw[j]), v);
+      y[2 * j] = v.x;
+      y[2 * j + 1] = v.y;
+    }
   } else if constexpr (EPI == SVX_EPI_ROPE) {
     if (n < ep.rope_cols) {
       // Axial RoPE (`unconditional_md4_timefree.py:24-30`): pair (2f, 2f+1) of a head rotates by table entry f;
@@ -143,7 +156,8 @@ __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, i
       const int oo = o0 + j;
       const int oy = oo >> 4, oz = (oo >> 2) & 3;
       const int64_t idx = ((int64_t)(py * P + oy) * ep.depth + (pz * P + oz)) * ep.width + px * P;
-      *reinterpret_cast<uint2*>(base + idx) = make_uint2(pack2(y[j], y[j + 1]), pack2(y[j + 2], y[j + 3]));
+      *reinterpret_cast<uint2*>(base + idx) =
+          make_uint2(tc::pack_bf16x2(y[j], y[j + 1]), tc::pack_bf16x2(y[j + 2], y[j + 3]));
     }
   } else {
     store_bf16x32(out + (int64_t)row * N + n, y);
@@ -187,32 +201,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 48;");
+    if (warp == 0 && lane == 0) {
       int it = 0;  // ring position across all tiles of this CTA
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES, round = it / STAGES;
-          if (round > 0 && !tc::wait(empty + s, (round - 1) & 1, abort_flag)) { record_timeout(); goto done; }
+          if (round > 0 && !tc::wait(empty + s, (round - 1) & 1, abort_flag)) { record_timeout(); ok = false; break; }
           mbar_expect_tx(full + s, A_BYTES + B_BYTES);
           tc::tma_load_2d(a_s + s * A_BYTES, &tmA, kb * BK, m0, full + s);
           tc::tma_load_2d(b_s + s * B_BYTES, &tmB, kb * BK, n0, full + s);
         }
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       constexpr uint32_t idesc = tc::instr_desc(BM, BN);
       int it = 0, local = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++local) {
         const int buf = local & 1, use = local >> 1;
-        if (use > 0 && !tc::wait(acc_empty + buf, (use - 1) & 1, abort_flag)) { record_timeout(); goto done; }
+        if (use > 0 && !tc::wait(acc_empty + buf, (use - 1) & 1, abort_flag)) { record_timeout(); break; }
         tc::fence_after();
         const uint32_t acc = tmem + buf * BN;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES, round = it / STAGES;
-          if (!tc::wait(full + s, round & 1, abort_flag)) { record_timeout(); goto done; }
+          if (!tc::wait(full + s, round & 1, abort_flag)) { record_timeout(); ok = false; break; }
           tc::fence_after();
           const uint32_t a0 = smem_addr(a_s + s * A_BYTES), b0 = smem_addr(b_s + s * B_BYTES);
 #pragma unroll
@@ -220,48 +235,52 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             tc::umma(acc, tc::sw128_desc(a0 + kk * 32), tc::sw128_desc(b0 + kk * 32), idesc, (kb | kk) != 0);
           tc::commit(empty + s);
         }
-        tc::commit(acc_full + buf);
+        if (ok) tc::commit(acc_full + buf);
       }
     }
-  } else if (warp >= 4) {
-    // Epilogue warps 4..11: TMEM lane quarter (warp % 4) = rows 32*(warp%4) .. +31; column half (warp - 4) / 4.
-    const int quarter = warp & 3, half = (warp - 4) >> 2;
+    // Teardown: the TMEM owner frees the columns once all 20 warps are past their last TMEM access.
+    tc::fence_before();
+    __syncwarp();
+    asm volatile("barrier.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (warp == 1) {
+      tc::fence_after();
+      tc::tmem_dealloc(*tmem_slot, TMEM_COLS);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
+    // Epilogue warps 4..19: TMEM lane quarter (warp % 4) = rows 32*(warp%4) .. +31; 32-column chunks
+    // group, group + 4, ... of the tile, group = (warp - 4) / 4.
+    const int quarter = warp & 3, group = (warp - 4) >> 2;
+    constexpr int CHUNKS = BN / 32;
     int local = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
       const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
       const int buf = local & 1, use = local >> 1;
       const int row = m0 + quarter * 32 + lane;
-      constexpr int CHUNKS = BN / 64;   // 32-column chunks of this warp's column half
-      const int col0 = half * (BN / 2);
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + col0);
-      // Chunk 0's operands are fetched while the main loop still runs; then chunk c's math overlaps chunk c+1's loads.
-      Operands ops[2];
-      uint32_t acc[2][32];
-      prefetch32<EPI>(ep, N, row, n0 + col0, ops[0]);
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN);
+      // The first chunk's operands are fetched while the main loop still runs.
+      Operands ops;
+      if (group < CHUNKS) prefetch32<EPI>(ep, N, row, n0 + group * 32, ops);
       if (!tc::wait(acc_full + buf, use & 1, abort_flag)) { record_timeout(); break; }
       tc::fence_after();
-      tc::ld32(taddr, acc[0]);
-      tc::wait_ld();
 #pragma unroll
-      for (int c = 0; c < CHUNKS; ++c) {
-        if (c + 1 < CHUNKS) {
-          prefetch32<EPI>(ep, N, row, n0 + col0 + (c + 1) * 32, ops[(c + 1) & 1]);
-          tc::ld32(taddr + (c + 1) * 32, acc[(c + 1) & 1]);
+      for (int c = 0; c < (CHUNKS + 3) / 4; ++c) {
+        const int chunk = group + 4 * c;
+        if (chunk < CHUNKS) {
+          if (c > 0) prefetch32<EPI>(ep, N, row, n0 + chunk * 32, ops);
+          uint32_t acc[32];
+          tc::ld32(taddr + chunk * 32, acc);
+          tc::wait_ld();
+          if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + chunk * 32, acc, ops);
         }
-        if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + col0 + c * 32, acc[c & 1], ops[c & 1]);
-        if (c + 1 < CHUNKS) tc::wait_ld();
       }
       tc::fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(acc_empty + buf);
     }
-  }
-done:
-  tc::fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc::fence_after();
-    tc::tmem_dealloc(tmem, TMEM_COLS);
+    tc::fence_before();
+    __syncwarp();
+    asm volatile("barrier.arrive 1, %0;" ::"n"(kThreads) : "memory");
   }
 }
 
