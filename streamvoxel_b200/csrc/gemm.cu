@@ -284,6 +284,163 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   }
 }
 
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): a pair owns 256 x BN output tiles. CTA r of the pair streams
+// rows [128 r, +128) of the A slice and rows [BN/2 r, +BN/2) of the W slice into its own ring, counting both CTAs'
+// bytes on the even CTA's full barrier; the even CTA issues M=256 products that read each CTA's A rows and both W
+// halves, so every W byte crosses shared memory once per pair (a 128 x BN tile per SM reads 1.5x the operand bytes
+// per product, which leaves one SM's tensor core waiting on shared-memory bandwidth). Stage and accumulator
+// commits arrive on both CTAs' barriers; each CTA's epilogue reads its own 128 TMEM lanes and releases the
+// accumulator on the even CTA's barrier.
+constexpr int PM = 256;
+
+template <int BN, int STAGES, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     uint16_t* __restrict__ out, int M, int N, int K, const EpiParams ep) {
+  constexpr uint32_t HB_BYTES = (BN / 2) * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_s = smem;
+  uint8_t* b_s = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(b_s + STAGES * HB_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = tc::cluster_rank();
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int kblocks = K / BK;
+  const int n_tiles = N / BN;
+  const int tiles = (M / PM) * n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, 2 * kEpilogueWarps); }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tc::prefetch_map(&tmA);
+    tc::prefetch_map(&tmB);
+  }
+  if (warp == 1) tc::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc::fence_before();
+  __syncthreads();
+  tc::cluster_sync();   // both CTAs' barriers initialised and TMEM allocated before any cross-CTA signal
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t full0 = tc::cluster_addr(full, 0);        // the even CTA's full barriers
+  const uint32_t acc_empty0 = tc::cluster_addr(acc_empty, 0);
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 48;");
+    if (warp == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+        const int m0 = (tile / n_tiles) * PM + (int)rank * BM, n0 = (tile % n_tiles) * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES, round = it / STAGES;
+          if (round > 0 && !tc::wait_w(empty + s, (round - 1) & 1, abort_flag)) { record_timeout(); ok = false; break; }
+          if (rank == 0) tc::expect_tx_w(full + s, 2 * (A_BYTES + HB_BYTES));
+          tc::tma_load_2d_pair_w(a_s + s * A_BYTES, &tmA, kb * BK, m0, full0 + 8 * s);
+          tc::tma_load_2d_pair_w(b_s + s * HB_BYTES, &tmB, kb * BK, n0, full0 + 8 * s);
+        }
+      }
+    } else if (warp == 1 && rank == 0) {
+      constexpr uint32_t idesc = tc::instr_desc(PM, BN);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += pairs, ++local) {
+        const int buf = local & 1, use = local >> 1;
+        if (use > 0 && !tc::wait_w(acc_empty + buf, (use - 1) & 1, abort_flag)) { record_timeout(); break; }
+        tc::fence_after();
+        const uint32_t acc = tmem + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES, round = it / STAGES;
+          if (!tc::wait_w(full + s, round & 1, abort_flag)) { record_timeout(); ok = false; break; }
+          tc::fence_after();
+          const uint32_t a0 = smem_addr(a_s + s * A_BYTES), b0 = smem_addr(b_s + s * HB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc::umma_pair_w(acc, tc::sw128_desc(a0 + kk * 32), tc::sw128_desc(b0 + kk * 32), idesc, (kb | kk) != 0);
+          tc::commit_pair_w(empty + s, 0x3);
+        }
+        if (ok) tc::commit_pair_w(acc_full + buf, 0x3);
+      }
+    }
+    tc::fence_before();
+    __syncwarp();
+    tc::cluster_sync();   // no cross-CTA signal is pending once every thread of both CTAs is here
+    if (warp == 1) {
+      tc::fence_after();
+      tc::tmem_dealloc_pair(*tmem_slot, TMEM_COLS);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
+    const int quarter = warp & 3, group = (warp - 4) >> 2;
+    constexpr int CHUNKS = BN / 32;
+    int local = 0;
+    for (int tile = pair; tile < tiles; tile += pairs, ++local) {
+      const int m0 = (tile / n_tiles) * PM + (int)rank * BM, n0 = (tile % n_tiles) * BN;
+      const int buf = local & 1, use = local >> 1;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN);
+      Operands ops;
+      if (group < CHUNKS) prefetch32<EPI>(ep, N, row, n0 + group * 32, ops);
+      if (!tc::wait(acc_full + buf, use & 1, abort_flag)) { record_timeout(); break; }
+      tc::fence_after();
+#pragma unroll
+      for (int c = 0; c < (CHUNKS + 3) / 4; ++c) {
+        const int chunk = group + 4 * c;
+        if (chunk < CHUNKS) {
+          if (c > 0) prefetch32<EPI>(ep, N, row, n0 + chunk * 32, ops);
+          uint32_t acc[32];
+          tc::ld32(taddr + chunk * 32, acc);
+          tc::wait_ld();
+          if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + chunk * 32, acc, ops);
+        }
+      }
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(acc_empty0 + 8 * buf);
+    }
+    tc::fence_before();
+    __syncwarp();
+    tc::cluster_sync();
+  }
+}
+
+template <int BN, int STAGES>
+constexpr size_t pair_smem_bytes() {
+  return 1024 + STAGES * (A_BYTES + (size_t)(BN / 2) * BK * 2) + (2 * STAGES + 4) * 8 + 16;
+}
+
+template <int BN, int STAGES, int EPI>
+int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, int M, int N, int K,
+                     const EpiParams& ep, cudaStream_t stream) {
+  constexpr size_t bytes = pair_smem_bytes<BN, STAGES>();
+  static int max_pairs = 0;
+  if (!max_pairs) {
+    SVX_CHECK_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, STAGES, EPI>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = bytes;
+    int clusters = 0;
+    SVX_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<BN, STAGES, EPI>, &cfg));
+    SVX_REQUIRE(clusters > 0, "gemm: no CTA pair fits on this device");
+    max_pairs = clusters;
+  }
+  const int tiles = (N / BN) * (M / PM);
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  gemm_pair_kernel<BN, STAGES, EPI><<<2 * pairs, kThreads, bytes, stream>>>(a, b, out, M, N, K, ep);
+  return launch_status("gemm_pair_kernel");
+}
+
 template <int BN, int STAGES>
 constexpr size_t smem_bytes() {
   return 1024 + STAGES * (A_BYTES + (size_t)BN * BK * 2) + (2 * STAGES + 4) * 8 + 16;
@@ -305,6 +462,16 @@ int launch_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, int M
   const int tiles = (N / BN) * (M / BM);
   gemm_kernel<BN, STAGES, EPI><<<tiles < sms ? tiles : sms, kThreads, bytes, stream>>>(a, b, out, M, N, K, ep);
   return launch_status("gemm_kernel");
+}
+
+template <int EPI>
+int launch_pair_epi(const CUtensorMap& a, const CUtensorMap& b_half, int bn, uint16_t* out, int M, int N, int K,
+                    const EpiParams& ep, cudaStream_t stream) {
+  switch (bn) {
+    case 256: return launch_pair_tile<256, 6, EPI>(a, b_half, out, M, N, K, ep, stream);
+    case 128: return launch_pair_tile<128, 8, EPI>(a, b_half, out, M, N, K, ep, stream);
+    default: return fail(SVX_ERR_INVALID, "gemm: pair tile width must be 128 or 256");
+  }
 }
 
 template <int EPI>
@@ -390,6 +557,24 @@ static int pick_bn(int M, int N) {
   return best;
 }
 
+// Tile width for CTA pairs (256-row tiles, 74 pairs on 148 SMs): a CTA streams its 128 A rows and BN/2 W rows per
+// tile, so a tile costs (128 + BN/2) rows of traffic per SM; the wider tile on ties.
+static int pick_pair_bn(int M, int N) {
+  int sms = 148;
+  int device = 0;
+  if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const int pairs = sms / 2;
+  int best = 0;
+  long best_cost = 0;
+  for (int bn : {256, 128}) {
+    if (N % bn) continue;
+    const long tiles = (long)(N / bn) * (M / PM);
+    const long cost = ((tiles + pairs - 1) / pairs) * (128 + bn / 2);
+    if (!best || cost < best_cost) { best = bn; best_cost = cost; }
+  }
+  return best;
+}
+
 int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N, int K, int bn) {
   SVX_REQUIRE(M > 0 && M % BM == 0, "gemm: M must be a positive multiple of 128");
   SVX_REQUIRE(N > 0 && N % 64 == 0 && K > 0 && K % BK == 0, "gemm: N and K must be multiples of 64");
@@ -398,22 +583,30 @@ int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N
   SVX_REQUIRE(N % plan->bn == 0, "gemm: N must be a multiple of the tile width");
   int rc = make_kmajor_map(&plan->a, A, M, K, BM);
   if (rc) return rc;
-  return make_kmajor_map(&plan->b, W, N, K, plan->bn);
+  rc = make_kmajor_map(&plan->b, W, N, K, plan->bn);
+  if (rc) return rc;
+  // CTA pairs for row counts that tile by 256, unless the caller fixed a single-CTA tile width.
+  plan->pair_bn = (bn <= 0 && M % PM == 0) ? pick_pair_bn(M, N) : 0;
+  if (plan->pair_bn) return make_kmajor_map(&plan->b_half, W, N, K, plan->pair_bn / 2);
+  return SVX_OK;
+}
+
+template <int EPI>
+static int run_epi(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream) {
+  if (plan.pair_bn && M % PM == 0)
+    return launch_pair_epi<EPI>(plan.a, plan.b_half, plan.pair_bn, out, M, plan.N, plan.K, ep, stream);
+  return launch_epi<EPI>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
 }
 
 int gemm_run(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream) {
   SVX_REQUIRE(M > 0 && M <= plan.M && M % BM == 0, "gemm: run rows must be a multiple of 128 within the plan");
   switch (ep.epilogue) {
-    case SVX_EPI_BIAS: return launch_epi<SVX_EPI_BIAS>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
-    case SVX_EPI_BIAS_GELU:
-      return launch_epi<SVX_EPI_BIAS_GELU>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
-    case SVX_EPI_GATE_RESIDUAL:
-      return launch_epi<SVX_EPI_GATE_RESIDUAL>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
-    case SVX_EPI_RESIDUAL:
-      return launch_epi<SVX_EPI_RESIDUAL>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
-    case SVX_EPI_ROPE: return launch_epi<SVX_EPI_ROPE>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
-    case SVX_EPI_CLASS_MAJOR:
-      return launch_epi<SVX_EPI_CLASS_MAJOR>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
+    case SVX_EPI_BIAS: return run_epi<SVX_EPI_BIAS>(plan, M, out, ep, stream);
+    case SVX_EPI_BIAS_GELU: return run_epi<SVX_EPI_BIAS_GELU>(plan, M, out, ep, stream);
+    case SVX_EPI_GATE_RESIDUAL: return run_epi<SVX_EPI_GATE_RESIDUAL>(plan, M, out, ep, stream);
+    case SVX_EPI_RESIDUAL: return run_epi<SVX_EPI_RESIDUAL>(plan, M, out, ep, stream);
+    case SVX_EPI_ROPE: return run_epi<SVX_EPI_ROPE>(plan, M, out, ep, stream);
+    case SVX_EPI_CLASS_MAJOR: return run_epi<SVX_EPI_CLASS_MAJOR>(plan, M, out, ep, stream);
     default: return fail(SVX_ERR_INVALID, "gemm: unknown epilogue");
   }
 }

@@ -18,8 +18,9 @@ struct EpiParams {
 };
 
 struct GemmPlan {
-  CUtensorMap a, b;
-  int M, N, K, bn;
+  CUtensorMap a, b;      // A boxes of 128 rows, W boxes of `bn` rows (one CTA per tile)
+  CUtensorMap b_half;    // W boxes of pair_bn / 2 rows (CTA pairs, 256-row tiles)
+  int M, N, K, bn, pair_bn;
 };
 
 int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N, int K, int bn);

@@ -169,7 +169,7 @@ def _linear_ref(a, w, b):
 
 
 @pytest.mark.parametrize('m,n,k', [(256, 576, 192), (1024, 768, 768), (8192, 2304, 768), (2048, 768, 3072),
-                                   (1024, 3072, 768)])
+                                   (1024, 3072, 768), (384, 768, 256), (512, 1152, 256)])
 def test_gemm_bias_matches_fp32(ops, m, n, k):
     torch.manual_seed(m + n + k)
     a = (torch.randn((m, k), device='cuda') * 0.5).bfloat16()
