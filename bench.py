@@ -182,6 +182,28 @@ def run_api_steps(batch, steps, seeds):
     return committed, h2d, d2h
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch from one ncu capture of the kernel on the
+# profile_case input (`python -m streamvoxel_b200.profile_case <case>`), with that case's algorithmic bytes: the
+# roofline's `traffic` scales the measurement to the timed launch by its algorithmic bytes (traffic grows with the
+# valid keys / rows processed).
+MEASURED_TRAFFIC = {
+    # 8 slots x 8 heads, keys 1344 + 1024 i: K/V 121.1 MB + Q 12.6 MB + O 12.6 MB
+    'attention_cross': (140.1e6, 121.1e6 + 25.2e6),
+    # A 12.6 MB + W 4.7 MB + out 50.3 MB (the output mostly stays in L2 at kernel end)
+    'gemm_fc1_gelu': (18.6e6, 67.6e6),
+}
+
+
+def algorithmic_bytes(name, cfg, lengths):
+    """Bytes a launch must move at least once (inputs read + outputs written), for the traffic scaling."""
+    rows = SLOTS * cfg.patches
+    if name == 'attention_cross':
+        return float(np.sum(lengths)) * cfg.heads * 96 * 2 * 2 + 2 * rows * cfg.d * 2
+    if name == 'gemm_fc1_gelu':
+        return (rows * cfg.d + cfg.mlp * cfg.d + rows * cfg.mlp) * 2.0
+    return None
+
+
 def time_kernels(cfg, forward, batch, lengths):
     """Average launch duration of each kernel class of the step at the step's shapes (CUDA events, 20 launches)."""
     from streamvoxel_b200 import ops, _lib
@@ -338,6 +360,10 @@ def main_ours(args):
         peak, unit, bound = peaks.get('bf16_tflops', 1590.0), 'TFLOP/s', 'tensor'
         src = 'measured (burst; kernel timed alone)' if peaks else 'fallback'
         achieved = kd['work'] / kd['seconds'] / 1e12
+    traffic = None
+    if dominant in MEASURED_TRAFFIC:
+        measured, captured_alg = MEASURED_TRAFFIC[dominant]
+        traffic = measured * algorithmic_bytes(dominant, cfg, lengths) / captured_alg
     step_flops = sum(k['work'] * k['per_step'] for n, k in kernels.items() if not n.startswith('ease'))
     cpu = cpu_baseline(cfg, sd, lengths, args.cpu_sample)
     steps_per_s = args.steps / seconds
@@ -353,7 +379,7 @@ def main_ours(args):
         e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d / args.steps, d2h_bytes_per_step=d2h / args.steps),
         gpu_launches=launches,
         roofline=dict(kernel=dominant, bound=bound, achieved=achieved, peak=peak, unit=unit, frac=achieved / peak,
-                      peak_source=src, traffic=None,
+                      peak_source=src, traffic=traffic, traffic_unit='bytes per launch (ncu, scaled)',
                       algorithmic=f"{kd['work']:.4g} {'bytes' if bound == 'hbm' else 'FLOP'} per launch"),
         step_tflops=step_flops / (seconds / args.steps) / 1e12,
         kernels={k: dict(us=v['seconds'] * 1e6, per_step=v['per_step'],

@@ -2,8 +2,9 @@
 //
 // One CTA = two 128-query tiles of one (slot, head) sharing every K/V tile. Key tiles of 128 are streamed by TMA into
 // three-stage K and V rings, and only the ceil(length / 128) tiles of a slot are loaded: the packed-key block mask of
-// `streamvoxel/stream/fast_ops.py:149-159`. Every operand tile (Q, K, V) is exactly 96 dims wide: dims 0-63 as a
-// 128B-swizzled part (128-byte rows) and dims 64-95 as a 64B-swizzled part (64-byte rows), two TMA boxes per tile.
+// `streamvoxel/stream/fast_ops.py:149-159`. Q and K tiles are exactly 96 dims wide: dims 0-63 as a 128B-swizzled part
+// (128-byte rows) and dims 64-95 as a 64B-swizzled part (64-byte rows). V tiles are two 128B-swizzled 64-dim boxes
+// (dims 96-127 read as zero, no memory traffic) so that P V is one N=96 product per 16 keys.
 //
 // Tensor memory per query tile i (512 columns): S_i fp32 at [128 i, +128), O_i fp32 at [256 + 128 i, +96). The
 // softmax writes P_i as bf16 pairs over the first 64 columns of S_i, and P_i V takes its A operand from there, so
@@ -11,7 +12,7 @@
 //
 // Warp roles (384 threads): warp 0 loads Q and the K ring, warp 2 the V ring; warp 1 owns TMEM and issues the
 // products (each loop warp-converged, one elected lane issuing), per query tile i in turn:
-//   O_i += P_i(t) V(t)   M=128, N=64 + N=32, K=128   (A = P_i in TMEM, V read MN-major)
+//   O_i += P_i(t) V(t)   M=128, N=96, K=128          (A = P_i in TMEM, V read MN-major)
 //   S_i  = Q_i K(t+1)^T  M=128, N=128, K=96          (issued once P_i(t) V(t) has completed: S_i overwrites P_i)
 // Warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1, one query row per thread (TMEM lane): read the
 // row of S_i with tcgen05.ld, write P_i = 2^(S*scale - m) with tcgen05.st, signal the MMA warp. While one
@@ -40,11 +41,12 @@ constexpr int TQ = 128, TK = 128, HD = 96;
 constexpr int STAGES = 3;                  // K and V ring depth
 constexpr uint32_t WIDE = 128 * 128;       // 128 rows x 128 B: dims 0-63 of an operand tile (128B swizzle)
 constexpr uint32_t NARROW = 128 * 64;      // 128 rows x 64 B: dims 64-95 (64B swizzle)
-constexpr uint32_t OPER = WIDE + NARROW;   // one Q, K or V tile (24 KB)
+constexpr uint32_t OPER = WIDE + NARROW;   // one Q or K tile (24 KB)
+constexpr uint32_t VOPER = 2 * WIDE;       // one V tile: two 64-dim atoms along N (32 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int kThreads = 384;
 constexpr int kBars = 1 + 4 * STAGES + 6;
-constexpr size_t kSmem = 1024 + (2 + 2 * STAGES) * OPER + kBars * 8 + 16;
+constexpr size_t kSmem = 1024 + (2 + STAGES) * OPER + STAGES * VOPER + kBars * 8 + 16;
 
 struct AttnParams {
   int slots, heads, queries, keys, pairs;
@@ -58,15 +60,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
                                                                    const __grid_constant__ CUtensorMap mq_narrow,
                                                                    const __grid_constant__ CUtensorMap mk_wide,
                                                                    const __grid_constant__ CUtensorMap mk_narrow,
-                                                                   const __grid_constant__ CUtensorMap mv_wide,
-                                                                   const __grid_constant__ CUtensorMap mv_narrow,
+                                                                   const __grid_constant__ CUtensorMap mv,
                                                                    const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;                      // Q tiles 0, 1
   uint8_t* sk = sq + 2 * OPER;             // K ring
   uint8_t* sv = sk + STAGES * OPER;        // V ring
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + STAGES * OPER);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + STAGES * VOPER);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + STAGES;
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tc::prefetch_map(&mq_wide); tc::prefetch_map(&mq_narrow);
     tc::prefetch_map(&mk_wide); tc::prefetch_map(&mk_narrow);
-    tc::prefetch_map(&mv_wide); tc::prefetch_map(&mv_narrow);
+    tc::prefetch_map(&mv);
   }
   if (warp == 3) {
     // The slot of this rank in descending key-length order (ties by slot index): a permutation, one lane matches.
@@ -150,20 +151,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       for (int t = 0; t < tiles; ++t) {
         const int s = t % STAGES;
         if (t >= STAGES && !tc::wait_w(v_empty + s, (t / STAGES - 1) & 1, abort_flag)) break;
-        tc::expect_tx_w(v_full + s, OPER);
-        tc::tma_load_3d_w(sv + s * OPER, &mv_wide, 0, kg, kr0 + t * TK, v_full + s);
-        tc::tma_load_3d_w(sv + s * OPER + WIDE, &mv_narrow, 64, kg, kr0 + t * TK, v_full + s);
+        tc::expect_tx_w(v_full + s, VOPER);
+        tc::tma_load_3d_w(sv + s * VOPER, &mv, 0, kg, kr0 + t * TK, v_full + s);
+        tc::tma_load_3d_w(sv + s * VOPER + WIDE, &mv, 64, kg, kr0 + t * TK, v_full + s);
       }
     } else if (warp == 1 && tiles > 0) {
       constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
-      constexpr uint32_t idesc_wide = tc::instr_desc(TQ, 64, true);
-      constexpr uint32_t idesc_narrow = tc::instr_desc(TQ, 32, true);
+      constexpr uint32_t idesc_o = tc::instr_desc(TQ, HD, true);
       bool ok = tc::wait_w(q_full, 0, abort_flag) && tc::wait_w(k_full, 0, abort_flag);
       // Each query tile runs its own chain  S_i(t) -> softmax_i(t) -> P_i(t) V(t) -> S_i(t+1) -> ...; the two chains
       // interleave on the tensor core.
       for (int t = 0; ok && t <= tiles; ++t) {
         const int ks = t % STAGES, vs = (t - 1 + STAGES) % STAGES;
-        const uint32_t kb = smem_addr(sk + ks * OPER), vb = smem_addr(sv + vs * OPER);
+        const uint32_t kb = smem_addr(sk + ks * OPER), vb = smem_addr(sv + vs * VOPER);
         for (int i = 0; ok && i < nq; ++i) {
           if (t >= 1) {
             const int u = t - 1;
@@ -171,14 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
             if (ok) ok = tc::wait_w(p_full + i, u & 1, abort_flag);
             if (!ok) break;
             tc::fence_after();
-            const uint32_t o = tmem + 256 + i * 128;
-#pragma unroll
-            for (int kk = 0; kk < TK / 16; ++kk) {
-              const uint32_t a = tmem + i * 128 + kk * 8;
-              const uint32_t acc = (u > 0 || kk > 0) ? 1u : 0u;
-              tc::umma_ts_w(o, a, tc::sw128_desc(vb + kk * 2048, WIDE, 1024), idesc_wide, acc);
-              tc::umma_ts_w(o + 64, a, tc::sw64_desc(vb + WIDE + kk * 1024, NARROW, 512), idesc_narrow, acc);
-            }
+            tc::mma_pv128_w(tmem + 256 + i * 128, tmem + i * 128, tc::sw128_desc(vb, WIDE, 1024), idesc_o,
+                            u > 0 ? 1u : 0u);
             tc::commit_w(pv_done + i);
             if (i == nq - 1) tc::commit_w(v_empty + vs);
           }
@@ -188,13 +182,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
             if (!ok) break;
             tc::fence_after();
             const uint32_t qa = smem_addr(sq + i * OPER);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc::umma_w(tmem + i * 128, tc::sw128_desc(qa + kk * 32), tc::sw128_desc(kb + kk * 32), idesc_s, kk > 0);
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-              tc::umma_w(tmem + i * 128, tc::sw64_desc(qa + WIDE + kk * 32), tc::sw64_desc(kb + WIDE + kk * 32),
-                         idesc_s, 1u);
+            tc::mma_qk96_w(tmem + i * 128, tc::sw128_desc(qa), tc::sw128_desc(kb), tc::sw64_desc(qa + WIDE),
+                           tc::sw64_desc(kb + WIDE), idesc_s);
             tc::commit_w(s_full + i);
             if (i == nq - 1) tc::commit_w(k_empty + ks);
           }
@@ -341,7 +330,7 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
   } else {
     return fail(SVX_ERR_INVALID, "attention: K/V strides must be [slot*keys][head] or [slot][head][key] layouts");
   }
-  CUtensorMap m[6];
+  CUtensorMap m[5];
   const uint64_t qrows = (uint64_t)slots * queries;
   constexpr CUtensorMapSwizzle SW64 = CU_TENSOR_MAP_SWIZZLE_64B;
   int rc = make_map_3d(&m[0], q, HD, heads, qrows, HD * 2, q_row_stride * 2, 64, TQ);
@@ -349,7 +338,6 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
   if (!rc) rc = make_map_3d(&m[2], k, HD, groups, rows, group_stride, row_stride, 64, TK);
   if (!rc) rc = make_map_3d(&m[3], k, HD, groups, rows, group_stride, row_stride, 32, TK, SW64);
   if (!rc) rc = make_map_3d(&m[4], v, HD, groups, rows, group_stride, row_stride, 64, TK);
-  if (!rc) rc = make_map_3d(&m[5], v, HD, groups, rows, group_stride, row_stride, 32, TK, SW64);
   if (rc) return rc;
   static bool configured = false;
   if (!configured) {
@@ -359,7 +347,7 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
   const int pairs = (queries / TQ + 1) / 2;
   AttnParams prm{slots, heads, queries, keys, pairs, kv_mode, lengths, out,
                  (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
-  attention_tc_kernel<<<slots * heads * pairs, kThreads, kSmem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], prm);
+  attention_tc_kernel<<<slots * heads * pairs, kThreads, kSmem, stream>>>(m[0], m[1], m[2], m[3], m[4], prm);
   return launch_status("attention_tc_kernel");
 }
 

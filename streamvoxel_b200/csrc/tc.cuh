@@ -106,6 +106,54 @@ __device__ __forceinline__ void umma_ts_w(uint32_t tmem_d, uint32_t tmem_a, uint
       ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc));
 }
 
+// Batched issue for attention tiles (warp-collective, one elect for the whole batch; descriptors advance by
+// constants, so the issuing warp spends a few instructions per product).
+// S = Q K^T over K = 96: four K-steps in the 128B-swizzled parts (qw, kw), two in the 64B-swizzled parts (qn, kn);
+// each K-step advances the start address by 32 bytes (+2 in descriptor units).
+__device__ __forceinline__ void mma_qk96_w(uint32_t d, uint64_t qw, uint64_t kw, uint64_t qn, uint64_t kn,
+                                           uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 a, b;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, %5, %5;\n\tsetp.eq.b32 pt, %5, %5;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %5, pf;\n\t"
+      "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, pt;\n\t"
+      "add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, pt;\n\t"
+      "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %4, %5, pt;\n\t"
+      "add.s64 a, %3, 2;\n\tadd.s64 b, %4, 2;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, pt;\n\t}"
+      ::"r"(d), "l"(qw), "l"(kw), "l"(qn), "l"(kn), "r"(idesc));
+}
+
+// O += P V over K = 128 keys: A = P in TMEM (8 columns per K-step), B = V MN-major 128B-swizzled (16 keys x 128 B =
+// 2048 bytes per K-step, +128 in descriptor units). `acc` = 0 starts O from the first product.
+__device__ __forceinline__ void mma_pv128_w(uint32_t d, uint32_t a, uint64_t v, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, pt;\n\t.reg .b64 b;\n\t.reg .b32 t;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p0, %4, 0;\n\tsetp.eq.b32 pt, %3, %3;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
+      "add.s32 t, %1, 8;\n\tadd.s64 b, %2, 128;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
+      "add.s32 t, %1, 16;\n\tadd.s64 b, %2, 256;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
+      "add.s32 t, %1, 24;\n\tadd.s64 b, %2, 384;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
+      "add.s32 t, %1, 32;\n\tadd.s64 b, %2, 512;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
+      "add.s32 t, %1, 40;\n\tadd.s64 b, %2, 640;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
+      "add.s32 t, %1, 48;\n\tadd.s64 b, %2, 768;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
+      "add.s32 t, %1, 56;\n\tadd.s64 b, %2, 896;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t}"
+      ::"r"(d), "r"(a), "l"(v), "r"(idesc), "r"(acc));
+}
+
 __device__ __forceinline__ void commit_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
