@@ -69,7 +69,8 @@ struct Operands {
   uint4 res[4];     // residual row slice (GATE_RESIDUAL, RESIDUAL)
 };
 
-template <int EPI>
+// GLOBAL_RES = false: the residual comes from a staging box in shared memory instead.
+template <int EPI, bool GLOBAL_RES = true>
 __device__ __forceinline__ void prefetch32(const EpiParams& ep, int N, int row, int n, Operands& o) {
   const uint4* b = reinterpret_cast<const uint4*>(ep.bias + n);
 #pragma unroll
@@ -79,7 +80,7 @@ __device__ __forceinline__ void prefetch32(const EpiParams& ep, int N, int row, 
 #pragma unroll
     for (int i = 0; i < 4; ++i) o.extra[i] = g[i];
   }
-  if constexpr (EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL) {
+  if constexpr ((EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL) && GLOBAL_RES) {
     const uint4* r = reinterpret_cast<const uint4*>(ep.residual + (int64_t)row * N + n);
 #pragma unroll
     for (int i = 0; i < 4; ++i) o.res[i] = r[i];
@@ -96,11 +97,11 @@ __device__ __forceinline__ void prefetch32(const EpiParams& ep, int N, int row, 
   }
 }
 
-// Epilogue of one row x 32 columns [n, n+32) of the tile; acc holds fp32 accumulators.
+// Epilogue arithmetic of one row x 32 columns [n, n+32) of the tile; acc holds fp32 accumulators, o the bias, gate,
+// RoPE table and residual words of the row.
 template <int EPI>
-__device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, int N, int row, int n,
-                                           const uint32_t (&acc)[32], const Operands& o) {
-  float y[32];
+__device__ __forceinline__ void epilogue_math(const EpiParams& ep, int row, int n, const uint32_t (&acc)[32],
+                                              const Operands& o, float (&y)[32]) {
   const uint32_t* bw = reinterpret_cast<const uint32_t*>(o.bias);
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -143,6 +144,14 @@ __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, i
       }
     }
   }
+}
+
+// Epilogue of one row x 32 columns [n, n+32) of the tile, stored straight to global memory.
+template <int EPI>
+__device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, int N, int row, int n,
+                                           const uint32_t (&acc)[32], const Operands& o) {
+  float y[32];
+  epilogue_math<EPI>(ep, row, n, acc, o, y);
   if constexpr (EPI == SVX_EPI_CLASS_MAJOR) {
     // W rows are ordered n = v * 64 + o, so the 32 columns are one class v and offsets o..o+31 of one patch.
     constexpr int P = 4, P3 = 64;
@@ -291,23 +300,34 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // per product, which leaves one SM's tensor core waiting on shared-memory bandwidth). Stage and accumulator
 // commits arrive on both CTAs' barriers; each CTA's epilogue reads its own 128 TMEM lanes and releases the
 // accumulator on the even CTA's barrier.
+// Epilogue through shared memory: each epilogue warp owns two 32 x 32 staging boxes (64B-swizzled, so a row per
+// thread reads and writes them without bank conflicts). The residual tile of its chunk is TMA-loaded into the box
+// while the main loop still runs; the warp combines it with the accumulator in place and TMA-stores the box, so
+// global memory sees whole lines instead of one 16-byte piece per row and instruction. The class-major head keeps
+// the direct scatter.
 constexpr int PM = 256;
+constexpr uint32_t BOX = 32 * 32 * 2;   // one staging box: 32 rows x 32 bf16
 
 template <int BN, int STAGES, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                      uint16_t* __restrict__ out, int M, int N, int K, const EpiParams ep) {
   constexpr uint32_t HB_BYTES = (BN / 2) * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr bool STAGED = EPI != SVX_EPI_CLASS_MAJOR;
+  constexpr bool RES = EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_s = smem;
   uint8_t* b_s = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(b_s + STAGES * HB_BYTES);
+  uint8_t* stage_s = b_s + STAGES * HB_BYTES;                      // 2 boxes per epilogue warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_s + kEpilogueWarps * 2 * BOX);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* res_full = acc_empty + 2;                              // per epilogue warp and box
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2 * kEpilogueWarps);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = warp_id(), lane = lane_id();
@@ -320,10 +340,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, 2 * kEpilogueWarps); }
+    for (int b = 0; b < 2 * kEpilogueWarps; ++b) mbar_init(res_full + b, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tc::prefetch_map(&tmA);
     tc::prefetch_map(&tmB);
+    if (STAGED) tc::prefetch_map(&tmO);
+    if (RES) tc::prefetch_map(&tmR);
   }
   if (warp == 1) tc::tmem_alloc_pair(tmem_slot, TMEM_COLS);
   tc::fence_before();
@@ -380,32 +403,79 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
-    const int quarter = warp & 3, group = (warp - 4) >> 2;
+    const int quarter = warp & 3, group = (warp - 4) >> 2, ws = warp - 4;
     constexpr int CHUNKS = BN / 32;
+    constexpr int MINE = (CHUNKS + 3) / 4;   // 32-column chunks of this warp per tile: group, group + 4
+    uint8_t* wbox = stage_s + ws * 2 * BOX;
+    // Row `lane` of a 64B-swizzled 32 x 32 box: 16-byte piece q sits at q ^ ((lane / 2) % 4).
+    const int swz = (lane >> 1) & 3;
     int local = 0;
     for (int tile = pair; tile < tiles; tile += pairs, ++local) {
       const int m0 = (tile / n_tiles) * PM + (int)rank * BM, n0 = (tile % n_tiles) * BN;
       const int buf = local & 1, use = local >> 1;
-      const int row = m0 + quarter * 32 + lane;
+      const int row0 = m0 + quarter * 32, row = row0 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN);
+      if constexpr (STAGED) {
+        if (lane == 0) {
+          tc::bulk_wait_read();   // the previous tile's stores have left this warp's boxes
+          if constexpr (RES) {
+#pragma unroll
+            for (int j = 0; j < MINE; ++j) {
+              const int chunk = group + 4 * j;
+              if (chunk < CHUNKS) {
+                mbar_expect_tx(res_full + 2 * ws + j, BOX);
+                tc::tma_load_2d(wbox + j * BOX, &tmR, n0 + chunk * 32, row0, res_full + 2 * ws + j);
+              }
+            }
+          }
+        }
+        __syncwarp();
+      }
       Operands ops;
-      if (group < CHUNKS) prefetch32<EPI>(ep, N, row, n0 + group * 32, ops);
+      if (group < CHUNKS) prefetch32<EPI, !STAGED>(ep, N, row, n0 + group * 32, ops);
       if (!tc::wait(acc_full + buf, use & 1, abort_flag)) { record_timeout(); break; }
       tc::fence_after();
+      bool ok = true;
 #pragma unroll
-      for (int c = 0; c < (CHUNKS + 3) / 4; ++c) {
-        const int chunk = group + 4 * c;
+      for (int j = 0; j < MINE; ++j) {
+        const int chunk = group + 4 * j;
         if (chunk < CHUNKS) {
-          if (c > 0) prefetch32<EPI>(ep, N, row, n0 + chunk * 32, ops);
+          if (j > 0) prefetch32<EPI, !STAGED>(ep, N, row, n0 + chunk * 32, ops);
           uint32_t acc[32];
           tc::ld32(taddr + chunk * 32, acc);
           tc::wait_ld();
-          if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + chunk * 32, acc, ops);
+          if constexpr (STAGED) {
+            uint4* rb = reinterpret_cast<uint4*>(wbox + j * BOX + lane * 64);
+            if constexpr (RES) {
+              if (!tc::wait(res_full + 2 * ws + j, local & 1, abort_flag)) { record_timeout(); ok = false; break; }
+#pragma unroll
+              for (int q = 0; q < 4; ++q) ops.res[q] = rb[q ^ swz];
+            }
+            float y[32];
+            epilogue_math<EPI>(ep, row, n0 + chunk * 32, acc, ops, y);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              rb[q ^ swz] = make_uint4(tc::pack_bf16x2(y[8 * q], y[8 * q + 1]), tc::pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
+                                       tc::pack_bf16x2(y[8 * q + 4], y[8 * q + 5]),
+                                       tc::pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+            tc::fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tc::tma_store_2d(&tmO, n0 + chunk * 32, row0, wbox + j * BOX);
+              tc::bulk_commit();
+            }
+          } else {
+            if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + chunk * 32, acc, ops);
+          }
         }
       }
       tc::fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cluster(acc_empty0 + 8 * buf);
+      if (!ok) break;
+    }
+    if constexpr (STAGED) {
+      if (lane == 0) tc::bulk_wait_all();   // every store of this warp is complete before the CTA ends
     }
     tc::fence_before();
     __syncwarp();
@@ -415,12 +485,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES>
 constexpr size_t pair_smem_bytes() {
-  return 1024 + STAGES * (A_BYTES + (size_t)(BN / 2) * BK * 2) + (2 * STAGES + 4) * 8 + 16;
+  return 1024 + STAGES * (A_BYTES + (size_t)(BN / 2) * BK * 2) + (size_t)kEpilogueWarps * 2 * BOX +
+         (2 * STAGES + 4 + 2 * kEpilogueWarps) * 8 + 16;
 }
 
 template <int BN, int STAGES, int EPI>
-int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, int M, int N, int K,
-                     const EpiParams& ep, cudaStream_t stream) {
+int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const CUtensorMap& r,
+                     uint16_t* out, int M, int N, int K, const EpiParams& ep, cudaStream_t stream) {
   constexpr size_t bytes = pair_smem_bytes<BN, STAGES>();
   static int max_pairs = 0;
   if (!max_pairs) {
@@ -437,7 +508,7 @@ int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, 
   }
   const int tiles = (N / BN) * (M / PM);
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  gemm_pair_kernel<BN, STAGES, EPI><<<2 * pairs, kThreads, bytes, stream>>>(a, b, out, M, N, K, ep);
+  gemm_pair_kernel<BN, STAGES, EPI><<<2 * pairs, kThreads, bytes, stream>>>(a, b, o, r, out, M, N, K, ep);
   return launch_status("gemm_pair_kernel");
 }
 
@@ -465,11 +536,11 @@ int launch_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, int M
 }
 
 template <int EPI>
-int launch_pair_epi(const CUtensorMap& a, const CUtensorMap& b_half, int bn, uint16_t* out, int M, int N, int K,
-                    const EpiParams& ep, cudaStream_t stream) {
+int launch_pair_epi(const CUtensorMap& a, const CUtensorMap& b_half, const CUtensorMap& o, const CUtensorMap& r,
+                    int bn, uint16_t* out, int M, int N, int K, const EpiParams& ep, cudaStream_t stream) {
   switch (bn) {
-    case 256: return launch_pair_tile<256, 6, EPI>(a, b_half, out, M, N, K, ep, stream);
-    case 128: return launch_pair_tile<128, 8, EPI>(a, b_half, out, M, N, K, ep, stream);
+    case 256: return launch_pair_tile<256, 4, EPI>(a, b_half, o, r, out, M, N, K, ep, stream);
+    case 128: return launch_pair_tile<128, 5, EPI>(a, b_half, o, r, out, M, N, K, ep, stream);
     default: return fail(SVX_ERR_INVALID, "gemm: pair tile width must be 128 or 256");
   }
 }
@@ -591,10 +662,37 @@ int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N
   return SVX_OK;
 }
 
+// 2-D bf16 map over a row-major [rows, cols] matrix: 32 x 32 boxes, 64B swizzle (the epilogue staging boxes).
+static int make_box_map(CUtensorMap* map, const void* ptr, int rows, int cols) {
+  EncodeTiled encode = encode_fn();
+  if (!encode) return fail(SVX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  SVX_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && cols % 32 == 0 && rows % 32 == 0,
+              "gemm: epilogue operand must be 16-byte aligned and tile by 32 x 32");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SVX_ERR_CUDA, "cuTensorMapEncodeTiled (box) failed: " + std::to_string((int)r));
+  return SVX_OK;
+}
+
 template <int EPI>
 static int run_epi(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream) {
-  if (plan.pair_bn && M % PM == 0)
-    return launch_pair_epi<EPI>(plan.a, plan.b_half, plan.pair_bn, out, M, plan.N, plan.K, ep, stream);
+  if (plan.pair_bn && M % PM == 0) {
+    CUtensorMap o{}, r{};
+    if (EPI != SVX_EPI_CLASS_MAJOR) {
+      int rc = make_box_map(&o, out, M, plan.N);
+      if (!rc && (EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL)) {
+        SVX_REQUIRE(ep.residual, "gemm: residual epilogue needs a residual");
+        rc = make_box_map(&r, ep.residual, M, plan.N);
+      }
+      if (rc) return rc;
+    }
+    return launch_pair_epi<EPI>(plan.a, plan.b_half, o, r, plan.pair_bn, out, M, plan.N, plan.K, ep, stream);
+  }
   return launch_epi<EPI>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
 }
 
