@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   const int rank = blockIdx.x / per_slot, rem = blockIdx.x % per_slot;
   const int head = rem / p.pairs, q0 = (rem % p.pairs) * 2 * TQ;
   const int nq = min(2, (p.queries - q0) / TQ);
+  grid_launch_dependents();
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -102,6 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     tc::prefetch_map(&mk_wide); tc::prefetch_map(&mk_narrow);
     tc::prefetch_map(&mv);
   }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
+  grid_dependency_wait();   // Q, K, V and the lengths come from earlier kernels
   if (warp == 3) {
     // The slot of this rank in descending key-length order (ties by slot index): a permutation, one lane matches.
     if (p.lengths) {
@@ -118,7 +121,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       *slot_of = rank;
     }
   }
-  if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -347,8 +349,8 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
   const int pairs = (queries / TQ + 1) / 2;
   AttnParams prm{slots, heads, queries, keys, pairs, kv_mode, lengths, out,
                  (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
-  attention_tc_kernel<<<slots * heads * pairs, kThreads, kSmem, stream>>>(m[0], m[1], m[2], m[3], m[4], prm);
-  return launch_status("attention_tc_kernel");
+  return launch_dependent("attention_tc_kernel", attention_tc_kernel, dim3(slots * heads * pairs), dim3(kThreads),
+                          kSmem, stream, m[0], m[1], m[2], m[3], m[4], prm);
 }
 
 uint32_t attention_timeouts() {

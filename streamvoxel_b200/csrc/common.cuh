@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <string>
+#include <utility>
 
 #include "svx.h"
 
@@ -30,6 +31,28 @@ int fail(int status, const std::string& text);
 int launch_status(const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Launch with programmatic stream serialization (the kernel must call grid_dependency_wait before dependent reads).
+template <typename... Exp, typename... Act>
+inline int launch_dependent(const char* what, void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t stream, Act&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(SVX_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+  return launch_status(what);
+}
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
 
@@ -83,6 +106,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (global_timer_ns() - start > kWaitNanoseconds) return false;
   return true;
 }
+
+// Programmatic dependent launch. Kernels of the forward signal grid_launch_dependents() on entry, so the next
+// kernel of the stream (launched with launch_dependent) may be scheduled onto SMs as they free up and run its
+// prologue; every such kernel calls grid_dependency_wait() before its first read of memory an earlier kernel wrote.
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }

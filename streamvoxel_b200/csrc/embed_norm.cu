@@ -41,6 +41,8 @@ __global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int heigh
                                    const uint16_t* __restrict__ table_c, const uint16_t* __restrict__ bias_c,
                                    const uint16_t* __restrict__ add_c, uint16_t* __restrict__ out_c) {
   constexpr int P = 4, P3 = 64;
+  grid_launch_dependents();
+  grid_dependency_wait();
   const int gz = depth / P, gx = width / P;
   const int patches = (height / P) * gz * gx;
   const int row = blockIdx.x;  // slot * patches + p
@@ -79,6 +81,8 @@ template <int PER>
 __global__ void layernorm_modulate_kernel(const uint16_t* __restrict__ x, int rows, int d, float eps,
                                           const uint16_t* __restrict__ ops, const uint16_t* __restrict__ shift,
                                           uint16_t* __restrict__ out) {
+  grid_launch_dependents();
+  grid_dependency_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
   if (row >= rows) return;
   const int lane = lane_id();
@@ -139,25 +143,26 @@ int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int
   const int patches = (height / 4) * (depth / 4) * (width / 4);
   int threads = ((d / 8 + 31) / 32) * 32;
   if (threads < 64) threads = 64;
-  patch_embed_kernel<<<slots * patches, threads, 0, stream>>>(tokens, height, depth, width, classes, d, table_b,
-                                                              bias_b, add_b, out_b, table_c, bias_c, add_c, out_c);
-  return launch_status("patch_embed_kernel");
+  return launch_dependent("patch_embed_kernel", patch_embed_kernel, dim3(slots * patches), dim3(threads), 0, stream,
+                          tokens, height, depth, width, classes, d, table_b, bias_b, add_b, out_b, table_c, bias_c,
+                          add_c, out_c);
 }
 
 int layernorm_run(const uint16_t* x, int rows, int d, float eps, const uint16_t* ops, const uint16_t* shift,
                   uint16_t* out, cudaStream_t stream) {
   const int warps = 8;
   const int grid = (rows + warps - 1) / warps;
+  const dim3 g(grid), b(warps * 32);
+  const char* what = "layernorm_modulate_kernel";
   switch ((d / 8 + 31) / 32) {
-    case 1: layernorm_modulate_kernel<1><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
-    case 2: layernorm_modulate_kernel<2><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
-    case 3: layernorm_modulate_kernel<3><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
-    case 4: layernorm_modulate_kernel<4><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
-    case 5: layernorm_modulate_kernel<5><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
-    case 6: layernorm_modulate_kernel<6><<<grid, warps * 32, 0, stream>>>(x, rows, d, eps, ops, shift, out); break;
+    case 1: return launch_dependent(what, layernorm_modulate_kernel<1>, g, b, 0, stream, x, rows, d, eps, ops, shift, out);
+    case 2: return launch_dependent(what, layernorm_modulate_kernel<2>, g, b, 0, stream, x, rows, d, eps, ops, shift, out);
+    case 3: return launch_dependent(what, layernorm_modulate_kernel<3>, g, b, 0, stream, x, rows, d, eps, ops, shift, out);
+    case 4: return launch_dependent(what, layernorm_modulate_kernel<4>, g, b, 0, stream, x, rows, d, eps, ops, shift, out);
+    case 5: return launch_dependent(what, layernorm_modulate_kernel<5>, g, b, 0, stream, x, rows, d, eps, ops, shift, out);
+    case 6: return launch_dependent(what, layernorm_modulate_kernel<6>, g, b, 0, stream, x, rows, d, eps, ops, shift, out);
     default: return fail(SVX_ERR_INVALID, "layernorm: d must be at most 1536");
   }
-  return launch_status("layernorm_modulate_kernel");
 }
 
 }  // namespace svx

@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   const int kblocks = K / BK;
   const int n_tiles = N / BN;
   const int tiles = (M / BM) * n_tiles;
+  grid_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
@@ -208,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
+  grid_dependency_wait();
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
@@ -336,6 +338,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int kblocks = K / BK;
   const int n_tiles = N / BN;
   const int tiles = (M / PM) * n_tiles;
+  grid_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
@@ -353,6 +356,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::cluster_sync();   // both CTAs' barriers initialised and TMEM allocated before any cross-CTA signal
   tc::fence_after();
+  grid_dependency_wait();   // A and the residual come from the previous kernel
   const uint32_t tmem = *tmem_slot;
   const uint32_t full0 = tc::cluster_addr(full, 0);        // the even CTA's full barriers
   const uint32_t acc_empty0 = tc::cluster_addr(acc_empty, 0);
@@ -508,8 +512,8 @@ int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
   }
   const int tiles = (N / BN) * (M / PM);
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  gemm_pair_kernel<BN, STAGES, EPI><<<2 * pairs, kThreads, bytes, stream>>>(a, b, o, r, out, M, N, K, ep);
-  return launch_status("gemm_pair_kernel");
+  return launch_dependent("gemm_pair_kernel", gemm_pair_kernel<BN, STAGES, EPI>, dim3(2 * pairs), dim3(kThreads),
+                          bytes, stream, a, b, o, r, out, M, N, K, ep);
 }
 
 template <int BN, int STAGES>
@@ -531,8 +535,8 @@ int launch_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, int M
   SVX_CHECK_CUDA(cudaGetDevice(&device));
   SVX_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   const int tiles = (N / BN) * (M / BM);
-  gemm_kernel<BN, STAGES, EPI><<<tiles < sms ? tiles : sms, kThreads, bytes, stream>>>(a, b, out, M, N, K, ep);
-  return launch_status("gemm_kernel");
+  return launch_dependent("gemm_kernel", gemm_kernel<BN, STAGES, EPI>, dim3(tiles < sms ? tiles : sms), dim3(kThreads),
+                          bytes, stream, a, b, out, M, N, K, ep);
 }
 
 template <int EPI>
