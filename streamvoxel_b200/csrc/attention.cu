@@ -10,8 +10,9 @@
 // softmax writes P_i as bf16 pairs over the first 64 columns of S_i, and P_i V takes its A operand from there, so
 // P never touches shared memory (whose bandwidth bounds the small-N products when both operands come from it).
 //
-// Warp roles (384 threads): warp 0 loads Q and the K ring, warp 2 the V ring; warp 1 owns TMEM and issues the
-// products (each loop warp-converged, one elected lane issuing), per query tile i in turn:
+// Warp roles (384 threads): warp 0 loads Q and the K ring, warp 2 the V ring; warp 1 (which owns TMEM) issues the
+// products of query tile 0 and warp 3 those of tile 1, so the two chains never wait on each other's barriers (each
+// loop warp-converged, one elected lane issuing):
 //   O_i += P_i(t) V(t)   M=128, N=96, K=128          (A = P_i in TMEM, V read MN-major)
 //   S_i  = Q_i K(t+1)^T  M=128, N=128, K=96          (issued once P_i(t) V(t) has completed: S_i overwrites P_i)
 // Warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1, one query row per thread (TMEM lane): read the
@@ -90,9 +91,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(k_full + i, 1); mbar_init(k_empty + i, 1);
-      mbar_init(v_full + i, 1); mbar_init(v_empty + i, 1);
+    for (int i = 0; i < STAGES; ++i) {   // a K/V stage is released by the products of every query tile
+      mbar_init(k_full + i, 1); mbar_init(k_empty + i, nq);
+      mbar_init(v_full + i, 1); mbar_init(v_empty + i, nq);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1); mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1);
@@ -157,38 +158,38 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
         tc::tma_load_3d_w(sv + s * VOPER, &mv, 0, kg, kr0 + t * TK, v_full + s);
         tc::tma_load_3d_w(sv + s * VOPER + WIDE, &mv, 64, kg, kr0 + t * TK, v_full + s);
       }
-    } else if (warp == 1 && tiles > 0) {
+    } else if ((warp == 1 || warp == 3) && tiles > 0 && (warp == 1 || nq == 2)) {
+      const int i = warp == 1 ? 0 : 1;
       constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
       constexpr uint32_t idesc_o = tc::instr_desc(TQ, HD, true);
+      const uint32_t qa = smem_addr(sq + i * OPER);
+      const uint32_t s_tmem = tmem + i * 128, o_tmem = tmem + 256 + i * 128;
       bool ok = tc::wait_w(q_full, 0, abort_flag) && tc::wait_w(k_full, 0, abort_flag);
-      // Each query tile runs its own chain  S_i(t) -> softmax_i(t) -> P_i(t) V(t) -> S_i(t+1) -> ...; the two chains
-      // interleave on the tensor core.
+      // This tile's chain  S(t) -> softmax(t) -> P(t) V(t) -> S(t+1) -> ...
       for (int t = 0; ok && t <= tiles; ++t) {
-        const int ks = t % STAGES, vs = (t - 1 + STAGES) % STAGES;
-        const uint32_t kb = smem_addr(sk + ks * OPER), vb = smem_addr(sv + vs * VOPER);
-        for (int i = 0; ok && i < nq; ++i) {
-          if (t >= 1) {
-            const int u = t - 1;
-            if (i == 0) ok = tc::wait_w(v_full + vs, (u / STAGES) & 1, abort_flag);
-            if (ok) ok = tc::wait_w(p_full + i, u & 1, abort_flag);
+        if (t >= 1) {
+          const int u = t - 1, vs = u % STAGES;
+          ok = tc::wait_w(v_full + vs, (u / STAGES) & 1, abort_flag) && tc::wait_w(p_full + i, u & 1, abort_flag);
+          if (!ok) break;
+          tc::fence_after();
+          tc::mma_pv128_w(o_tmem, s_tmem, tc::sw128_desc(smem_addr(sv + vs * VOPER), WIDE, 1024), idesc_o,
+                          u > 0 ? 1u : 0u);
+          tc::commit_w(pv_done + i);
+          tc::commit_w(v_empty + vs);
+        }
+        if (t < tiles) {
+          const int ks = t % STAGES;
+          if (t >= 1) {   // S overwrites P(t-1): wait for its product
+            ok = tc::wait_w(k_full + ks, (t / STAGES) & 1, abort_flag) &&
+                 tc::wait_w(pv_done + i, (t - 1) & 1, abort_flag);
             if (!ok) break;
-            tc::fence_after();
-            tc::mma_pv128_w(tmem + 256 + i * 128, tmem + i * 128, tc::sw128_desc(vb, WIDE, 1024), idesc_o,
-                            u > 0 ? 1u : 0u);
-            tc::commit_w(pv_done + i);
-            if (i == nq - 1) tc::commit_w(v_empty + vs);
           }
-          if (t < tiles) {
-            if (i == 0 && t >= 1) ok = tc::wait_w(k_full + ks, (t / STAGES) & 1, abort_flag);
-            if (ok && t >= 1) ok = tc::wait_w(pv_done + i, (t - 1) & 1, abort_flag);   // P_i(t-1) consumed
-            if (!ok) break;
-            tc::fence_after();
-            const uint32_t qa = smem_addr(sq + i * OPER);
-            tc::mma_qk96_w(tmem + i * 128, tc::sw128_desc(qa), tc::sw128_desc(kb), tc::sw64_desc(qa + WIDE),
-                           tc::sw64_desc(kb + WIDE), idesc_s);
-            tc::commit_w(s_full + i);
-            if (i == nq - 1) tc::commit_w(k_empty + ks);
-          }
+          tc::fence_after();
+          const uint32_t kb = smem_addr(sk + ks * OPER);
+          tc::mma_qk96_w(s_tmem, tc::sw128_desc(qa), tc::sw128_desc(kb), tc::sw64_desc(qa + WIDE),
+                         tc::sw64_desc(kb + WIDE), idesc_s);
+          tc::commit_w(s_full + i);
+          tc::commit_w(k_empty + ks);
         }
       }
     }
