@@ -140,6 +140,10 @@ class SlotBatch:
                 finished.append(i)
         return finished
 
+    def column(self, slot):
+        """The slot's tokens as a host int16 array [Y, Z, X] (a finished window's committed column)."""
+        return self.forward.tokens[slot].cpu().numpy().astype(np.int16, copy=True)
+
     def _finish(self, i):
         """`_finish` (`slot.py:166-176`): deferred voxels take air_token; returns the window record."""
         st = self.state[i]

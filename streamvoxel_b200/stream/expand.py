@@ -1,0 +1,225 @@
+"""World expansion on one or more GPUs: the host driver of BASELINE configs 4/5 (a committed start region grown window
+by window in `pick_window` order around the player).
+
+Multi-GPU without a collective on the data path (`streamvoxel/stream/scheduler.py:37-151`, `session.py:419-500`):
+every rank keeps the same committed snapshot and in-flight set and runs the same deterministic admission, so each
+knows which windows it owns; after every engine step the ranks exchange the columns they finished (128 KiB of int16
+tokens each) and their free slot counts with one host all-gather (a gloo group), apply all commits in rank order and
+admit again. The in-flight windows are pairwise Chebyshev >= 2 apart and condition only on committed columns, so no
+rank ever waits for another's window; a rank's in-flight count is bounded by its `member_shares` share of the batch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import time
+
+import numpy as np
+
+from .scheduler import make_item, member_shares, separated, window_seed
+
+
+class Expansion:
+    """Committed snapshot, in-flight windows and admission of one expansion (one replica per rank)."""
+
+    def __init__(self, committed, biomes, spec, player_zx, region, *, ranks=1, slots=8, cap=32, l2_cap=81, world=0,
+                 cell_size=16, diagonal=False, batch=None):
+        self.committed = {tuple(c): np.asarray(t, np.int16) for c, t in committed.items()}
+        self.biomes, self.spec, self.player = biomes, spec, tuple(float(v) for v in player_zx)
+        self.region = {tuple(c) for c in region}
+        self.ranks, self.cap, self.l2_cap, self.world = int(ranks), int(cap), int(l2_cap), int(world)
+        self.cell_size, self.diagonal = cell_size, diagonal
+        total = self.ranks * int(slots) if batch is None else int(batch)
+        self.share = member_shares(total, [(r, int(slots), 1) for r in range(self.ranks)])
+        self.inflight = {}          # cell -> owning rank
+        self.ready = set()          # uncommitted cells with a committed 8-neighbour, inside the region
+        for c in self.committed:
+            self._touch(c)
+        self.blocked_admissions = 0  # free slots left empty because no admissible cell existed
+
+    def _touch(self, cell):
+        z, x = cell
+        for a in (z - 1, z, z + 1):
+            for b in (x - 1, x, x + 1):
+                if (a, b) not in self.committed and (a, b) in self.region:
+                    self.ready.add((a, b))
+        self.ready.discard(cell)
+
+    @property
+    def done(self):
+        return self.region.issubset(self.committed.keys())
+
+    def pick(self):
+        """`pick_window` restricted to the region, over the incrementally kept ready set (same key and rule)."""
+        pz, px = self.player
+        best_key, best = None, None
+        for cell in self.ready:
+            if cell in self.inflight or not separated(cell, self.inflight, diagonal=self.diagonal):
+                continue
+            z, x = cell
+            key = (((z + .5) * self.cell_size - pz) ** 2 + ((x + .5) * self.cell_size - px) ** 2, z, x)
+            if best_key is None or key < best_key:
+                best_key, best = key, cell
+        return best
+
+    def apply(self, commits):
+        """Commit finished windows [(cell, tokens)] (every rank applies every rank's commits in rank order)."""
+        for cell, tokens in commits:
+            cell = tuple(cell)
+            self.committed[cell] = np.asarray(tokens, np.int16)
+            self.inflight.pop(cell, None)
+            self._touch(cell)
+
+    def admit(self, free):
+        """Windows each rank starts now: round-robin over ranks in order, one admission at a time, each rank up to
+        its free slots and its share. Returns {rank: [cell, ...]} (identical on every replica)."""
+        active = {r: 0 for r in range(self.ranks)}
+        for r in self.inflight.values():
+            active[r] += 1
+        room = {r: max(0, min(int(free[r]), self.share[r] - active[r])) for r in range(self.ranks)}
+        picks = {r: [] for r in range(self.ranks)}
+        while any(room.values()):
+            for r in range(self.ranks):
+                if not room[r]:
+                    continue
+                cell = self.pick()
+                if cell is None:
+                    self.blocked_admissions += sum(room.values())
+                    return picks
+                self.inflight[cell] = r
+                picks[r].append(cell)
+                room[r] -= 1
+        return picks
+
+    def item(self, cell):
+        return make_item(self.committed, cell, self.biomes, self.spec, self.world, self.cap, self.l2_cap)
+
+    def seed(self, cell):
+        return window_seed(self.world, *cell)
+
+    def digest(self):
+        """Order-independent digest of the committed snapshot (replicas must agree)."""
+        import hashlib
+        h = hashlib.sha256()
+        for cell in sorted(self.committed):
+            h.update(np.asarray(cell, np.int64).tobytes())
+            h.update(self.committed[cell].tobytes())
+        return h.hexdigest()
+
+
+def host_exchange(obj, group=None):
+    """All-gather a picklable object over the host group (identity on one rank)."""
+    import torch.distributed as dist
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return [obj]
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, obj, group=group)
+    return out
+
+
+def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000):
+    """Drive `engine` (a `SlotBatch`, or any object with `slots`, `arm`, `step` and `column`) until the region is
+    committed. Returns statistics of this rank."""
+    slot_cell = [None] * engine.slots
+    stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0)
+    for _ in range(max_rounds):
+        finished = []
+        if any(c is not None for c in slot_cell):
+            results = engine.step()
+            stats['forwards'] += 1
+            for i, (record, _commit) in results.items():
+                if record is not None and slot_cell[i] is not None:
+                    tokens = engine.column(i)
+                    finished.append((slot_cell[i], tokens))
+                    stats['windows'] += 1
+                    stats['committed_voxels'] += int(tokens.size)
+                    slot_cell[i] = None
+        t0 = time.perf_counter()
+        free_slots = [i for i, c in enumerate(slot_cell) if c is None]
+        gathered = host_exchange((finished, len(free_slots)), group)
+        for commits, _ in gathered:
+            expansion.apply(commits)
+        picks = expansion.admit([n for _, n in gathered])
+        for cell in picks[rank]:
+            i = free_slots.pop(0)
+            engine.arm(i, expansion.seed(cell), expansion.cap, item=expansion.item(cell), target=cell)
+            slot_cell[i] = cell
+        stats['admission_seconds'] += time.perf_counter() - t0
+        stats['rounds'] += 1
+        if expansion.done:
+            break
+        if not expansion.inflight:
+            raise RuntimeError('expansion blocked: no window in flight and none admissible')
+    stats['blocked_admissions'] = expansion.blocked_admissions
+    return stats
+
+
+def start_region(seed, side0, side1, spec, classes=None):
+    """A side0 x side0 committed square from the synthetic world generator, centred in the side1 x side1 target
+    region (configs 4/5: 32 -> 64 and 32 -> 128), the biome labels and the player at the centre."""
+    from streamvoxel_b200 import synth
+    cols = synth.world(seed, side1, side1, height=spec.height, tile=spec.tile)
+    if classes is not None:
+        cols = {c: synth.clip_classes(t, classes) for c, t in cols.items()}
+    lo = (side1 - side0) // 2
+    committed = {c: t for c, t in cols.items() if lo <= c[0] < lo + side0 and lo <= c[1] < lo + side0}
+    region = set(cols)
+    rng = np.random.default_rng(seed + 1)
+    biomes = rng.integers(0, 16, (spec.height // 4, 66, 66)).astype(np.int64)
+    player = (side1 * spec.tile / 2.0, side1 * spec.tile / 2.0)
+    return committed, region, biomes, player
+
+
+def main():
+    """python -m streamvoxel_b200.stream.expand [--side0 8 --side1 16] (torchrun for several GPUs): one expansion
+    through the real engine; prints one JSON line with committed voxels/s and the admission statistics."""
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    from streamvoxel_b200 import model as sm
+    from streamvoxel_b200.stream.batch import SlotBatch
+    from streamvoxel_b200.stream.condition import ModelSpec
+    from streamvoxel_b200.stream.fast_ops import FastSlotForward
+
+    parser = argparse.ArgumentParser()
+    parser.add_argument('--side0', type=int, default=8)
+    parser.add_argument('--side1', type=int, default=16)
+    parser.add_argument('--slots', type=int, default=8)
+    parser.add_argument('--small', action='store_true', help='the small test model instead of DiT-B/4 + ControlNet')
+    args = parser.parse_args()
+    world_size = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    group = None
+    if world_size > 1:
+        dist.init_process_group('gloo', init_method='env://')
+        group = dist.group.WORLD
+    cfg = sm.small_test_config() if args.small else sm.dit_b4_control()
+    sd = sm.synthetic_state_dict(cfg, seed=0)
+    spec = ModelSpec.of(cfg)
+    forward = FastSlotForward((cfg, sd), spec, f'cuda:{local}', args.slots, 8, 81)
+    engine = SlotBatch(forward)
+    committed, region, biomes, player = start_region(11, args.side0, args.side1, spec, classes=cfg.classes)
+    exp = Expansion(committed, biomes, spec, player, region, ranks=world_size, slots=args.slots, l2_cap=81)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    stats = run(engine, exp, rank, group=group)
+    torch.cuda.synchronize()
+    seconds = time.perf_counter() - t0
+    totals = host_exchange((stats['committed_voxels'], seconds, exp.digest()), group)
+    if rank == 0:
+        voxels = sum(t[0] for t in totals)
+        wall = max(t[1] for t in totals)
+        print(json.dumps(dict(workload=f'expansion {args.side0}^2 -> {args.side1}^2', ranks=world_size,
+                              committed_voxels=voxels, seconds=wall, voxels_per_s=voxels / wall,
+                              windows=len(region) - len(committed), replicas_agree=len({t[2] for t in totals}) == 1,
+                              rank0=stats)))
+    if world_size > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -236,18 +236,83 @@ def model_cases():
     _save('control_tiny.npz', **out)
 
 
+# ---------------------------------------------------------------------------------------------- window admission
+
+def _blob(rng, n):
+    """A connected committed region: a random walk of n steps from (0, 0)."""
+    cells, z, x = set(), 0, 0
+    for _ in range(n):
+        cells.add((z, x))
+        dz, dx = ((1, 0), (-1, 0), (0, 1), (0, -1))[int(rng.integers(0, 4))]
+        z, x = z + dz, x + dx
+    return cells
+
+
+def scheduler_cases():
+    """The reference scheduler on seeded cases: pick_window, member_shares, window seeds and make_item."""
+    from streamvoxel.stream.condition import ModelSpec
+    from streamvoxel.stream.scheduler import make_item, member_shares, pick_window, seed
+    rng = np.random.default_rng(41)
+    out = {}
+    for i in range(80):
+        committed = _blob(rng, int(rng.integers(1, 48)))
+        inflight, diagonal = set(), bool(i % 3 == 0)
+        for _ in range(int(rng.integers(0, 7))):
+            c = pick_window(committed, inflight, tuple(float(v) for v in rng.uniform(-90, 90, 2)), diagonal=diagonal)
+            if c is None:
+                break
+            inflight.add(c)
+        player = rng.uniform(-120, 120, 2)
+        got = pick_window(committed, inflight, (float(player[0]), float(player[1])), diagonal=diagonal)
+        out[f'p{i}_committed'] = np.asarray(sorted(committed), np.int64).reshape(-1, 2)
+        out[f'p{i}_inflight'] = np.asarray(sorted(inflight), np.int64).reshape(-1, 2)
+        out[f'p{i}_player'] = player
+        out[f'p{i}_diagonal'] = diagonal
+        out[f'p{i}_pick'] = np.asarray(got if got is not None else (-(2 ** 40), -(2 ** 40)), np.int64)
+    for i in range(60):
+        k = int(rng.integers(0, 6))
+        wids = sorted(int(w) for w in rng.choice(12, k, replace=False))
+        members = [(w, int(rng.integers(1, 17)), int(rng.integers(1, 17))) for w in wids]
+        batch = int(rng.integers(0, sum(c for _, c, _ in members) + 4))
+        shares = member_shares(batch, members)
+        out[f'm{i}_members'] = np.asarray(members, np.int64).reshape(-1, 3)
+        out[f'm{i}_batch'] = batch
+        out[f'm{i}_shares'] = np.asarray([shares[w] for w, _, _ in members], np.int64)
+    cells = [(int(a), int(b)) for a, b in rng.integers(-5000, 5000, (64, 2))]
+    out['seed_cells'] = np.asarray(cells, np.int64)
+    out['seed_values'] = np.asarray([seed(7, a, b) for a, b in cells], np.uint64)
+    spec = ModelSpec(height=64, tile=16, num_classes=32, biome_classes=16, biome_halo=4, y_origin=-64.0)
+    biomes = rng.integers(0, 16, (16, 66, 66)).astype(np.int64)
+    for i in range(6):
+        committed = _blob(rng, int(rng.integers(3, 30)))
+        cells = {c: rng.integers(0, 33, (64, 16, 16)).astype(np.int16) for c in sorted(committed)}
+        target = sorted(set((a + da, b + db) for a, b in committed for da in (-1, 0, 1) for db in (-1, 0, 1))
+                        - committed)[int(rng.integers(0, 4))]
+        item = make_item(cells, target, biomes, spec, 7, 32, 5)
+        out[f'i{i}_cells'] = np.asarray(sorted(cells), np.int64)
+        out[f'i{i}_tiles'] = np.stack([cells[c] for c in sorted(cells)])
+        out[f'i{i}_target'] = np.asarray(target, np.int64)
+        for name in ('l1_blocks', 'l1_xz', 'l2_blocks', 'l2_xz', 'biomes'):
+            out[f'i{i}_{name}'] = getattr(item, name)
+        out[f'i{i}_seed'] = np.uint64(item.seed)
+    out['biomes'] = biomes
+    _save('scheduler.npz', **out)
+
+
+CASES = dict(quota=lambda: quota_cases(), top_mask=lambda: top_mask_cases(), schedule=lambda: schedule_cases(),
+             scores=lambda: score_cases(), slots=lambda: slot_cases(), models=lambda: model_cases(),
+             scheduler=lambda: scheduler_cases())
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument('--reference', required=True)
+    parser.add_argument('--only', nargs='*', choices=sorted(CASES), help='regenerate only these fixture groups')
     args = parser.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    quota_cases()
-    top_mask_cases()
-    schedule_cases()
-    score_cases()
-    slot_cases()
-    model_cases()
+    for name in (args.only or CASES):
+        CASES[name]()
 
 
 if __name__ == '__main__':
