@@ -119,7 +119,9 @@ def build(device, seed=0):
 
 def run_device_steps(batch, steps, seeds):
     """Exactly `steps` forwards, device-resident inside each window (see `SlotBatch.run_cycles`). Returns
-    (committed voxels, kernel launches, marking forwards)."""
+    (committed voxels, kernel launches, marking forwards). Each forward of a window is credited with an equal share of
+    the window's voxels (its column commits them all: solid steps plus the deferred low-entropy-last voxels at finish):
+    exact for whole windows, and the steady-state rate when the timed region ends inside a window."""
     from streamvoxel_b200.stream.batch import EASE_LAUNCHES
     committed = launches = markings = 0
     per_step = batch.launches()
@@ -136,11 +138,10 @@ def run_device_steps(batch, steps, seeds):
         launches += per_step + 2 * batch.slots
         markings += 1
         done += 1
-        staged, ks = [], []
+        staged = []
         while done + len(staged) < steps and any(st['solid_calls'] < len(st['quotas']) for st in batch.state):
             rows = batch._rows()
             staged.append(batch._pack(rows))
-            ks.append(sum(r[0] for r in rows))
             for st in batch.state:
                 if st['solid_calls'] < len(st['quotas']):
                     st['solid_calls'] += 1
@@ -152,16 +153,17 @@ def run_device_steps(batch, steps, seeds):
                 batch.graph.replay()
             launches += len(staged) * per_step
             done += len(staged)
-            committed += sum(ks)
+        for st in batch.state:   # the forwards each window ran in this cycle (marking + solid steps)
+            committed += batch.total * (1 + st['solid_calls']) / (1 + len(st['quotas']))
         if all(st['solid_calls'] >= len(st['quotas']) for st in batch.state):
             for i in range(batch.slots):
                 batch._finish(i)
-                committed += counts[i]   # deferred voxels are committed at finish
     return committed, launches, markings
 
 
 def run_api_steps(batch, steps, seeds):
-    """Exactly `steps` forwards through `SlotBatch.step` (per-step H2D scalars, D2H commits, host bookkeeping)."""
+    """Exactly `steps` forwards through `SlotBatch.step` (per-step H2D scalars, D2H commits, host bookkeeping); the
+    same per-forward share of each window's voxels as `run_device_steps`."""
     committed = h2d = d2h = 0
     it = iter(seeds)
     for i in range(batch.slots):
@@ -174,11 +176,12 @@ def run_api_steps(batch, steps, seeds):
         d2h += (2 * batch.slots) * 4 + (batch.slots * kmax * (4 + 2) if kmax else 0)
         results = batch.step()
         for i, (record, commit) in results.items():
-            if commit is not None:
-                committed += len(commit['positions'])
             if record is not None:
-                committed += record['last_count']
+                committed += batch.total   # a finished window committed its whole column
                 batch.arm(i, next(it), CAP)
+    for st in batch.state:   # windows still running: their share for the forwards they had
+        if st['phase'] == 'solid' and st['quotas']:
+            committed += batch.total * st['nfe'] / (1 + len(st['quotas']))
     return committed, h2d, d2h
 
 
@@ -373,6 +376,8 @@ def main_ours(args):
         dtype='bf16', data='synthetic (seeded world generator, random-init N(0,0.02) weights)',
         config=dict(workload=WORKLOAD, slots_per_gpu=SLOTS, cap=CAP, l1_cap=L1_CAP, l2_cap=L2_CAP,
                     mean_packed_keys=float(np.mean(lengths)), sampler='EASE native Philox draw',
+                    committed_accounting=('each forward of a window credited with an equal share of the window\'s '
+                                          '65536 voxels (exact for whole windows; steady-state rate otherwise)'),
                     l2_policy='inputs larger than L2 (268 MB logits + 0.86 GB weights per step)',
                     parallelism=f'{world} independent engines, no collective'),
         forwards_per_s=steps_per_s * world, marking_forwards=markings,
@@ -414,7 +419,13 @@ def main():
     if args.impl == 'reference':
         main_reference(args)
     else:
-        main_ours(args)
+        try:
+            main_ours(args)
+        finally:
+            import torch.distributed as dist
+            if dist.is_available() and dist.is_initialized():
+                dist.barrier()
+                dist.destroy_process_group()
 
 
 if __name__ == '__main__':
