@@ -316,7 +316,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                      uint16_t* __restrict__ out, int M, int N, int K, const EpiParams ep) {
   constexpr uint32_t HB_BYTES = (BN / 2) * BK * 2;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;   // allocations are powers of two
   constexpr bool STAGED = EPI != SVX_EPI_CLASS_MAJOR;
   constexpr bool RES = EPI == SVX_EPI_GATE_RESIDUAL || EPI == SVX_EPI_RESIDUAL;
   extern __shared__ uint8_t smem_raw[];
@@ -544,8 +544,9 @@ int launch_pair_epi(const CUtensorMap& a, const CUtensorMap& b_half, const CUten
                     int bn, uint16_t* out, int M, int N, int K, const EpiParams& ep, cudaStream_t stream) {
   switch (bn) {
     case 256: return launch_pair_tile<256, 4, EPI>(a, b_half, o, r, out, M, N, K, ep, stream);
+    case 192: return launch_pair_tile<192, 5, EPI>(a, b_half, o, r, out, M, N, K, ep, stream);
     case 128: return launch_pair_tile<128, 5, EPI>(a, b_half, o, r, out, M, N, K, ep, stream);
-    default: return fail(SVX_ERR_INVALID, "gemm: pair tile width must be 128 or 256");
+    default: return fail(SVX_ERR_INVALID, "gemm: pair tile width must be 128, 192 or 256");
   }
 }
 
@@ -632,8 +633,10 @@ static int pick_bn(int M, int N) {
   return best;
 }
 
-// Tile width for CTA pairs (256-row tiles, 74 pairs on 148 SMs): a CTA streams its 128 A rows and BN/2 W rows per
-// tile, so a tile costs (128 + BN/2) rows of traffic per SM; the wider tile on ties.
+// Tile width for CTA pairs (256-row tiles, 74 pairs on 148 SMs). A tile's main loop is bound by its products, which
+// scale with BN, plus a per-tile cost of about 32 columns' worth (epilogue tail, accumulator hand-off): the cost of a
+// width is (rounds of tiles over the pairs) x (BN + 32); the wider tile on ties. Measured on B200 at M = 8192:
+// BN = 128 never beat 256; 192 fills the pairs better when N is 768 or 3072.
 static int pick_pair_bn(int M, int N) {
   int sms = 148;
   int device = 0;
@@ -641,10 +644,10 @@ static int pick_pair_bn(int M, int N) {
   const int pairs = sms / 2;
   int best = 0;
   long best_cost = 0;
-  for (int bn : {256, 128}) {
+  for (int bn : {256, 192, 128}) {
     if (N % bn) continue;
     const long tiles = (long)(N / bn) * (M / PM);
-    const long cost = ((tiles + pairs - 1) / pairs) * (128 + bn / 2);
+    const long cost = ((tiles + pairs - 1) / pairs) * (bn + 32);
     if (!best || cost < best_cost) { best = bn; best_cost = cost; }
   }
   return best;
