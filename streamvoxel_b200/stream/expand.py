@@ -107,6 +107,16 @@ class Expansion:
         return h.hexdigest()
 
 
+def _publish(publisher, record, cell, tokens, slot, rank, world, raw_map):
+    from . import wire
+    record = dict(record, target=cell)
+    ids = raw_map if raw_map is not None else np.arange(int(tokens.max()) + 1, dtype=np.uint16)
+    row = wire.frame_row(wire.whole_cell_commit(cell, tokens, record['nfe']), ids, slot, rank)
+    if row is not None:
+        publisher.publish('frame', gpu=rank, world=world, frames=[row])
+    publisher.publish('window_commit', **wire.window_commit_fields(record, rank, slot, world))
+
+
 def host_exchange(obj, group=None):
     """All-gather a picklable object over the host group (identity on one rank)."""
     import torch.distributed as dist
@@ -117,9 +127,11 @@ def host_exchange(obj, group=None):
     return out
 
 
-def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000):
+def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=None, raw_map=None):
     """Drive `engine` (a `SlotBatch`, or any object with `slots`, `arm`, `step` and `column`) until the region is
-    committed. Returns statistics of this rank."""
+    committed. Returns statistics of this rank. With a `publisher` (`wire.Publisher`), every window this rank
+    finishes is published as a frame packet carrying its whole cell (global ids through `raw_map`) followed by its
+    `window_commit` packet, as the reference's worker does without progressive frames."""
     slot_cell = [None] * engine.slots
     stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0)
     for _ in range(max_rounds):
@@ -131,6 +143,8 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000):
                 if record is not None and slot_cell[i] is not None:
                     tokens = engine.column(i)
                     finished.append((slot_cell[i], tokens))
+                    if publisher is not None:
+                        _publish(publisher, record, slot_cell[i], tokens, i, rank, expansion.ranks, raw_map)
                     stats['windows'] += 1
                     stats['committed_voxels'] += int(tokens.size)
                     slot_cell[i] = None

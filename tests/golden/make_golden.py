@@ -299,9 +299,52 @@ def scheduler_cases():
     _save('scheduler.npz', **out)
 
 
+# ---------------------------------------------------------------------------------------------- commit wire format
+
+def wire_cases():
+    """Frame rows, merged commits, packet hashes and batch lines made by the reference's live protocol code."""
+    import json
+    from streamvoxel.common.live_rows import pack_row, unpack_row
+    from streamvoxel.common.live_wire import batch_line, packet_sha
+    from streamvoxel.stream.worker import _merge_commits
+    rng = np.random.default_rng(53)
+    out, rows = {}, []
+    for i in range(12):
+        n = int(rng.integers(0, 3000)) if i else 0
+        positions = rng.choice(65536, n, replace=False).astype(np.int32)
+        raw = rng.integers(0, 981, n).astype(np.uint16)
+        raw[rng.random(n) < 0.3] = 0
+        row = pack_row((int(rng.integers(-50, 50)), int(rng.integers(-50, 50))), positions, raw)
+        out[f'r{i}_positions'], out[f'r{i}_raw'] = positions, raw
+        out[f'r{i}_row'] = np.array(json.dumps(row, sort_keys=True))
+        pos, val = unpack_row(row)
+        out[f'r{i}_unpacked_pos'], out[f'r{i}_unpacked_val'] = pos, val
+        rows.append(row)
+    for i in range(6):
+        commits = []
+        for step in range(int(rng.integers(1, 4))):
+            n = int(rng.integers(1, 500))
+            commits.append(dict(positions=rng.integers(0, 2048, n).astype(np.int32),
+                                values=rng.integers(0, 256, n).astype(np.int16), step=step + 1, target=(3, -4)))
+        merged = _merge_commits(commits)
+        for j, c in enumerate(commits):
+            out[f'm{i}_c{j}_positions'], out[f'm{i}_c{j}_values'] = c['positions'], c['values']
+        out[f'm{i}_count'] = len(commits)
+        out[f'm{i}_positions'], out[f'm{i}_values'] = merged['positions'], merged['values']
+    packets = []
+    for seq in range(5):
+        packet = dict(seq=seq, kind='frame' if seq % 2 else 'window_commit', forward=seq * 7, gpu=seq % 2,
+                      frames=rows[seq:seq + 2] if seq % 2 else [], target=[seq, -seq], nfe=33, last_frac=0.25)
+        packet['sha256'] = packet_sha(packet)
+        packets.append(packet)
+    out['packets'] = np.array(json.dumps(packets))
+    out['batch'] = np.array(json.dumps(batch_line(packets), sort_keys=True))
+    _save('wire.npz', **out)
+
+
 CASES = dict(quota=lambda: quota_cases(), top_mask=lambda: top_mask_cases(), schedule=lambda: schedule_cases(),
              scores=lambda: score_cases(), slots=lambda: slot_cases(), models=lambda: model_cases(),
-             scheduler=lambda: scheduler_cases())
+             scheduler=lambda: scheduler_cases(), wire=lambda: wire_cases())
 
 
 def main():

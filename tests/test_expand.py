@@ -31,7 +31,8 @@ class FakeEngine:
         for i in range(self.slots):
             if self.left[i]:
                 self.left[i] -= 1
-                out[i] = (dict(target=self.targets[i]) if self.left[i] == 0 else None, None)
+                done = dict(target=self.targets[i], nfe=self.steps, last_frac=0.0, cap=32, actual=self.steps)
+                out[i] = (done if self.left[i] == 0 else None, None)
         return out
 
     def column(self, i):
@@ -107,3 +108,25 @@ def test_two_gloo_ranks_keep_identical_replicas():
     assert rows[0][0] == rows[1][0] == single.digest()       # same world as one rank: columns depend on seeds only
     assert int(rows[0][1]) + int(rows[1][1]) == 100 - 16     # every window ran on exactly one rank
     assert int(rows[0][1]) > 0 and int(rows[1][1]) > 0
+
+
+def test_published_packets_rebuild_the_committed_columns():
+    from streamvoxel_b200.stream import wire
+    exp = _setup(1, 4)
+    pub = wire.Publisher()
+    raw_map = np.arange(32, dtype=np.uint16) + 100   # compact id -> global id (air stays 0 only if mapped to 0)
+    raw_map[0] = 0
+    expand.run(FakeEngine(4), exp, 0, publisher=pub, raw_map=raw_map)
+    commits = [p for p in pub.packets if p['kind'] == 'window_commit']
+    assert len(commits) == 100 - 16
+    for seq, packet in enumerate(pub.packets):
+        wire.verify_packet(packet, seq)
+    for packet in pub.packets:
+        if packet['kind'] != 'frame':
+            continue
+        row = packet['frames'][0]
+        pos, ids = wire.unpack_row(row)
+        flat = raw_map[exp.committed[tuple(row['target'])].reshape(-1)]
+        np.testing.assert_array_equal(pos, np.flatnonzero(flat))
+        np.testing.assert_array_equal(ids, flat[flat != 0])
+    assert wire.unbatch(wire.batch_line(pub.packets[:10])) == pub.packets[:10]
