@@ -209,6 +209,8 @@ class PreparedModel:
         if cfg.layer_indices:
             self.table_l1, self.bias_l1 = self._table('l1_patch')
             self.table_l2, self.bias_l2 = self._table('l2_patch')
+        self.kv_weight = [_bf16(sd[f'cross.{j}.key_value.weight'], dev) for j in range(len(cfg.layer_indices))]
+        self.kv_bias = [_bf16(sd[f'cross.{j}.key_value.bias'], dev) for j in range(len(cfg.layer_indices))]
 
     # -- constants
     def _ada(self, prefix, time_key, count):
@@ -235,33 +237,52 @@ class PreparedModel:
 
     # -- per-window condition encoder (runs once per window, on the caller's stream)
     @torch.no_grad()
-    def encode_item(self, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes):
+    def encode_item(self, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes, l2_keys=None, cache=None):
         """Packed per-layer cross K/V of one window: `FastSlotForward.encode` (`streamvoxel/stream/fast_ops.py:228-239`)
         = `encode_item` (`streamvoxel/stream/engine.py:75-84`) -> `encode_group` / `prefix_kv` / `local_condition`
         (`streamvoxel/models/streaming_controlnet.py:160-219`) -> `local_kv` (`fast_ops.py:90-95`).
-        Returns [(k, v)] per control layer, each [heads, L, 96] bf16 (RoPE on k), prefix keys first."""
+        Returns [(k, v)] per control layer, each [heads, L, 96] bf16 (RoPE on k), prefix keys first.
+        With `l2_keys` (one hashable key per L2 column) and a `cache` (an `L2TokenCache`), each L2 column's encoded
+        tokens (LayerNorm of its 16 down-sampled tokens, bf16) are computed once and reused: they depend on the
+        column alone, its position enters through the RoPE of the keys only."""
         cfg, dev, sd = self.cfg, self.device, self.sd
         height, tile = cfg.voxel_shape[0], cfg.voxel_shape[1]
         pos1, pos2, bio_pos = _group_positions(l1_xz, l2_xz, height, tile, dev)
         with torch.autocast('cuda', dtype=torch.bfloat16):
-            l2 = self._encode_columns(np.asarray(l2_blocks), 1).flatten(0, 1)
-            prefix = F.layer_norm(l2.float(), (cfg.d,), eps=1e-6)
+            if l2_keys and cache is not None:
+                prefix = cache.tokens(l2_keys, l2_blocks, self._l2_prefix)
+            else:
+                prefix = self._l2_prefix(np.asarray(l2_blocks))
             l1 = F.layer_norm(self._encode_columns(np.asarray(l1_blocks), 0).float(), (cfg.d,), eps=1e-6)
             bio, bio_positions = self._biome(torch.as_tensor(np.asarray(biomes), device=dev).long(), bio_pos)
             local = torch.cat((l1.flatten(0, 1), bio), 0)
             local_positions = torch.cat((pos1.reshape(-1, 3), bio_positions), 0)
-            layers = []
-            freq = rope_frequencies(96).to(dev)
-            for j in range(len(cfg.layer_indices)):
-                w, b = sd[f'cross.{j}.key_value.weight'], sd[f'cross.{j}.key_value.bias']
-                ks, vs = [], []
-                for value, positions in ((prefix, pos2), (local, local_positions)):
-                    k, v = F.linear(value, w, b).reshape(len(value), 2, cfg.heads, 96).unbind(1)
-                    k, v = k.transpose(0, 1), v.transpose(0, 1)
-                    ks.append(_rope(k, positions, freq))
-                    vs.append(v)
-                layers.append((torch.cat(ks, 1).to(torch.bfloat16), torch.cat(vs, 1).to(torch.bfloat16)))
+        # Every layer's key_value linear over all condition tokens at once (prefix rows, then local rows): the bf16
+        # input autocast would cast, one tcgen05 GEMM per layer with the bias and the axial RoPE of the K half fused
+        # in its epilogue (the same bf16 rounding points as `F.linear` then `AxialRoPE`), tables built once.
+        tokens = torch.cat((prefix.to(torch.bfloat16), local.float().to(torch.bfloat16)), 0)
+        positions = torch.cat((pos2, local_positions.float()), 0)
+        n = len(tokens)
+        rows = -(-n // 256) * 256
+        padded = torch.zeros((rows, cfg.d), device=dev, dtype=torch.bfloat16)
+        padded[:n] = tokens
+        phase = (positions.float()[..., None] * rope_frequencies(96).to(dev)).reshape(n, 48)
+        sin = torch.zeros((rows, 48), device=dev, dtype=torch.bfloat16)
+        cos = torch.zeros((rows, 48), device=dev, dtype=torch.bfloat16)
+        sin[:n], cos[:n] = phase.sin().to(torch.bfloat16), phase.cos().to(torch.bfloat16)
+        layers = []
+        for j in range(len(cfg.layer_indices)):
+            out = ops.gemm(padded, self.kv_weight[j], self.kv_bias[j], _lib.EPI_ROPE, rope=(sin, cos),
+                           rope_cols=cfg.d, rows_per_slot=rows)
+            kv = out[:n].view(n, 2, cfg.heads, 96)
+            layers.append((kv[:, 0].transpose(0, 1), kv[:, 1].transpose(0, 1)))
         return layers
+
+    def _l2_prefix(self, blocks):
+        """Encoded prefix tokens of L2 columns [n, H, T, T] -> [n * 16, d] bf16 (the cast the key_value linear makes)."""
+        with torch.autocast('cuda', dtype=torch.bfloat16):
+            l2 = self._encode_columns(blocks, 1).flatten(0, 1)
+            return F.layer_norm(l2.float(), (self.cfg.d,), eps=1e-6).to(torch.bfloat16)
 
     def _encode_columns(self, tokens, level):
         """`_encode_columns` (`streaming_controlnet.py:142-158`): one-hot conv patchify (the gather kernel), for L2 then
@@ -312,6 +333,32 @@ class PreparedModel:
         size = sd['biome_size8'] if cfg.biome_patch == 2 else sd['size_embed.weight'][int(cfg.biome_patch == 4)]
         values = values + sd['type_embed.weight'][2] + size
         return F.layer_norm(values.float(), (cfg.d,), eps=1e-6), positions
+
+
+class L2TokenCache:
+    """Encoded L2 tokens per committed column (LRU, at most `capacity` columns; 24 KB each at d = 768)."""
+
+    def __init__(self, capacity=32768):
+        from collections import OrderedDict
+        self.capacity, self.entries = int(capacity), OrderedDict()
+        self.hits = self.misses = 0
+
+    def tokens(self, keys, blocks, encode):
+        missing = [i for i, key in enumerate(keys) if key not in self.entries]
+        self.hits += len(keys) - len(missing)
+        self.misses += len(missing)
+        if missing:
+            fresh = encode(np.asarray(blocks)[missing])
+            per = len(fresh) // len(missing)
+            for n, i in enumerate(missing):
+                self.entries[keys[i]] = fresh[n * per:(n + 1) * per]
+        rows = []
+        for key in keys:
+            self.entries.move_to_end(key)
+            rows.append(self.entries[key])
+        while len(self.entries) > self.capacity:
+            self.entries.popitem(last=False)
+        return torch.cat(rows, 0)
 
 
 def _rope(x, positions, freq):

@@ -46,6 +46,9 @@ class Item:
     biomes: np.ndarray       # [H/4,12,12] int64, zero padded outside the supplied window
     known: np.ndarray | None = None
     warnings: list = field(default_factory=list)
+    # Absolute (world, z, x) keys of the L2 columns, when the item was built from a committed snapshot: committed
+    # columns never change, so the engine may reuse their encoded tokens across windows (None: encode every time).
+    l2_keys: list | None = None
 
 
 def probe_item(spec):

@@ -52,6 +52,7 @@ class FastSlotForward:
             cfg, state_dict = model
             model = PreparedModel(cfg, state_dict, self.device)
         self.model, self.spec = model, spec
+        self.l2_cache = None   # created on the first item that names its L2 columns (`Item.l2_keys`)
         cfg = model.cfg
         self.cfg = cfg
         self.batch, self.l1_cap, self.l2_cap = int(batch), int(l1_cap), int(l2_cap)
@@ -85,7 +86,12 @@ class FastSlotForward:
     # -- conditions
     def encode(self, item):
         """Per-layer packed (K, V) [H, P+L, 96] of one item (`fast_ops.py:228-239`)."""
-        layers = self.model.encode_item(item.l1_blocks, item.l1_xz, item.l2_blocks, item.l2_xz, item.biomes)
+        keys = getattr(item, 'l2_keys', None)
+        if keys is not None and self.l2_cache is None:
+            from streamvoxel_b200.model import L2TokenCache
+            self.l2_cache = L2TokenCache()
+        layers = self.model.encode_item(item.l1_blocks, item.l1_xz, item.l2_blocks, item.l2_xz, item.biomes,
+                                        l2_keys=keys, cache=self.l2_cache)
         prefix = len(np.asarray(item.l2_blocks)) * self.l2_tokens
         if prefix > self.prefix_len or layers[0][0].shape[1] - prefix > self.local_len:
             raise ValueError('Condition exceeds the slot capacity')

@@ -147,4 +147,4 @@ def make_item(cells, target, biomes, spec, world, cap, l2_cap):
         raise ValueError('Condition tile has the wrong shape')
     return Item(id=f'{z}_{x}', seed=window_seed(world, z, x), steps=int(cap), temperature=1.0,
                 l1_blocks=l1, l1_xz=_relative_xz(near, z, x), l2_blocks=l2, l2_xz=_relative_xz(far, z, x),
-                biomes=biome_volume(biomes, z, x, spec), known=None)
+                biomes=biome_volume(biomes, z, x, spec), known=None, l2_keys=[(world,) + c for c in far])
