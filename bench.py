@@ -135,7 +135,7 @@ def run_device_steps(batch, steps, seeds):
         batch._mark(range(batch.slots))
         counts = batch.last_count.tolist()
         batch._after_mark(range(batch.slots), counts)
-        launches += per_step + 2 * batch.slots
+        launches += per_step + 2   # one marking launch (all slots) and its column-run launch
         markings += 1
         done += 1
         staged = []

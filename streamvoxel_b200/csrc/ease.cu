@@ -4,26 +4,30 @@
 // so a warp reading one class for 32 x VPT consecutive voxels issues fully coalesced 16-byte loads.
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace svx {
 namespace {
 
 constexpr int kScoreThreads = 256;
+// Entropy and marking kernels: 4 voxels per lane, 2 lanes per voxel group, 8 class rows in flight per lane (the best
+// of the shapes measured on B200; more rows per lane or wider loads lower the occupancy more than they add).
+constexpr int kStatVoxels = 4, kStatSplit = 2, kStatRows = 8;
 constexpr int kSelectThreads = 1024;
 
 // ----------------------------------------------------------------------------------------------- scores
 
 template <typename T, int VPT> struct Vec;
-template <> struct Vec<uint16_t, 8> {
-  static __device__ __forceinline__ void load(const uint16_t* p, float (&x)[8]) {
-    uint4 raw = *reinterpret_cast<const uint4*>(p);
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[2 * i] = __uint_as_float(w[i] << 16);
-      x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-    }
+template <> struct Vec<uint16_t, 4> {
+  static __device__ __forceinline__ void load(const uint16_t* p, float (&x)[4]) {
+    uint2 raw = *reinterpret_cast<const uint2*>(p);
+    x[0] = __uint_as_float(raw.x << 16);
+    x[1] = __uint_as_float(raw.x & 0xFFFF0000u);
+    x[2] = __uint_as_float(raw.y << 16);
+    x[3] = __uint_as_float(raw.y & 0xFFFF0000u);
   }
 };
 template <> struct Vec<float, 4> {
@@ -33,69 +37,137 @@ template <> struct Vec<float, 4> {
   }
 };
 
-// Online softmax statistics over the class axis: m = running max, s = sum e^(x-m), t = sum e^(x-m) (x-m).
-// Rescaling to a new max m': t' = e^d (t + d s), s' = e^d s with d = m - m' (exact identity).
-struct Stats {
-  float m, s, t;
-  __device__ __forceinline__ void init() { m = -INFINITY; s = 0.f; t = 0.f; }
-  __device__ __forceinline__ void rescale(float new_max) {
-    if (new_max > m) {
-      float d = (m == -INFINITY) ? 0.f : m - new_max;
-      float scale = expf(d);
-      t = scale * (t + d * s);
-      s = scale * s;
-      m = new_max;
+__device__ __forceinline__ float fast_exp2(float x) { return tc::ex2(x); }
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.69314718055994531f;
+
+// Online softmax statistics of one voxel over the class axis, in base 2: b = a reference near the running max logit
+// times log2(e), s = sum 2^z and t = sum 2^z z with z = x log2(e) - b, so p = 2^z / s and sum_c p ln p = ln2 t/s - ln s
+// for any b. Moving to a larger reference b' is the exact identity s' = 2^d s, t' = 2^d (t + d s) with d = b - b'. The
+// move is lazy: it happens only when a logit exceeds b by more than kRebaseSlack, so z <= kRebaseSlack and every term
+// stays below 2^kRebaseSlack (the conditional rescaling of FlashAttention-4); after the first rows it is rarely taken.
+constexpr float kRebaseSlack = 8.f;
+
+__device__ __forceinline__ void rebase(float& b, float& s, float& t, float nb) {
+  if (nb > b + kRebaseSlack) {
+    if (b != -INFINITY) {
+      const float d = b - nb;
+      const float e = fast_exp2(d);
+      t = e * fmaf(d, s, t);
+      s = e * s;
+    }
+    b = nb;
+  }
+}
+
+// Merge another lane's statistics (b2, s2, t2) into (b, s, t).
+__device__ __forceinline__ void merge(float& b, float& s, float& t, float b2, float s2, float t2) {
+  const float nb = fmaxf(b, b2);
+  float ns = 0.f, nt = 0.f;
+  if (b != -INFINITY) {
+    const float d = b - nb, e = fast_exp2(d);
+    ns = e * s;
+    nt = e * fmaf(d, s, t);
+  }
+  if (b2 != -INFINITY) {
+    const float d = b2 - nb, e = fast_exp2(d);
+    ns = fmaf(e, s2, ns);
+    nt = fmaf(e, fmaf(d, s2, t2), nt);
+  }
+  b = nb;
+  s = ns;
+  t = nt;
+}
+
+// The statistics of VPT voxels starting at `base` (class-major rows `voxels` apart). SPLIT adjacent lanes share the
+// voxels and take every SPLIT-th class row each, CH rows in flight per lane, so one warp load covers 32/SPLIT x VPT
+// contiguous voxels of SPLIT rows; on return every lane of the group holds the merged statistics of all classes.
+// Base-2 exponentials on the MUFU and paired fp32 arithmetic keep it near 7 instructions per logit, so the kernels
+// stay close to the HBM time of reading the logits once (measured on B200 for [8, 256, 65536] bf16: 57.5 us, against
+// 45 us for the same reads without the arithmetic).
+template <typename T, int VPT, int SPLIT, int CH, bool ENTROPY>
+__device__ __forceinline__ void class_stats(const T* base, int classes, int voxels, int q, bool valid,
+                                            float (&b)[VPT], float (&s)[VPT], float (&t)[VPT]) {
+  static_assert(VPT % 2 == 0 && CH >= 2, "voxel pairs");
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    b[v] = -INFINITY;
+    s[v] = t[v] = 0.f;
+  }
+  const float2 l2e = make_float2(kLog2e, kLog2e);
+  // Folds rows x[0..R) into the statistics: one (lazy) rebase per voxel, then 2^z on voxel pairs.
+  auto fold = [&](auto& x, auto rows) {
+    constexpr int R = decltype(rows)::value;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      float mx = x[0][v];
+#pragma unroll
+      for (int j = 1; j + 1 < R; j += 2) mx = tc::fmax3(mx, x[j][v], x[j + 1][v]);
+      if (R % 2 == 0) mx = fmaxf(mx, x[R - 1][v]);
+      rebase(b[v], s[v], t[v], mx * kLog2e);
+    }
+#pragma unroll
+    for (int v = 0; v < VPT; v += 2) {
+      const float2 nb = make_float2(-b[v], -b[v + 1]);
+      float2 sv = make_float2(s[v], s[v + 1]), tv = make_float2(t[v], t[v + 1]);
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const float2 z = __ffma2_rn(make_float2(x[j][v], x[j][v + 1]), l2e, nb);
+        const float2 e = make_float2(fast_exp2(z.x), fast_exp2(z.y));
+        sv = __fadd2_rn(sv, e);
+        if (ENTROPY) tv = __ffma2_rn(e, z, tv);
+      }
+      s[v] = sv.x; s[v + 1] = sv.y;
+      t[v] = tv.x; t[v + 1] = tv.y;
+    }
+  };
+  int c = q;
+  if (valid) {
+    for (; c + (CH - 1) * SPLIT < classes; c += CH * SPLIT) {
+      float x[CH][VPT];
+#pragma unroll
+      for (int j = 0; j < CH; ++j) Vec<T, VPT>::load(base + (int64_t)(c + j * SPLIT) * voxels, x[j]);
+      fold(x, std::integral_constant<int, CH>());
+    }
+    for (; c < classes; c += SPLIT) {
+      float x[1][VPT];
+      Vec<T, VPT>::load(base + (int64_t)c * voxels, x[0]);
+      fold(x, std::integral_constant<int, 1>());
     }
   }
-  __device__ __forceinline__ void add(float x) {
-    float z = x - m;
-    float e = expf(z);
-    s += e;
-    t = fmaf(e, z, t);
+#pragma unroll
+  for (int off = 1; off < SPLIT; off <<= 1) {
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const float b2 = __shfl_xor_sync(0xffffffffu, b[v], off);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s[v], off);
+      const float t2 = __shfl_xor_sync(0xffffffffu, t[v], off);
+      merge(b[v], s[v], t[v], b2, s2, t2);
+    }
   }
-};
+}
 
-// Negative entropy sum_c p log p = t/s - log s  (== `(logp.exp()*logp).sum(0)`, `sampling/entropy.py:3-4`).
-template <typename T, int VPT>
+// Negative entropy sum_c p log p (== `(logp.exp()*logp).sum(0)`, `sampling/entropy.py:3-4`), in nats.
+template <typename T, int VPT, int SPLIT, int CH>
 __global__ void __launch_bounds__(kScoreThreads) ease_scores_kernel(const T* __restrict__ logits, int classes,
                                                                     int voxels, int64_t slot_stride,
                                                                     float* __restrict__ scores,
                                                                     uint32_t* __restrict__ status) {
   const int slot = blockIdx.y;
-  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * VPT;
-  if (n0 >= voxels) return;
-  const T* base = logits + slot * slot_stride + n0;
-  Stats st[VPT];
-#pragma unroll
-  for (int v = 0; v < VPT; ++v) st[v].init();
-  constexpr int CH = 4;
-  int c = 0;
-  for (; c + CH <= classes; c += CH) {
-    float x[CH][VPT];
-#pragma unroll
-    for (int j = 0; j < CH; ++j) Vec<T, VPT>::load(base + (int64_t)(c + j) * voxels, x[j]);
-#pragma unroll
-    for (int v = 0; v < VPT; ++v) {
-      float cm = fmaxf(fmaxf(x[0][v], x[1][v]), fmaxf(x[2][v], x[3][v]));
-      st[v].rescale(cm);
-#pragma unroll
-      for (int j = 0; j < CH; ++j) st[v].add(x[j][v]);
-    }
-  }
-  for (; c < classes; ++c) {
-    float x[VPT];
-    Vec<T, VPT>::load(base + (int64_t)c * voxels, x);
-#pragma unroll
-    for (int v = 0; v < VPT; ++v) {
-      st[v].rescale(x[v]);
-      st[v].add(x[v]);
-    }
-  }
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int q = g % SPLIT;
+  const int n0 = (g / SPLIT) * VPT;
+  const bool valid = n0 < voxels;
+  float b[VPT], s[VPT], t[VPT];
+  class_stats<T, VPT, SPLIT, CH, true>(logits + slot * slot_stride + (valid ? n0 : 0), classes, voxels, q, valid, b,
+                                       s, t);
+  if (!valid || q != 0) return;
   bool nan = false;
   float out[VPT];
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
-    out[v] = st[v].t / st[v].s - logf(st[v].s);
+    out[v] = kLn2 * (t[v] / s[v]) - logf(s[v]);
     nan |= isnan(out[v]);
   }
   float* dst = scores + (int64_t)slot * voxels + n0;
@@ -107,41 +179,33 @@ __global__ void __launch_bounds__(kScoreThreads) ease_scores_kernel(const T* __r
 
 // ----------------------------------------------------------------------------------------------- marking
 
-// good[n] = !(air(n) <= threshold), air = sum over air ids of softmax(logits)[a] (`stream/slot.py:126`).
-template <typename T, int VPT>
+// good[n] = !(air(n) <= threshold), air = sum over air ids of softmax(logits)[a] (`stream/slot.py:126`): the softmax
+// denominator from the same class statistics, then the air probabilities summed in id order.
+template <typename T, int VPT, int SPLIT, int CH>
 __global__ void __launch_bounds__(kScoreThreads) ease_air_kernel(const T* __restrict__ logits, int classes, int voxels,
                                                                  int64_t slot_stride, const int32_t* __restrict__ air_ids,
                                                                  int n_air, float threshold, uint8_t* __restrict__ good) {
+  static_assert(VPT == 4, "one 32-bit store of 4 flags");
   const int slot = blockIdx.y;
-  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * VPT;
-  if (n0 >= voxels) return;
-  const T* base = logits + slot * slot_stride + n0;
-  float m[VPT], s[VPT];
-#pragma unroll
-  for (int v = 0; v < VPT; ++v) { m[v] = -INFINITY; s[v] = 0.f; }
-  for (int c = 0; c < classes; ++c) {
-    float x[VPT];
-    Vec<T, VPT>::load(base + (int64_t)c * voxels, x);
-#pragma unroll
-    for (int v = 0; v < VPT; ++v) {
-      if (x[v] > m[v]) {
-        s[v] = (m[v] == -INFINITY) ? 0.f : s[v] * expf(m[v] - x[v]);
-        m[v] = x[v];
-      }
-      s[v] += expf(x[v] - m[v]);
-    }
-  }
-  float air[VPT];
-#pragma unroll
-  for (int v = 0; v < VPT; ++v) air[v] = 0.f;
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int q = g % SPLIT;
+  const int n0 = (g / SPLIT) * VPT;
+  const bool valid = n0 < voxels;
+  const T* base = logits + slot * slot_stride + (valid ? n0 : 0);
+  float b[VPT], s[VPT], t[VPT];
+  class_stats<T, VPT, SPLIT, CH, false>(base, classes, voxels, q, valid, b, s, t);
+  if (!valid || q != 0) return;
+  float air[VPT] = {};
   for (int a = 0; a < n_air; ++a) {
     float x[VPT];
     Vec<T, VPT>::load(base + (int64_t)air_ids[a] * voxels, x);
 #pragma unroll
-    for (int v = 0; v < VPT; ++v) air[v] += expf(x[v] - m[v]) / s[v];
+    for (int v = 0; v < VPT; ++v) air[v] += fast_exp2(fmaf(x[v], kLog2e, -b[v])) / s[v];
   }
+  uint32_t flags = 0;
 #pragma unroll
-  for (int v = 0; v < VPT; ++v) good[(int64_t)slot * voxels + n0 + v] = !(air[v] <= threshold);
+  for (int v = 0; v < VPT; ++v) flags |= (uint32_t)!(air[v] <= threshold) << (8 * v);
+  *reinterpret_cast<uint32_t*>(good + (int64_t)slot * voxels + n0) = flags;
 }
 
 // last[y,z,x] = good[y'..] for all y' >= y: the per-column top run (`low_entropy_last.py:11-13`, col=True).
@@ -586,6 +650,14 @@ void softmax_geometry(int classes, int& width, int& iters) {
   iters = npot / width;
 }
 
+template <typename T, int VPT, int SPLIT, int CH>
+void launch_scores(const void* logits, int slots, int classes, int voxels, int64_t slot_stride, float* scores,
+                   uint32_t* status, cudaStream_t s) {
+  dim3 grid((voxels / VPT * SPLIT + kScoreThreads - 1) / kScoreThreads, slots);
+  ease_scores_kernel<T, VPT, SPLIT, CH><<<grid, kScoreThreads, 0, s>>>(static_cast<const T*>(logits), classes,
+                                                                       voxels, slot_stride, scores, status);
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -600,14 +672,12 @@ extern "C" int svx_ease_scores(const void* logits, int dtype, int slots, int cla
   cudaStream_t s = as_stream(stream);
   if (dtype == SVX_BF16) {
     SVX_REQUIRE(voxels % 8 == 0 && logit_slot_stride % 8 == 0, "svx_ease_scores: voxels must be a multiple of 8");
-    dim3 grid((voxels / 8 + kScoreThreads - 1) / kScoreThreads, slots);
-    ease_scores_kernel<uint16_t, 8><<<grid, kScoreThreads, 0, s>>>(static_cast<const uint16_t*>(logits), classes,
-                                                                 voxels, logit_slot_stride, scores, status);
+    launch_scores<uint16_t, kStatVoxels, kStatSplit, kStatRows>(logits, slots, classes, voxels, logit_slot_stride,
+                                                                scores, status, s);
   } else if (dtype == SVX_F32) {
     SVX_REQUIRE(voxels % 4 == 0 && logit_slot_stride % 4 == 0, "svx_ease_scores: voxels must be a multiple of 4");
-    dim3 grid((voxels / 4 + kScoreThreads - 1) / kScoreThreads, slots);
-    ease_scores_kernel<float, 4><<<grid, kScoreThreads, 0, s>>>(static_cast<const float*>(logits), classes, voxels,
-                                                              logit_slot_stride, scores, status);
+    launch_scores<float, kStatVoxels, kStatSplit, kStatRows>(logits, slots, classes, voxels, logit_slot_stride, scores,
+                                                             status, s);
   } else {
     return fail(SVX_ERR_INVALID, "svx_ease_scores: dtype must be SVX_F32 or SVX_BF16");
   }
@@ -623,16 +693,16 @@ extern "C" int svx_ease_mark(const void* logits, int dtype, int slots, int class
   SVX_REQUIRE(aligned16(logits), "svx_ease_mark: logits must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   const float threshold = (float)(1.0 - last_eps);  // torch compares the fp32 tensor with the scalar cast to fp32
+  SVX_REQUIRE((reinterpret_cast<uintptr_t>(last) & 3u) == 0, "svx_ease_mark: last must be 4-byte aligned");
+  dim3 grid((voxels / kStatVoxels * kStatSplit + kScoreThreads - 1) / kScoreThreads, slots);
   if (dtype == SVX_BF16) {
     SVX_REQUIRE(voxels % 8 == 0 && logit_slot_stride % 8 == 0, "svx_ease_mark: voxels must be a multiple of 8");
-    dim3 grid((voxels / 8 + kScoreThreads - 1) / kScoreThreads, slots);
-    ease_air_kernel<uint16_t, 8><<<grid, kScoreThreads, 0, s>>>(static_cast<const uint16_t*>(logits), classes, voxels,
-                                                              logit_slot_stride, air_ids, n_air, threshold, last);
+    ease_air_kernel<uint16_t, kStatVoxels, kStatSplit, kStatRows><<<grid, kScoreThreads, 0, s>>>(
+        static_cast<const uint16_t*>(logits), classes, voxels, logit_slot_stride, air_ids, n_air, threshold, last);
   } else if (dtype == SVX_F32) {
     SVX_REQUIRE(voxels % 4 == 0 && logit_slot_stride % 4 == 0, "svx_ease_mark: voxels must be a multiple of 4");
-    dim3 grid((voxels / 4 + kScoreThreads - 1) / kScoreThreads, slots);
-    ease_air_kernel<float, 4><<<grid, kScoreThreads, 0, s>>>(static_cast<const float*>(logits), classes, voxels,
-                                                           logit_slot_stride, air_ids, n_air, threshold, last);
+    ease_air_kernel<float, kStatVoxels, kStatSplit, kStatRows><<<grid, kScoreThreads, 0, s>>>(
+        static_cast<const float*>(logits), classes, voxels, logit_slot_stride, air_ids, n_air, threshold, last);
   } else {
     return fail(SVX_ERR_INVALID, "svx_ease_mark: dtype must be SVX_F32 or SVX_BF16");
   }

@@ -2,8 +2,8 @@
 
     python -m streamvoxel_b200.profile_case <case> [--launches N]
 
-Cases: attention_cross, attention_self, gemm_fc1, gemm_qkv, gemm_dxd, gemm_head, ease_scores, ease_select,
-ease_sample. Inputs are seeded random tensors with the bench's shapes (8 slots, d=768, 8 heads x 96, V=256,
+Cases: attention_cross, attention_self, gemm_fc1, gemm_qkv, gemm_dxd, gemm_head, ease_scores, ease_mark,
+ease_select, ease_sample, patch_embed (both branches; tokens uniform over the 257 ids, the gather's worst case). Inputs are seeded random tensors with the bench's shapes (8 slots, d=768, 8 heads x 96, V=256,
 65536 voxels, packed keys of k = 0..7 L1 tiles); every case's working set is larger than the 126 MB L2 except the
 selection. Prints the mean launch time measured with CUDA events.
 """
@@ -44,6 +44,12 @@ def cases():
     last = torch.zeros((SLOTS, 256, 16, 16), dtype=torch.uint8, device='cuda')
     rng = np.random.default_rng(0)
     pos = torch.from_numpy(np.stack([rng.permutation(1024) for _ in range(SLOTS)]).astype(np.int32)).cuda()
+    table = rnd((V + 1) * 64, D, s=0.02)
+    table_bias = rnd(D, s=0.02)
+    y_add = rnd(PATCHES, D, s=0.02)
+    embed_tokens = torch.randint(0, V + 1, (SLOTS, 256, 16, 16), device='cuda', dtype=torch.int16, generator=g)
+    embed_out = (torch.empty((rows, D), **bf), torch.empty((rows, D), **bf))
+    last_count = torch.empty(SLOTS, dtype=torch.int32, device='cuda')
     params = ops.step_params([(2048, 5, 2048 * 4, 2048 * 5 / VOXELS, i) for i in range(SLOTS)], 'cuda')
     ops.ease_scores(logits, out=scores)
     chosen, index, count = ops.ease_select(scores, tokens, last, pos, params, V, VOXELS)
@@ -65,6 +71,11 @@ def cases():
                                        rows_per_slot=PATCHES, classes=V, geometry=(256, 16, 16)),
                       2.0 * rows * D * 64 * V),
         'ease_scores': (lambda: ops.ease_scores(logits, out=scores), float(logits.numel() * 2 + scores.numel() * 4)),
+        'ease_mark': (lambda: ops.ease_mark(logits, (0,), 1e-3, last=last, last_count=last_count),
+                      float(logits.numel() * 2 + 2 * last.numel())),
+        'patch_embed': (lambda: ops.patch_embed(embed_tokens, V, table, table_bias, y_add, table, table_bias, y_add,
+                                                out_b=embed_out[0], out_c=embed_out[1]),
+                        float(embed_tokens.numel() * 2 + 2 * rows * D * 2)),
         'ease_select': (lambda: ops.ease_select(scores, tokens, last, pos, params, V, VOXELS, chosen=chosen,
                                                 index=index, count=count), float(SLOTS * VOXELS * 8)),
         'ease_sample': (lambda: ops.ease_sample(logits, index, params, tokens.clone()),
@@ -89,7 +100,7 @@ def main():
     stop.record()
     stop.synchronize()
     seconds = start.elapsed_time(stop) * 1e-3 / args.launches
-    unit = 'GB/s' if args.case.startswith('ease') else 'TFLOP/s'
+    unit = 'GB/s' if args.case.startswith(('ease', 'patch')) else 'TFLOP/s'
     rate = work / seconds / (1e9 if unit == 'GB/s' else 1e12)
     print(f'{args.case}: {seconds * 1e6:.1f} us per launch, {rate:.1f} {unit} (work {work:.4g})')
 

@@ -123,10 +123,17 @@ class SlotBatch:
         return torch.from_numpy(arr.view(np.uint8))
 
     def _mark(self, marking):
+        """One marking launch per run of consecutive slots."""
         logits = self.forward.logits
-        for i in marking:
-            ops.ease_mark(logits[i:i + 1], self.air_ids, self.last_eps, last=self.last[i:i + 1],
-                          last_count=self.last_count[i:i + 1])
+        slots = sorted(marking)
+        while slots:
+            n = 1
+            while n < len(slots) and slots[n] == slots[0] + n:
+                n += 1
+            lo, hi = slots[0], slots[0] + n
+            ops.ease_mark(logits[lo:hi], self.air_ids, self.last_eps, last=self.last[lo:hi],
+                          last_count=self.last_count[lo:hi])
+            slots = slots[n:]
 
     def _after_mark(self, marking, counts):
         finished = []
