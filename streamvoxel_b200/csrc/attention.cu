@@ -46,16 +46,42 @@ constexpr uint32_t OPER = WIDE + NARROW;   // one Q or K tile (24 KB)
 constexpr uint32_t VOPER = 2 * WIDE;       // one V tile: two 64-dim atoms along N (32 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int kThreads = 384;
-constexpr int kBars = 1 + 4 * STAGES + 6;
-constexpr size_t kSmem = 1024 + (2 + STAGES) * OPER + STAGES * VOPER + kBars * 8 + 16;
+constexpr int kBars = 2 + 4 * STAGES + 8;
+constexpr int kMaxSlots = 512;             // slot ranking table in shared memory
+constexpr size_t kSmem = 1024 + (2 + STAGES) * OPER + STAGES * VOPER + kBars * 8 + 16 + kMaxSlots * 4;
 
 struct AttnParams {
-  int slots, heads, queries, keys, pairs;
+  int slots, heads, queries, keys, pairs, units;
   int kv_mode;  // 0: K/V groups = heads, rows = slot*keys + key; 1: groups = slot*heads + head, rows = key
   const int32_t* lengths;
   uint16_t* out;
   float scale_log2;
 };
+
+// One work unit: two 128-query tiles of one (slot, head). Units are numbered longest slot first; a tile index past
+// the slot's queries (odd tile counts) repeats the last tile, whose result is not stored.
+struct Unit {
+  int slot, head, q0, nq, length, tiles, kg, kr0;
+  __device__ __forceinline__ Unit(const AttnParams& p, const int* rank_slot, int w) {
+    const int per_slot = p.heads * p.pairs;
+    const int rem = w % per_slot;
+    slot = rank_slot[w / per_slot];
+    head = rem / p.pairs;
+    q0 = (rem % p.pairs) * 2 * TQ;
+    nq = min(2, (p.queries - q0) / TQ);
+    length = p.lengths ? max(0, min(p.lengths[slot], p.keys)) : p.keys;
+    tiles = (length + TK - 1) / TK;
+    kg = p.kv_mode == 0 ? head : slot * p.heads + head;
+    kr0 = p.kv_mode == 0 ? slot * p.keys : 0;
+  }
+};
+
+// The k-th unit of CTA c in a grid of G: passes over the longest-first unit list alternate direction (c, then
+// 2G - 1 - c, ...), which balances the summed lengths of the CTAs; -1 for a pass that has no unit for c.
+__device__ __forceinline__ int unit_of(int c, int k, int G, int units) {
+  const int w = k * G + ((k & 1) ? G - 1 - c : c);
+  return w < units ? w : -1;
+}
 
 __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_constant__ CUtensorMap mq_wide,
                                                                    const __grid_constant__ CUtensorMap mq_narrow,
@@ -70,33 +96,33 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   uint8_t* sv = sk + STAGES * OPER;        // V ring
   uint64_t* bars = reinterpret_cast<uint64_t*>(sv + STAGES * VOPER);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_empty = bars + 1;          // both chains' last S of a unit completed: Q may be replaced
+  uint64_t* k_full = bars + 2;
   uint64_t* k_empty = k_full + STAGES;
   uint64_t* v_full = k_empty + STAGES;
   uint64_t* v_empty = v_full + STAGES;
   uint64_t* s_full = v_empty + STAGES;   // per query tile: S_i computed
   uint64_t* p_full = s_full + 2;         // per query tile, 128 arrivals: P_i written (and O_i rescaled)
   uint64_t* pv_done = p_full + 2;        // per query tile: P_i V completed
+  uint64_t* o_empty = pv_done + 2;       // per query tile, 128 arrivals: a unit's O_i has been read out
   uint32_t* misc = reinterpret_cast<uint32_t*>(bars + kBars);
   uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
-  volatile int* slot_of = reinterpret_cast<volatile int*>(misc + 2);
+  int* rank_slot = reinterpret_cast<int*>(misc + 4);
 
   const int warp = warp_id(), lane = lane_id();
-  const int per_slot = p.heads * p.pairs;
-  const int rank = blockIdx.x / per_slot, rem = blockIdx.x % per_slot;
-  const int head = rem / p.pairs, q0 = (rem % p.pairs) * 2 * TQ;
-  const int nq = min(2, (p.queries - q0) / TQ);
+  const int G = gridDim.x, c = blockIdx.x;
   grid_launch_dependents();
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < STAGES; ++i) {   // a K/V stage is released by the products of every query tile
-      mbar_init(k_full + i, 1); mbar_init(k_empty + i, nq);
-      mbar_init(v_full + i, 1); mbar_init(v_empty + i, nq);
+    mbar_init(q_empty, 2);
+    for (int i = 0; i < STAGES; ++i) {   // a K/V stage is released by the products of both query tiles
+      mbar_init(k_full + i, 1); mbar_init(k_empty + i, 2);
+      mbar_init(v_full + i, 1); mbar_init(v_empty + i, 2);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full + i, 1); mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1);
+      mbar_init(s_full + i, 1); mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1); mbar_init(o_empty + i, 128);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -107,90 +133,115 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
   grid_dependency_wait();   // Q, K, V and the lengths come from earlier kernels
   if (warp == 3) {
-    // The slot of this rank in descending key-length order (ties by slot index): a permutation, one lane matches.
-    if (p.lengths) {
-      for (int s = lane; s < p.slots; s += 32) {
+    // Slots in descending key-length order (ties by slot index): rank_slot[rank] = slot.
+    for (int s = lane; s < p.slots; s += 32) {
+      int r = s;
+      if (p.lengths) {
         const int ls = max(0, min(p.lengths[s], p.keys));
-        int r = 0;
+        r = 0;
         for (int u = 0; u < p.slots; ++u) {
           const int lu = max(0, min(p.lengths[u], p.keys));
           r += (lu > ls) || (lu == ls && u < s);
         }
-        if (r == rank) *slot_of = s;
       }
-    } else if (lane == 0) {
-      *slot_of = rank;
+      rank_slot[r] = s;
     }
   }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int slot = *slot_of;
-  const int length = p.lengths ? max(0, min(p.lengths[slot], p.keys)) : p.keys;
-  const int tiles = (length + TK - 1) / TK;
-  const int kg = p.kv_mode == 0 ? head : slot * p.heads + head;
-  const int kr0 = p.kv_mode == 0 ? slot * p.keys : 0;
 
   // Register split: the load/MMA warpgroup keeps 64 per thread, the two softmax warpgroups take 216
   // (128 x 64 + 256 x 216 <= 384 x 168, the launch's allocation).
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
-    if (warp == 0 && tiles > 0) {
-      tc::expect_tx_w(q_full, nq * OPER);
-      for (int i = 0; i < nq; ++i) {
-        const int qr = slot * p.queries + q0 + i * TQ;
-        tc::tma_load_3d_w(sq + i * OPER, &mq_wide, 0, head, qr, q_full);
-        tc::tma_load_3d_w(sq + i * OPER + WIDE, &mq_narrow, 64, head, qr, q_full);
+    if (warp == 0) {   // Q and the K ring
+      int T = 0, qn = 0;
+      bool ok = true;
+      for (int k = 0; ok && k * G < p.units; ++k) {
+        const int w = unit_of(c, k, G, p.units);
+        if (w < 0) continue;
+        const Unit U(p, rank_slot, w);
+        if (U.tiles == 0) continue;
+        if (qn >= 1 && !tc::wait_w(q_empty, (qn - 1) & 1, abort_flag)) break;
+        tc::expect_tx_w(q_full, 2 * OPER);
+        for (int i = 0; i < 2; ++i) {
+          const int qr = U.slot * p.queries + U.q0 + min(i, U.nq - 1) * TQ;
+          tc::tma_load_3d_w(sq + i * OPER, &mq_wide, 0, U.head, qr, q_full);
+          tc::tma_load_3d_w(sq + i * OPER + WIDE, &mq_narrow, 64, U.head, qr, q_full);
+        }
+        for (int t = 0; t < U.tiles; ++t) {
+          const int g = T + t, s = g % STAGES;
+          if (g >= STAGES && !tc::wait_w(k_empty + s, (g / STAGES - 1) & 1, abort_flag)) { ok = false; break; }
+          tc::expect_tx_w(k_full + s, OPER);
+          tc::tma_load_3d_w(sk + s * OPER, &mk_wide, 0, U.kg, U.kr0 + t * TK, k_full + s);
+          tc::tma_load_3d_w(sk + s * OPER + WIDE, &mk_narrow, 64, U.kg, U.kr0 + t * TK, k_full + s);
+        }
+        T += U.tiles;
+        ++qn;
       }
-      for (int t = 0; t < tiles; ++t) {
-        const int s = t % STAGES;
-        if (t >= STAGES && !tc::wait_w(k_empty + s, (t / STAGES - 1) & 1, abort_flag)) break;
-        tc::expect_tx_w(k_full + s, OPER);
-        tc::tma_load_3d_w(sk + s * OPER, &mk_wide, 0, kg, kr0 + t * TK, k_full + s);
-        tc::tma_load_3d_w(sk + s * OPER + WIDE, &mk_narrow, 64, kg, kr0 + t * TK, k_full + s);
+    } else if (warp == 2) {   // the V ring
+      int T = 0;
+      bool ok = true;
+      for (int k = 0; ok && k * G < p.units; ++k) {
+        const int w = unit_of(c, k, G, p.units);
+        if (w < 0) continue;
+        const Unit U(p, rank_slot, w);
+        for (int t = 0; t < U.tiles; ++t) {
+          const int g = T + t, s = g % STAGES;
+          if (g >= STAGES && !tc::wait_w(v_empty + s, (g / STAGES - 1) & 1, abort_flag)) { ok = false; break; }
+          tc::expect_tx_w(v_full + s, VOPER);
+          tc::tma_load_3d_w(sv + s * VOPER, &mv, 0, U.kg, U.kr0 + t * TK, v_full + s);
+          tc::tma_load_3d_w(sv + s * VOPER + WIDE, &mv, 64, U.kg, U.kr0 + t * TK, v_full + s);
+        }
+        T += U.tiles;
       }
-    } else if (warp == 2 && tiles > 0) {
-      for (int t = 0; t < tiles; ++t) {
-        const int s = t % STAGES;
-        if (t >= STAGES && !tc::wait_w(v_empty + s, (t / STAGES - 1) & 1, abort_flag)) break;
-        tc::expect_tx_w(v_full + s, VOPER);
-        tc::tma_load_3d_w(sv + s * VOPER, &mv, 0, kg, kr0 + t * TK, v_full + s);
-        tc::tma_load_3d_w(sv + s * VOPER + WIDE, &mv, 64, kg, kr0 + t * TK, v_full + s);
-      }
-    } else if ((warp == 1 || warp == 3) && tiles > 0 && (warp == 1 || nq == 2)) {
+    } else {   // warp 1: products of query tile 0; warp 3: of query tile 1
       const int i = warp == 1 ? 0 : 1;
       constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
       constexpr uint32_t idesc_o = tc::instr_desc(TQ, HD, true);
       const uint32_t qa = smem_addr(sq + i * OPER);
       const uint32_t s_tmem = tmem + i * 128, o_tmem = tmem + 256 + i * 128;
-      bool ok = tc::wait_w(q_full, 0, abort_flag) && tc::wait_w(k_full, 0, abort_flag);
-      // This tile's chain  S(t) -> softmax(t) -> P(t) V(t) -> S(t+1) -> ...
-      for (int t = 0; ok && t <= tiles; ++t) {
-        if (t >= 1) {
-          const int u = t - 1, vs = u % STAGES;
-          ok = tc::wait_w(v_full + vs, (u / STAGES) & 1, abort_flag) && tc::wait_w(p_full + i, u & 1, abort_flag);
-          if (!ok) break;
-          tc::fence_after();
-          tc::mma_pv128_w(o_tmem, s_tmem, tc::sw128_desc(smem_addr(sv + vs * VOPER), WIDE, 1024), idesc_o,
-                          u > 0 ? 1u : 0u);
-          tc::commit_w(pv_done + i);
-          tc::commit_w(v_empty + vs);
-        }
-        if (t < tiles) {
-          const int ks = t % STAGES;
-          if (t >= 1) {   // S overwrites P(t-1): wait for its product
-            ok = tc::wait_w(k_full + ks, (t / STAGES) & 1, abort_flag) &&
-                 tc::wait_w(pv_done + i, (t - 1) & 1, abort_flag);
+      int T = 0, qn = 0;
+      bool ok = true;
+      for (int k = 0; ok && k * G < p.units; ++k) {
+        const int w = unit_of(c, k, G, p.units);
+        if (w < 0) continue;
+        const Unit U(p, rank_slot, w);
+        if (U.tiles == 0) continue;
+        if (!tc::wait_w(q_full, qn & 1, abort_flag)) break;
+        // This tile's chain  S(t) -> softmax(t) -> P(t) V(t) -> S(t+1) -> ...; the tile counter g runs on across
+        // units, so S of a unit's first tile also waits for the previous unit's last P V.
+        for (int t = 0; t <= U.tiles; ++t) {
+          if (t >= 1) {
+            const int g = T + t - 1, vs = g % STAGES;
+            ok = tc::wait_w(v_full + vs, (g / STAGES) & 1, abort_flag) && tc::wait_w(p_full + i, g & 1, abort_flag);
+            if (ok && t == 1 && qn >= 1)   // the first P V overwrites O_i: the previous unit's O_i has been read
+              ok = tc::wait_w(o_empty + i, (qn - 1) & 1, abort_flag);
             if (!ok) break;
+            tc::fence_after();
+            tc::mma_pv128_w(o_tmem, s_tmem, tc::sw128_desc(smem_addr(sv + vs * VOPER), WIDE, 1024), idesc_o,
+                            t > 1 ? 1u : 0u);
+            tc::commit_w(pv_done + i);
+            tc::commit_w(v_empty + vs);
           }
-          tc::fence_after();
-          const uint32_t kb = smem_addr(sk + ks * OPER);
-          tc::mma_qk96_w(s_tmem, tc::sw128_desc(qa), tc::sw128_desc(kb), tc::sw64_desc(qa + WIDE),
-                         tc::sw64_desc(kb + WIDE), idesc_s);
-          tc::commit_w(s_full + i);
-          tc::commit_w(k_empty + ks);
+          if (t < U.tiles) {
+            const int g = T + t, ks = g % STAGES;
+            ok = tc::wait_w(k_full + ks, (g / STAGES) & 1, abort_flag) &&
+                 (g == 0 || tc::wait_w(pv_done + i, (g - 1) & 1, abort_flag));   // S overwrites P(g - 1)
+            if (!ok) break;
+            tc::fence_after();
+            const uint32_t kb = smem_addr(sk + ks * OPER);
+            tc::mma_qk96_w(s_tmem, tc::sw128_desc(qa), tc::sw128_desc(kb), tc::sw64_desc(qa + WIDE),
+                           tc::sw64_desc(kb + WIDE), idesc_s);
+            tc::commit_w(s_full + i);
+            tc::commit_w(k_empty + ks);
+            if (t == U.tiles - 1) tc::commit_w(q_empty);
+          }
         }
+        T += U.tiles;
+        ++qn;
       }
     }
     // Teardown: the TMEM owner frees the columns once all 12 warps are past their last TMEM access.
@@ -208,107 +259,119 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
     const uint32_t ts = tmem + lanes + i * 128, to = tmem + lanes + 256 + i * 128;
-    const int qrow = q0 + i * TQ + row;
-    uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)slot * p.queries + qrow) * (p.heads * HD) + head * HD);
     const float sl2 = p.scale_log2;
-    float m_used = -INFINITY, l_run = 0.f;
+    int T = 0;
     bool ok = true;
-    for (int t = 0; i < nq && t < tiles; ++t) {
-      if (!tc::wait(s_full + i, t & 1, abort_flag)) { ok = false; break; }
-      tc::fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tc::ld32(ts + c * 32, r[c]);
-      tc::wait_ld();
-      const int key0 = t * TK;
-      if (key0 + TK > length) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (key0 + c * 32 + j >= length) r[c][j] = __float_as_uint(-INFINITY);
+    for (int k = 0; ok && k * G < p.units; ++k) {
+      const int w = unit_of(c, k, G, p.units);
+      if (w < 0) continue;
+      const Unit U(p, rank_slot, w);
+      const int qrow = U.q0 + i * TQ + row;
+      uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)U.slot * p.queries + qrow) * (p.heads * HD) + U.head * HD);
+      if (U.tiles == 0) {
+        if (i < U.nq)
+          for (int k8 = 0; k8 < HD / 8; ++k8) dst[k8] = make_uint4(0, 0, 0, 0);
+        continue;
       }
-      float mc[4];
+      float m_used = -INFINITY, l_run = 0.f;
+      for (int t = 0; t < U.tiles; ++t) {
+        const int g = T + t;
+        if (!tc::wait(s_full + i, g & 1, abort_flag)) { ok = false; break; }
+        tc::fence_after();
+        uint32_t r[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float a = __uint_as_float(r[c][0]), b = __uint_as_float(r[c][1]);
+        for (int c4 = 0; c4 < 4; ++c4) tc::ld32(ts + c4 * 32, r[c4]);
+        tc::wait_ld();
+        const int key0 = t * TK;
+        if (key0 + TK > U.length) {
 #pragma unroll
-        for (int j = 2; j < 32; j += 4) {
-          a = tc::fmax3(a, __uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1]));
-          b = tc::fmax3(b, __uint_as_float(r[c][j + 2]), __uint_as_float(r[c][j + 3]));
+          for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (key0 + c4 * 32 + j >= U.length) r[c4][j] = __float_as_uint(-INFINITY);
         }
-        mc[c] = fmaxf(a, b);
-      }
-      const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])) * sl2;
-      // Raise the exponent base only when the row max outgrows it by more than 8 (warp-uniform rescale of O).
-      const bool raise = mx > m_used + 8.f;
-      const bool any_raise = __any_sync(0xffffffffu, raise);
-      float alpha = 1.f;
-      if (any_raise) {
-        const float m_new = raise ? mx : m_used;
-        alpha = tc::ex2(m_used - m_new);   // m_used = -inf on the first tile: alpha = 0
-        m_used = m_new;
-      }
-      // P = 2^(S*scale - m) as bf16 pairs: keys 64h .. 64h+63 -> TMEM columns [32h, +32) of S_i.
-      const float2 scale2 = make_float2(sl2, sl2), nbase2 = make_float2(-m_used, -m_used);
-      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        float mc[4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t packed[32];
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float a = __uint_as_float(r[c4][0]), b = __uint_as_float(r[c4][1]);
 #pragma unroll
-        for (int j = 0; j < 64; j += 2) {
-          const int c = 2 * h + (j >> 5), jj = j & 31;
-          const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[c][jj]), __uint_as_float(r[c][jj + 1])), scale2,
-                                      nbase2);
-          const float2 e = make_float2(tc::ex2(x.x), tc::ex2(x.y));
-          acc[(j >> 1) & 3] = __fadd2_rn(acc[(j >> 1) & 3], e);
-          packed[j >> 1] = tc::pack_bf16x2(e.x, e.y);
+          for (int j = 2; j < 32; j += 4) {
+            a = tc::fmax3(a, __uint_as_float(r[c4][j]), __uint_as_float(r[c4][j + 1]));
+            b = tc::fmax3(b, __uint_as_float(r[c4][j + 2]), __uint_as_float(r[c4][j + 3]));
+          }
+          mc[c4] = fmaxf(a, b);
         }
-        tc::st32(ts + h * 32, packed);
-      }
-      // O_i holds the products of tiles < t (the P_i V of tile t-1 completed before S_i(t) was issued).
-      if (any_raise && t >= 1) {
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t o[32];
-          tc::ld32(to + c * 32, o);
-          tc::wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-          tc::st32(to + c * 32, o);
+        const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])) * sl2;
+        // Raise the exponent base only when the row max outgrows it by more than 8 (warp-uniform rescale of O).
+        const bool raise = mx > m_used + 8.f;
+        const bool any_raise = __any_sync(0xffffffffu, raise);
+        float alpha = 1.f;
+        if (any_raise) {
+          const float m_new = raise ? mx : m_used;
+          alpha = tc::ex2(m_used - m_new);   // m_used = -inf on the first tile: alpha = 0
+          m_used = m_new;
         }
-      }
-      tc::wait_st();
-      const float2 s01 = __fadd2_rn(acc[0], acc[1]), s23 = __fadd2_rn(acc[2], acc[3]);
-      l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
-      tc::fence_before();
-      tc::mbar_arrive(p_full + i);
-    }
-    if (i < nq) {
-      if (ok && tiles > 0) {
-        const int u = tiles - 1;
-        ok = tc::wait(pv_done + i, u & 1, abort_flag);
-        if (ok) {
-          tc::fence_after();
-          const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        // P = 2^(S*scale - m) as bf16 pairs: keys 64h .. 64h+63 -> TMEM columns [32h, +32) of S_i.
+        const float2 scale2 = make_float2(sl2, sl2), nbase2 = make_float2(-m_used, -m_used);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
+        for (int h = 0; h < 2; ++h) {
+          uint32_t packed[32];
+#pragma unroll
+          for (int j = 0; j < 64; j += 2) {
+            const int c4 = 2 * h + (j >> 5), jj = j & 31;
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[c4][jj]), __uint_as_float(r[c4][jj + 1])),
+                                        scale2, nbase2);
+            const float2 e = make_float2(tc::ex2(x.x), tc::ex2(x.y));
+            acc[(j >> 1) & 3] = __fadd2_rn(acc[(j >> 1) & 3], e);
+            packed[j >> 1] = tc::pack_bf16x2(e.x, e.y);
+          }
+          tc::st32(ts + h * 32, packed);
+        }
+        // O_i holds the products of this unit's tiles < t (the P_i V of tile t-1 completed before S_i(t) was issued).
+        if (any_raise && t >= 1) {
+#pragma unroll
+          for (int c4 = 0; c4 < HD / 32; ++c4) {
             uint32_t o[32];
-            tc::ld32(to + c * 32, o);
+            tc::ld32(to + c4 * 32, o);
             tc::wait_ld();
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float* f = reinterpret_cast<const float*>(o) + 8 * k;
-              dst[c * 4 + k] = make_uint4(tc::pack_bf16x2(f[0] * inv, f[1] * inv), tc::pack_bf16x2(f[2] * inv, f[3] * inv),
-                                          tc::pack_bf16x2(f[4] * inv, f[5] * inv), tc::pack_bf16x2(f[6] * inv, f[7] * inv));
-            }
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+            tc::st32(to + c4 * 32, o);
           }
         }
-      } else if (ok) {
-        for (int k = 0; k < HD / 8; ++k) dst[k] = make_uint4(0, 0, 0, 0);
+        tc::wait_st();
+        const float2 s01 = __fadd2_rn(acc[0], acc[1]), s23 = __fadd2_rn(acc[2], acc[3]);
+        l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
+        tc::fence_before();
+        tc::mbar_arrive(p_full + i);
       }
-      if (!ok && lane == 0) atomicOr(&g_svx_attention_timeouts, SVX_STATUS_WAIT_TIMEOUT);
+      if (ok) ok = tc::wait(pv_done + i, (T + U.tiles - 1) & 1, abort_flag);
+      if (!ok) break;
+      tc::fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < HD / 32; ++c4) {
+        uint32_t o[32];
+        tc::ld32(to + c4 * 32, o);
+        tc::wait_ld();
+        if (i < U.nq) {
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const float* f = reinterpret_cast<const float*>(o) + 8 * k4;
+            dst[c4 * 4 + k4] = make_uint4(tc::pack_bf16x2(f[0] * inv, f[1] * inv),
+                                          tc::pack_bf16x2(f[2] * inv, f[3] * inv),
+                                          tc::pack_bf16x2(f[4] * inv, f[5] * inv),
+                                          tc::pack_bf16x2(f[6] * inv, f[7] * inv));
+          }
+        }
+      }
+      // O_i has been read: the next unit's first P V may overwrite it.
+      tc::fence_before();
+      tc::mbar_arrive(o_empty + i);
+      T += U.tiles;
     }
+    if (!ok && lane == 0) atomicOr(&g_svx_attention_timeouts, SVX_STATUS_WAIT_TIMEOUT);
     // Teardown: every TMEM access of this warpgroup is done; the TMEM owner frees the columns after all 12 warps.
     tc::fence_before();
     __syncwarp();
@@ -347,10 +410,18 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
     SVX_CHECK_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
     configured = true;
   }
+  SVX_REQUIRE(slots <= kMaxSlots, "attention: at most 512 slots");
+  static int sms = 0;
+  if (!sms) {
+    int device = 0;
+    SVX_CHECK_CUDA(cudaGetDevice(&device));
+    SVX_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  }
   const int pairs = (queries / TQ + 1) / 2;
-  AttnParams prm{slots, heads, queries, keys, pairs, kv_mode, lengths, out,
+  const int units = slots * heads * pairs;
+  AttnParams prm{slots, heads, queries, keys, pairs, units, kv_mode, lengths, out,
                  (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
-  return launch_dependent("attention_tc_kernel", attention_tc_kernel, dim3(slots * heads * pairs), dim3(kThreads),
+  return launch_dependent("attention_tc_kernel", attention_tc_kernel, dim3(units < sms ? units : sms), dim3(kThreads),
                           kSmem, stream, m[0], m[1], m[2], m[3], m[4], prm);
 }
 
