@@ -1,29 +1,30 @@
 // Non-causal attention, head_dim 96, over per-slot variable-length keys, on the 5th-generation tensor cores.
 //
-// One CTA = two 128-query tiles of one (slot, head) sharing every K/V tile. Key tiles of 128 are streamed by TMA into
-// three-stage K and V rings, and only the ceil(length / 128) tiles of a slot are loaded: the packed-key block mask of
-// `streamvoxel/stream/fast_ops.py:149-159`. Q and K tiles are exactly 96 dims wide: dims 0-63 as a 128B-swizzled part
-// (128-byte rows) and dims 64-95 as a 64B-swizzled part (64-byte rows). V tiles are two 128B-swizzled 64-dim boxes
-// (dims 96-127 read as zero, no memory traffic) so that P V is one N=96 product per 16 keys.
+// A persistent CTA per SM takes work units of two 128-query tiles of one (slot, head), longest slots first. Key tiles
+// of 96 are streamed by TMA into four-stage K and V rings, and only the ceil(length / 96) tiles of a slot are loaded:
+// the packed-key block mask of `streamvoxel/stream/fast_ops.py:149-159`. Q and K tiles are exactly 96 dims wide: dims
+// 0-63 as a 128B-swizzled part (128-byte rows) and dims 64-95 as a 64B-swizzled part (64-byte rows). V tiles are two
+// 128B-swizzled 64-dim boxes (dims 96-127 read as zero, no memory traffic) so that P V is one N=96 product per 16 keys.
 //
-// Tensor memory per query tile i (512 columns): S_i fp32 at [128 i, +128), O_i fp32 at [256 + 128 i, +96). The
-// softmax writes P_i as bf16 pairs over the first 64 columns of S_i, and P_i V takes its A operand from there, so
-// P never touches shared memory (whose bandwidth bounds the small-N products when both operands come from it).
+// Tensor memory per query tile i: S_i fp32 at [128 i, +96), O_i fp32 at [256 + 128 i, +96), and P_i (bf16 pairs, 48
+// columns) in the two tails: keys 0-63 at [128 i + 96, +32), keys 64-95 at [256 + 128 i + 96, +16) (the products take
+// P per 16-key step, so it need not be contiguous). S, P and O are separate, so nothing serialises a query tile's chain but the data
+// itself: S_i(t+1) is computed as soon as the softmax has read S_i(t), while it still computes exponentials, and
+// P_i(t) V(t) runs while the softmax works on tile t+1. The softmax therefore runs back to back and bounds the step
+// together with the tensor core (with 128-key tiles P must share S's columns, and S(t+1) then waits for P(t) V(t)).
 //
 // Warp roles (384 threads): warp 0 loads Q and the K ring, warp 2 the V ring; warp 1 (which owns TMEM) issues the
-// products of query tile 0 and warp 3 those of tile 1, so the two chains never wait on each other's barriers (each
-// loop warp-converged, one elected lane issuing):
-//   O_i += P_i(t) V(t)   M=128, N=96, K=128          (A = P_i in TMEM, V read MN-major)
-//   S_i  = Q_i K(t+1)^T  M=128, N=128, K=96          (issued once P_i(t) V(t) has completed: S_i overwrites P_i)
+// products of query tile 0 and warp 3 those of tile 1 (each loop warp-converged, one elected lane issuing):
+//   S_i  = Q_i K(t)^T     M=128, N=96, K=96          (once the softmax has read S_i(t-1))
+//   O_i += P_i(t) V(t)    M=128, N=96, K=96          (A = P_i in TMEM, V read MN-major)
 // Warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1, one query row per thread (TMEM lane): read the
-// row of S_i with tcgen05.ld, write P_i = 2^(S*scale - m) with tcgen05.st, signal the MMA warp. While one
-// warpgroup computes exponentials the tensor core works for the other. The exponent base m is raised lazily: only
-// when a row's max grows by more than 8 (a factor 256, so P <= 256 stays exact in the fp32 sums), and then the warp
-// rescales its O rows in TMEM (P_i V of the previous tile has completed before S_i was issued) -- exact, since P, O
-// and the sum share one m. P is rounded to bf16 before P.V and the row sums stay fp32, as in SDPA's flash kernels;
-// the output is normalised in fp32 and written as bf16.
-// CTAs are numbered longest slot first (the hardware starts them in index order), so the long cross-attention
-// slots do not trail the grid.
+// row of S_i with tcgen05.ld, release S_i, compute P_i = 2^(S*scale - m), and once P_i(t-1) V(t-1) has completed write
+// P_i with tcgen05.st and signal the MMA warp. A quarter of the exponentials are evaluated on the FMA pipe (a fitted
+// polynomial, relative error 2.7e-6) and the rest on the MUFU, which alone would bound the softmax. The exponent base
+// m is raised lazily: only when a row's max grows by more than 8 (a factor 256, so P <= 256 stays exact in the fp32
+// sums), and then the warp rescales its O rows in TMEM (after P_i(t-1) V(t-1) has completed, before P_i(t) V(t) is
+// issued) -- exact, since P, O and the sum share one m. P is rounded to bf16 before P.V and the row sums stay fp32, as
+// in SDPA's flash kernels; the output is normalised in fp32 and written as bf16.
 // Every mbarrier wait is bounded (tc::wait); a timeout raises a CTA-wide abort, sets SVX_STATUS_WAIT_TIMEOUT in the
 // library's timeout word and skips the rest of the CTA's work.
 #include <math.h>
@@ -38,17 +39,41 @@ __device__ uint32_t g_svx_attention_timeouts = 0;
 
 namespace {
 
-constexpr int TQ = 128, TK = 128, HD = 96;
-constexpr int STAGES = 3;                  // K and V ring depth
-constexpr uint32_t WIDE = 128 * 128;       // 128 rows x 128 B: dims 0-63 of an operand tile (128B swizzle)
-constexpr uint32_t NARROW = 128 * 64;      // 128 rows x 64 B: dims 64-95 (64B swizzle)
-constexpr uint32_t OPER = WIDE + NARROW;   // one Q or K tile (24 KB)
-constexpr uint32_t VOPER = 2 * WIDE;       // one V tile: two 64-dim atoms along N (32 KB)
+constexpr int TQ = 128, TK = 96, HD = 96;
+constexpr int STAGES = 4;                      // K and V ring depth
+constexpr uint32_t QWIDE = TQ * 128;           // Q tile dims 0-63: 128 rows x 128 B (128B swizzle)
+constexpr uint32_t QOPER = QWIDE + TQ * 64;    // + dims 64-95: 128 rows x 64 B (64B swizzle)
+constexpr uint32_t KWIDE = TK * 128;           // K tile dims 0-63: 96 rows x 128 B
+constexpr uint32_t KOPER = KWIDE + TK * 64;    // + dims 64-95
+constexpr uint32_t VWIDE = TK * 128;           // one 64-dim atom of a V tile: 96 keys x 128 B
+constexpr uint32_t VOPER = 2 * VWIDE;          // one V tile: two atoms along N
 constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t S_COL = 0, O_COL = 256;      // + 128 i; P_i in the 32-column tails of both (S_COL/O_COL + 96)
 constexpr int kThreads = 384;
 constexpr int kBars = 2 + 4 * STAGES + 8;
-constexpr int kMaxSlots = 512;             // slot ranking table in shared memory
-constexpr size_t kSmem = 1024 + (2 + STAGES) * OPER + STAGES * VOPER + kBars * 8 + 16 + kMaxSlots * 4;
+constexpr int kMaxSlots = 512;                 // slot ranking table in shared memory
+constexpr size_t kSmem = 1024 + 2 * QOPER + STAGES * (KOPER + VOPER) + kBars * 8 + 16 + kMaxSlots * 4;
+// Of every 8 pairs of exponentials, this many go to the FMA pipe (measured on B200: 2 of 8 is the balance point).
+constexpr int kFmaPairs = 2;
+
+// 2^x on the FMA pipe for a pair: x = j + f with j = rint(x) from the 1.5 * 2^23 magic sum and f in [-0.5, 0.5], a
+// degree-4 polynomial for 2^f (coefficients fitted for least relative error on [-0.5, 0.5]: 2.7e-6), and j added to
+// the exponent field. x is clamped at -125.5 so that the result stays a normal float (2^-125.5 where the MUFU would
+// give 0 or a denormal; both vanish against the row sum, which is at least 1).
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  x.x = fmaxf(x.x, -125.5f);
+  x.y = fmaxf(x.y, -125.5f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(make_float2(0.009570068679749966f, 0.009570068679749966f), f,
+                        make_float2(0.055917806923389435f, 0.055917806923389435f));
+  q = __ffma2_rn(q, f, make_float2(0.240247443318367f, 0.240247443318367f));
+  q = __ffma2_rn(q, f, make_float2(0.6931218504905701f, 0.6931218504905701f));
+  q = __ffma2_rn(q, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
 
 struct AttnParams {
   int slots, heads, queries, keys, pairs, units;
@@ -92,8 +117,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;                      // Q tiles 0, 1
-  uint8_t* sk = sq + 2 * OPER;             // K ring
-  uint8_t* sv = sk + STAGES * OPER;        // V ring
+  uint8_t* sk = sq + 2 * QOPER;            // K ring
+  uint8_t* sv = sk + STAGES * KOPER;       // V ring
   uint64_t* bars = reinterpret_cast<uint64_t*>(sv + STAGES * VOPER);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;          // both chains' last S of a unit completed: Q may be replaced
@@ -102,9 +127,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   uint64_t* v_full = k_empty + STAGES;
   uint64_t* v_empty = v_full + STAGES;
   uint64_t* s_full = v_empty + STAGES;   // per query tile: S_i computed
-  uint64_t* p_full = s_full + 2;         // per query tile, 128 arrivals: P_i written (and O_i rescaled)
-  uint64_t* pv_done = p_full + 2;        // per query tile: P_i V completed
-  uint64_t* o_empty = pv_done + 2;       // per query tile, 128 arrivals: a unit's O_i has been read out
+  uint64_t* s_empty = s_full + 2;        // per query tile, 128 arrivals: S_i has been read
+  uint64_t* p_full = s_empty + 2;        // per query tile, 128 arrivals: P_i written (and O_i rescaled)
+  uint64_t* pv_done = p_full + 2;        // per query tile: P_i V completed (P_i free, O_i quiescent)
   uint32_t* misc = reinterpret_cast<uint32_t*>(bars + kBars);
   uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
@@ -122,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       mbar_init(v_full + i, 1); mbar_init(v_empty + i, 2);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full + i, 1); mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1); mbar_init(o_empty + i, 128);
+      mbar_init(s_full + i, 1); mbar_init(s_empty + i, 128); mbar_init(p_full + i, 128); mbar_init(pv_done + i, 1);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -165,18 +190,18 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
         const Unit U(p, rank_slot, w);
         if (U.tiles == 0) continue;
         if (qn >= 1 && !tc::wait_w(q_empty, (qn - 1) & 1, abort_flag)) break;
-        tc::expect_tx_w(q_full, 2 * OPER);
+        tc::expect_tx_w(q_full, 2 * QOPER);
         for (int i = 0; i < 2; ++i) {
           const int qr = U.slot * p.queries + U.q0 + min(i, U.nq - 1) * TQ;
-          tc::tma_load_3d_w(sq + i * OPER, &mq_wide, 0, U.head, qr, q_full);
-          tc::tma_load_3d_w(sq + i * OPER + WIDE, &mq_narrow, 64, U.head, qr, q_full);
+          tc::tma_load_3d_w(sq + i * QOPER, &mq_wide, 0, U.head, qr, q_full);
+          tc::tma_load_3d_w(sq + i * QOPER + QWIDE, &mq_narrow, 64, U.head, qr, q_full);
         }
         for (int t = 0; t < U.tiles; ++t) {
           const int g = T + t, s = g % STAGES;
           if (g >= STAGES && !tc::wait_w(k_empty + s, (g / STAGES - 1) & 1, abort_flag)) { ok = false; break; }
-          tc::expect_tx_w(k_full + s, OPER);
-          tc::tma_load_3d_w(sk + s * OPER, &mk_wide, 0, U.kg, U.kr0 + t * TK, k_full + s);
-          tc::tma_load_3d_w(sk + s * OPER + WIDE, &mk_narrow, 64, U.kg, U.kr0 + t * TK, k_full + s);
+          tc::expect_tx_w(k_full + s, KOPER);
+          tc::tma_load_3d_w(sk + s * KOPER, &mk_wide, 0, U.kg, U.kr0 + t * TK, k_full + s);
+          tc::tma_load_3d_w(sk + s * KOPER + KWIDE, &mk_narrow, 64, U.kg, U.kr0 + t * TK, k_full + s);
         }
         T += U.tiles;
         ++qn;
@@ -193,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
           if (g >= STAGES && !tc::wait_w(v_empty + s, (g / STAGES - 1) & 1, abort_flag)) { ok = false; break; }
           tc::expect_tx_w(v_full + s, VOPER);
           tc::tma_load_3d_w(sv + s * VOPER, &mv, 0, U.kg, U.kr0 + t * TK, v_full + s);
-          tc::tma_load_3d_w(sv + s * VOPER + WIDE, &mv, 64, U.kg, U.kr0 + t * TK, v_full + s);
+          tc::tma_load_3d_w(sv + s * VOPER + VWIDE, &mv, 64, U.kg, U.kr0 + t * TK, v_full + s);
         }
         T += U.tiles;
       }
@@ -201,8 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       const int i = warp == 1 ? 0 : 1;
       constexpr uint32_t idesc_s = tc::instr_desc(TQ, TK, false);
       constexpr uint32_t idesc_o = tc::instr_desc(TQ, HD, true);
-      const uint32_t qa = smem_addr(sq + i * OPER);
-      const uint32_t s_tmem = tmem + i * 128, o_tmem = tmem + 256 + i * 128;
+      const uint32_t qa = smem_addr(sq + i * QOPER);
+      const uint32_t s_tmem = tmem + S_COL + 128 * i, o_tmem = tmem + O_COL + 128 * i;
       int T = 0, qn = 0;
       bool ok = true;
       for (int k = 0; ok && k * G < p.units; ++k) {
@@ -211,33 +236,29 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
         const Unit U(p, rank_slot, w);
         if (U.tiles == 0) continue;
         if (!tc::wait_w(q_full, qn & 1, abort_flag)) break;
-        // This tile's chain  S(t) -> softmax(t) -> P(t) V(t) -> S(t+1) -> ...; the tile counter g runs on across
-        // units, so S of a unit's first tile also waits for the previous unit's last P V.
         for (int t = 0; t <= U.tiles; ++t) {
-          if (t >= 1) {
-            const int g = T + t - 1, vs = g % STAGES;
-            ok = tc::wait_w(v_full + vs, (g / STAGES) & 1, abort_flag) && tc::wait_w(p_full + i, g & 1, abort_flag);
-            if (ok && t == 1 && qn >= 1)   // the first P V overwrites O_i: the previous unit's O_i has been read
-              ok = tc::wait_w(o_empty + i, (qn - 1) & 1, abort_flag);
-            if (!ok) break;
-            tc::fence_after();
-            tc::mma_pv128_w(o_tmem, s_tmem, tc::sw128_desc(smem_addr(sv + vs * VOPER), WIDE, 1024), idesc_o,
-                            t > 1 ? 1u : 0u);
-            tc::commit_w(pv_done + i);
-            tc::commit_w(v_empty + vs);
-          }
-          if (t < U.tiles) {
+          if (t < U.tiles) {   // S(t): its K tile has landed and the softmax has read S(t-1)
             const int g = T + t, ks = g % STAGES;
             ok = tc::wait_w(k_full + ks, (g / STAGES) & 1, abort_flag) &&
-                 (g == 0 || tc::wait_w(pv_done + i, (g - 1) & 1, abort_flag));   // S overwrites P(g - 1)
+                 (g == 0 || tc::wait_w(s_empty + i, (g - 1) & 1, abort_flag));
             if (!ok) break;
             tc::fence_after();
-            const uint32_t kb = smem_addr(sk + ks * OPER);
-            tc::mma_qk96_w(s_tmem, tc::sw128_desc(qa), tc::sw128_desc(kb), tc::sw64_desc(qa + WIDE),
-                           tc::sw64_desc(kb + WIDE), idesc_s);
+            const uint32_t kb = smem_addr(sk + ks * KOPER);
+            tc::mma_qk96_w(s_tmem, tc::sw128_desc(qa), tc::sw128_desc(kb), tc::sw64_desc(qa + QWIDE),
+                           tc::sw64_desc(kb + KWIDE), idesc_s);
             tc::commit_w(s_full + i);
             tc::commit_w(k_empty + ks);
             if (t == U.tiles - 1) tc::commit_w(q_empty);
+          }
+          if (t >= 1) {   // O += P(t-1) V(t-1); the unit's first product starts O afresh
+            const int g = T + t - 1, vs = g % STAGES;
+            ok = tc::wait_w(v_full + vs, (g / STAGES) & 1, abort_flag) && tc::wait_w(p_full + i, g & 1, abort_flag);
+            if (!ok) break;
+            tc::fence_after();
+            tc::mma_pv96_w(o_tmem, s_tmem + 96, o_tmem + 96, tc::sw128_desc(smem_addr(sv + vs * VOPER), VWIDE, 1024),
+                           idesc_o, t > 1 ? 1u : 0u);
+            tc::commit_w(pv_done + i);
+            tc::commit_w(v_empty + vs);
           }
         }
         T += U.tiles;
@@ -258,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-    const uint32_t ts = tmem + lanes + i * 128, to = tmem + lanes + 256 + i * 128;
+    const uint32_t ts = tmem + lanes + S_COL + 128 * i, to = tmem + lanes + O_COL + 128 * i;
     const float sl2 = p.scale_log2;
     int T = 0;
     bool ok = true;
@@ -278,30 +299,32 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
         const int g = T + t;
         if (!tc::wait(s_full + i, g & 1, abort_flag)) { ok = false; break; }
         tc::fence_after();
-        uint32_t r[4][32];
+        uint32_t r[3][32];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) tc::ld32(ts + c4 * 32, r[c4]);
+        for (int c3 = 0; c3 < 3; ++c3) tc::ld32(ts + c3 * 32, r[c3]);
         tc::wait_ld();
+        tc::fence_before();
+        tc::mbar_arrive(s_empty + i);   // S_i(t+1) may now be computed into the same columns
         const int key0 = t * TK;
         if (key0 + TK > U.length) {
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4)
+          for (int c3 = 0; c3 < 3; ++c3)
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (key0 + c4 * 32 + j >= U.length) r[c4][j] = __float_as_uint(-INFINITY);
+              if (key0 + c3 * 32 + j >= U.length) r[c3][j] = __float_as_uint(-INFINITY);
         }
-        float mc[4];
+        float mc[3];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          float a = __uint_as_float(r[c4][0]), b = __uint_as_float(r[c4][1]);
+        for (int c3 = 0; c3 < 3; ++c3) {
+          float a = __uint_as_float(r[c3][0]), b = __uint_as_float(r[c3][1]);
 #pragma unroll
           for (int j = 2; j < 32; j += 4) {
-            a = tc::fmax3(a, __uint_as_float(r[c4][j]), __uint_as_float(r[c4][j + 1]));
-            b = tc::fmax3(b, __uint_as_float(r[c4][j + 2]), __uint_as_float(r[c4][j + 3]));
+            a = tc::fmax3(a, __uint_as_float(r[c3][j]), __uint_as_float(r[c3][j + 1]));
+            b = tc::fmax3(b, __uint_as_float(r[c3][j + 2]), __uint_as_float(r[c3][j + 3]));
           }
-          mc[c4] = fmaxf(a, b);
+          mc[c3] = fmaxf(a, b);
         }
-        const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])) * sl2;
+        const float mx = tc::fmax3(mc[0], mc[1], mc[2]) * sl2;
         // Raise the exponent base only when the row max outgrows it by more than 8 (warp-uniform rescale of O).
         const bool raise = mx > m_used + 8.f;
         const bool any_raise = __any_sync(0xffffffffu, raise);
@@ -311,34 +334,41 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
           alpha = tc::ex2(m_used - m_new);   // m_used = -inf on the first tile: alpha = 0
           m_used = m_new;
         }
-        // P = 2^(S*scale - m) as bf16 pairs: keys 64h .. 64h+63 -> TMEM columns [32h, +32) of S_i.
+        // P = 2^(S*scale - m) as bf16 pairs: keys 2j, 2j+1 -> P column j (0-31 after S_i, 32-47 after O_i).
         const float2 scale2 = make_float2(sl2, sl2), nbase2 = make_float2(-m_used, -m_used);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        uint32_t packed[48];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t packed[32];
-#pragma unroll
-          for (int j = 0; j < 64; j += 2) {
-            const int c4 = 2 * h + (j >> 5), jj = j & 31;
-            const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[c4][jj]), __uint_as_float(r[c4][jj + 1])),
-                                        scale2, nbase2);
-            const float2 e = make_float2(tc::ex2(x.x), tc::ex2(x.y));
-            acc[(j >> 1) & 3] = __fadd2_rn(acc[(j >> 1) & 3], e);
-            packed[j >> 1] = tc::pack_bf16x2(e.x, e.y);
-          }
-          tc::st32(ts + h * 32, packed);
+        for (int j = 0; j < TK; j += 2) {
+          const int c3 = j >> 5, jj = j & 31;
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[c3][jj]), __uint_as_float(r[c3][jj + 1])), scale2,
+                                      nbase2);
+          const float2 e = ((j >> 1) & 7) < kFmaPairs ? exp2_fma2(x) : make_float2(tc::ex2(x.x), tc::ex2(x.y));
+          acc[(j >> 1) & 3] = __fadd2_rn(acc[(j >> 1) & 3], e);
+          packed[j >> 1] = tc::pack_bf16x2(e.x, e.y);
         }
-        // O_i holds the products of this unit's tiles < t (the P_i V of tile t-1 completed before S_i(t) was issued).
+        // P_i(t-1) V(t-1) has completed: P_i may be overwritten and O_i holds the products of tiles < t.
+        if (g >= 1 && !tc::wait(pv_done + i, (g - 1) & 1, abort_flag)) { ok = false; break; }
+        tc::fence_after();
         if (any_raise && t >= 1) {
 #pragma unroll
-          for (int c4 = 0; c4 < HD / 32; ++c4) {
+          for (int c3 = 0; c3 < HD / 32; ++c3) {
             uint32_t o[32];
-            tc::ld32(to + c4 * 32, o);
+            tc::ld32(to + c3 * 32, o);
             tc::wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-            tc::st32(to + c4 * 32, o);
+            tc::st32(to + c3 * 32, o);
           }
+        }
+        {
+          uint32_t lo[32], hi[16];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) lo[j] = packed[j];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) hi[j] = packed[32 + j];
+          tc::st32(ts + 96, lo);
+          tc::st16(to + 96, hi);
         }
         tc::wait_st();
         const float2 s01 = __fadd2_rn(acc[0], acc[1]), s23 = __fadd2_rn(acc[2], acc[3]);
@@ -351,24 +381,23 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       tc::fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll
-      for (int c4 = 0; c4 < HD / 32; ++c4) {
+      for (int c3 = 0; c3 < HD / 32; ++c3) {
         uint32_t o[32];
-        tc::ld32(to + c4 * 32, o);
+        tc::ld32(to + c3 * 32, o);
         tc::wait_ld();
         if (i < U.nq) {
 #pragma unroll
           for (int k4 = 0; k4 < 4; ++k4) {
             const float* f = reinterpret_cast<const float*>(o) + 8 * k4;
-            dst[c4 * 4 + k4] = make_uint4(tc::pack_bf16x2(f[0] * inv, f[1] * inv),
+            dst[c3 * 4 + k4] = make_uint4(tc::pack_bf16x2(f[0] * inv, f[1] * inv),
                                           tc::pack_bf16x2(f[2] * inv, f[3] * inv),
                                           tc::pack_bf16x2(f[4] * inv, f[5] * inv),
                                           tc::pack_bf16x2(f[6] * inv, f[7] * inv));
           }
         }
       }
-      // O_i has been read: the next unit's first P V may overwrite it.
-      tc::fence_before();
-      tc::mbar_arrive(o_empty + i);
+      // O_i has been read (tcgen05.wait::ld above); the next unit's first P V, which overwrites it, is issued only
+      // after this warpgroup's next p_full arrival.
       T += U.tiles;
     }
     if (!ok && lane == 0) atomicOr(&g_svx_attention_timeouts, SVX_STATUS_WAIT_TIMEOUT);

@@ -166,6 +166,28 @@ __device__ __forceinline__ void mma_pv128_w(uint32_t d, uint32_t a, uint64_t v, 
       ::"r"(d), "r"(a), "l"(v), "r"(idesc), "r"(acc));
 }
 
+// O += P V over K = 96 keys: A = P in TMEM (8 columns per K-step; steps 0-3 at `a_lo`, steps 4-5 at `a_hi`), B = V
+// MN-major 128B-swizzled (16 keys x 128 B = 2048 bytes per K-step, +128 in descriptor units).
+__device__ __forceinline__ void mma_pv96_w(uint32_t d, uint32_t a_lo, uint32_t a_hi, uint64_t v, uint32_t idesc,
+                                           uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, pt;\n\t.reg .b64 b;\n\t.reg .b32 t;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p0, %5, 0;\n\tsetp.eq.b32 pt, %4, %4;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %4, p0;\n\t"
+      "add.s32 t, %1, 8;\n\tadd.s64 b, %3, 128;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %4, pt;\n\t"
+      "add.s32 t, %1, 16;\n\tadd.s64 b, %3, 256;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %4, pt;\n\t"
+      "add.s32 t, %1, 24;\n\tadd.s64 b, %3, 384;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %4, pt;\n\t"
+      "add.s64 b, %3, 512;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], b, %4, pt;\n\t"
+      "add.s32 t, %2, 8;\n\tadd.s64 b, %3, 640;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %4, pt;\n\t}"
+      ::"r"(d), "r"(a_lo), "r"(a_hi), "l"(v), "r"(idesc), "r"(acc));
+}
+
 __device__ __forceinline__ void commit_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
@@ -199,6 +221,15 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
         "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
         "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
         "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 
