@@ -54,15 +54,51 @@ def dist_env():
 # ------------------------------------------------------------------------------------------------- clocks
 
 class Clocks:
-    """nvidia-smi samples of SM clocks and throttle reasons during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML in a thread every 20 ms (read-only
+    queries, the device found by its UUID), else `nvidia-smi -lms 200`. One sample is also taken on entry and exit,
+    so a short timed region still has a record."""
     QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
              'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
              'clocks_event_reasons.sw_power_cap')
+    # NVML clocks-event reason bits (nvml.h): the ones that reject or annotate a measurement.
+    REASONS = {0x8: 'hw_slowdown', 0x40: 'hw_thermal_slowdown', 0x20: 'sw_thermal_slowdown', 0x4: 'sw_power_cap'}
 
     def __init__(self, index):
-        self.index, self.rows, self.proc = index, [], None
+        self.index, self.rows, self.proc, self.nvml, self.stop = index, [], None, None, threading.Event()
+
+    def _nvml_handle(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith('GPU-') else 'GPU-' + uuid)
+        except Exception:
+            return None
+
+    def _sample(self):
+        nv, h = self.nvml
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.rows.append(dict(sm=float(sm), max=float(mx), reasons={n for b, n in self.REASONS.items() if bits & b}))
+
+    def _poll(self):
+        while not self.stop.wait(0.02):
+            try:
+                self._sample()
+            except Exception:
+                return
 
     def __enter__(self):
+        self.nvml = self._nvml_handle()
+        if self.nvml is not None:
+            try:
+                self._sample()
+                self.thread = threading.Thread(target=self._poll, daemon=True)
+                self.thread.start()
+                return self
+            except Exception:
+                self.nvml = None
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.QUERY}',
                                           '--format=csv,noheader,nounits', '-lms', '200'],
@@ -74,10 +110,21 @@ class Clocks:
         return self
 
     def _read(self):
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
         for line in self.proc.stdout:
-            self.rows.append([v.strip() for v in line.split(',')])
+            r = [v.strip() for v in line.split(',')]
+            if len(r) >= 9 and r[1].replace('.', '').isdigit():
+                self.rows.append(dict(sm=float(r[1]), max=float(r[2]) if r[2].replace('.', '').isdigit() else None,
+                                      reasons={n for n, v in zip(names, r[5:9]) if v.lower() == 'active'}))
 
     def __exit__(self, *exc):
+        if self.nvml is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self._sample()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -87,13 +134,13 @@ class Clocks:
 
     def summary(self):
         if not self.rows:
-            return dict(sm_mhz=None, sm_max_mhz=None, reasons=['nvidia-smi unavailable'], samples=0)
-        sm = [float(r[1]) for r in self.rows if r[1].replace('.', '').isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace('.', '').isdigit()]
-        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.strip().lower() == 'active'})
-        return dict(sm_mhz=float(np.median(sm)) if sm else None, sm_max_mhz=max(mx) if mx else None,
-                    reasons=reasons, samples=len(self.rows))
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=['no clock samples (NVML and nvidia-smi unavailable)'],
+                        samples=0)
+        sm = [r['sm'] for r in self.rows]
+        mx = [r['max'] for r in self.rows if r['max']]
+        return dict(sm_mhz=float(np.median(sm)), sm_max_mhz=max(mx) if mx else None,
+                    reasons=sorted(set().union(*(r['reasons'] for r in self.rows))), samples=len(self.rows),
+                    source='nvml' if self.nvml is not None else 'nvidia-smi')
 
 
 # ------------------------------------------------------------------------------------------------ ours
@@ -230,6 +277,9 @@ def time_kernels(cfg, forward, batch, lengths):
         return a.elapsed_time(b) / reps * 1e-3
 
     mean_len = float(np.mean(lengths))
+    # The engine's cross-attention plan for these lengths (the same host LPT assignment svx_engine_set_lengths builds).
+    plan = ops.attention_plan(lengths, SLOTS, heads, cfg.patches, k0.shape[2],
+                              torch.cuda.get_device_properties(dev).multi_processor_count, dev)
     kernels = {
         'gemm_qkv_rope': (lambda: ops.gemm(ws['h'], bw['attn.qkv.weight'], bw['attn.qkv.bias'], _lib.EPI_ROPE,
                                            out=ws['qkv'], rope=tables, rope_cols=2 * d, rows_per_slot=cfg.patches),
@@ -253,7 +303,7 @@ def time_kernels(cfg, forward, batch, lengths):
         'attention_cross': (lambda: ops.attention(ws['qkv'], k0, v0, SLOTS, heads, cfg.patches, k0.shape[2],
                                                   q_row_stride=d, kv_slot_stride=heads * k0.shape[2] * 96,
                                                   kv_head_stride=k0.shape[2] * 96, kv_row_stride=96,
-                                                  lengths=forward.engine.lengths, out=ws['attn']),
+                                                  lengths=forward.engine.lengths, out=ws['attn'], plan=plan),
                             4.0 * SLOTS * heads * cfg.patches * mean_len * 96, 12),
         'ease_scores': (lambda: ops.ease_scores(forward.logits, batch.status, out=batch.scores),
                         float(forward.logits.numel() * 2 + batch.scores.numel() * 4), 1),

@@ -174,7 +174,16 @@ SVX_API int svx_gemm(const uint16_t* A, const uint16_t* W, uint16_t* out, int M,
 SVX_API int svx_attention(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
                           int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride,
                           const int32_t* lengths, int slots, int heads, int queries, int keys, uint16_t* out,
-                          void* stream);
+                          const int32_t* plan, int plan_ctas, void* stream);
+/* Work-unit assignment for svx_attention (plan, device copy) on plan_ctas CTAs. A unit is two 128-query tiles of one
+ * (slot, head); units go longest first to the least-loaded CTA (cost: key tiles + 1), which balances slots of unequal
+ * key lengths. plan = [G + 1 offsets][units natural ids (slot*heads + head)*pairs + pair], G = min(ctas, units).
+ * The plan affects only which CTA computes a unit, never the result: a plan built for other lengths stays correct.
+ * lengths: host array [slots] or NULL (all `keys`). plan_ints returns the ints a plan takes (0: bad shape).
+ * No reference counterpart (FlexAttention schedules its own blocks, `fast_ops.py:104-108`). */
+SVX_API int svx_attention_plan_ints(int slots, int heads, int queries, int ctas);
+SVX_API int svx_attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas,
+                               int32_t* plan, int capacity);
 
 /* ------------------------------------------------------------------------------------------------ the engine */
 
@@ -222,6 +231,11 @@ SVX_API int svx_engine_create(const svx_engine_config* config, const svx_engine_
 /* One slot-batched forward of the first n slots (`FastSlotForward.forward`, `fast_ops.py:274-308`):
  * tokens [n][Y][Z][X] int16 -> logits [n][V][Y][Z][X] bf16. */
 SVX_API int svx_engine_forward(svx_engine* engine, int n, const int16_t* tokens, uint16_t* logits, void* stream);
+/* Host key lengths of every slot [slots] (the values written to weights->lengths): rebuilds the cross-attention
+ * work plans of every bucket and copies them to the engine's device table on `stream` (stream-ordered before later
+ * forwards). Optional: without it the plans stay those of equal lengths, which is correct but less balanced.
+ * Called where `FastSlotForward._write` stores a slot's length (`fast_ops.py:241-250`). */
+SVX_API int svx_engine_set_lengths(svx_engine* engine, const int32_t* lengths, void* stream);
 /* Number of kernel launches one svx_engine_forward(n) enqueues. */
 SVX_API int svx_engine_launches(const svx_engine* engine, int n);
 SVX_API void svx_engine_destroy(svx_engine* engine);

@@ -86,10 +86,13 @@ _SIGNATURES = {
     'svx_layernorm_modulate': (c_int, [c_ptr, c_int, c_int, ctypes.c_float, c_ptr, c_ptr, c_ptr, c_ptr]),
     'svx_gemm': (c_int, [c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, ctypes.POINTER(EpilogueArgs), c_ptr]),
     'svx_attention': (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_int, c_int, c_int, c_int,
-                              c_ptr, c_ptr]),
+                              c_ptr, c_ptr, c_int, c_ptr]),
+    'svx_attention_plan_ints': (c_int, [c_int, c_int, c_int, c_int]),
+    'svx_attention_plan': (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_int, c_ptr, c_int]),
     'svx_engine_create': (c_int, [ctypes.POINTER(EngineConfig), ctypes.POINTER(EngineWeights),
                                   ctypes.POINTER(EngineWorkspace), ctypes.POINTER(c_ptr)]),
     'svx_engine_forward': (c_int, [c_ptr, c_int, c_ptr, c_ptr, c_ptr]),
+    'svx_engine_set_lengths': (c_int, [c_ptr, c_ptr, c_ptr]),
     'svx_engine_launches': (c_int, [c_ptr, c_int]),
     'svx_engine_destroy': (None, [c_ptr]),
 }

@@ -29,6 +29,10 @@
 // library's timeout word and skips the rest of the CTA's work.
 #include <math.h>
 
+#include <algorithm>
+#include <queue>
+#include <vector>
+
 #include "common.cuh"
 #include "gemm.cuh"
 #include "tc.cuh"
@@ -79,18 +83,23 @@ struct AttnParams {
   int slots, heads, queries, keys, pairs, units;
   int kv_mode;  // 0: K/V groups = heads, rows = slot*keys + key; 1: groups = slot*heads + head, rows = key
   const int32_t* lengths;
+  // Optional unit assignment built on the host (attention_plan): [G + 1] offsets into the unit list that follows,
+  // CTA c taking units [plan[c], plan[c + 1]); ids are natural, (slot * heads + head) * pairs + pair. Null: the
+  // boustrophedon passes over the longest-first numbering.
+  const int32_t* plan;
   uint16_t* out;
   float scale_log2;
 };
 
-// One work unit: two 128-query tiles of one (slot, head). Units are numbered longest slot first; a tile index past
-// the slot's queries (odd tile counts) repeats the last tile, whose result is not stored.
+// One work unit: two 128-query tiles of one (slot, head). Without a plan, units are numbered longest slot first; with
+// one, naturally. A tile index past the slot's queries (odd tile counts) repeats the last tile, whose result is not
+// stored.
 struct Unit {
   int slot, head, q0, nq, length, tiles, kg, kr0;
   __device__ __forceinline__ Unit(const AttnParams& p, const int* rank_slot, int w) {
     const int per_slot = p.heads * p.pairs;
     const int rem = w % per_slot;
-    slot = rank_slot[w / per_slot];
+    slot = p.plan ? w / per_slot : rank_slot[w / per_slot];
     head = rem / p.pairs;
     q0 = (rem % p.pairs) * 2 * TQ;
     nq = min(2, (p.queries - q0) / TQ);
@@ -106,6 +115,22 @@ struct Unit {
 __device__ __forceinline__ int unit_of(int c, int k, int G, int units) {
   const int w = k * G + ((k & 1) ? G - 1 - c : c);
   return w < units ? w : -1;
+}
+
+// How many units CTA c takes (an upper bound of passes without a plan), and its k-th unit (-1: none). Plan entries
+// are clamped to the unit range, so a malformed plan can drop or repeat units but never index out of bounds.
+__device__ __forceinline__ int units_of(const AttnParams& p, int c, int G) {
+  if (!p.plan) return (p.units + G - 1) / G;
+  const int b = min(max(__ldg(p.plan + c), 0), p.units);
+  const int e = min(max(__ldg(p.plan + c + 1), b), p.units);
+  return e - b;
+}
+
+__device__ __forceinline__ int unit_at(const AttnParams& p, int c, int k, int G) {
+  if (!p.plan) return unit_of(c, k, G, p.units);
+  const int b = min(max(__ldg(p.plan + c), 0), p.units);
+  const int w = __ldg(p.plan + G + 1 + b + k);
+  return (w >= 0 && w < p.units) ? w : -1;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_constant__ CUtensorMap mq_wide,
@@ -184,8 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     if (warp == 0) {   // Q and the K ring
       int T = 0, qn = 0;
       bool ok = true;
-      for (int k = 0; ok && k * G < p.units; ++k) {
-        const int w = unit_of(c, k, G, p.units);
+      const int nk = units_of(p, c, G);
+      for (int k = 0; ok && k < nk; ++k) {
+        const int w = unit_at(p, c, k, G);
         if (w < 0) continue;
         const Unit U(p, rank_slot, w);
         if (U.tiles == 0) continue;
@@ -209,8 +235,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     } else if (warp == 2) {   // the V ring
       int T = 0;
       bool ok = true;
-      for (int k = 0; ok && k * G < p.units; ++k) {
-        const int w = unit_of(c, k, G, p.units);
+      const int nk = units_of(p, c, G);
+      for (int k = 0; ok && k < nk; ++k) {
+        const int w = unit_at(p, c, k, G);
         if (w < 0) continue;
         const Unit U(p, rank_slot, w);
         for (int t = 0; t < U.tiles; ++t) {
@@ -230,8 +257,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       const uint32_t s_tmem = tmem + S_COL + 128 * i, o_tmem = tmem + O_COL + 128 * i;
       int T = 0, qn = 0;
       bool ok = true;
-      for (int k = 0; ok && k * G < p.units; ++k) {
-        const int w = unit_of(c, k, G, p.units);
+      const int nk = units_of(p, c, G);
+      for (int k = 0; ok && k < nk; ++k) {
+        const int w = unit_at(p, c, k, G);
         if (w < 0) continue;
         const Unit U(p, rank_slot, w);
         if (U.tiles == 0) continue;
@@ -283,8 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     const float sl2 = p.scale_log2;
     int T = 0;
     bool ok = true;
-    for (int k = 0; ok && k * G < p.units; ++k) {
-      const int w = unit_of(c, k, G, p.units);
+    const int nk = units_of(p, c, G);
+    for (int k = 0; ok && k < nk; ++k) {
+      const int w = unit_at(p, c, k, G);
       if (w < 0) continue;
       const Unit U(p, rank_slot, w);
       const int qrow = U.q0 + i * TQ + row;
@@ -410,9 +439,86 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
 
 }  // namespace
 
+int attention_plan_ints(int slots, int heads, int queries, int ctas) {
+  if (slots <= 0 || heads <= 0 || queries <= 0 || queries % TQ || ctas <= 0) return 0;
+  const int64_t units = (int64_t)slots * heads * ((queries / TQ + 1) / 2);
+  if (units > (1 << 28)) return 0;
+  return (int)(std::min<int64_t>(ctas, units) + 1 + units);
+}
+
+int attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas, int32_t* plan,
+                   int capacity) {
+  const int need = attention_plan_ints(slots, heads, queries, ctas);
+  SVX_REQUIRE(need > 0 && keys > 0, "attention_plan: bad shape");
+  SVX_REQUIRE(plan && capacity >= need, "attention_plan: plan buffer too small");
+  const int pairs = (queries / TQ + 1) / 2, per_slot = heads * pairs, units = slots * per_slot;
+  const int G = std::min(ctas, units);
+  // Cost of a unit in quarter key tiles: its tiles plus one tile of per-unit work (Q load, ring fill, epilogue);
+  // a unit without keys only writes zeros.
+  std::vector<int64_t> cost(units);
+  for (int u = 0; u < units; ++u) {
+    const int len = lengths ? std::max(0, std::min(lengths[u / per_slot], keys)) : keys;
+    const int tiles = (len + TK - 1) / TK;
+    cost[u] = tiles ? 4 * (int64_t)tiles + 4 : 1;
+  }
+  std::vector<int> order(units);
+  for (int u = 0; u < units; ++u) order[u] = u;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+  // Longest processing time first (LPT): each unit to the least-loaded CTA (lowest index on ties).
+  std::priority_queue<std::pair<int64_t, int>, std::vector<std::pair<int64_t, int>>, std::greater<>> heap;
+  for (int c = 0; c < G; ++c) heap.emplace(0, c);
+  std::vector<int> owner(units), trial(units);
+  int64_t best = 0, total = 0;
+  for (int u : order) {
+    auto [load, c] = heap.top();
+    heap.pop();
+    owner[u] = c;
+    heap.emplace(load + cost[u], c);
+    best = std::max(best, load + cost[u]);
+    total += cost[u];
+  }
+  // MULTIFIT: the smallest capacity at which first-fit decreasing packs the units into G CTAs, by bisection between
+  // the lower bound and the LPT makespan; kept when it beats LPT (a few long slots among many short ones).
+  std::vector<int64_t> bin(G);
+  auto first_fit = [&](int64_t cap) {
+    std::fill(bin.begin(), bin.end(), 0);
+    int open = 0;
+    for (int u : order) {
+      int c = 0;
+      while (c < open && bin[c] + cost[u] > cap) ++c;
+      if (c == open) {
+        if (open == G) return false;
+        ++open;
+      }
+      bin[c] += cost[u];
+      trial[u] = c;
+    }
+    return true;
+  };
+  int64_t lo = std::max<int64_t>(cost[order[0]], (total + G - 1) / G), hi = best - 1;
+  while (lo <= hi) {
+    const int64_t mid = lo + (hi - lo) / 2;
+    if (first_fit(mid)) {
+      owner = trial;
+      best = mid;
+      hi = mid - 1;
+    } else {
+      lo = mid + 1;
+    }
+  }
+  std::vector<int> count(G + 1, 0);
+  for (int u = 0; u < units; ++u) ++count[owner[u]];
+  plan[0] = 0;
+  for (int c = 0; c < G; ++c) plan[c + 1] = plan[c] + count[c];
+  std::vector<int> fill(plan, plan + G);
+  for (int u : order) plan[G + 1 + fill[owner[u]]++] = u;   // each CTA's units longest first
+  return SVX_OK;
+}
+
 int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
                   int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride, const int32_t* lengths,
-                  int slots, int heads, int queries, int keys, uint16_t* out, cudaStream_t stream) {
+                  int slots, int heads, int queries, int keys, uint16_t* out, const int32_t* plan, int plan_ctas,
+                  cudaStream_t stream) {
   SVX_REQUIRE(queries % TQ == 0, "attention: queries must be a multiple of 128");
   int kv_mode;
   uint64_t groups, rows, group_stride, row_stride;
@@ -448,10 +554,13 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
   }
   const int pairs = (queries / TQ + 1) / 2;
   const int units = slots * heads * pairs;
-  AttnParams prm{slots, heads, queries, keys, pairs, units, kv_mode, lengths, out,
+  SVX_REQUIRE(!plan || (plan_ctas >= 1 && plan_ctas == std::min(plan_ctas, units)),
+              "attention: a plan needs 1 <= ctas <= units");
+  AttnParams prm{slots, heads, queries, keys, pairs, units, kv_mode, lengths, plan, out,
                  (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
-  return launch_dependent("attention_tc_kernel", attention_tc_kernel, dim3(units < sms ? units : sms), dim3(kThreads),
-                          kSmem, stream, m[0], m[1], m[2], m[3], m[4], prm);
+  const int grid = plan ? plan_ctas : (units < sms ? units : sms);
+  return launch_dependent("attention_tc_kernel", attention_tc_kernel, dim3(grid), dim3(kThreads), kSmem, stream,
+                          m[0], m[1], m[2], m[3], m[4], prm);
 }
 
 uint32_t attention_timeouts() {
@@ -464,10 +573,19 @@ uint32_t attention_timeouts() {
 
 using namespace svx;
 
+extern "C" int svx_attention_plan_ints(int slots, int heads, int queries, int ctas) {
+  return attention_plan_ints(slots, heads, queries, ctas);
+}
+
+extern "C" int svx_attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas,
+                                  int32_t* plan, int capacity) {
+  return attention_plan(lengths, slots, heads, queries, keys, ctas, plan, capacity);
+}
+
 extern "C" int svx_attention(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
                              int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride,
                              const int32_t* lengths, int slots, int heads, int queries, int keys, uint16_t* out,
-                             void* stream) {
+                             const int32_t* plan, int plan_ctas, void* stream) {
   SVX_REQUIRE(q && k && v && out && slots > 0 && heads > 0 && queries > 0 && keys > 0, "svx_attention: bad arguments");
   SVX_REQUIRE(q_row_stride % 8 == 0 && kv_row_stride % 8 == 0 && kv_head_stride % 8 == 0 && kv_slot_stride % 8 == 0,
               "svx_attention: strides must be multiples of 8 elements");
@@ -475,5 +593,5 @@ extern "C" int svx_attention(const uint16_t* q, int64_t q_row_stride, const uint
                           reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
   SVX_REQUIRE((align & 15u) == 0, "svx_attention: operands must be 16-byte aligned");
   return attention_run(q, q_row_stride, k, v, kv_slot_stride, kv_head_stride, kv_row_stride, lengths, slots, heads,
-                       queries, keys, out, as_stream(stream));
+                       queries, keys, out, plan, plan_ctas, as_stream(stream));
 }

@@ -24,6 +24,14 @@ struct svx_engine {
   // GEMM plans: per backbone layer [qkv, proj, fc1, fc2]; per control layer [qkv, proj, fc1, fc2, query, cproj, zero].
   std::vector<svx::GemmPlan> bplan, cplan;
   svx::GemmPlan head;
+  // Cross-attention work plans (svx::attention_plan on plan_ctas CTAs), one row of plan_stride ints per bucket
+  // n = 1..slots, rebuilt on the host by svx_engine_set_lengths and copied to plan_dev.
+  int32_t* plan_dev = nullptr;
+  int plan_stride = 0, plan_ctas = 0;
+  std::vector<int32_t> plan_host;
+  ~svx_engine() {
+    if (plan_dev) cudaFree(plan_dev);
+  }
 };
 
 namespace svx {
@@ -66,7 +74,7 @@ int run_block(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* 
   if ((rc = gemm_run(plans[0], rows, ws.qkv, e, s))) return rc;
   const int64_t ld = 3 * d;
   if ((rc = attention_run(ws.qkv, ld, ws.qkv + d, ws.qkv + 2 * d, (int64_t)E.patches * ld, HD, ld, nullptr, n,
-                          E.cfg.heads, E.patches, E.patches, ws.attn, s)))
+                          E.cfg.heads, E.patches, E.patches, ws.attn, nullptr, 0, s)))
     return rc;
   e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);
   e.gate = bw.gate1; e.residual = x;
@@ -90,12 +98,25 @@ int run_cross(const svx_engine& E, const svx_cross_weights& cw, const GemmPlan* 
   e.rope_cols = d; e.rows_per_slot = E.patches; e.head_dim = HD;
   if ((rc = gemm_run(plans[0], rows, ws.qkv, e, s))) return rc;
   const int64_t cap = E.cfg.key_capacity;
+  const int units = n * E.cfg.heads * ((E.patches / 128 + 1) / 2);
+  const int32_t* plan = E.plan_dev ? E.plan_dev + (size_t)(n - 1) * E.plan_stride : nullptr;
   if ((rc = attention_run(ws.qkv, d, cw.k, cw.v, (int64_t)E.cfg.heads * cap * HD, cap * HD, HD, E.w.lengths, n,
-                          E.cfg.heads, E.patches, E.cfg.key_capacity, ws.attn, s)))
+                          E.cfg.heads, E.patches, E.cfg.key_capacity, ws.attn, plan, std::min(E.plan_ctas, units),
+                          s)))
     return rc;
   e = epi(SVX_EPI_RESIDUAL, cw.proj_b);
   e.residual = ws.xc;
   return gemm_run(plans[1], rows, ws.xc, e, s);
+}
+
+// Plans of every bucket n = 1..slots for the host key lengths (NULL: all slots at the key capacity).
+int build_plans(svx_engine& E, const int32_t* lengths) {
+  for (int n = 1; n <= E.cfg.slots; ++n) {
+    const int rc = attention_plan(lengths, n, E.cfg.heads, E.patches, E.cfg.key_capacity, E.plan_ctas,
+                                  E.plan_host.data() + (size_t)(n - 1) * E.plan_stride, E.plan_stride);
+    if (rc) return rc;
+  }
+  return SVX_OK;
 }
 
 }  // namespace
@@ -150,6 +171,22 @@ extern "C" int svx_engine_create(const svx_engine_config* config, const svx_engi
     if (!rc) e->cplan.push_back(p);
   }
   if (!rc) rc = gemm_plan(&e->head, e->ws.h, weights->head_w, e->rows_max, c.classes * 64, c.d, 0);
+  if (!rc && c.n_control) {
+    int device = 0, sms = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (err == cudaSuccess) {
+      e->plan_ctas = sms;
+      e->plan_stride = attention_plan_ints(c.slots, c.heads, e->patches, sms);
+      e->plan_host.assign((size_t)c.slots * e->plan_stride, 0);
+      rc = e->plan_stride > 0 ? build_plans(*e, nullptr) : fail(SVX_ERR_INVALID, "svx_engine_create: bad plan shape");
+      if (!rc) err = cudaMalloc(&e->plan_dev, e->plan_host.size() * sizeof(int32_t));
+      if (!rc && err == cudaSuccess)
+        err = cudaMemcpy(e->plan_dev, e->plan_host.data(), e->plan_host.size() * sizeof(int32_t),
+                         cudaMemcpyHostToDevice);
+    }
+    if (!rc && err != cudaSuccess) rc = fail(SVX_ERR_CUDA, cudaGetErrorString(err));
+  }
   if (rc) {
     delete e;
     return rc;
@@ -193,6 +230,17 @@ extern "C" int svx_engine_forward(svx_engine* E, int n, const int16_t* tokens, u
   e.classes = c.classes;
   e.height = c.height; e.depth = c.depth; e.width = c.width; e.patch = 4;
   return gemm_run(E->head, rows, logits, e, s);
+}
+
+extern "C" int svx_engine_set_lengths(svx_engine* E, const int32_t* lengths, void* stream) {
+  SVX_REQUIRE(E && lengths, "svx_engine_set_lengths: null argument");
+  if (!E->plan_dev) return SVX_OK;   // no cross-attention layers
+  const int rc = build_plans(*E, lengths);
+  if (rc) return rc;
+  // Pageable source: the runtime stages it before returning, so plan_host may be rebuilt by the next call.
+  SVX_CHECK_CUDA(cudaMemcpyAsync(E->plan_dev, E->plan_host.data(), E->plan_host.size() * sizeof(int32_t),
+                                 cudaMemcpyHostToDevice, as_stream(stream)));
+  return SVX_OK;
 }
 
 extern "C" int svx_engine_launches(const svx_engine* E, int n) {

@@ -34,7 +34,12 @@ uint32_t attention_timeouts();
 int epi_from_args(const svx_epilogue_args* e, EpiParams* ep, int N);
 int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
                   int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride, const int32_t* lengths,
-                  int slots, int heads, int queries, int keys, uint16_t* out, cudaStream_t stream);
+                  int slots, int heads, int queries, int keys, uint16_t* out, const int32_t* plan, int plan_ctas,
+                  cudaStream_t stream);
+// Host-side LPT assignment of attention work units to CTAs (layout in attention.cu); ints a plan takes.
+int attention_plan_ints(int slots, int heads, int queries, int ctas);
+int attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas, int32_t* plan,
+                   int capacity);
 int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int width, int classes, int d,
                     const uint16_t* table_b, const uint16_t* bias_b, const uint16_t* add_b, uint16_t* out_b,
                     const uint16_t* table_c, const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c,

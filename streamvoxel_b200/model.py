@@ -399,6 +399,7 @@ class Engine:
         self.kv = [(torch.zeros((self.slots, cfg.heads, self.key_capacity, 96), **bf),
                     torch.zeros((self.slots, cfg.heads, self.key_capacity, 96), **bf)) for _ in range(n_control)]
         self.lengths = torch.zeros(self.slots, dtype=torch.int32, device=dev)
+        self.host_lengths = (ctypes.c_int32 * self.slots)()
         self.ws = {n: torch.zeros((rows, w), **bf) for n, w in
                    (('xb', cfg.d), ('xc', cfg.d), ('h', cfg.d), ('qkv', 3 * cfg.d), ('attn', cfg.d), ('mlp', cfg.mlp))}
         p = lambda t: t.data_ptr()
@@ -440,6 +441,9 @@ class Engine:
             sk[index, :, length:].zero_()
             sv[index, :, length:].zero_()
         self.lengths[index] = length
+        self.host_lengths[index] = length
+        check(_lib.load().svx_engine_set_lengths(self.handle, self.host_lengths, _lib.stream_ptr(None)),
+              'svx_engine_set_lengths')
 
     def forward(self, n, tokens, logits, stream=None):
         """Logits of the first n slots into `logits` [>= n, V, Y, Z, X] bf16 from int16 tokens."""

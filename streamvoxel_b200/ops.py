@@ -170,13 +170,31 @@ def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None,
     return out
 
 
+def attention_plan(lengths, slots, heads, queries, keys, ctas, device=None):
+    """Work-unit plan of `svx_attention_plan` for host key lengths (sequence or None) on `ctas` CTAs. Returns the
+    int32 plan (on `device`, or a host tensor) and the CTA count the launch must use."""
+    lib = _lib.load()
+    size = lib.svx_attention_plan_ints(slots, heads, queries, ctas)
+    if size <= 0:
+        raise ValueError('attention_plan: bad shape')
+    plan = torch.empty(size, dtype=torch.int32)
+    host = None if lengths is None else torch.as_tensor(list(lengths), dtype=torch.int32)
+    check(lib.svx_attention_plan(ptr(host), slots, heads, queries, keys, ctas, ptr(plan), size),
+          'svx_attention_plan')
+    units = slots * heads * ((queries // 128 + 1) // 2)
+    return (plan if device is None else plan.to(device)), min(ctas, units)
+
+
 def attention(q, k, v, slots, heads, queries, keys, *, q_row_stride, kv_slot_stride, kv_head_stride, kv_row_stride,
-              lengths=None, out=None):
-    """Non-causal head_dim-96 attention over per-slot key lengths; out [slots*queries, heads*96] bf16."""
+              lengths=None, out=None, plan=None):
+    """Non-causal head_dim-96 attention over per-slot key lengths; out [slots*queries, heads*96] bf16.
+    `plan`: an `attention_plan` result (device plan, CTA count) or None."""
     if out is None:
         out = torch.empty((slots * queries, heads * 96), device=q.device, dtype=torch.bfloat16)
     raw = _lib.raw_ptr
+    table, ctas = plan if plan is not None else (None, 0)
     check(_lib.load().svx_attention(raw(q), q_row_stride, raw(k), raw(v), kv_slot_stride, kv_head_stride,
-                                    kv_row_stride, ptr(lengths), slots, heads, queries, keys, ptr(out), stream_ptr()),
+                                    kv_row_stride, ptr(lengths), slots, heads, queries, keys, ptr(out), ptr(table),
+                                    ctas, stream_ptr()),
           'svx_attention')
     return out

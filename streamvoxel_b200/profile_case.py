@@ -32,6 +32,8 @@ def cases():
     k = rnd(SLOTS, HEADS, CAPACITY, 96)
     v = rnd(SLOTS, HEADS, CAPACITY, 96)
     lengths = torch.tensor([1344 + 1024 * i for i in range(SLOTS)], dtype=torch.int32, device='cuda')
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    plan = ops.attention_plan(lengths.tolist(), SLOTS, HEADS, PATCHES, CAPACITY, sms, 'cuda')
     w = {n: rnd(*shape, s=0.02) for n, shape in
          (('qkv', (3 * D, D)), ('fc1', (MLP, D)), ('dxd', (D, D)), ('head', (64 * V, D)))}
     b = {n: rnd(t.shape[0], s=0.02) for n, t in w.items()}
@@ -56,7 +58,7 @@ def cases():
     return {
         'attention_cross': (lambda: ops.attention(qkv, k, v, SLOTS, HEADS, PATCHES, CAPACITY, q_row_stride=3 * D,
                                                   kv_slot_stride=HEADS * CAPACITY * 96, kv_head_stride=CAPACITY * 96,
-                                                  kv_row_stride=96, lengths=lengths, out=out),
+                                                  kv_row_stride=96, lengths=lengths, out=out, plan=plan),
                             4.0 * HEADS * PATCHES * 96 * float(lengths.sum())),
         'attention_self': (lambda: ops.attention(qkv, qkv[:, D:], qkv[:, 2 * D:], SLOTS, HEADS, PATCHES, PATCHES,
                                                  q_row_stride=3 * D, kv_slot_stride=PATCHES * 3 * D, kv_head_stride=96,

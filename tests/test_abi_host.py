@@ -86,3 +86,60 @@ def test_synthetic_data_follows_the_benchmark_distribution():
     assert item.biomes.shape == (64, 12, 12) and item.biomes[:, :3].sum() == 0
     logits, truth = synth.ease_logits(0, 2, classes=8, voxels=1000)
     assert logits.shape == (2, 8, 1000) and truth.shape == (2, 1000)
+
+
+def _lpt_makespan(costs, ctas):
+    """Longest-processing-time assignment restated in Python: each unit, largest first, to the least-loaded CTA."""
+    import heapq
+    heap = [(0, c) for c in range(ctas)]
+    for cost in sorted(costs, reverse=True):
+        load, c = heapq.heappop(heap)
+        heapq.heappush(heap, (load + cost, c))
+    return max(load for load, _ in heap)
+
+
+@pytest.mark.parametrize('lengths, heads, queries, ctas', [
+    ([2368, 3392, 2368, 9536, 4416, 4416, 6464, 9536], 8, 1024, 148),   # the bench's eight slots
+    ([0, 96, 97, 9600], 8, 1024, 148),
+    ([577, 0, 577, 1280], 2, 384, 5),                                     # odd query tiles, fewer CTAs than units
+    (None, 4, 256, 300),                                                  # more CTAs than units
+])
+def test_attention_plan_partitions_units_longest_first(lib, lengths, heads, queries, ctas):
+    """svx_attention_plan assigns every (slot, head, query-pair) unit to exactly one CTA, with a makespan between
+    the lower bound and that of the longest-processing-time rule."""
+    from streamvoxel_b200 import ops
+    slots = 4 if lengths is None else len(lengths)
+    keys = 9600
+    plan, grid = ops.attention_plan(lengths, slots, heads, queries, keys, ctas)
+    pairs = (queries // 128 + 1) // 2
+    units = slots * heads * pairs
+    assert grid == min(ctas, units) and plan.numel() == grid + 1 + units
+    offsets, ids = plan[:grid + 1].tolist(), plan[grid + 1:].tolist()
+    assert offsets[0] == 0 and offsets[-1] == units and all(a <= b for a, b in zip(offsets, offsets[1:]))
+    assert sorted(ids) == list(range(units))
+    lens = [keys] * slots if lengths is None else lengths
+    cost = [(4 * t + 4 if t else 1) for t in ((lens[u // (heads * pairs)] + 95) // 96 for u in range(units))]
+    loads = [sum(cost[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
+    assert max(max(cost), -(-sum(cost) // grid)) <= max(loads) <= _lpt_makespan(cost, grid)
+    for c in range(grid):   # each CTA's units longest first
+        own = [cost[u] for u in ids[offsets[c]:offsets[c + 1]]]
+        assert own == sorted(own, reverse=True)
+
+
+def test_attention_plan_rejects_bad_shapes_and_small_buffers(lib):
+    from streamvoxel_b200 import _lib
+    assert lib.svx_attention_plan_ints(2, 8, 1000, 148) == 0   # queries not a multiple of 128
+    buf = (ctypes.c_int32 * 4)()
+    assert lib.svx_attention_plan(None, 2, 8, 1024, 4096, 148, buf, 4) == _lib.SVX_ERR_INVALID
+
+
+def test_attention_plan_balances_the_bench_lengths(lib):
+    """For the bench's eight slots the boustrophedon order gives a makespan of 125 key tiles (+2 units) against an
+    average of 96.4; the plan reaches 104 quarter-tile-costed units of work within 6% of the average."""
+    from streamvoxel_b200 import ops
+    lengths = [2368, 3392, 2368, 9536, 4416, 4416, 6464, 9536]
+    plan, grid = ops.attention_plan(lengths, 8, 8, 1024, 9600, 148)
+    offsets, ids = plan[:grid + 1].tolist(), plan[grid + 1:].tolist()
+    tiles = [(lengths[u // 32] + 95) // 96 + 1 for u in range(256)]
+    loads = [sum(tiles[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
+    assert max(loads) <= 104 and sum(loads) / grid > 98

@@ -271,6 +271,35 @@ def test_attention_self_and_varlen_cross(ops):
         torch.testing.assert_close(got[s * n:(s + 1) * n], want.transpose(0, 1).reshape(n, d), atol=1e-2, rtol=1e-2)
 
 
+def test_attention_plan_changes_only_the_schedule(ops):
+    """A host-built work plan (LPT/MULTIFIT over the slots' key lengths), a stale plan built for other lengths and a
+    plan for a small grid give bitwise the output of the default order: a plan moves units between CTAs, and each
+    unit's arithmetic does not depend on its CTA."""
+    torch.manual_seed(21)
+    slots, heads, n, cap = 5, 8, 1024, 4096
+    d = heads * 96
+    kc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    vc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    host = [4096, 96, 0, 2500, 1000]
+    lengths = torch.tensor(host, dtype=torch.int32, device='cuda')
+    qx = (torch.randn((slots * n, d), device='cuda') * 1.5).bfloat16()
+    run = lambda plan=None: ops.attention(qx, kc, vc, slots, heads, n, cap, q_row_stride=d,
+                                          kv_slot_stride=heads * cap * 96, kv_head_stride=cap * 96, kv_row_stride=96,
+                                          lengths=lengths, plan=plan)
+    base = run()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for plan_lengths, ctas in ((host, sms), (None, sms), (host, 7)):
+        got = run(ops.attention_plan(plan_lengths, slots, heads, n, cap, ctas, 'cuda'))
+        assert torch.equal(got, base), (plan_lengths, ctas)
+    for s in (0, 3):
+        L = host[s]
+        qs = qx[s * n:(s + 1) * n].float().reshape(n, heads, 96).transpose(0, 1)
+        want = torch.nn.functional.scaled_dot_product_attention(qs, kc[s, :, :L].float(), vc[s, :, :L].float())
+        torch.testing.assert_close(base[s * n:(s + 1) * n].float(), want.transpose(0, 1).reshape(n, d), atol=1e-2,
+                                   rtol=1e-2)
+    assert torch.count_nonzero(base[2 * n:3 * n]) == 0
+
+
 def test_attention_odd_query_tiles_ties_and_empty_slots(ops):
     """384 queries (a CTA with one query tile), tied and zero key lengths, and logits large enough to raise the
     exponent base several times within a row."""
