@@ -185,6 +185,27 @@ SVX_API int svx_attention_plan_ints(int slots, int heads, int queries, int ctas)
 SVX_API int svx_attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas,
                                int32_t* plan, int capacity);
 
+/* One attention problem, in svx_attention's layouts. */
+typedef struct {
+  const uint16_t *q, *k, *v;
+  int64_t q_row_stride, kv_slot_stride, kv_head_stride, kv_row_stride;
+  const int32_t* lengths;    /* device [slots] or NULL (all `keys`) */
+  int keys;
+  uint16_t* out;
+} svx_attention_problem;
+
+/* One or two independent attention problems over the same slots, heads and queries in one persistent launch: the
+ * engine runs a control layer's cross-attention together with its backbone layer's self-attention, so that the
+ * short self-attention units fill the CTAs the long cross-attention units leave idle. Two problems need a plan
+ * from svx_attention_multi_plan (unit ids problem-major); each problem's output equals its own svx_attention.
+ * lengths: host arrays per problem (entries may be NULL). No reference counterpart (the reference launches SDPA and
+ * FlexAttention separately, `timefree.py:46`, `fast_ops.py:104-108`). */
+SVX_API int svx_attention_multi(const svx_attention_problem* problems, int count, int slots, int heads, int queries,
+                                const int32_t* plan, int plan_ctas, void* stream);
+SVX_API int svx_attention_multi_plan_ints(int problems, int slots, int heads, int queries, int ctas);
+SVX_API int svx_attention_multi_plan(const int32_t* const* lengths, const int* keys, int problems, int slots,
+                                     int heads, int queries, int ctas, int32_t* plan, int capacity);
+
 /* ------------------------------------------------------------------------------------------------ the engine */
 
 /* Per-layer weights of one time-free AdaLN block. AdaLN vectors are the constant-time ada outputs
@@ -220,6 +241,7 @@ typedef struct {
 
 typedef struct {
   uint16_t *xb, *xc, *h, *qkv, *attn, *mlp;     /* [slots*patches][d], [..][d], [..][d], [..][3d], [..][d], [..][mlp] */
+  uint16_t *qx, *ax;                            /* cross-attention query and output [slots*patches][d] */
 } svx_engine_workspace;
 
 typedef struct svx_engine svx_engine;

@@ -60,8 +60,14 @@ class EngineWeights(ctypes.Structure):
                                      'cross_sin', 'cross_cos', 'lengths')]
 
 
+class AttentionProblem(ctypes.Structure):
+    _fields_ = [('q', c_ptr), ('k', c_ptr), ('v', c_ptr), ('q_row_stride', c_i64), ('kv_slot_stride', c_i64),
+                ('kv_head_stride', c_i64), ('kv_row_stride', c_i64), ('lengths', c_ptr), ('keys', c_int),
+                ('out', c_ptr)]
+
+
 class EngineWorkspace(ctypes.Structure):
-    _fields_ = [(n, c_ptr) for n in ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp')]
+    _fields_ = [(n, c_ptr) for n in ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp', 'qx', 'ax')]
 
 
 _SIGNATURES = {
@@ -89,6 +95,11 @@ _SIGNATURES = {
                               c_ptr, c_ptr, c_int, c_ptr]),
     'svx_attention_plan_ints': (c_int, [c_int, c_int, c_int, c_int]),
     'svx_attention_plan': (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_int, c_ptr, c_int]),
+    'svx_attention_multi': (c_int, [ctypes.POINTER(AttentionProblem), c_int, c_int, c_int, c_int, c_ptr, c_int,
+                                    c_ptr]),
+    'svx_attention_multi_plan_ints': (c_int, [c_int, c_int, c_int, c_int, c_int]),
+    'svx_attention_multi_plan': (c_int, [ctypes.POINTER(c_ptr), ctypes.POINTER(c_int), c_int, c_int, c_int, c_int,
+                                         c_int, c_ptr, c_int]),
     'svx_engine_create': (c_int, [ctypes.POINTER(EngineConfig), ctypes.POINTER(EngineWeights),
                                   ctypes.POINTER(EngineWorkspace), ctypes.POINTER(c_ptr)]),
     'svx_engine_forward': (c_int, [c_ptr, c_int, c_ptr, c_ptr, c_ptr]),

@@ -1,6 +1,10 @@
 // Non-causal attention, head_dim 96, over per-slot variable-length keys, on the 5th-generation tensor cores.
 //
-// A persistent CTA per SM takes work units of two 128-query tiles of one (slot, head), longest slots first. Key tiles
+// A launch runs one attention problem, or two independent ones over the same slots, heads and queries (the engine
+// pairs a control layer's cross-attention with its backbone layer's self-attention). A persistent CTA per SM takes
+// work units of two 128-query tiles of one (problem, slot, head): from a host-built plan (attention_plan: longest
+// units first onto the least-loaded CTA, refined by MULTIFIT, so that CTAs finish together when slot lengths differ)
+// or, for one problem without a plan, longest slots first in boustrophedon passes. Key tiles
 // of 96 are streamed by TMA into four-stage K and V rings, and only the ceil(length / 96) tiles of a slot are loaded:
 // the packed-key block mask of `streamvoxel/stream/fast_ops.py:149-159`. Q and K tiles are exactly 96 dims wide: dims
 // 0-63 as a 128B-swizzled part (128-byte rows) and dims 64-95 as a 64B-swizzled part (64-byte rows). V tiles are two
@@ -79,15 +83,28 @@ __device__ __forceinline__ float2 exp2_fma2(float2 x) {
                      __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
-struct AttnParams {
-  int slots, heads, queries, keys, pairs, units;
+// One attention problem of a launch. A launch runs one or two problems over the same slots, heads and queries (the
+// cross-attention of a control layer together with the independent self-attention of its backbone layer).
+struct AttnProblem {
+  int keys, units;
   int kv_mode;  // 0: K/V groups = heads, rows = slot*keys + key; 1: groups = slot*heads + head, rows = key
   const int32_t* lengths;
-  // Optional unit assignment built on the host (attention_plan): [G + 1] offsets into the unit list that follows,
-  // CTA c taking units [plan[c], plan[c + 1]); ids are natural, (slot * heads + head) * pairs + pair. Null: the
-  // boustrophedon passes over the longest-first numbering.
-  const int32_t* plan;
   uint16_t* out;
+};
+
+// The tensor maps of one problem: Q dims 0-63 (128B swizzle) and 64-95 (64B), K likewise, V as 64-dim boxes.
+struct AttnMaps {
+  CUtensorMap m[2][5];
+};
+
+struct AttnParams {
+  int slots, heads, queries, pairs, units, problems;   // units: over all problems
+  AttnProblem pr[2];
+  // Optional unit assignment built on the host (attention_plan): [G + 1] offsets into the unit list that follows,
+  // CTA c taking units [plan[c], plan[c + 1]); ids are natural, problem-major: units of problem 0, then problem 1,
+  // each (slot * heads + head) * pairs + pair. Null (one problem only): the boustrophedon passes over the
+  // longest-first numbering.
+  const int32_t* plan;
   float scale_log2;
 };
 
@@ -95,18 +112,24 @@ struct AttnParams {
 // one, naturally. A tile index past the slot's queries (odd tile counts) repeats the last tile, whose result is not
 // stored.
 struct Unit {
-  int slot, head, q0, nq, length, tiles, kg, kr0;
+  int prob, slot, head, q0, nq, length, tiles, kg, kr0;
   __device__ __forceinline__ Unit(const AttnParams& p, const int* rank_slot, int w) {
+    prob = w >= p.pr[0].units;
+    if (prob) w -= p.pr[0].units;
+    // Field selects rather than p.pr[prob]: a dynamic index into the parameters would copy them to local memory.
+    const int keys = prob ? p.pr[1].keys : p.pr[0].keys;
+    const int kv_mode = prob ? p.pr[1].kv_mode : p.pr[0].kv_mode;
+    const int32_t* lengths = prob ? p.pr[1].lengths : p.pr[0].lengths;
     const int per_slot = p.heads * p.pairs;
     const int rem = w % per_slot;
     slot = p.plan ? w / per_slot : rank_slot[w / per_slot];
     head = rem / p.pairs;
     q0 = (rem % p.pairs) * 2 * TQ;
     nq = min(2, (p.queries - q0) / TQ);
-    length = p.lengths ? max(0, min(p.lengths[slot], p.keys)) : p.keys;
+    length = lengths ? max(0, min(lengths[slot], keys)) : keys;
     tiles = (length + TK - 1) / TK;
-    kg = p.kv_mode == 0 ? head : slot * p.heads + head;
-    kr0 = p.kv_mode == 0 ? slot * p.keys : 0;
+    kg = kv_mode == 0 ? head : slot * p.heads + head;
+    kr0 = kv_mode == 0 ? slot * keys : 0;
   }
 };
 
@@ -133,11 +156,7 @@ __device__ __forceinline__ int unit_at(const AttnParams& p, int c, int k, int G)
   return (w >= 0 && w < p.units) ? w : -1;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_constant__ CUtensorMap mq_wide,
-                                                                   const __grid_constant__ CUtensorMap mq_narrow,
-                                                                   const __grid_constant__ CUtensorMap mk_wide,
-                                                                   const __grid_constant__ CUtensorMap mk_narrow,
-                                                                   const __grid_constant__ CUtensorMap mv,
+__global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_constant__ AttnMaps maps,
                                                                    const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -176,9 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    tc::prefetch_map(&mq_wide); tc::prefetch_map(&mq_narrow);
-    tc::prefetch_map(&mk_wide); tc::prefetch_map(&mk_narrow);
-    tc::prefetch_map(&mv);
+    for (int pb = 0; pb < p.problems; ++pb)
+      for (int j = 0; j < 5; ++j) tc::prefetch_map(&maps.m[pb][j]);
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, TMEM_COLS);
   grid_dependency_wait();   // Q, K, V and the lengths come from earlier kernels
@@ -186,11 +204,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
     // Slots in descending key-length order (ties by slot index): rank_slot[rank] = slot.
     for (int s = lane; s < p.slots; s += 32) {
       int r = s;
-      if (p.lengths) {
-        const int ls = max(0, min(p.lengths[s], p.keys));
+      if (p.pr[0].lengths) {
+        const int ls = max(0, min(p.pr[0].lengths[s], p.pr[0].keys));
         r = 0;
         for (int u = 0; u < p.slots; ++u) {
-          const int lu = max(0, min(p.lengths[u], p.keys));
+          const int lu = max(0, min(p.pr[0].lengths[u], p.pr[0].keys));
           r += (lu > ls) || (lu == ls && u < s);
         }
       }
@@ -205,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   // Register split: the load/MMA warpgroup keeps 64 per thread, the two softmax warpgroups take 216
   // (128 x 64 + 256 x 216 <= 384 x 168, the launch's allocation).
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
     if (warp == 0) {   // Q and the K ring
       int T = 0, qn = 0;
       bool ok = true;
@@ -219,15 +237,15 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
         tc::expect_tx_w(q_full, 2 * QOPER);
         for (int i = 0; i < 2; ++i) {
           const int qr = U.slot * p.queries + U.q0 + min(i, U.nq - 1) * TQ;
-          tc::tma_load_3d_w(sq + i * QOPER, &mq_wide, 0, U.head, qr, q_full);
-          tc::tma_load_3d_w(sq + i * QOPER + QWIDE, &mq_narrow, 64, U.head, qr, q_full);
+          tc::tma_load_3d_w(sq + i * QOPER, &maps.m[U.prob][0], 0, U.head, qr, q_full);
+          tc::tma_load_3d_w(sq + i * QOPER + QWIDE, &maps.m[U.prob][1], 64, U.head, qr, q_full);
         }
         for (int t = 0; t < U.tiles; ++t) {
           const int g = T + t, s = g % STAGES;
           if (g >= STAGES && !tc::wait_w(k_empty + s, (g / STAGES - 1) & 1, abort_flag)) { ok = false; break; }
           tc::expect_tx_w(k_full + s, KOPER);
-          tc::tma_load_3d_w(sk + s * KOPER, &mk_wide, 0, U.kg, U.kr0 + t * TK, k_full + s);
-          tc::tma_load_3d_w(sk + s * KOPER + KWIDE, &mk_narrow, 64, U.kg, U.kr0 + t * TK, k_full + s);
+          tc::tma_load_3d_w(sk + s * KOPER, &maps.m[U.prob][2], 0, U.kg, U.kr0 + t * TK, k_full + s);
+          tc::tma_load_3d_w(sk + s * KOPER + KWIDE, &maps.m[U.prob][3], 64, U.kg, U.kr0 + t * TK, k_full + s);
         }
         T += U.tiles;
         ++qn;
@@ -244,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
           const int g = T + t, s = g % STAGES;
           if (g >= STAGES && !tc::wait_w(v_empty + s, (g / STAGES - 1) & 1, abort_flag)) { ok = false; break; }
           tc::expect_tx_w(v_full + s, VOPER);
-          tc::tma_load_3d_w(sv + s * VOPER, &mv, 0, U.kg, U.kr0 + t * TK, v_full + s);
-          tc::tma_load_3d_w(sv + s * VOPER + VWIDE, &mv, 64, U.kg, U.kr0 + t * TK, v_full + s);
+          tc::tma_load_3d_w(sv + s * VOPER, &maps.m[U.prob][4], 0, U.kg, U.kr0 + t * TK, v_full + s);
+          tc::tma_load_3d_w(sv + s * VOPER + VWIDE, &maps.m[U.prob][4], 64, U.kg, U.kr0 + t * TK, v_full + s);
         }
         T += U.tiles;
       }
@@ -316,11 +334,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       const int w = unit_at(p, c, k, G);
       if (w < 0) continue;
       const Unit U(p, rank_slot, w);
-      const int qrow = U.q0 + i * TQ + row;
-      uint4* dst = reinterpret_cast<uint4*>(p.out + ((int64_t)U.slot * p.queries + qrow) * (p.heads * HD) + U.head * HD);
+      // The output row of this thread, computed where it is written so that it is not live across the tile loop.
+      auto out_row = [&](const Unit& V) {
+        return reinterpret_cast<uint4*>((V.prob ? p.pr[1].out : p.pr[0].out) +
+                                        ((int64_t)V.slot * p.queries + V.q0 + i * TQ + row) * (p.heads * HD) +
+                                        V.head * HD);
+      };
       if (U.tiles == 0) {
-        if (i < U.nq)
+        if (i < U.nq) {
+          uint4* dst = out_row(U);
           for (int k8 = 0; k8 < HD / 8; ++k8) dst[k8] = make_uint4(0, 0, 0, 0);
+        }
         continue;
       }
       float m_used = -INFINITY, l_run = 0.f;
@@ -409,12 +433,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       if (!ok) break;
       tc::fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const Unit V(p, rank_slot, w);
+      uint4* dst = out_row(V);
 #pragma unroll
       for (int c3 = 0; c3 < HD / 32; ++c3) {
         uint32_t o[32];
         tc::ld32(to + c3 * 32, o);
         tc::wait_ld();
-        if (i < U.nq) {
+        if (i < V.nq) {
 #pragma unroll
           for (int k4 = 0; k4 < 4; ++k4) {
             const float* f = reinterpret_cast<const float*>(o) + 8 * k4;
@@ -439,25 +465,28 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
 
 }  // namespace
 
-int attention_plan_ints(int slots, int heads, int queries, int ctas) {
-  if (slots <= 0 || heads <= 0 || queries <= 0 || queries % TQ || ctas <= 0) return 0;
-  const int64_t units = (int64_t)slots * heads * ((queries / TQ + 1) / 2);
+int attention_plan_ints(int problems, int slots, int heads, int queries, int ctas) {
+  if (problems < 1 || problems > 2 || slots <= 0 || heads <= 0 || queries <= 0 || queries % TQ || ctas <= 0) return 0;
+  const int64_t units = (int64_t)problems * slots * heads * ((queries / TQ + 1) / 2);
   if (units > (1 << 28)) return 0;
   return (int)(std::min<int64_t>(ctas, units) + 1 + units);
 }
 
-int attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas, int32_t* plan,
-                   int capacity) {
-  const int need = attention_plan_ints(slots, heads, queries, ctas);
-  SVX_REQUIRE(need > 0 && keys > 0, "attention_plan: bad shape");
+int attention_plan(const int32_t* const* lengths, const int* keys, int problems, int slots, int heads, int queries,
+                   int ctas, int32_t* plan, int capacity) {
+  const int need = attention_plan_ints(problems, slots, heads, queries, ctas);
+  SVX_REQUIRE(need > 0 && keys, "attention_plan: bad shape");
+  for (int pb = 0; pb < problems; ++pb) SVX_REQUIRE(keys[pb] > 0, "attention_plan: bad key count");
   SVX_REQUIRE(plan && capacity >= need, "attention_plan: plan buffer too small");
-  const int pairs = (queries / TQ + 1) / 2, per_slot = heads * pairs, units = slots * per_slot;
+  const int pairs = (queries / TQ + 1) / 2, per_slot = heads * pairs, per_prob = slots * per_slot;
+  const int units = problems * per_prob;
   const int G = std::min(ctas, units);
   // Cost of a unit in quarter key tiles: its tiles plus one tile of per-unit work (Q load, ring fill, epilogue);
   // a unit without keys only writes zeros.
   std::vector<int64_t> cost(units);
   for (int u = 0; u < units; ++u) {
-    const int len = lengths ? std::max(0, std::min(lengths[u / per_slot], keys)) : keys;
+    const int pb = u / per_prob, slot = (u % per_prob) / per_slot;
+    const int len = lengths && lengths[pb] ? std::max(0, std::min(lengths[pb][slot], keys[pb])) : keys[pb];
     const int tiles = (len + TK - 1) / TK;
     cost[u] = tiles ? 4 * (int64_t)tiles + 4 : 1;
   }
@@ -515,52 +544,66 @@ int attention_plan(const int32_t* lengths, int slots, int heads, int queries, in
   return SVX_OK;
 }
 
-int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
-                  int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride, const int32_t* lengths,
-                  int slots, int heads, int queries, int keys, uint16_t* out, const int32_t* plan, int plan_ctas,
-                  cudaStream_t stream) {
+int attention_launch(const svx_attention_problem* probs, int problems, int slots, int heads, int queries,
+                     const int32_t* plan, int plan_ctas, cudaStream_t stream) {
+  SVX_REQUIRE(problems == 1 || (problems == 2 && plan), "attention: one problem, or two with a plan");
   SVX_REQUIRE(queries % TQ == 0, "attention: queries must be a multiple of 128");
-  int kv_mode;
-  uint64_t groups, rows, group_stride, row_stride;
-  if (kv_slot_stride == (int64_t)keys * kv_row_stride) {          // [slot*keys + key][.. head*stride ..]
-    kv_mode = 0; groups = heads; rows = (uint64_t)slots * keys;
-    group_stride = kv_head_stride * 2; row_stride = kv_row_stride * 2;
-  } else if (kv_slot_stride == (int64_t)heads * kv_head_stride) {  // [slot][head][key][dim]
-    kv_mode = 1; groups = (uint64_t)slots * heads; rows = keys;
-    group_stride = kv_head_stride * 2; row_stride = kv_row_stride * 2;
-  } else {
-    return fail(SVX_ERR_INVALID, "attention: K/V strides must be [slot*keys][head] or [slot][head][key] layouts");
-  }
-  CUtensorMap m[5];
-  const uint64_t qrows = (uint64_t)slots * queries;
+  SVX_REQUIRE(slots <= kMaxSlots, "attention: at most 512 slots");
+  const int pairs = (queries / TQ + 1) / 2;
+  const int per_prob = slots * heads * pairs, units = problems * per_prob;
+  AttnMaps maps;
+  AttnParams prm{};
+  prm.slots = slots; prm.heads = heads; prm.queries = queries; prm.pairs = pairs; prm.units = units;
+  prm.problems = problems; prm.plan = plan;
+  prm.scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
   constexpr CUtensorMapSwizzle SW64 = CU_TENSOR_MAP_SWIZZLE_64B;
-  int rc = make_map_3d(&m[0], q, HD, heads, qrows, HD * 2, q_row_stride * 2, 64, TQ);
-  if (!rc) rc = make_map_3d(&m[1], q, HD, heads, qrows, HD * 2, q_row_stride * 2, 32, TQ, SW64);
-  if (!rc) rc = make_map_3d(&m[2], k, HD, groups, rows, group_stride, row_stride, 64, TK);
-  if (!rc) rc = make_map_3d(&m[3], k, HD, groups, rows, group_stride, row_stride, 32, TK, SW64);
-  if (!rc) rc = make_map_3d(&m[4], v, HD, groups, rows, group_stride, row_stride, 64, TK);
-  if (rc) return rc;
+  for (int pb = 0; pb < 2; ++pb) {
+    const svx_attention_problem& a = probs[pb < problems ? pb : 0];
+    const int keys = a.keys;
+    SVX_REQUIRE(keys > 0, "attention: keys must be positive");
+    int kv_mode;
+    uint64_t groups, rows;
+    if (a.kv_slot_stride == (int64_t)keys * a.kv_row_stride) {          // [slot*keys + key][.. head*stride ..]
+      kv_mode = 0; groups = heads; rows = (uint64_t)slots * keys;
+    } else if (a.kv_slot_stride == (int64_t)heads * a.kv_head_stride) {  // [slot][head][key][dim]
+      kv_mode = 1; groups = (uint64_t)slots * heads; rows = keys;
+    } else {
+      return fail(SVX_ERR_INVALID, "attention: K/V strides must be [slot*keys][head] or [slot][head][key] layouts");
+    }
+    const uint64_t gs = a.kv_head_stride * 2, rs = a.kv_row_stride * 2, qrows = (uint64_t)slots * queries;
+    CUtensorMap* m = maps.m[pb];
+    int rc = make_map_3d(&m[0], a.q, HD, heads, qrows, HD * 2, a.q_row_stride * 2, 64, TQ);
+    if (!rc) rc = make_map_3d(&m[1], a.q, HD, heads, qrows, HD * 2, a.q_row_stride * 2, 32, TQ, SW64);
+    if (!rc) rc = make_map_3d(&m[2], a.k, HD, groups, rows, gs, rs, 64, TK);
+    if (!rc) rc = make_map_3d(&m[3], a.k, HD, groups, rows, gs, rs, 32, TK, SW64);
+    if (!rc) rc = make_map_3d(&m[4], a.v, HD, groups, rows, gs, rs, 64, TK);
+    if (rc) return rc;
+    prm.pr[pb] = AttnProblem{keys, per_prob, kv_mode, a.lengths, a.out};
+  }
   static bool configured = false;
   if (!configured) {
     SVX_CHECK_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
     configured = true;
   }
-  SVX_REQUIRE(slots <= kMaxSlots, "attention: at most 512 slots");
   static int sms = 0;
   if (!sms) {
     int device = 0;
     SVX_CHECK_CUDA(cudaGetDevice(&device));
     SVX_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   }
-  const int pairs = (queries / TQ + 1) / 2;
-  const int units = slots * heads * pairs;
-  SVX_REQUIRE(!plan || (plan_ctas >= 1 && plan_ctas == std::min(plan_ctas, units)),
-              "attention: a plan needs 1 <= ctas <= units");
-  AttnParams prm{slots, heads, queries, keys, pairs, units, kv_mode, lengths, plan, out,
-                 (1.0f / sqrtf((float)HD)) * 1.4426950408889634f};
+  SVX_REQUIRE(!plan || (plan_ctas >= 1 && plan_ctas <= units), "attention: a plan needs 1 <= ctas <= units");
   const int grid = plan ? plan_ctas : (units < sms ? units : sms);
   return launch_dependent("attention_tc_kernel", attention_tc_kernel, dim3(grid), dim3(kThreads), kSmem, stream,
-                          m[0], m[1], m[2], m[3], m[4], prm);
+                          maps, prm);
+}
+
+int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
+                  int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride, const int32_t* lengths,
+                  int slots, int heads, int queries, int keys, uint16_t* out, const int32_t* plan, int plan_ctas,
+                  cudaStream_t stream) {
+  const svx_attention_problem a{q, k, v, q_row_stride, kv_slot_stride, kv_head_stride, kv_row_stride, lengths, keys,
+                                out};
+  return attention_launch(&a, 1, slots, heads, queries, plan, plan_ctas, stream);
 }
 
 uint32_t attention_timeouts() {
@@ -574,24 +617,52 @@ uint32_t attention_timeouts() {
 using namespace svx;
 
 extern "C" int svx_attention_plan_ints(int slots, int heads, int queries, int ctas) {
-  return attention_plan_ints(slots, heads, queries, ctas);
+  return attention_plan_ints(1, slots, heads, queries, ctas);
 }
 
 extern "C" int svx_attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas,
                                   int32_t* plan, int capacity) {
-  return attention_plan(lengths, slots, heads, queries, keys, ctas, plan, capacity);
+  return attention_plan(&lengths, &keys, 1, slots, heads, queries, ctas, plan, capacity);
 }
+
+extern "C" int svx_attention_multi_plan_ints(int problems, int slots, int heads, int queries, int ctas) {
+  return attention_plan_ints(problems, slots, heads, queries, ctas);
+}
+
+extern "C" int svx_attention_multi_plan(const int32_t* const* lengths, const int* keys, int problems, int slots,
+                                        int heads, int queries, int ctas, int32_t* plan, int capacity) {
+  return attention_plan(lengths, keys, problems, slots, heads, queries, ctas, plan, capacity);
+}
+
+namespace {
+int check_problem(const svx_attention_problem& a) {
+  SVX_REQUIRE(a.q && a.k && a.v && a.out && a.keys > 0, "svx_attention: bad arguments");
+  SVX_REQUIRE(a.q_row_stride % 8 == 0 && a.kv_row_stride % 8 == 0 && a.kv_head_stride % 8 == 0 &&
+                  a.kv_slot_stride % 8 == 0,
+              "svx_attention: strides must be multiples of 8 elements");
+  const uintptr_t align = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                          reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out);
+  SVX_REQUIRE((align & 15u) == 0, "svx_attention: operands must be 16-byte aligned");
+  return SVX_OK;
+}
+}  // namespace
 
 extern "C" int svx_attention(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, const uint16_t* v,
                              int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride,
                              const int32_t* lengths, int slots, int heads, int queries, int keys, uint16_t* out,
                              const int32_t* plan, int plan_ctas, void* stream) {
-  SVX_REQUIRE(q && k && v && out && slots > 0 && heads > 0 && queries > 0 && keys > 0, "svx_attention: bad arguments");
-  SVX_REQUIRE(q_row_stride % 8 == 0 && kv_row_stride % 8 == 0 && kv_head_stride % 8 == 0 && kv_slot_stride % 8 == 0,
-              "svx_attention: strides must be multiples of 8 elements");
-  const uintptr_t align = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
-                          reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
-  SVX_REQUIRE((align & 15u) == 0, "svx_attention: operands must be 16-byte aligned");
-  return attention_run(q, q_row_stride, k, v, kv_slot_stride, kv_head_stride, kv_row_stride, lengths, slots, heads,
-                       queries, keys, out, plan, plan_ctas, as_stream(stream));
+  SVX_REQUIRE(slots > 0 && heads > 0 && queries > 0, "svx_attention: bad arguments");
+  const svx_attention_problem a{q, k, v, q_row_stride, kv_slot_stride, kv_head_stride, kv_row_stride, lengths, keys,
+                                out};
+  if (const int rc = check_problem(a)) return rc;
+  return attention_launch(&a, 1, slots, heads, queries, plan, plan_ctas, as_stream(stream));
+}
+
+extern "C" int svx_attention_multi(const svx_attention_problem* problems, int count, int slots, int heads,
+                                   int queries, const int32_t* plan, int plan_ctas, void* stream) {
+  SVX_REQUIRE(problems && (count == 1 || count == 2) && slots > 0 && heads > 0 && queries > 0,
+              "svx_attention_multi: one or two problems over positive shapes");
+  for (int i = 0; i < count; ++i)
+    if (const int rc = check_problem(problems[i])) return rc;
+  return attention_launch(problems, count, slots, heads, queries, plan, plan_ctas, as_stream(stream));
 }

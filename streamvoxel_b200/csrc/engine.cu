@@ -5,6 +5,8 @@
 //   b, c = embed(tokens) + y_embed
 //   for i in layers: if i feeds control layer j: c = block_c(c); c = c + cross_j(c); b = block_b(b) + zero_j(c)
 //                    else:                      b = block_b(b)
+// The cross-attention of control layer j and the self-attention of backbone layer i are independent, so they run
+// as one attention launch (LN, query, LN, qkv first; proj, cross proj after), with one work plan over both.
 //   logits = head(modulate(LN(b)))  in class-major [slot][V][Y][Z][X]
 // Every TMA descriptor is built once in svx_engine_create; svx_engine_forward only enqueues kernels, so it can be
 // captured in a CUDA graph per slot bucket.
@@ -24,8 +26,8 @@ struct svx_engine {
   // GEMM plans: per backbone layer [qkv, proj, fc1, fc2]; per control layer [qkv, proj, fc1, fc2, query, cproj, zero].
   std::vector<svx::GemmPlan> bplan, cplan;
   svx::GemmPlan head;
-  // Cross-attention work plans (svx::attention_plan on plan_ctas CTAs), one row of plan_stride ints per bucket
-  // n = 1..slots, rebuilt on the host by svx_engine_set_lengths and copied to plan_dev.
+  // Work plans of the joint cross + self attention launch (svx::attention_plan, two problems, on plan_ctas CTAs),
+  // one row of plan_stride ints per bucket n = 1..slots, rebuilt on the host by svx_engine_set_lengths.
   int32_t* plan_dev = nullptr;
   int plan_stride = 0, plan_ctas = 0;
   std::vector<int32_t> plan_host;
@@ -61,9 +63,18 @@ EpiParams epi(int kind, const uint16_t* bias) {
   return e;
 }
 
-// One time-free AdaLN block on x (`UnconditionalBlock.forward`, `unconditional_md4_timefree.py:60-63`).
-int run_block(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
-              cudaStream_t s) {
+// The self-attention problem of a block: q, k, v interleaved in the qkv workspace, out to the attn workspace.
+svx_attention_problem self_problem(const svx_engine& E) {
+  const svx_engine_workspace& ws = E.ws;
+  const int d = E.cfg.d;
+  const int64_t ld = 3 * d;
+  return svx_attention_problem{ws.qkv, ws.qkv + d, ws.qkv + 2 * d, ld, (int64_t)E.patches * ld, HD, ld, nullptr,
+                               E.patches, ws.attn};
+}
+
+// The first half of a block: h = modulate(LN(x)), qkv = RoPE(h W_qkv^T + b).
+int run_block_qkv(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
+                  cudaStream_t s) {
   const int d = E.cfg.d, rows = n * E.patches;
   const svx_engine_workspace& ws = E.ws;
   int rc;
@@ -71,12 +82,16 @@ int run_block(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* 
   EpiParams e = epi(SVX_EPI_ROPE, bw.qkv_b);
   e.rope_sin = E.w.rope_sin; e.rope_cos = E.w.rope_cos;
   e.rope_cols = 2 * d; e.rows_per_slot = E.patches; e.head_dim = HD;
-  if ((rc = gemm_run(plans[0], rows, ws.qkv, e, s))) return rc;
-  const int64_t ld = 3 * d;
-  if ((rc = attention_run(ws.qkv, ld, ws.qkv + d, ws.qkv + 2 * d, (int64_t)E.patches * ld, HD, ld, nullptr, n,
-                          E.cfg.heads, E.patches, E.patches, ws.attn, nullptr, 0, s)))
-    return rc;
-  e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);
+  return gemm_run(plans[0], rows, ws.qkv, e, s);
+}
+
+// The second half, after the attention: x += g1 proj(attn); x += g2 fc2(GELU(fc1(modulate(LN(x))))).
+int run_block_rest(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
+                   cudaStream_t s) {
+  const int d = E.cfg.d, rows = n * E.patches;
+  const svx_engine_workspace& ws = E.ws;
+  int rc;
+  EpiParams e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);
   e.gate = bw.gate1; e.residual = x;
   if ((rc = gemm_run(plans[1], rows, x, e, s))) return rc;
   if ((rc = layernorm_run(x, rows, d, 1e-6f, bw.one_plus_scale2, bw.shift2, ws.h, s))) return rc;
@@ -86,33 +101,57 @@ int run_block(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* 
   return gemm_run(plans[3], rows, x, e, s);
 }
 
-// c = c + cross_j(c): LN -> query -> RoPE -> attention over the slot's packed keys -> proj
-// (`RotaryCrossAttention.forward`, `streaming_controlnet.py:37-61`, as `cross_flex` `fast_ops.py:104-108`).
-int run_cross(const svx_engine& E, const svx_cross_weights& cw, const GemmPlan* plans, int n, cudaStream_t s) {
+// One time-free AdaLN block on x (`UnconditionalBlock.forward`, `unconditional_md4_timefree.py:60-63`).
+int run_block(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
+              cudaStream_t s) {
+  int rc;
+  if ((rc = run_block_qkv(E, bw, plans, x, n, s))) return rc;
+  const svx_attention_problem a = self_problem(E);
+  if ((rc = attention_launch(&a, 1, n, E.cfg.heads, E.patches, nullptr, 0, s))) return rc;
+  return run_block_rest(E, bw, plans, x, n, s);
+}
+
+// Control layer j with backbone layer i (`RotaryCrossAttention.forward`, `streaming_controlnet.py:37-61`, as
+// `cross_flex` `fast_ops.py:104-108`, and `compact_controlnet.py:100-159`): c = block_c(c); qx = RoPE(LN(c) Wq);
+// qkv = block_b's first half; [cross-attention of qx over the slot's packed keys -> ax, self-attention -> attn]
+// in one launch; c += proj(ax); block_b's second half; b += zero(c).
+int run_control_layer(const svx_engine& E, int i, int j, int n, cudaStream_t s) {
   const int d = E.cfg.d, rows = n * E.patches;
   const svx_engine_workspace& ws = E.ws;
+  const svx_cross_weights& cw = E.cross[j];
+  const GemmPlan* cp = &E.cplan[(size_t)j * 7];
+  const GemmPlan* bp = &E.bplan[(size_t)i * 4];
   int rc;
+  if ((rc = run_block(E, E.control[j], cp, ws.xc, n, s))) return rc;
   if ((rc = layernorm_run(ws.xc, rows, d, 1e-6f, nullptr, nullptr, ws.h, s))) return rc;
   EpiParams e = epi(SVX_EPI_ROPE, cw.query_b);
   e.rope_sin = E.w.cross_sin; e.rope_cos = E.w.cross_cos;
   e.rope_cols = d; e.rows_per_slot = E.patches; e.head_dim = HD;
-  if ((rc = gemm_run(plans[0], rows, ws.qkv, e, s))) return rc;
+  if ((rc = gemm_run(cp[4], rows, ws.qx, e, s))) return rc;
+  if ((rc = run_block_qkv(E, E.backbone[i], bp, ws.xb, n, s))) return rc;
   const int64_t cap = E.cfg.key_capacity;
-  const int units = n * E.cfg.heads * ((E.patches / 128 + 1) / 2);
-  const int32_t* plan = E.plan_dev ? E.plan_dev + (size_t)(n - 1) * E.plan_stride : nullptr;
-  if ((rc = attention_run(ws.qkv, d, cw.k, cw.v, (int64_t)E.cfg.heads * cap * HD, cap * HD, HD, E.w.lengths, n,
-                          E.cfg.heads, E.patches, E.cfg.key_capacity, ws.attn, plan, std::min(E.plan_ctas, units),
-                          s)))
-    return rc;
+  const svx_attention_problem both[2] = {
+      {ws.qx, cw.k, cw.v, d, (int64_t)E.cfg.heads * cap * HD, cap * HD, HD, E.w.lengths, E.cfg.key_capacity, ws.ax},
+      self_problem(E)};
+  const int units = 2 * n * E.cfg.heads * ((E.patches / 128 + 1) / 2);
+  const int32_t* plan = E.plan_dev + (size_t)(n - 1) * E.plan_stride;
+  if ((rc = attention_launch(both, 2, n, E.cfg.heads, E.patches, plan, std::min(E.plan_ctas, units), s))) return rc;
   e = epi(SVX_EPI_RESIDUAL, cw.proj_b);
   e.residual = ws.xc;
-  return gemm_run(plans[1], rows, ws.xc, e, s);
+  if ((rc = gemm_run(cp[5], rows, ws.xc, e, s))) return rc;
+  if ((rc = run_block_rest(E, E.backbone[i], bp, ws.xb, n, s))) return rc;
+  e = epi(SVX_EPI_RESIDUAL, cw.zero_b);
+  e.residual = ws.xb;
+  return gemm_run(cp[6], rows, ws.xb, e, s);
 }
 
-// Plans of every bucket n = 1..slots for the host key lengths (NULL: all slots at the key capacity).
+// Joint cross + self attention plans of every bucket n = 1..slots for the host key lengths (NULL: all slots at the
+// key capacity).
 int build_plans(svx_engine& E, const int32_t* lengths) {
+  const int32_t* lens[2] = {lengths, nullptr};
+  const int keys[2] = {E.cfg.key_capacity, E.patches};
   for (int n = 1; n <= E.cfg.slots; ++n) {
-    const int rc = attention_plan(lengths, n, E.cfg.heads, E.patches, E.cfg.key_capacity, E.plan_ctas,
+    const int rc = attention_plan(lens, keys, 2, n, E.cfg.heads, E.patches, E.plan_ctas,
                                   E.plan_host.data() + (size_t)(n - 1) * E.plan_stride, E.plan_stride);
     if (rc) return rc;
   }
@@ -165,7 +204,7 @@ extern "C" int svx_engine_create(const svx_engine_config* config, const svx_engi
     GemmPlan p;
     if (!rc) rc = gemm_plan(&p, e->ws.h, e->cross[j].query_w, e->rows_max, c.d, c.d, 0);
     if (!rc) e->cplan.push_back(p);
-    if (!rc) rc = gemm_plan(&p, e->ws.attn, e->cross[j].proj_w, e->rows_max, c.d, c.d, 0);
+    if (!rc) rc = gemm_plan(&p, e->ws.ax, e->cross[j].proj_w, e->rows_max, c.d, c.d, 0);
     if (!rc) e->cplan.push_back(p);
     if (!rc) rc = gemm_plan(&p, e->ws.xc, e->cross[j].zero_w, e->rows_max, c.d, c.d, 0);
     if (!rc) e->cplan.push_back(p);
@@ -177,7 +216,7 @@ extern "C" int svx_engine_create(const svx_engine_config* config, const svx_engi
     if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (err == cudaSuccess) {
       e->plan_ctas = sms;
-      e->plan_stride = attention_plan_ints(c.slots, c.heads, e->patches, sms);
+      e->plan_stride = attention_plan_ints(2, c.slots, c.heads, e->patches, sms);
       e->plan_host.assign((size_t)c.slots * e->plan_stride, 0);
       rc = e->plan_stride > 0 ? build_plans(*e, nullptr) : fail(SVX_ERR_INVALID, "svx_engine_create: bad plan shape");
       if (!rc) err = cudaMalloc(&e->plan_dev, e->plan_host.size() * sizeof(int32_t));
@@ -208,19 +247,9 @@ extern "C" int svx_engine_forward(svx_engine* E, int n, const int16_t* tokens, u
   if (rc) return rc;
   for (int i = 0; i < c.depth_layers; ++i) {
     const int j = E->layer_map[i];
-    if (j >= 0) {
-      const GemmPlan* cp = &E->cplan[(size_t)j * 7];
-      if ((rc = run_block(*E, E->control[j], cp, ws.xc, n, s))) return rc;
-      if ((rc = run_cross(*E, E->cross[j], cp + 4, n, s))) return rc;
-    }
-    if ((rc = run_block(*E, E->backbone[i], &E->bplan[(size_t)i * 4], ws.xb, n, s))) return rc;
-    if (j >= 0) {
-      EpiParams e{};
-      e.epilogue = SVX_EPI_RESIDUAL;
-      e.bias = E->cross[j].zero_b;
-      e.residual = ws.xb;
-      if ((rc = gemm_run(E->cplan[(size_t)j * 7 + 6], rows, ws.xb, e, s))) return rc;
-    }
+    rc = j >= 0 ? run_control_layer(*E, i, j, n, s)
+                : run_block(*E, E->backbone[i], &E->bplan[(size_t)i * 4], ws.xb, n, s);
+    if (rc) return rc;
   }
   if ((rc = layernorm_run(ws.xb, rows, c.d, 1e-6f, E->w.final_one_plus_scale, E->w.final_shift, ws.h, s))) return rc;
   EpiParams e{};
@@ -246,7 +275,7 @@ extern "C" int svx_engine_set_lengths(svx_engine* E, const int32_t* lengths, voi
 extern "C" int svx_engine_launches(const svx_engine* E, int n) {
   if (!E || n < 1) return 0;
   const int per_block = 7;   // LN, qkv, attention, proj, LN, fc1, fc2
-  const int per_cross = 5;   // LN, query, attention, proj, zero
+  const int per_cross = 4;   // LN, query, proj, zero (its attention shares the backbone block's launch)
   return 1 + E->cfg.depth_layers * per_block + E->cfg.n_control * (per_block + per_cross) + 2;
 }
 

@@ -36,10 +36,13 @@ int attention_run(const uint16_t* q, int64_t q_row_stride, const uint16_t* k, co
                   int64_t kv_slot_stride, int64_t kv_head_stride, int64_t kv_row_stride, const int32_t* lengths,
                   int slots, int heads, int queries, int keys, uint16_t* out, const int32_t* plan, int plan_ctas,
                   cudaStream_t stream);
-// Host-side LPT assignment of attention work units to CTAs (layout in attention.cu); ints a plan takes.
-int attention_plan_ints(int slots, int heads, int queries, int ctas);
-int attention_plan(const int32_t* lengths, int slots, int heads, int queries, int keys, int ctas, int32_t* plan,
-                   int capacity);
+// One or two attention problems over the same slots, heads and queries in one persistent launch (two need a plan).
+int attention_launch(const svx_attention_problem* problems, int count, int slots, int heads, int queries,
+                     const int32_t* plan, int plan_ctas, cudaStream_t stream);
+// Host-side assignment of the attention work units of 1-2 problems to CTAs (layout in attention.cu); ints it takes.
+int attention_plan_ints(int problems, int slots, int heads, int queries, int ctas);
+int attention_plan(const int32_t* const* lengths, const int* keys, int problems, int slots, int heads, int queries,
+                   int ctas, int32_t* plan, int capacity);
 int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int width, int classes, int d,
                     const uint16_t* table_b, const uint16_t* bias_b, const uint16_t* add_b, uint16_t* out_b,
                     const uint16_t* table_c, const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c,

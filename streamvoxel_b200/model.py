@@ -401,7 +401,8 @@ class Engine:
         self.lengths = torch.zeros(self.slots, dtype=torch.int32, device=dev)
         self.host_lengths = (ctypes.c_int32 * self.slots)()
         self.ws = {n: torch.zeros((rows, w), **bf) for n, w in
-                   (('xb', cfg.d), ('xc', cfg.d), ('h', cfg.d), ('qkv', 3 * cfg.d), ('attn', cfg.d), ('mlp', cfg.mlp))}
+                   (('xb', cfg.d), ('xc', cfg.d), ('h', cfg.d), ('qkv', 3 * cfg.d), ('attn', cfg.d), ('mlp', cfg.mlp),
+                    ('qx', cfg.d), ('ax', cfg.d))}
         p = lambda t: t.data_ptr()
 
         def block(w):
@@ -424,7 +425,8 @@ class Engine:
             self._backbone, self._control, self._cross, p(model.final_shift), p(model.final_ops), p(model.head_w),
             p(model.head_b), p(model.rope_sin), p(model.rope_cos), p(model.cross_sin), p(model.cross_cos),
             p(self.lengths))
-        self._workspace = _lib.EngineWorkspace(*[p(self.ws[n]) for n in ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp')])
+        self._workspace = _lib.EngineWorkspace(*[p(self.ws[n]) for n in
+                                                 ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp', 'qx', 'ax')])
         handle = ctypes.c_void_p()
         check(_lib.load().svx_engine_create(ctypes.byref(self._config), ctypes.byref(self._weights),
                                             ctypes.byref(self._workspace), ctypes.byref(handle)), 'svx_engine_create')

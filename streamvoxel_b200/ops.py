@@ -185,6 +185,41 @@ def attention_plan(lengths, slots, heads, queries, keys, ctas, device=None):
     return (plan if device is None else plan.to(device)), min(ctas, units)
 
 
+def attention_multi_plan(problems, slots, heads, queries, ctas, device=None):
+    """Joint work plan of `svx_attention_multi_plan` for one or two problems, each given as (host key lengths or
+    None, keys). Returns the int32 plan (on `device`, or a host tensor) and the CTA count the launch must use."""
+    lib = _lib.load()
+    count = len(problems)
+    size = lib.svx_attention_multi_plan_ints(count, slots, heads, queries, ctas)
+    if size <= 0:
+        raise ValueError('attention_multi_plan: bad shape')
+    hosts = [None if lengths is None else torch.as_tensor(list(lengths), dtype=torch.int32)
+             for lengths, _ in problems]
+    lens = (ctypes.c_void_p * count)(*[None if h is None else h.data_ptr() for h in hosts])
+    keys = (ctypes.c_int * count)(*[int(k) for _, k in problems])
+    plan = torch.empty(size, dtype=torch.int32)
+    check(lib.svx_attention_multi_plan(lens, keys, count, slots, heads, queries, ctas, ptr(plan), size),
+          'svx_attention_multi_plan')
+    units = count * slots * heads * ((queries // 128 + 1) // 2)
+    return (plan if device is None else plan.to(device)), min(ctas, units)
+
+
+def attention_multi(problems, slots, heads, queries, plan):
+    """One launch over one or two attention problems (dicts of `attention`'s arguments: q, k, v, keys, the four
+    strides, lengths, out), with a plan from `attention_multi_plan`. Returns the outputs."""
+    raw = _lib.raw_ptr
+    table, ctas = plan
+    structs = []
+    for pr in problems:
+        structs.append(_lib.AttentionProblem(raw(pr['q']), raw(pr['k']), raw(pr['v']), pr['q_row_stride'],
+                                             pr['kv_slot_stride'], pr['kv_head_stride'], pr['kv_row_stride'],
+                                             ptr(pr.get('lengths')), pr['keys'], ptr(pr['out'])))
+    arr = (_lib.AttentionProblem * len(structs))(*structs)
+    check(_lib.load().svx_attention_multi(arr, len(structs), slots, heads, queries, ptr(table), ctas, stream_ptr()),
+          'svx_attention_multi')
+    return [pr['out'] for pr in problems]
+
+
 def attention(q, k, v, slots, heads, queries, keys, *, q_row_stride, kv_slot_stride, kv_head_stride, kv_row_stride,
               lengths=None, out=None, plan=None):
     """Non-causal head_dim-96 attention over per-slot key lengths; out [slots*queries, heads*96] bf16.

@@ -143,3 +143,17 @@ def test_attention_plan_balances_the_bench_lengths(lib):
     tiles = [(lengths[u // 32] + 95) // 96 + 1 for u in range(256)]
     loads = [sum(tiles[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
     assert max(loads) <= 104 and sum(loads) / grid > 98
+
+
+def test_attention_multi_plan_covers_both_problems(lib):
+    """The joint plan of a cross-attention (bench lengths) and a self-attention assigns all 512 units once, problem
+    0 first in the numbering, and balances better than the two launches' makespans added (104 + 24 unit costs)."""
+    from streamvoxel_b200 import ops
+    lengths = [2368, 3392, 2368, 9536, 4416, 4416, 6464, 9536]
+    plan, grid = ops.attention_multi_plan([(lengths, 9600), (None, 1024)], 8, 8, 1024, 148)
+    offsets, ids = plan[:grid + 1].tolist(), plan[grid + 1:].tolist()
+    assert grid == 148 and sorted(ids) == list(range(512))
+    tiles = [((lengths[u // 32] if u < 256 else 1024) + 95) // 96 + 1 for u in range(512)]
+    loads = [sum(tiles[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
+    assert max(loads) < 104 + 24
+    assert lib.svx_attention_multi_plan_ints(3, 8, 8, 1024, 148) == 0

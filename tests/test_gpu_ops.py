@@ -300,6 +300,33 @@ def test_attention_plan_changes_only_the_schedule(ops):
     assert torch.count_nonzero(base[2 * n:3 * n]) == 0
 
 
+def test_attention_multi_equals_separate_launches(ops):
+    """The joint launch of a varlen cross-attention and a self-attention over the same slots (the engine's control
+    layer) gives each problem bitwise the output of its own launch, with a joint plan and a stale one."""
+    torch.manual_seed(22)
+    slots, heads, n, cap = 3, 8, 1024, 2048
+    d = heads * 96
+    kc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    vc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    host = [2048, 0, 700]
+    lengths = torch.tensor(host, dtype=torch.int32, device='cuda')
+    qx = (torch.randn((slots * n, d), device='cuda') * 1.5).bfloat16()
+    qkv = (torch.randn((slots * n, 3 * d), device='cuda') * 1.5).bfloat16()
+    cross = dict(q=qx, k=kc, v=vc, keys=cap, q_row_stride=d, kv_slot_stride=heads * cap * 96, kv_head_stride=cap * 96,
+                 kv_row_stride=96, lengths=lengths)
+    self_ = dict(q=qkv, k=qkv[:, d:], v=qkv[:, 2 * d:], keys=n, q_row_stride=3 * d, kv_slot_stride=n * 3 * d,
+                 kv_head_stride=96, kv_row_stride=3 * d)
+    alone = [ops.attention(p['q'], p['k'], p['v'], slots, heads, n, p['keys'], q_row_stride=p['q_row_stride'],
+                           kv_slot_stride=p['kv_slot_stride'], kv_head_stride=p['kv_head_stride'],
+                           kv_row_stride=p['kv_row_stride'], lengths=p.get('lengths')) for p in (cross, self_)]
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for plan_lengths, ctas in ((host, sms), (None, sms), (host, 5)):
+        plan = ops.attention_multi_plan([(plan_lengths, cap), (None, n)], slots, heads, n, ctas, 'cuda')
+        outs = [torch.full((slots * n, d), 7.0, device='cuda').bfloat16() for _ in range(2)]
+        ops.attention_multi([dict(cross, out=outs[0]), dict(self_, out=outs[1])], slots, heads, n, plan)
+        assert torch.equal(outs[0], alone[0]) and torch.equal(outs[1], alone[1]), (plan_lengths, ctas)
+
+
 def test_attention_odd_query_tiles_ties_and_empty_slots(ops):
     """384 queries (a CTA with one query tile), tied and zero key lengths, and logits large enough to raise the
     exponent base several times within a row."""
