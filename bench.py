@@ -237,8 +237,9 @@ def run_api_steps(batch, steps, seeds):
 # roofline's `traffic` scales the measurement to the timed launch by its algorithmic bytes (traffic grows with the
 # valid keys / rows processed).
 MEASURED_TRAFFIC = {
-    # 8 slots x 8 heads, keys 1344 + 1024 i: K/V 121.1 MB + Q 12.6 MB + O 12.6 MB
-    'attention_cross': (139.1e6, 121.1e6 + 25.2e6),
+    # cross (8 slots x 8 heads, keys 1344 + 1024 i: K/V 121.1 MB + Q 12.6 MB + O 12.6 MB) + self (Q/K/V 37.7 MB +
+    # O 12.6 MB) in one launch
+    'attention_joint': (222.1e6, 196.6e6),
     # A 12.6 MB + W 4.7 MB + out 50.3 MB (the output mostly stays in L2 at kernel end)
     'gemm_fc1_gelu': (20.5e6, 67.6e6),
 }
@@ -247,8 +248,8 @@ MEASURED_TRAFFIC = {
 def algorithmic_bytes(name, cfg, lengths):
     """Bytes a launch must move at least once (inputs read + outputs written), for the traffic scaling."""
     rows = SLOTS * cfg.patches
-    if name == 'attention_cross':
-        return float(np.sum(lengths)) * cfg.heads * 96 * 2 * 2 + 2 * rows * cfg.d * 2
+    if name == 'attention_joint':   # cross K/V + Q + O, self Q/K/V + O
+        return float(np.sum(lengths)) * cfg.heads * 96 * 2 * 2 + 2 * rows * cfg.d * 2 + 4 * rows * cfg.d * 2
     if name == 'gemm_fc1_gelu':
         return (rows * cfg.d + cfg.mlp * cfg.d + rows * cfg.mlp) * 2.0
     return None
@@ -277,9 +278,16 @@ def time_kernels(cfg, forward, batch, lengths):
         return a.elapsed_time(b) / reps * 1e-3
 
     mean_len = float(np.mean(lengths))
-    # The engine's cross-attention plan for these lengths (the same host LPT assignment svx_engine_set_lengths builds).
-    plan = ops.attention_plan(lengths, SLOTS, heads, cfg.patches, k0.shape[2],
-                              torch.cuda.get_device_properties(dev).multi_processor_count, dev)
+    # The engine's joint plan (cross-attention over these lengths + backbone self-attention), as svx_engine_set_lengths
+    # builds it.
+    cap = k0.shape[2]
+    plan = ops.attention_multi_plan([(lengths, cap), (None, cfg.patches)], SLOTS, heads, cfg.patches,
+                                    torch.cuda.get_device_properties(dev).multi_processor_count, dev)
+    cross = dict(q=ws['qx'], k=k0, v=v0, keys=cap, q_row_stride=d, kv_slot_stride=heads * cap * 96,
+                 kv_head_stride=cap * 96, kv_row_stride=96, lengths=forward.engine.lengths, out=ws['ax'])
+    self_ = dict(q=ws['qkv'], k=ws['qkv'][:, d:], v=ws['qkv'][:, 2 * d:], keys=cfg.patches, q_row_stride=3 * d,
+                 kv_slot_stride=cfg.patches * 3 * d, kv_head_stride=96, kv_row_stride=3 * d, out=ws['attn'])
+    self_flops = 4.0 * SLOTS * heads * cfg.patches * cfg.patches * 96
     kernels = {
         'gemm_qkv_rope': (lambda: ops.gemm(ws['h'], bw['attn.qkv.weight'], bw['attn.qkv.bias'], _lib.EPI_ROPE,
                                            out=ws['qkv'], rope=tables, rope_cols=2 * d, rows_per_slot=cfg.patches),
@@ -295,16 +303,14 @@ def time_kernels(cfg, forward, batch, lengths):
         'gemm_head': (lambda: ops.gemm(ws['h'], m.head_w, m.head_b, _lib.EPI_CLASS_MAJOR, out=forward.logits,
                                        rows_per_slot=cfg.patches, classes=cfg.classes, geometry=cfg.voxel_shape),
                       2.0 * rows * d * 64 * cfg.classes, 1),
+        # the control branch's self-attention (alone: the cross-attention that follows depends on it)
         'attention_self': (lambda: ops.attention(ws['qkv'], ws['qkv'][:, d:], ws['qkv'][:, 2 * d:], SLOTS, heads,
                                                  cfg.patches, cfg.patches, q_row_stride=3 * d,
                                                  kv_slot_stride=cfg.patches * 3 * d, kv_head_stride=96,
-                                                 kv_row_stride=3 * d, out=ws['attn']),
-                           4.0 * SLOTS * heads * cfg.patches * cfg.patches * 96, 24),
-        'attention_cross': (lambda: ops.attention(ws['qkv'], k0, v0, SLOTS, heads, cfg.patches, k0.shape[2],
-                                                  q_row_stride=d, kv_slot_stride=heads * k0.shape[2] * 96,
-                                                  kv_head_stride=k0.shape[2] * 96, kv_row_stride=96,
-                                                  lengths=forward.engine.lengths, out=ws['attn'], plan=plan),
-                            4.0 * SLOTS * heads * cfg.patches * mean_len * 96, 12),
+                                                 kv_row_stride=3 * d, out=ws['attn']), self_flops, 12),
+        # the cross-attention with the backbone's self-attention in one launch
+        'attention_joint': (lambda: ops.attention_multi([cross, self_], SLOTS, heads, cfg.patches, plan),
+                            4.0 * SLOTS * heads * cfg.patches * mean_len * 96 + self_flops, 12),
         'ease_scores': (lambda: ops.ease_scores(forward.logits, batch.status, out=batch.scores),
                         float(forward.logits.numel() * 2 + batch.scores.numel() * 4), 1),
     }

@@ -2,7 +2,7 @@
 
     python -m streamvoxel_b200.profile_case <case> [--launches N]
 
-Cases: attention_cross, attention_self, gemm_fc1, gemm_qkv, gemm_dxd, gemm_head, ease_scores, ease_mark,
+Cases: attention_cross, attention_joint (cross + self in one launch), attention_self, gemm_fc1, gemm_qkv, gemm_dxd, gemm_head, ease_scores, ease_mark,
 ease_select, ease_sample, patch_embed (both branches; tokens uniform over the 257 ids, the gather's worst case). Inputs are seeded random tensors with the bench's shapes (8 slots, d=768, 8 heads x 96, V=256,
 65536 voxels, packed keys of k = 0..7 L1 tiles); every case's working set is larger than the 126 MB L2 except the
 selection. Prints the mean launch time measured with CUDA events.
@@ -34,6 +34,11 @@ def cases():
     lengths = torch.tensor([1344 + 1024 * i for i in range(SLOTS)], dtype=torch.int32, device='cuda')
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     plan = ops.attention_plan(lengths.tolist(), SLOTS, HEADS, PATCHES, CAPACITY, sms, 'cuda')
+    joint_plan = ops.attention_multi_plan([(lengths.tolist(), CAPACITY), (None, PATCHES)], SLOTS, HEADS, PATCHES, sms,
+                                          'cuda')
+    qx = rnd(rows, D)
+    cross = dict(q=qx, k=k, v=v, keys=CAPACITY, q_row_stride=D, kv_slot_stride=HEADS * CAPACITY * 96,
+                 kv_head_stride=CAPACITY * 96, kv_row_stride=96, lengths=lengths, out=torch.empty((rows, D), **bf))
     w = {n: rnd(*shape, s=0.02) for n, shape in
          (('qkv', (3 * D, D)), ('fc1', (MLP, D)), ('dxd', (D, D)), ('head', (64 * V, D)))}
     b = {n: rnd(t.shape[0], s=0.02) for n, t in w.items()}
@@ -60,6 +65,11 @@ def cases():
                                                   kv_slot_stride=HEADS * CAPACITY * 96, kv_head_stride=CAPACITY * 96,
                                                   kv_row_stride=96, lengths=lengths, out=out, plan=plan),
                             4.0 * HEADS * PATCHES * 96 * float(lengths.sum())),
+        'attention_joint': (lambda: ops.attention_multi(
+            [cross, dict(q=qkv, k=qkv[:, D:], v=qkv[:, 2 * D:], keys=PATCHES, q_row_stride=3 * D,
+                         kv_slot_stride=PATCHES * 3 * D, kv_head_stride=96, kv_row_stride=3 * D, out=out)],
+            SLOTS, HEADS, PATCHES, joint_plan),
+            4.0 * HEADS * PATCHES * 96 * float(lengths.sum()) + 4.0 * SLOTS * HEADS * PATCHES * PATCHES * 96),
         'attention_self': (lambda: ops.attention(qkv, qkv[:, D:], qkv[:, 2 * D:], SLOTS, HEADS, PATCHES, PATCHES,
                                                  q_row_stride=3 * D, kv_slot_stride=PATCHES * 3 * D, kv_head_stride=96,
                                                  kv_row_stride=3 * D, out=out),
