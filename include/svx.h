@@ -101,6 +101,35 @@ SVX_API int svx_ease_select_noalloc(const float* scores, const int16_t* tokens, 
                                     int block, int mask_id, uint8_t* chosen, int32_t* index_out, int index_capacity,
                                     int32_t* chosen_count, uint32_t* status, void* stream);
 
+/* ----------------------------------------------------------------------------------------- evaluation decoders */
+
+#define SVX_EVAL_RANDOM    0  /* top_mask(draw, masked, k) */
+#define SVX_EVAL_ENTROPY   1  /* top_mask(score, masked, k) */
+#define SVX_EVAL_MIXED     2  /* top k by score among the top `candidates` by draw */
+#define SVX_EVAL_BLOCK     3  /* linear 4^3 block apportioning of the cumulative count, best scores inside */
+#define SVX_EVAL_THRESHOLD 4  /* masked & draw < threshold (native_quarter) */
+
+/* Per-slot scalars of one evaluation-decoder step (host-filled, device array). */
+typedef struct {
+  int32_t mode;        /* SVX_EVAL_* */
+  int32_t k;           /* voxels to reveal (every mode but THRESHOLD): already min(quota, masked count) */
+  int32_t candidates;  /* MIXED: min(masked count, ceil(multiplier * k)) */
+  int32_t committed;   /* BLOCK: voxels revealed before this step */
+  float threshold;     /* THRESHOLD: reveal probability of the step */
+  int32_t step;        /* written to commit_step for every chosen voxel (0: commit_step untouched) */
+} svx_eval_params;
+
+/* The selections of the evaluation decoders (`streamvoxel/eval/samplers.py:23-64`: random, entropy, mixed, block;
+ * the native_quarter threshold of `:98-101`) over the masked voxels (tokens == mask_id) of each slot's column.
+ * scores/draw: [slots][Y][Z][X] fp32 (negative entropy; uniform draws); pos: [slots][blocks] rank of each 4^3 block
+ * in the seeded order (BLOCK). Writes chosen (uint8), the ascending voxel indices (index_out [slots][capacity],
+ * -1 padded), chosen_count [slots], commit_step (optional) and the per-block quota range [slots][2] (BLOCK,
+ * optional); the reference's assertions (quota range, count) set SVX_STATUS_QUOTA_MISSED in status. */
+SVX_API int svx_eval_select(const float* scores, const float* draw, const int16_t* tokens, const int32_t* pos,
+                            const svx_eval_params* params, int slots, int height, int depth, int width, int mask_id,
+                            uint8_t* chosen, int32_t* index_out, int index_capacity, int32_t* chosen_count,
+                            int32_t* commit_step, int32_t* quota_range, uint32_t* status, void* stream);
+
 /* Categorical draw + token commit for the chosen voxels (`streamvoxel/stream/fast_ops.py:549-551`,
  * `streamvoxel/stream/slot.py:149-151`): p = softmax over classes in fp32, value = argmax(p / q).
  * noise != NULL (parity mode): q = noise[slot][i][classes] fp32, the exponential draws torch.multinomial takes from

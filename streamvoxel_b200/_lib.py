@@ -60,6 +60,11 @@ class EngineWeights(ctypes.Structure):
                                      'cross_sin', 'cross_cos', 'lengths')]
 
 
+class EvalParams(ctypes.Structure):
+    _fields_ = [('mode', ctypes.c_int32), ('k', ctypes.c_int32), ('candidates', ctypes.c_int32),
+                ('committed', ctypes.c_int32), ('threshold', ctypes.c_float), ('step', ctypes.c_int32)]
+
+
 class AttentionProblem(ctypes.Structure):
     _fields_ = [('q', c_ptr), ('k', c_ptr), ('v', c_ptr), ('q_row_stride', c_i64), ('kv_slot_stride', c_i64),
                 ('kv_head_stride', c_i64), ('kv_row_stride', c_i64), ('lengths', c_ptr), ('keys', c_int),
@@ -86,6 +91,8 @@ _SIGNATURES = {
     'svx_ease_sample': (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_int, c_ptr,
                                 c_ptr, c_ptr, c_ptr]),
     'svx_softmax_rows': (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
+    'svx_eval_select': (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, c_int, c_int, c_ptr, c_ptr,
+                                c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     'svx_ease_finish': (c_int, [c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, c_ptr]),
     'svx_patch_embed': (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr, c_ptr,
                                 c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),

@@ -6,6 +6,8 @@
 
 #include <type_traits>
 
+#include <limits.h>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -469,6 +471,180 @@ __global__ void __launch_bounds__(kSelectThreads) ease_fixup_compact_kernel(
   }
 }
 
+// ----------------------------------------------------------------------------------------------- eval selection
+
+// Radix select over a 64-bit order key inside one CTA: the key of the c-th best candidate (c >= 1; with fewer than
+// c candidates 0, so that every candidate is at or above it). Keys are unique (the voxel index is in the low word),
+// so exactly min(c, candidates) candidates have key >= the result. 8-bit digits from the top; a digit whose bucket
+// holds exactly the remaining count ends the search early.
+template <typename Cand, typename Key>
+__device__ uint64_t cta_select_key(int voxels, int c, Cand cand, Key key, uint32_t* hist, unsigned long long* sh) {
+  const int t = threadIdx.x;
+  unsigned long long& prefix = sh[0];
+  unsigned long long& mask = sh[1];
+  unsigned long long& rem = sh[2];
+  unsigned long long& done = sh[3];
+  if (t == 0) { prefix = 0; mask = 0; rem = (unsigned long long)c; done = 0; }
+  __syncthreads();
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = t; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    if (!done) {
+      for (int n = t; n < voxels; n += blockDim.x) {
+        if (!cand(n)) continue;
+        const uint64_t k = key(n);
+        if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+      }
+    }
+    __syncthreads();
+    if (t == 0 && !done) {
+      unsigned long long acc = 0;
+      int d = 255;
+      for (; d >= 0; --d) {
+        if (acc + hist[d] >= rem) break;
+        acc += hist[d];
+      }
+      if (d < 0) {   // fewer candidates than c: all of them
+        prefix = 0; mask = ~0ull; done = 1;
+      } else {
+        rem -= acc;
+        prefix |= (unsigned long long)d << shift;
+        mask |= 255ull << shift;
+        if (hist[d] == rem) done = 1;   // the whole bucket is taken: its smallest key is the threshold
+      }
+    }
+    __syncthreads();
+  }
+  const uint64_t result = prefix;
+  __syncthreads();
+  return result;
+}
+
+// The evaluation decoders' selections (`streamvoxel/eval/samplers.py:23-64`), one CTA per slot over the masked voxels
+// (tokens == mask_id): RANDOM/ENTROPY = top_mask of the draw / the score (`block_quota.py:4-12`: largest first, lower
+// flat index on ties); MIXED = top k by score among the top `candidates` by draw (`samplers.py:23-28`); BLOCK = the
+// linear block apportioning of `block_select` (`samplers.py:31-48`): target q (+1 for the first rem blocks of the
+// seeded order) of the cumulative after = committed + k, quota = target - already committed, then the quota's
+// best-scored masked voxels of each 4^3 block (stable descending); THRESHOLD = masked & draw < threshold (the
+// native_quarter schedule, `samplers.py:98-101`). Then the ascending index list, the commit step of every chosen
+// voxel, and the reference's assertions as SVX_STATUS_QUOTA_MISSED.
+__global__ void __launch_bounds__(kSelectThreads) ease_eval_select_kernel(
+    const float* __restrict__ scores, const float* __restrict__ draw, const int16_t* __restrict__ tokens,
+    const int32_t* __restrict__ pos, const svx_eval_params* __restrict__ params, BlockGeom g, int mask_id,
+    uint8_t* __restrict__ chosen, int32_t* __restrict__ index_out, int index_capacity, int32_t* __restrict__ count_out,
+    int32_t* __restrict__ commit_step, int32_t* __restrict__ quota_range, uint32_t* __restrict__ status) {
+  const int slot = blockIdx.x;
+  const int t = threadIdx.x;
+  const int voxels = g.height * g.depth * g.width;
+  const int64_t off = (int64_t)slot * voxels;
+  const svx_eval_params P = params[slot];
+  const int16_t* tok = tokens + off;
+  const float* sc = scores + off;
+  const float* dr = draw + off;
+  uint8_t* ch = chosen + off;
+  __shared__ uint32_t hist[256];
+  __shared__ unsigned long long sh[4];
+  __shared__ int quota[kSelectThreads];
+  __shared__ int scan[kSelectThreads];
+  __shared__ int qsum, qmin, qmax, qbad;
+  auto masked = [&](int n) { return tok[n] == mask_id; };
+  bool bad = false;
+  if (P.mode == SVX_EVAL_THRESHOLD) {
+    for (int n = t; n < voxels; n += blockDim.x) ch[n] = masked(n) && dr[n] < P.threshold;
+  } else if (P.mode == SVX_EVAL_RANDOM || P.mode == SVX_EVAL_ENTROPY || P.mode == SVX_EVAL_MIXED) {
+    const float* first = P.mode != SVX_EVAL_ENTROPY ? dr : sc;
+    const int c = P.mode == SVX_EVAL_MIXED ? P.candidates : P.k;
+    auto key1 = [&](int n) { return order_key(first[n], n); };
+    const uint64_t thr = c > 0 ? cta_select_key(voxels, c, masked, key1, hist, sh) : ~0ull;
+    for (int n = t; n < voxels; n += blockDim.x) ch[n] = c > 0 && masked(n) && key1(n) >= thr;
+    __syncthreads();
+    if (P.mode == SVX_EVAL_MIXED) {   // the best k scores among the candidates
+      auto cand = [&](int n) { return ch[n] != 0; };
+      auto key2 = [&](int n) { return order_key(sc[n], n); };
+      const uint64_t thr2 = P.k > 0 ? cta_select_key(voxels, P.k, cand, key2, hist, sh) : ~0ull;
+      for (int n = t; n < voxels; n += blockDim.x) ch[n] = P.k > 0 && ch[n] && key2(n) >= thr2;
+    }
+  } else if (P.mode == SVX_EVAL_BLOCK) {
+    if (t == 0) { qsum = 0; qmin = INT_MAX; qmax = INT_MIN; qbad = 0; }
+    __syncthreads();
+    const long long after = (long long)P.committed + P.k;
+    const long long q = after / g.blocks, rem = after % g.blocks;
+    for (int j = t; j < g.blocks; j += blockDim.x) {
+      int legal = 0;
+      for (int i = 0; i < 64; ++i) legal += masked(g.voxel(j, i));
+      const long long target = q + (pos[(int64_t)slot * g.blocks + j] < rem ? 1 : 0);
+      const long long qj = target - (64 - legal);
+      if (qj < 0 || qj > legal) atomicOr(&qbad, 1);
+      const int qc = (int)max(0ll, min(qj, (long long)legal));
+      quota[j] = qc;
+      atomicAdd(&qsum, qc);
+      atomicMin(&qmin, (int)qj);
+      atomicMax(&qmax, (int)qj);
+    }
+    __syncthreads();
+    bad = qbad || qsum != P.k;
+    // In-block ranking: a warp per block, voxel i chosen when fewer than quota masked voxels beat it.
+    const int warp = warp_id(), lane = lane_id(), warps = blockDim.x >> 5;
+    for (int j = warp; j < g.blocks; j += warps) {
+      int n[2];
+      float sm[2];
+      bool sel[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        n[h] = g.voxel(j, lane + 32 * h);
+        sel[h] = masked(n[h]);
+        sm[h] = sel[h] ? sc[n[h]] : -INFINITY;
+      }
+      int rank[2] = {0, 0};
+#pragma unroll 4
+      for (int l = 0; l < 64; ++l) {
+        const float other = __shfl_sync(0xffffffffu, l < 32 ? sm[0] : sm[1], l & 31);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) rank[h] += (other > sm[h]) || (other == sm[h] && l < lane + 32 * h);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) ch[n[h]] = sel[h] && rank[h] < quota[j];
+    }
+    if (quota_range && t == 0) {
+      quota_range[2 * slot] = qmin;
+      quota_range[2 * slot + 1] = qmax;
+    }
+  } else {
+    bad = true;
+    for (int n = t; n < voxels; n += blockDim.x) ch[n] = 0;
+  }
+  __syncthreads();
+  // Ascending compaction (thread t owns voxels [t*per, (t+1)*per)) and the commit step.
+  const int per = (voxels + blockDim.x - 1) / blockDim.x;
+  const int lo = min(voxels, t * per), hi = min(voxels, lo + per);
+  int count = 0;
+  for (int n = lo; n < hi; ++n) count += ch[n] != 0;
+  scan[t] = count;
+  __syncthreads();
+  for (int s = 1; s < (int)blockDim.x; s <<= 1) {
+    const int v = t >= s ? scan[t - s] : 0;
+    __syncthreads();
+    scan[t] += v;
+    __syncthreads();
+  }
+  int w = scan[t] - count;
+  for (int n = lo; n < hi; ++n)
+    if (ch[n]) {
+      if (w < index_capacity) index_out[(int64_t)slot * index_capacity + w] = n;
+      if (commit_step && P.step) commit_step[off + n] = P.step;
+      ++w;
+    }
+  const int total = scan[blockDim.x - 1];
+  for (int i = total + t; i < index_capacity; i += blockDim.x) index_out[(int64_t)slot * index_capacity + i] = -1;
+  bad = __syncthreads_or(bad);
+  if (t == 0) {
+    count_out[slot] = total;
+    const bool exact = P.mode != SVX_EVAL_THRESHOLD;
+    if ((bad || (exact && total != P.k) || total > index_capacity) && status)
+      atomicOr(status + slot, SVX_STATUS_QUOTA_MISSED);
+  }
+}
+
 // ----------------------------------------------------------------------------------------------- sampling
 
 // Row softmax in torch's CUDA order (persistent warp softmax for rows of <= 1024 fp32 elements): W = min(npot, 32)
@@ -743,6 +919,24 @@ extern "C" int svx_ease_select(const float* scores, const int16_t* tokens, const
   ease_fixup_compact_kernel<<<slots, kSelectThreads, 0, s>>>(scores, tokens, last, params, voxels, mask_id, chosen, got,
                                                             index_out, index_capacity, chosen_count, status);
   return launch_status("ease_fixup_compact_kernel");
+}
+
+extern "C" int svx_eval_select(const float* scores, const float* draw, const int16_t* tokens, const int32_t* pos,
+                               const svx_eval_params* params, int slots, int height, int depth, int width,
+                               int mask_id, uint8_t* chosen, int32_t* index_out, int index_capacity,
+                               int32_t* chosen_count, int32_t* commit_step, int32_t* quota_range, uint32_t* status,
+                               void* stream) {
+  SVX_REQUIRE(scores && draw && tokens && pos && params && chosen && index_out && chosen_count && slots > 0 &&
+                  index_capacity > 0,
+              "svx_eval_select: bad arguments (scores, draw and pos are required whatever the mode)");
+  SVX_REQUIRE(height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 && height > 0 && depth > 0 && width > 0,
+              "svx_eval_select: the column must tile by 4^3 blocks");
+  BlockGeom g{height, depth, width, depth / 4, width / 4, (height / 4) * (depth / 4) * (width / 4)};
+  SVX_REQUIRE(g.blocks <= kSelectThreads, "svx_eval_select: at most 1024 blocks per column");
+  ease_eval_select_kernel<<<slots, kSelectThreads, 0, as_stream(stream)>>>(
+      scores, draw, tokens, pos, params, g, mask_id, chosen, index_out, index_capacity, chosen_count, commit_step,
+      quota_range, status);
+  return launch_status("ease_eval_select_kernel");
 }
 
 template <typename T>

@@ -98,6 +98,32 @@ def ease_select(scores, tokens, last, pos, params, mask_id, index_capacity, *, c
     return chosen, index, count
 
 
+EVAL_MODES = dict(random=0, entropy=1, mixed=2, block=3, threshold=4)
+
+
+def eval_params(rows, device):
+    """Pack per-slot evaluation-step scalars [(mode, k, candidates, committed, threshold, step)] (`svx_eval_params`)
+    into a device uint8 tensor."""
+    arr = (_lib.EvalParams * len(rows))(*[_lib.EvalParams(EVAL_MODES[m] if isinstance(m, str) else int(m), int(k),
+                                                          int(c), int(done), float(th), int(st))
+                                          for m, k, c, done, th, st in rows])
+    host = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
+    return host.to(device)
+
+
+def eval_select(scores, draw, tokens, pos, params, mask_id, *, chosen, index, count, commit_step=None,
+                quota_range=None, status=None):
+    """Selections of the evaluation decoders (random / entropy / mixed / block / threshold) over the masked voxels
+    of each slot: fills chosen [S, Y, Z, X] uint8, index [S, capacity] (ascending, -1 padded), count [S] and, when
+    given, commit_step [S, Y, Z, X] int32 and quota_range [S, 2] int32."""
+    s, height, depth, width = tokens.shape
+    check(_lib.load().svx_eval_select(ptr(scores), ptr(draw), ptr(tokens), ptr(pos), ptr(params), s, height, depth,
+                                      width, mask_id, ptr(chosen), ptr(index), index.shape[1], ptr(count),
+                                      ptr(commit_step), ptr(quota_range), ptr(status), stream_ptr()),
+          'svx_eval_select')
+    return chosen, index, count
+
+
 def ease_sample(logits, index, params, tokens, noise=None, values=None, status=None):
     """Categorical draw for the chosen voxels; writes tokens in place. noise [S, capacity, C] fp32 or None (native)."""
     s, c, voxels, stride = _slots_view(logits)

@@ -165,6 +165,57 @@ def slot_cases():
     _save('slot_windows.npz', **out)
 
 
+EVAL_SPECS = [
+    dict(selection='random', schedule='quartercos', steps=8),
+    dict(selection='entropy', schedule='linear', steps=6),
+    dict(selection='mixed', schedule='halfcos', steps=8, candidate_multiplier=2.0),
+    dict(selection='mixed', schedule='reversequarter', steps=5, candidate_multiplier=1.0),
+    dict(selection='block', schedule='quartercos', steps=8, block_size=4),
+    dict(selection='block', schedule='front2', steps=5, block_size=4),
+    dict(selection='entropy', schedule='halfcos', steps=7, rounding='legacy'),
+    dict(selection='random', schedule='native_quarter', steps=6),
+    dict(selection='entropy', schedule='power2', steps=9),
+]
+
+
+def eval_logits(tokens, classes=6):
+    """The evaluation fixtures' forward: fp32 logits [C, Y, Z, X], a pure function of how many voxels are masked."""
+    masked = int((torch.as_tensor(tokens) == classes).sum())
+    generator = torch.Generator().manual_seed(masked + 7)
+    logits = torch.randn((classes, *tuple(tokens.shape)), generator=generator) * 1.5
+    logits[0, 10:] += 4.
+    return logits
+
+
+def eval_cases():
+    """Whole decodes of the reference evaluation decoder `decode` (`streamvoxel/eval/samplers.py:69-115`) on the CPU
+    for every selection mode and several schedules, with every `torch.rand` draw, the exponential noise of every
+    categorical draw (replayed from the seeded generator in the reference's call order) and the block order."""
+    from streamvoxel.eval.samplers import decode
+    shape, classes = (16, 8, 8), 6
+    out = {}
+    for i, spec in enumerate(EVAL_SPECS):
+        seed = 100 + 17 * i
+        forward = lambda tokens, t: eval_logits(tokens[0], classes)[None]
+        result, meta = decode(forward, dict(spec), seed, 'cpu', shape=shape, classes=classes, trace=True)
+        g = torch.Generator().manual_seed(seed)
+        for j, ev in enumerate(meta['events']):
+            out[f'e{i}_s{j}_draw'] = torch.rand(shape, generator=g).numpy()
+            if ev['committed']:
+                out[f'e{i}_s{j}_noise'] = torch.empty((ev['committed'], classes)).exponential_(generator=g).numpy()
+        if spec['selection'] == 'block':
+            bg = torch.Generator().manual_seed(seed + 9173)
+            out[f'e{i}_order'] = torch.randperm(int(np.prod(shape)) // 64, generator=bg).numpy()
+        out[f'e{i}_tokens'] = result['compact']
+        out[f'e{i}_commit'] = result['commit_step'].astype(np.int32)
+        keys = sorted({k for ev in meta['events'] for k in ev})
+        out[f'e{i}_event_keys'] = np.asarray(keys)
+        out[f'e{i}_events'] = np.asarray([[float(ev.get(k, np.nan)) for k in keys] for ev in meta['events']])
+        out[f'e{i}_seed'] = np.int64(seed)
+    out['count'] = np.int64(len(EVAL_SPECS))
+    _save('eval_decode.npz', **out)
+
+
 # ------------------------------------------------------------------------------------------------ models
 
 def _reinit(model, std, seed):
@@ -344,7 +395,7 @@ def wire_cases():
 
 CASES = dict(quota=lambda: quota_cases(), top_mask=lambda: top_mask_cases(), schedule=lambda: schedule_cases(),
              scores=lambda: score_cases(), slots=lambda: slot_cases(), models=lambda: model_cases(),
-             scheduler=lambda: scheduler_cases(), wire=lambda: wire_cases())
+             scheduler=lambda: scheduler_cases(), wire=lambda: wire_cases(), eval=lambda: eval_cases())
 
 
 def main():

@@ -1,4 +1,7 @@
-"""The config-1 driver: one column decoded from all-MASK by the time-free model on our engine and the shipped sampler."""
+"""The config-1 driver (one column decoded from all-MASK by the time-free model on our engine and the shipped sampler)
+and the evaluation decoders on the same kernels."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -21,3 +24,46 @@ def test_decode_low_entropy_last_completes_and_is_deterministic():
     assert tokens.min() >= 0 and tokens.max() < cfg.classes          # every voxel decoded, no mask id left
     assert steps.min() >= 1 and steps.max() == info['nfe']            # every voxel has a commit step
     assert np.array_equal(tokens, again['compact']) and np.array_equal(steps, again['commit_step'])
+
+
+def _eval_fixture_module():
+    import importlib.util
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden', 'make_golden.py')
+    spec = importlib.util.spec_from_file_location('make_golden', path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def test_eval_decoders_match_oracle_given_the_same_draws():
+    """`decode` (random, entropy, mixed, block, native_quarter; every schedule family) on libsvx equals the oracle
+    decoder, pinned to the reference by `tests/test_oracle_golden.py`, fed the same CUDA generator stream (draws,
+    multinomial noise, block order) and the kernel's entropy scores: tokens, commit steps and per-step events."""
+    from oracle import eval_samplers as oes
+    from streamvoxel_b200 import _lib, ops
+    from streamvoxel_b200.decode import decode
+    _lib.require_device()
+    mg = _eval_fixture_module()
+    shape, classes = (16, 8, 8), 6
+
+    def forward(tokens, t):
+        return mg.eval_logits(tokens[0].cpu(), classes)[None].cuda()
+
+    for i, spec in enumerate(mg.EVAL_SPECS):
+        seed = 100 + 17 * i
+        result, meta = decode(forward, dict(spec), seed, 'cuda', shape=shape, classes=classes, trace=True)
+        g = torch.Generator(device='cuda').manual_seed(seed)
+        draw = lambda: torch.rand(shape, device='cuda', generator=g).cpu().numpy()
+        noise = lambda k, c: torch.empty((1, k, c), device='cuda').exponential_(generator=g)[0].cpu().numpy()
+        order = None
+        if spec['selection'] == 'block':
+            bg = torch.Generator(device='cuda').manual_seed(seed + 9173)
+            order = torch.randperm(16, device='cuda', generator=bg).cpu().numpy()
+        score_fn = lambda logits: ops.ease_scores(torch.from_numpy(logits)[None].cuda())[0].cpu().numpy()
+        tokens, commit, events = oes.decode(lambda tok, t: mg.eval_logits(torch.from_numpy(tok), classes).numpy(),
+                                            dict(spec), draw, noise, order=order, shape=shape, classes=classes,
+                                            score_fn=score_fn)
+        assert np.array_equal(result['compact'], tokens), spec
+        assert np.array_equal(result['commit_step'], commit), spec
+        assert meta['events'] == events, spec
+        assert meta['complete'] == (meta['remaining'] == 0)

@@ -384,3 +384,64 @@ def test_patch_embed_matches_gather(ops):
                                    add.cuda(), table, sd['t.bias'].bfloat16().cuda(), add.cuda())
     torch.testing.assert_close(out_b.float().cpu().reshape(2, 256, d), want, atol=1e-2, rtol=1e-2)
     assert torch.equal(out_b, out_c)
+
+
+@pytest.mark.parametrize('seed', [0, 1, 2])
+def test_eval_select_full_size_matches_oracle(ops, seed):
+    """`svx_eval_select` on full-size columns (256 x 16 x 16, 1024 blocks, one slot per mode, tied scores and draws)
+    equals the oracle's random / entropy / mixed / block / threshold selections voxel for voxel."""
+    from oracle import eval_samplers as oes
+    rng = np.random.default_rng(seed)
+    shape, classes, slots = (256, 16, 16), 256, 5
+    total = int(np.prod(shape))
+    tokens = np.where(rng.random((slots, *shape)) < rng.uniform(0.2, 0.9, (slots, 1, 1, 1)),
+                      classes, rng.integers(0, classes, (slots, *shape))).astype(np.int16)
+    scores = (np.round(rng.standard_normal((slots, *shape)) * 4) / 4).astype(np.float32)   # many ties
+    draw = (np.round(rng.random((slots, *shape)) * 512) / 512).astype(np.float32)
+    orders = [rng.permutation(total // 64) for _ in range(slots)]
+    rows, want = [], []
+    for s in range(slots):
+        mask = tokens[s] == classes
+        m = int(mask.sum())
+        mode = ['random', 'entropy', 'mixed', 'block', 'threshold'][s]
+        q = int(rng.integers(1, m // 3))
+        if mode == 'random':
+            want.append(oes.top_mask(draw[s], mask, q)); rows.append((mode, q, 0, 0, 0., 3))
+        elif mode == 'entropy':
+            want.append(oes.top_mask(scores[s], mask, q)); rows.append((mode, q, 0, 0, 0., 3))
+        elif mode == 'mixed':
+            chosen, info = oes.mixed_select(scores[s], mask, draw[s], q, 2.5)
+            want.append(chosen); rows.append((mode, q, info['candidate_count'], 0, 0., 3))
+        elif mode == 'block':   # a prefix of block steps from an all-MASK column (quotas stay valid), then one step
+            tokens[s] = classes
+            mask = tokens[s] == classes
+            for q_prev in (3000, 9000, 20000):
+                step_scores = rng.standard_normal(shape).astype(np.float32)
+                done, _ = oes.block_select(step_scores, mask, q_prev, 4, orders[s], total - int(mask.sum()))
+                tokens[s][done] = rng.integers(0, classes, int(done.sum()))
+                mask = tokens[s] == classes
+            committed = total - int(mask.sum())
+            q = 7777
+            chosen, _ = oes.block_select(scores[s], mask, q, 4, orders[s], committed)
+            want.append(chosen); rows.append((mode, q, 0, committed, 0., 3))
+        else:
+            p = np.float32(0.37)
+            want.append(mask & (draw[s] < p)); rows.append((mode, 0, 0, 0, float(p), 3))
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    pos = np.zeros((slots, total // 64), np.int32)
+    for s in range(slots):
+        pos[s, orders[s]] = np.arange(total // 64)
+    chosen = torch.zeros((slots, *shape), dtype=torch.uint8, device='cuda')
+    index = torch.zeros((slots, total), dtype=torch.int32, device='cuda')
+    count = torch.zeros(slots, dtype=torch.int32, device='cuda')
+    commit = torch.zeros((slots, *shape), dtype=torch.int32, device='cuda')
+    status = torch.zeros(slots, dtype=torch.int32, device='cuda')
+    ops.eval_select(dev(scores), dev(draw), dev(tokens), dev(pos), ops.eval_params(rows, 'cuda'), classes, chosen=chosen,
+                    index=index, count=count, commit_step=commit, status=status)
+    got = chosen.cpu().numpy().astype(bool)
+    for s in range(slots):
+        assert np.array_equal(got[s], want[s]), rows[s][0]
+        n = int(want[s].sum())
+        assert int(count[s]) == n and np.array_equal(index[s, :n].cpu().numpy(), np.flatnonzero(want[s]))
+        assert (index[s, n:] == -1).all() and int(status[s]) == 0
+        assert np.array_equal(commit[s].cpu().numpy() == 3, want[s])

@@ -133,3 +133,43 @@ def test_philox_known_answers():
     assert [int(v) for v in ones] == [0x408f276d, 0x41c83b0e, 0xa20bc7c6, 0x6d5451fd]
     pi = osm.philox4x32_10(0x243f6a88, 0x85a308d3, 0x13198a2e, 0x03707344, 0xa4093822, 0x299f31d0)
     assert [int(v) for v in pi] == [0xd16cfe09, 0x94fdcceb, 0x5001e420, 0x24126ea1]
+
+
+def _eval_fixture_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('make_golden', os.path.join(GOLDEN, 'make_golden.py'))
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def test_eval_decoders_match_reference_given_its_draws():
+    """The evaluation decoders (`streamvoxel/eval/samplers.py`: random, entropy, mixed, block, native_quarter; linear,
+    quartercos, halfcos, reversequarter, front/power and legacy-rounded schedules) reproduce the reference's whole
+    decodes: tokens, commit steps and per-step events, given its draws."""
+    from oracle import eval_samplers as oes
+    mg = _eval_fixture_module()
+    g = _load('eval_decode.npz')
+    assert int(g['count']) == len(mg.EVAL_SPECS)
+    for i, spec in enumerate(mg.EVAL_SPECS):
+        step = {'draw': 0, 'noise': 0}
+
+        def draw(i=i):
+            key = f'e{i}_s{step["draw"]}_draw'
+            step['noise'] = step['draw']
+            step['draw'] += 1
+            return g[key]
+
+        def noise(k, c, i=i):
+            q = g[f'e{i}_s{step["noise"]}_noise']
+            assert q.shape == (k, c)
+            return q
+
+        order = g[f'e{i}_order'] if f'e{i}_order' in g.files else None
+        forward = lambda tokens, t: mg.eval_logits(torch.from_numpy(tokens)).numpy()
+        tokens, commit, events = oes.decode(forward, dict(spec), draw, noise, order=order, shape=(16, 8, 8), classes=6)
+        assert np.array_equal(tokens, g[f'e{i}_tokens']), spec
+        assert np.array_equal(commit, g[f'e{i}_commit']), spec
+        keys = [str(k) for k in g[f'e{i}_event_keys']]
+        got = np.asarray([[float(ev.get(k, np.nan)) for k in keys] for ev in events])
+        np.testing.assert_array_equal(got, g[f'e{i}_events'])
