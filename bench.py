@@ -264,6 +264,7 @@ def time_kernels(cfg, forward, batch, lengths):
     m = forward.model
     bw, cw = m.backbone[0], m.cross[0]
     k0, v0 = forward.engine.kv[0]
+    stats = forward.engine.stats['b']
     tables = m.rope_sin, m.rope_cos
 
     def clock(fn, reps=20):
@@ -289,19 +290,24 @@ def time_kernels(cfg, forward, batch, lengths):
                  kv_slot_stride=cfg.patches * 3 * d, kv_head_stride=96, kv_row_stride=3 * d, out=ws['attn'])
     self_flops = 4.0 * SLOTS * heads * cfg.patches * cfg.patches * 96
     kernels = {
-        'gemm_qkv_rope': (lambda: ops.gemm(ws['h'], bw['attn.qkv.weight'], bw['attn.qkv.bias'], _lib.EPI_ROPE,
-                                           out=ws['qkv'], rope=tables, rope_cols=2 * d, rows_per_slot=cfg.patches),
+        # as the engine runs them: the LayerNorm folded into qkv / fc1 / head, row statistics from fc2 / proj / zero
+        'gemm_qkv_rope': (lambda: ops.gemm(ws['xb'], bw['qkv_fold'][0], bw['attn.qkv.bias'], _lib.EPI_ROPE,
+                                           out=ws['qkv'], rope=tables, rope_cols=2 * d, rows_per_slot=cfg.patches,
+                                           ln=(stats, *bw['qkv_fold'][1:], 1e-6)),
                           2.0 * rows * d * 3 * d, 24),
-        'gemm_fc1_gelu': (lambda: ops.gemm(ws['h'], bw['mlp.0.weight'], bw['mlp.0.bias'], _lib.EPI_BIAS_GELU,
-                                           out=ws['mlp']), 2.0 * rows * d * cfg.mlp, 24),
+        'gemm_fc1_gelu': (lambda: ops.gemm(ws['xb'], bw['fc1_fold'][0], bw['mlp.0.bias'], _lib.EPI_BIAS_GELU,
+                                           out=ws['mlp'], ln=(stats, *bw['fc1_fold'][1:], 1e-6)),
+                          2.0 * rows * d * cfg.mlp, 24),
         'gemm_fc2_gate': (lambda: ops.gemm(ws['mlp'], bw['mlp.2.weight'], bw['mlp.2.bias'], _lib.EPI_GATE_RESIDUAL,
-                                           out=ws['xb'], gate=bw['gate2'], residual=ws['xb']),
+                                           out=ws['xb'], gate=bw['gate2'], residual=ws['xb'], stats_out=stats),
                           2.0 * rows * cfg.mlp * d, 24),
         'gemm_dxd': (lambda: ops.gemm(ws['attn'], bw['attn.proj.weight'], bw['attn.proj.bias'],
-                                      _lib.EPI_GATE_RESIDUAL, out=ws['xb'], gate=bw['gate1'], residual=ws['xb']),
-                     2.0 * rows * d * d, 24 + 4 * 12),
-        'gemm_head': (lambda: ops.gemm(ws['h'], m.head_w, m.head_b, _lib.EPI_CLASS_MAJOR, out=forward.logits,
-                                       rows_per_slot=cfg.patches, classes=cfg.classes, geometry=cfg.voxel_shape),
+                                      _lib.EPI_GATE_RESIDUAL, out=ws['xb'], gate=bw['gate1'], residual=ws['xb'],
+                                      stats_out=stats),
+                     2.0 * rows * d * d, 24 + 3 * 12),
+        'gemm_head': (lambda: ops.gemm(ws['xb'], m.head_fold[0], m.head_b, _lib.EPI_CLASS_MAJOR, out=forward.logits,
+                                       rows_per_slot=cfg.patches, classes=cfg.classes, geometry=cfg.voxel_shape,
+                                       ln=(stats, *m.head_fold[1:], 1e-6)),
                       2.0 * rows * d * 64 * cfg.classes, 1),
         # the control branch's self-attention (alone: the cross-attention that follows depends on it)
         'attention_self': (lambda: ops.attention(ws['qkv'], ws['qkv'][:, d:], ws['qkv'][:, 2 * d:], SLOTS, heads,

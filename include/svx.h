@@ -154,11 +154,12 @@ SVX_API int svx_ease_finish(int16_t* tokens, const uint8_t* last, const uint8_t*
  * per-position y-embedding `unconditional_md4_timefree.py:166-168`):
  * out = bf16(bf16(bf16(sum_o T[t_o*64+o]) + bias) + add[p]).
  * tokens [slots][Y][Z][X] int16; table [(classes+1)*64][d] bf16; add [patches][d] bf16; out [slots*patches][d].
- * table_c == NULL skips the control branch. */
+ * table_c == NULL skips the control branch. stats_b / stats_c (optional, d % 32 == 0): [d/32][slots*patches]
+ * (mean, M2) float pairs of each output row's 32-column chunks, for the LayerNorm fold of the next linear. */
 SVX_API int svx_patch_embed(const int16_t* tokens, int slots, int height, int depth, int width, int patch,
                             int classes, int d, const uint16_t* table_b, const uint16_t* bias_b,
                             const uint16_t* add_b, uint16_t* out_b, const uint16_t* table_c, const uint16_t* bias_c,
-                            const uint16_t* add_c, uint16_t* out_c, void* stream);
+                            const uint16_t* add_c, uint16_t* out_c, float* stats_b, float* stats_c, void* stream);
 
 /* LayerNorm without affine (fp32) + AdaLN modulate (`unconditional_md4_timefree.py:12-13,53-54`):
  * out = bf16(LN(x) * one_plus_scale + shift); one_plus_scale/shift may be NULL (plain LN). x,out [rows][d] bf16. */
@@ -188,6 +189,16 @@ typedef struct {
   int head_dim;              /* ROPE: 96 */
   int classes;               /* CLASS_MAJOR: V; W rows are ordered n = v*64 + o */
   int height, depth, width, patch; /* CLASS_MAJOR geometry */
+  /* LayerNorm fold (bias, GELU, RoPE, class-major epilogues): A holds the raw rows x and W the modulated weights
+   * W'[n][k] = W[n][k] (1 + scale[k]); out = epilogue(r (acc - mu u[n]) + v[n]) with mu, r = 1/sqrt(var + ln_eps)
+   * of each A row from ln_stats_in ([K/32][M] (mean, M2) pairs of its 32-column chunks, chunk-major),
+   * u[n] = sum_k W'[n][k] (bf16), v[n] = b[n] + sum_k W[n][k] shift[k] (fp32). Replaces LayerNorm + modulate +
+   * linear (`unconditional_md4_timefree.py:12-13,53-63`). */
+  const float* ln_stats_in;  /* NULL: out = epilogue(acc + b) */
+  const uint16_t* ln_u;
+  const float* ln_v;
+  float ln_eps;
+  float* ln_stats_out;       /* optional (residual epilogues) [N/32][M] (mean, M2) of the bf16 output rows' chunks */
 } svx_epilogue_args;
 
 /* D = A . W^T with a fused epilogue on the tcgen05 tensor cores (TMA-fed, TMEM accumulator).
@@ -242,11 +253,19 @@ SVX_API int svx_attention_multi_plan(const int32_t* const* lengths, const int* k
 typedef struct {
   const uint16_t *qkv_w, *qkv_b, *proj_w, *proj_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
   const uint16_t *shift1, *one_plus_scale1, *gate1, *shift2, *one_plus_scale2, *gate2;
+  /* LayerNorm fold of the two linears that follow a LayerNorm (see svx_epilogue_args): qkv_w and fc1_w hold the
+   * modulated weights W (1 + scale), u = their row sums (bf16 [N]), v = b + W shift (fp32 [N]). */
+  const uint16_t *qkv_u;
+  const float *qkv_v;
+  const uint16_t *fc1_u;
+  const float *fc1_v;
 } svx_block_weights;
 
 typedef struct {
   const uint16_t *query_w, *query_b, *proj_w, *proj_b, *zero_w, *zero_b;
   const uint16_t *k, *v;     /* packed cached K/V of this layer: [slots][heads][key_capacity][96] bf16, RoPE applied */
+  const uint16_t* query_u;   /* LayerNorm fold of the query linear (no affine): row sums of W (bf16), v = b (fp32) */
+  const float* query_v;
 } svx_cross_weights;
 
 typedef struct {
@@ -266,11 +285,14 @@ typedef struct {
   const uint16_t *rope_sin, *rope_cos;          /* self-attention RoPE tables [patches][48] */
   const uint16_t *cross_sin, *cross_cos;        /* cross-attention query RoPE tables [patches][48] */
   const int32_t* lengths;                       /* [slots] valid packed keys per slot (device) */
+  const uint16_t* head_u;                       /* LayerNorm fold of the head: head_w = W (1 + final scale) */
+  const float* head_v;
 } svx_engine_weights;
 
 typedef struct {
   uint16_t *xb, *xc, *h, *qkv, *attn, *mlp;     /* [slots*patches][d], [..][d], [..][d], [..][3d], [..][d], [..][mlp] */
   uint16_t *qx, *ax;                            /* cross-attention query and output [slots*patches][d] */
+  float *stats_b, *stats_c;                     /* row statistics of xb, xc: (mean, M2) [d/32][n*patches] */
 } svx_engine_workspace;
 
 typedef struct svx_engine svx_engine;

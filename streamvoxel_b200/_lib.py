@@ -34,16 +34,20 @@ class EpilogueArgs(ctypes.Structure):
     """`svx_epilogue_args`."""
     _fields_ = [('epilogue', c_int), ('bias', c_ptr), ('gate', c_ptr), ('residual', c_ptr), ('rope_sin', c_ptr),
                 ('rope_cos', c_ptr), ('rope_cols', c_int), ('rows_per_slot', c_int), ('head_dim', c_int),
-                ('classes', c_int), ('height', c_int), ('depth', c_int), ('width', c_int), ('patch', c_int)]
+                ('classes', c_int), ('height', c_int), ('depth', c_int), ('width', c_int), ('patch', c_int),
+                ('ln_stats_in', c_ptr), ('ln_u', c_ptr), ('ln_v', c_ptr), ('ln_eps', ctypes.c_float),
+                ('ln_stats_out', c_ptr)]
 
 
 class BlockWeights(ctypes.Structure):
     _fields_ = [(n, c_ptr) for n in ('qkv_w', 'qkv_b', 'proj_w', 'proj_b', 'fc1_w', 'fc1_b', 'fc2_w', 'fc2_b',
-                                     'shift1', 'one_plus_scale1', 'gate1', 'shift2', 'one_plus_scale2', 'gate2')]
+                                     'shift1', 'one_plus_scale1', 'gate1', 'shift2', 'one_plus_scale2', 'gate2',
+                                     'qkv_u', 'qkv_v', 'fc1_u', 'fc1_v')]
 
 
 class CrossWeights(ctypes.Structure):
-    _fields_ = [(n, c_ptr) for n in ('query_w', 'query_b', 'proj_w', 'proj_b', 'zero_w', 'zero_b', 'k', 'v')]
+    _fields_ = [(n, c_ptr) for n in ('query_w', 'query_b', 'proj_w', 'proj_b', 'zero_w', 'zero_b', 'k', 'v',
+                                     'query_u', 'query_v')]
 
 
 class EngineConfig(ctypes.Structure):
@@ -57,7 +61,7 @@ class EngineWeights(ctypes.Structure):
                [('backbone', ctypes.POINTER(BlockWeights)), ('control', ctypes.POINTER(BlockWeights)),
                 ('cross', ctypes.POINTER(CrossWeights))] + \
                [(n, c_ptr) for n in ('final_shift', 'final_one_plus_scale', 'head_w', 'head_b', 'rope_sin', 'rope_cos',
-                                     'cross_sin', 'cross_cos', 'lengths')]
+                                     'cross_sin', 'cross_cos', 'lengths', 'head_u', 'head_v')]
 
 
 class EvalParams(ctypes.Structure):
@@ -72,7 +76,7 @@ class AttentionProblem(ctypes.Structure):
 
 
 class EngineWorkspace(ctypes.Structure):
-    _fields_ = [(n, c_ptr) for n in ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp', 'qx', 'ax')]
+    _fields_ = [(n, c_ptr) for n in ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp', 'qx', 'ax', 'stats_b', 'stats_c')]
 
 
 _SIGNATURES = {
@@ -95,7 +99,7 @@ _SIGNATURES = {
                                 c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     'svx_ease_finish': (c_int, [c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, c_ptr]),
     'svx_patch_embed': (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr, c_ptr,
-                                c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+                                c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     'svx_layernorm_modulate': (c_int, [c_ptr, c_int, c_int, ctypes.c_float, c_ptr, c_ptr, c_ptr, c_ptr]),
     'svx_gemm': (c_int, [c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, ctypes.POINTER(EpilogueArgs), c_ptr]),
     'svx_attention': (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_int, c_int, c_int, c_int,

@@ -34,12 +34,15 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float (&v)[8]) {
 
 // out[p] = bf16(bf16(bf16(sum_o T[t_o * 64 + o]) + bias) + add[p]): the gather form of the one-hot Conv3d
 // (`streamvoxel/stream/fast_ops.py:69-75`: fp32 accumulation over the 64 patch offsets, the conv bias added in bf16),
-// then the per-position y-embedding (`fast_ops.py:282-283`). One CTA per patch, 8 channels per thread.
+// then the per-position y-embedding (`fast_ops.py:282-283`). One CTA per patch, 8 channels per thread. With stats
+// buffers it also writes (mean, M2) of every 32-column chunk of the bf16 output row (four adjacent lanes), chunk-major
+// ([d/32][rows]), the statistics the first LayerNorm of each branch takes from the GEMM that follows.
 __global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int height, int depth, int width, int classes,
                                    int d, const uint16_t* __restrict__ table_b, const uint16_t* __restrict__ bias_b,
                                    const uint16_t* __restrict__ add_b, uint16_t* __restrict__ out_b,
                                    const uint16_t* __restrict__ table_c, const uint16_t* __restrict__ bias_c,
-                                   const uint16_t* __restrict__ add_c, uint16_t* __restrict__ out_c) {
+                                   const uint16_t* __restrict__ add_c, uint16_t* __restrict__ out_c,
+                                   float2* __restrict__ stats_b, float2* __restrict__ stats_c) {
   constexpr int P = 4, P3 = 64;
   grid_launch_dependents();
   grid_dependency_wait();
@@ -71,6 +74,22 @@ __global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int heigh
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = round_bf16(round_bf16(round_bf16(acc[j]) + bias[j]) + add[j]);
     *reinterpret_cast<uint4*>((branch ? out_c : out_b) + (int64_t)row * d + c0) = pack_bf16x8(acc);
+    float2* stats = branch ? stats_c : stats_b;
+    if (stats) {   // d % 32 == 0: the four lanes of a chunk are all active (lanes past d have returned)
+      const unsigned group = 0xFu << (threadIdx.x & 28);
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += acc[j];
+      sum += __shfl_xor_sync(group, sum, 1);
+      sum += __shfl_xor_sync(group, sum, 2);
+      const float mean = sum * (1.f / 32.f);
+      float m2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m2 = fmaf(acc[j] - mean, acc[j] - mean, m2);
+      m2 += __shfl_xor_sync(group, m2, 1);
+      m2 += __shfl_xor_sync(group, m2, 2);
+      if ((threadIdx.x & 3) == 0) stats[(int64_t)(threadIdx.x / 4) * gridDim.x + row] = make_float2(mean, m2);
+    }
   }
 }
 
@@ -139,13 +158,14 @@ __global__ void layernorm_modulate_kernel(const uint16_t* __restrict__ x, int ro
 int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int width, int classes, int d,
                     const uint16_t* table_b, const uint16_t* bias_b, const uint16_t* add_b, uint16_t* out_b,
                     const uint16_t* table_c, const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c,
-                    cudaStream_t stream) {
+                    float* stats_b, float* stats_c, cudaStream_t stream) {
+  SVX_REQUIRE((!stats_b && !stats_c) || d % 32 == 0, "patch_embed: row statistics need d % 32 == 0");
   const int patches = (height / 4) * (depth / 4) * (width / 4);
   int threads = ((d / 8 + 31) / 32) * 32;
   if (threads < 64) threads = 64;
   return launch_dependent("patch_embed_kernel", patch_embed_kernel, dim3(slots * patches), dim3(threads), 0, stream,
                           tokens, height, depth, width, classes, d, table_b, bias_b, add_b, out_b, table_c, bias_c,
-                          add_c, out_c);
+                          add_c, out_c, reinterpret_cast<float2*>(stats_b), reinterpret_cast<float2*>(stats_c));
 }
 
 int layernorm_run(const uint16_t* x, int rows, int d, float eps, const uint16_t* ops, const uint16_t* shift,
@@ -172,14 +192,16 @@ using namespace svx;
 extern "C" int svx_patch_embed(const int16_t* tokens, int slots, int height, int depth, int width, int patch,
                                int classes, int d, const uint16_t* table_b, const uint16_t* bias_b,
                                const uint16_t* add_b, uint16_t* out_b, const uint16_t* table_c,
-                               const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c, void* stream) {
+                               const uint16_t* bias_c, const uint16_t* add_c, uint16_t* out_c, float* stats_b,
+                               float* stats_c, void* stream) {
   SVX_REQUIRE(patch == 4, "svx_patch_embed: only patch 4 is implemented");
   SVX_REQUIRE(height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 && slots > 0, "svx_patch_embed: bad shape");
   SVX_REQUIRE(d % 8 == 0 && d <= 8192, "svx_patch_embed: d must be a multiple of 8");
   SVX_REQUIRE(tokens && table_b && bias_b && add_b && out_b, "svx_patch_embed: null backbone operand");
   SVX_REQUIRE(!table_c || (bias_c && add_c && out_c), "svx_patch_embed: incomplete control operands");
+  SVX_REQUIRE(!stats_c || table_c, "svx_patch_embed: control statistics without the control branch");
   return patch_embed_run(tokens, slots, height, depth, width, classes, d, table_b, bias_b, add_b, out_b, table_c,
-                         bias_c, add_c, out_c, as_stream(stream));
+                         bias_c, add_c, out_c, stats_b, stats_c, as_stream(stream));
 }
 
 extern "C" int svx_layernorm_modulate(const uint16_t* x, int rows, int d, float eps, const uint16_t* one_plus_scale,

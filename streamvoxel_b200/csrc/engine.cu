@@ -9,7 +9,10 @@
 // as one attention launch (LN, query, LN, qkv first; proj, cross proj after), with one work plan over both.
 //   logits = head(modulate(LN(b)))  in class-major [slot][V][Y][Z][X]
 // Every TMA descriptor is built once in svx_engine_create; svx_engine_forward only enqueues kernels, so it can be
-// captured in a CUDA graph per slot bucket.
+// captured in a CUDA graph per slot bucket. No LayerNorm kernel runs: every residual-stream producer (the embed and
+// the residual GEMM epilogues) writes the row statistics of its bf16 output, and every linear that follows a
+// LayerNorm + AdaLN modulate takes the raw stream with the modulation folded into its weights and the normalisation
+// into its epilogue (r (acc - mu u) + v).
 #include <vector>
 
 #include "common.cuh"
@@ -41,15 +44,16 @@ namespace {
 
 constexpr int HD = 96;
 
-int plan_block(std::vector<GemmPlan>& plans, const svx_block_weights& bw, const svx_engine_workspace& ws, int rows,
-               int d, int mlp) {
+// x: the block's residual stream, the A operand of its qkv and fc1 linears (LayerNorm folded in).
+int plan_block(std::vector<GemmPlan>& plans, const svx_block_weights& bw, const svx_engine_workspace& ws,
+               const uint16_t* x, int rows, int d, int mlp) {
   GemmPlan p;
   int rc;
-  if ((rc = gemm_plan(&p, ws.h, bw.qkv_w, rows, 3 * d, d, 0))) return rc;
+  if ((rc = gemm_plan(&p, x, bw.qkv_w, rows, 3 * d, d, 0))) return rc;
   plans.push_back(p);
   if ((rc = gemm_plan(&p, ws.attn, bw.proj_w, rows, d, d, 0))) return rc;
   plans.push_back(p);
-  if ((rc = gemm_plan(&p, ws.h, bw.fc1_w, rows, mlp, d, 0))) return rc;
+  if ((rc = gemm_plan(&p, x, bw.fc1_w, rows, mlp, d, 0))) return rc;
   plans.push_back(p);
   if ((rc = gemm_plan(&p, ws.mlp, bw.fc2_w, rows, d, mlp, 0))) return rc;
   plans.push_back(p);
@@ -63,6 +67,20 @@ EpiParams epi(int kind, const uint16_t* bias) {
   return e;
 }
 
+float2* stats_of(const svx_engine& E, const uint16_t* x) {
+  return reinterpret_cast<float2*>(x == E.ws.xb ? E.ws.stats_b : E.ws.stats_c);
+}
+
+// The LayerNorm (eps 1e-6, `unconditional_md4_timefree.py:53-54`) of x folded into a linear's epilogue.
+void fold(EpiParams& e, const svx_engine& E, const uint16_t* x, const uint16_t* u, const float* v) {
+  e.ln_stats_in = stats_of(E, x);
+  e.ln_u = u;
+  e.ln_v = v;
+  e.ln_chunks = E.cfg.d / 32;
+  e.ln_inv_chunks = 32.f / (float)E.cfg.d;
+  e.ln_eps = 1e-6f;
+}
+
 // The self-attention problem of a block: q, k, v interleaved in the qkv workspace, out to the attn workspace.
 svx_attention_problem self_problem(const svx_engine& E) {
   const svx_engine_workspace& ws = E.ws;
@@ -72,14 +90,13 @@ svx_attention_problem self_problem(const svx_engine& E) {
                                E.patches, ws.attn};
 }
 
-// The first half of a block: h = modulate(LN(x)), qkv = RoPE(h W_qkv^T + b).
+// The first half of a block: qkv = RoPE(modulate(LN(x)) W_qkv^T + b), the LayerNorm folded into the epilogue.
 int run_block_qkv(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
                   cudaStream_t s) {
   const int d = E.cfg.d, rows = n * E.patches;
   const svx_engine_workspace& ws = E.ws;
-  int rc;
-  if ((rc = layernorm_run(x, rows, d, 1e-6f, bw.one_plus_scale1, bw.shift1, ws.h, s))) return rc;
   EpiParams e = epi(SVX_EPI_ROPE, bw.qkv_b);
+  fold(e, E, x, bw.qkv_u, bw.qkv_v);
   e.rope_sin = E.w.rope_sin; e.rope_cos = E.w.rope_cos;
   e.rope_cols = 2 * d; e.rows_per_slot = E.patches; e.head_dim = HD;
   return gemm_run(plans[0], rows, ws.qkv, e, s);
@@ -92,12 +109,13 @@ int run_block_rest(const svx_engine& E, const svx_block_weights& bw, const GemmP
   const svx_engine_workspace& ws = E.ws;
   int rc;
   EpiParams e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);
-  e.gate = bw.gate1; e.residual = x;
+  e.gate = bw.gate1; e.residual = x; e.ln_stats_out = stats_of(E, x);
   if ((rc = gemm_run(plans[1], rows, x, e, s))) return rc;
-  if ((rc = layernorm_run(x, rows, d, 1e-6f, bw.one_plus_scale2, bw.shift2, ws.h, s))) return rc;
-  if ((rc = gemm_run(plans[2], rows, ws.mlp, epi(SVX_EPI_BIAS_GELU, bw.fc1_b), s))) return rc;
+  e = epi(SVX_EPI_BIAS_GELU, bw.fc1_b);
+  fold(e, E, x, bw.fc1_u, bw.fc1_v);
+  if ((rc = gemm_run(plans[2], rows, ws.mlp, e, s))) return rc;
   e = epi(SVX_EPI_GATE_RESIDUAL, bw.fc2_b);
-  e.gate = bw.gate2; e.residual = x;
+  e.gate = bw.gate2; e.residual = x; e.ln_stats_out = stats_of(E, x);
   return gemm_run(plans[3], rows, x, e, s);
 }
 
@@ -123,8 +141,8 @@ int run_control_layer(const svx_engine& E, int i, int j, int n, cudaStream_t s) 
   const GemmPlan* bp = &E.bplan[(size_t)i * 4];
   int rc;
   if ((rc = run_block(E, E.control[j], cp, ws.xc, n, s))) return rc;
-  if ((rc = layernorm_run(ws.xc, rows, d, 1e-6f, nullptr, nullptr, ws.h, s))) return rc;
   EpiParams e = epi(SVX_EPI_ROPE, cw.query_b);
+  fold(e, E, ws.xc, cw.query_u, cw.query_v);   // LayerNorm without affine (`streaming_controlnet.py:44`)
   e.rope_sin = E.w.cross_sin; e.rope_cos = E.w.cross_cos;
   e.rope_cols = d; e.rows_per_slot = E.patches; e.head_dim = HD;
   if ((rc = gemm_run(cp[4], rows, ws.qx, e, s))) return rc;
@@ -137,11 +155,11 @@ int run_control_layer(const svx_engine& E, int i, int j, int n, cudaStream_t s) 
   const int32_t* plan = E.plan_dev + (size_t)(n - 1) * E.plan_stride;
   if ((rc = attention_launch(both, 2, n, E.cfg.heads, E.patches, plan, std::min(E.plan_ctas, units), s))) return rc;
   e = epi(SVX_EPI_RESIDUAL, cw.proj_b);
-  e.residual = ws.xc;
+  e.residual = ws.xc; e.ln_stats_out = stats_of(E, ws.xc);
   if ((rc = gemm_run(cp[5], rows, ws.xc, e, s))) return rc;
   if ((rc = run_block_rest(E, E.backbone[i], bp, ws.xb, n, s))) return rc;
   e = epi(SVX_EPI_RESIDUAL, cw.zero_b);
-  e.residual = ws.xb;
+  e.residual = ws.xb; e.ln_stats_out = stats_of(E, ws.xb);
   return gemm_run(cp[6], rows, ws.xb, e, s);
 }
 
@@ -170,6 +188,16 @@ extern "C" int svx_engine_create(const svx_engine_config* config, const svx_engi
   SVX_REQUIRE(c.patch == 4, "svx_engine_create: patch must be 4");
   SVX_REQUIRE(c.height % 4 == 0 && c.depth % 4 == 0 && c.width % 4 == 0, "svx_engine_create: bad voxel shape");
   SVX_REQUIRE(c.heads > 0 && c.d == c.heads * HD, "svx_engine_create: head_dim must be 96 (d = heads * 96)");
+  SVX_REQUIRE(workspace->stats_b && workspace->stats_c && weights->head_u && weights->head_v,
+              "svx_engine_create: the LayerNorm fold needs the row-statistics workspace and the head's u and v");
+  for (int i = 0; i < c.depth_layers; ++i)
+    SVX_REQUIRE(weights->backbone[i].qkv_u && weights->backbone[i].qkv_v && weights->backbone[i].fc1_u &&
+                    weights->backbone[i].fc1_v,
+                "svx_engine_create: every block needs the LayerNorm fold's u and v");
+  for (int j = 0; j < c.n_control; ++j)
+    SVX_REQUIRE(weights->control[j].qkv_u && weights->control[j].qkv_v && weights->control[j].fc1_u &&
+                    weights->control[j].fc1_v && weights->cross[j].query_u && weights->cross[j].query_v,
+                "svx_engine_create: every control layer needs the LayerNorm fold's u and v");
   SVX_REQUIRE(c.slots > 0 && c.depth_layers > 0 && c.n_control >= 0 && c.n_control <= c.depth_layers,
               "svx_engine_create: bad layer counts");
   SVX_REQUIRE(c.n_control == 0 || (c.layer_index && c.key_capacity > 0 && c.key_capacity % 64 == 0),
@@ -198,18 +226,18 @@ extern "C" int svx_engine_create(const svx_engine_config* config, const svx_engi
   e->w.backbone = nullptr; e->w.control = nullptr; e->w.cross = nullptr;
   int rc = SVX_OK;
   for (int i = 0; i < c.depth_layers && !rc; ++i)
-    rc = plan_block(e->bplan, e->backbone[i], e->ws, e->rows_max, c.d, c.mlp);
+    rc = plan_block(e->bplan, e->backbone[i], e->ws, e->ws.xb, e->rows_max, c.d, c.mlp);
   for (int j = 0; j < c.n_control && !rc; ++j) {
-    rc = plan_block(e->cplan, e->control[j], e->ws, e->rows_max, c.d, c.mlp);
+    rc = plan_block(e->cplan, e->control[j], e->ws, e->ws.xc, e->rows_max, c.d, c.mlp);
     GemmPlan p;
-    if (!rc) rc = gemm_plan(&p, e->ws.h, e->cross[j].query_w, e->rows_max, c.d, c.d, 0);
+    if (!rc) rc = gemm_plan(&p, e->ws.xc, e->cross[j].query_w, e->rows_max, c.d, c.d, 0);
     if (!rc) e->cplan.push_back(p);
     if (!rc) rc = gemm_plan(&p, e->ws.ax, e->cross[j].proj_w, e->rows_max, c.d, c.d, 0);
     if (!rc) e->cplan.push_back(p);
     if (!rc) rc = gemm_plan(&p, e->ws.xc, e->cross[j].zero_w, e->rows_max, c.d, c.d, 0);
     if (!rc) e->cplan.push_back(p);
   }
-  if (!rc) rc = gemm_plan(&e->head, e->ws.h, weights->head_w, e->rows_max, c.classes * 64, c.d, 0);
+  if (!rc) rc = gemm_plan(&e->head, e->ws.xb, weights->head_w, e->rows_max, c.classes * 64, c.d, 0);
   if (!rc && c.n_control) {
     int device = 0, sms = 0;
     cudaError_t err = cudaGetDevice(&device);
@@ -243,7 +271,7 @@ extern "C" int svx_engine_forward(svx_engine* E, int n, const int16_t* tokens, u
   const int rows = n * E->patches;
   int rc = patch_embed_run(tokens, n, c.height, c.depth, c.width, c.classes, c.d, E->w.table_b, E->w.bias_b,
                            E->w.yadd_b, ws.xb, c.n_control ? E->w.table_c : nullptr, E->w.bias_c, E->w.yadd_c, ws.xc,
-                           s);
+                           ws.stats_b, c.n_control ? ws.stats_c : nullptr, s);
   if (rc) return rc;
   for (int i = 0; i < c.depth_layers; ++i) {
     const int j = E->layer_map[i];
@@ -251,10 +279,10 @@ extern "C" int svx_engine_forward(svx_engine* E, int n, const int16_t* tokens, u
                 : run_block(*E, E->backbone[i], &E->bplan[(size_t)i * 4], ws.xb, n, s);
     if (rc) return rc;
   }
-  if ((rc = layernorm_run(ws.xb, rows, c.d, 1e-6f, E->w.final_one_plus_scale, E->w.final_shift, ws.h, s))) return rc;
   EpiParams e{};
   e.epilogue = SVX_EPI_CLASS_MAJOR;
   e.bias = E->w.head_b;
+  fold(e, *E, ws.xb, E->w.head_u, E->w.head_v);   // final LN + modulate (`unconditional_md4_timefree.py:172-175`)
   e.rows_per_slot = E->patches;
   e.classes = c.classes;
   e.height = c.height; e.depth = c.depth; e.width = c.width; e.patch = 4;
@@ -274,9 +302,9 @@ extern "C" int svx_engine_set_lengths(svx_engine* E, const int32_t* lengths, voi
 
 extern "C" int svx_engine_launches(const svx_engine* E, int n) {
   if (!E || n < 1) return 0;
-  const int per_block = 7;   // LN, qkv, attention, proj, LN, fc1, fc2
-  const int per_cross = 4;   // LN, query, proj, zero (its attention shares the backbone block's launch)
-  return 1 + E->cfg.depth_layers * per_block + E->cfg.n_control * (per_block + per_cross) + 2;
+  const int per_block = 5;   // qkv, attention, proj, fc1, fc2 (LayerNorms folded into qkv and fc1)
+  const int per_cross = 3;   // query, proj, zero (its attention shares the backbone block's launch)
+  return 1 + E->cfg.depth_layers * per_block + E->cfg.n_control * (per_block + per_cross) + 1;
 }
 
 extern "C" void svx_engine_destroy(svx_engine* E) { delete E; }

@@ -27,6 +27,9 @@ constexpr int BM = 128, BK = 64;
 constexpr int kThreads = 640;  // warps 0-1 producer/MMA, 2-3 idle, 4-19 epilogue
 constexpr int kEpilogueWarps = 16;
 constexpr uint32_t A_BYTES = BM * BK * 2;
+// Kernel variants: the epilogue (svx_epilogue, bits 0-2) | kFold (LayerNorm folded into this GEMM's epilogue) |
+// kStats (row statistics for the next LayerNorm written by this epilogue).
+constexpr int kFold = 8, kStats = 16;
 
 __device__ __forceinline__ void record_timeout() { atomicOr(&g_svx_timeouts, SVX_STATUS_WAIT_TIMEOUT); }
 
@@ -85,17 +88,27 @@ __device__ __forceinline__ void unpack8(uint4 raw, float* v) {
 
 // Operands an epilogue chunk reads from global memory, fetched before the accumulator is ready (bf16, packed).
 struct Operands {
-  uint4 bias[4];
+  uint4 bias[4];    // bias | u (LayerNorm fold, bf16)
   uint4 extra[4];   // gate (GATE_RESIDUAL) | sin, cos (ROPE: 2 + 2)
   uint4 res[4];     // residual row slice (GATE_RESIDUAL, RESIDUAL)
+  float v;          // LayerNorm fold: v[n + lane], staged through shared memory for the whole warp
 };
 
 // GLOBAL_RES = false: the residual comes from a staging box in shared memory instead.
-template <int EPI, bool GLOBAL_RES = true>
+template <int E, bool GLOBAL_RES = true>
 __device__ __forceinline__ void prefetch32(const EpiParams& ep, int N, int row, int n, Operands& o) {
-  const uint4* b = reinterpret_cast<const uint4*>(ep.bias + n);
+  constexpr int EPI = E & 7;
+  [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
+  if constexpr (LN_FOLD) {   // u (bf16) and v (fp32) in place of the bias, which v holds
+    const uint4* u = reinterpret_cast<const uint4*>(ep.ln_u + n);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) o.bias[i] = b[i];
+    for (int i = 0; i < 4; ++i) o.bias[i] = __ldg(u + i);
+    o.v = __ldg(ep.ln_v + n + lane_id());
+  } else {
+    const uint4* b = reinterpret_cast<const uint4*>(ep.bias + n);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o.bias[i] = b[i];
+  }
   if constexpr (EPI == SVX_EPI_GATE_RESIDUAL) {
     const uint4* g = reinterpret_cast<const uint4*>(ep.gate + n);
 #pragma unroll
@@ -118,18 +131,82 @@ __device__ __forceinline__ void prefetch32(const EpiParams& ep, int N, int row, 
   }
 }
 
-// Epilogue arithmetic of one row x 32 columns [n, n+32) of the tile; acc holds fp32 accumulators, o the bias, gate,
-// RoPE table and residual words of the row.
-template <int EPI>
-__device__ __forceinline__ void epilogue_math(const EpiParams& ep, int row, int n, const uint32_t (&acc)[32],
-                                              const Operands& o, float (&y)[32]) {
-  const uint32_t* bw = reinterpret_cast<const uint32_t*>(o.bias);
+// Mean and 1/sqrt(var + eps) of a row from its 32-column chunk statistics (var: the biased variance of layer_norm).
+// Shifted sums about the first chunk's mean m0 (no division, and no cancellation when |mean| >> std):
+// mean = m0 + sum_c d_c / C and var = sum_c (M2_c + 32 d_c^2) / (32 C) - (sum_c d_c / C)^2 with d_c = mean_c - m0.
+// Statistics are chunk-major ([chunk][M]), so a warp's 32 consecutive rows read one 256-byte run per chunk; 12
+// chunks are loaded together so that their latencies overlap.
+__device__ __forceinline__ float2 row_norm(const EpiParams& ep, int row, int M) {
+  const float2* st = ep.ln_stats_in + row;
+  const float m0 = __ldg(st).x;
+  float s1 = 0.f, s2 = 0.f;
+  for (int c0 = 0; c0 < ep.ln_chunks; c0 += 12) {
+    float2 q[12];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float2 v = round2(__fadd2_rn(make_float2(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1])),
-                                       unpack2(bw[j])));
-    y[2 * j] = v.x;
-    y[2 * j + 1] = v.y;
+    for (int i = 0; i < 12; ++i)
+      q[i] = c0 + i < ep.ln_chunks ? __ldg(st + (int64_t)(c0 + i) * M) : make_float2(m0, 0.f);
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+      const float d = q[i].x - m0;
+      s1 += d;
+      s2 += fmaf(32.f * d, d, q[i].y);
+    }
+  }
+  const float dm = s1 * ep.ln_inv_chunks;
+  const float var = fmaxf(fmaf(-dm, dm, s2 * ep.ln_inv_chunks * (1.f / 32.f)), 0.f);
+  return make_float2(m0 + dm, rsqrtf(var + ep.ln_eps));
+}
+
+// (mean, M2) of the 32 bf16 values a thread stores for its row: the statistics of the next LayerNorm.
+__device__ __forceinline__ void chunk_stats(const EpiParams& ep, int M, int row, int n, const float (&y)[32]) {
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) sum += round_bf16(y[j]);
+  const float mean = sum * (1.f / 32.f);
+  float m2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float d = round_bf16(y[j]) - mean;
+    m2 = fmaf(d, d, m2);
+  }
+  ep.ln_stats_out[(int64_t)(n / 32) * M + row] = make_float2(mean, m2);   // chunk-major [N / 32][M]
+}
+
+// Epilogue arithmetic of one row x 32 columns [n, n+32) of the tile; acc holds fp32 accumulators, o the bias, gate,
+// RoPE table and residual words of the row; nr the row's (mean, 1/std) when the LayerNorm is folded in.
+// vs: the warp's 32 v values of this chunk in shared memory (LayerNorm fold; nullptr: read them from global memory).
+template <int E>
+__device__ __forceinline__ void epilogue_math(const EpiParams& ep, int row, int n, const uint32_t (&acc)[32],
+                                              const Operands& o, float2 nr, float (&y)[32],
+                                              const float* vs = nullptr) {
+  constexpr int EPI = E & 7;
+  [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
+  if constexpr (LN_FOLD) {
+    const float2 ra = make_float2(nr.y, nr.y), rb = make_float2(-nr.x * nr.y, -nr.x * nr.y);
+    const uint32_t* uw = reinterpret_cast<const uint32_t*>(o.bias);
+    const float4* vp = reinterpret_cast<const float4*>(vs ? vs : ep.ln_v + n);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 vq = vp[q];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * q + h;
+        const float2 v2 = h ? make_float2(vq.z, vq.w) : make_float2(vq.x, vq.y);
+        const float2 a = make_float2(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1]));
+        const float2 v = round2(__ffma2_rn(a, ra, __ffma2_rn(rb, unpack2(uw[j]), v2)));
+        y[2 * j] = v.x;
+        y[2 * j + 1] = v.y;
+      }
+    }
+  } else {
+    const uint32_t* bw = reinterpret_cast<const uint32_t*>(o.bias);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 v = round2(__fadd2_rn(make_float2(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1])),
+                                         unpack2(bw[j])));
+      y[2 * j] = v.x;
+      y[2 * j + 1] = v.y;
+    }
   }
   if constexpr (EPI == SVX_EPI_BIAS_GELU) {
 #pragma unroll
@@ -168,11 +245,15 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, int row, int 
 }
 
 // Epilogue of one row x 32 columns [n, n+32) of the tile, stored straight to global memory.
-template <int EPI>
-__device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, int N, int row, int n,
-                                           const uint32_t (&acc)[32], const Operands& o) {
+template <int E>
+__device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, int M, int N, int row, int n,
+                                           const uint32_t (&acc)[32], const Operands& o, float2 nr,
+                                           const float* vs = nullptr) {
+  constexpr int EPI = E & 7;
+  [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
   float y[32];
-  epilogue_math<EPI>(ep, row, n, acc, o, y);
+  epilogue_math<E>(ep, row, n, acc, o, nr, y, vs);
+  if constexpr (LN_STATS && EPI != SVX_EPI_CLASS_MAJOR) chunk_stats(ep, M, row, n, y);
   if constexpr (EPI == SVX_EPI_CLASS_MAJOR) {
     // W rows are ordered n = v * 64 + o, so the 32 columns are one class v and offsets o..o+31 of one patch.
     constexpr int P = 4, P3 = 64;
@@ -194,11 +275,13 @@ __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, i
   }
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int E>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            uint16_t* __restrict__ out, int M, int N, int K,
                                                            const EpiParams ep) {
+  constexpr int EPI = E & 7;
+  [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
   constexpr uint32_t B_BYTES = BN * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   extern __shared__ uint8_t smem_raw[];
@@ -291,19 +374,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN);
       // The first chunk's operands are fetched while the main loop still runs.
+      float2 nr = make_float2(0.f, 1.f);
+      if constexpr (LN_FOLD) {
+        if (row < M && group < CHUNKS) nr = row_norm(ep, row, M);
+      }
       Operands ops;
-      if (group < CHUNKS) prefetch32<EPI>(ep, N, row, n0 + group * 32, ops);
+      if (group < CHUNKS) prefetch32<E>(ep, N, row, n0 + group * 32, ops);
       if (!tc::wait(acc_full + buf, use & 1, abort_flag)) { record_timeout(); break; }
       tc::fence_after();
 #pragma unroll
       for (int c = 0; c < (CHUNKS + 3) / 4; ++c) {
         const int chunk = group + 4 * c;
         if (chunk < CHUNKS) {
-          if (c > 0) prefetch32<EPI>(ep, N, row, n0 + chunk * 32, ops);
+          if (c > 0) prefetch32<E>(ep, N, row, n0 + chunk * 32, ops);
           uint32_t acc[32];
           tc::ld32(taddr + chunk * 32, acc);
           tc::wait_ld();
-          if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + chunk * 32, acc, ops);
+          if (row < M) epilogue32<E>(ep, out, M, N, row, n0 + chunk * 32, acc, ops, nr);
         }
       }
       tc::fence_before();
@@ -331,11 +418,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 constexpr int PM = 256;
 constexpr uint32_t BOX = 32 * 32 * 2;   // one staging box: 32 rows x 32 bf16
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int E>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                      uint16_t* __restrict__ out, int M, int N, int K, const EpiParams ep) {
+  constexpr int EPI = E & 7;
+  [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
   constexpr uint32_t HB_BYTES = (BN / 2) * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;   // allocations are powers of two
   constexpr bool STAGED = EPI != SVX_EPI_CLASS_MAJOR;
@@ -352,6 +441,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* res_full = acc_empty + 2;                              // per epilogue warp and box
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2 * kEpilogueWarps);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  float* v_stage = reinterpret_cast<float*>(tmem_slot + 4);       // LayerNorm fold: 32 v values per epilogue warp
 
   const int warp = warp_id(), lane = lane_id();
   const uint32_t rank = tc::cluster_rank();
@@ -359,6 +449,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int kblocks = K / BK;
   const int n_tiles = N / BN;
   const int tiles = (M / PM) * n_tiles;
+  // Tiles of this pair: round-robin (tile = pair + k * pairs), or, with the LayerNorm fold, a contiguous run, so that
+  // consecutive tiles share their rows and the rows' statistics are merged once per row block (same makespan).
+  int t_first = pair, t_step = pairs, t_count = tiles > pair ? (tiles - pair + pairs - 1) / pairs : 0;
+  if constexpr (LN_FOLD) {
+    const int base = tiles / pairs, extra = tiles % pairs;
+    t_first = pair * base + min(pair, extra);
+    t_step = 1;
+    t_count = base + (pair < extra ? 1 : 0);
+  }
   grid_launch_dependents();
 
   if (threadIdx.x == 0) {
@@ -387,7 +486,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
       int it = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+      for (int k = 0; ok && k < t_count; ++k) {
+        const int tile = t_first + k * t_step;
         const int m0 = (tile / n_tiles) * PM + (int)rank * BM, n0 = (tile % n_tiles) * BN + (int)rank * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES, round = it / STAGES;
@@ -401,7 +501,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = tc::instr_desc(PM, BN);
       int it = 0, local = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < tiles; tile += pairs, ++local) {
+      for (int k = 0; ok && k < t_count; ++k, ++local) {
+        const int tile = t_first + k * t_step;
         const int buf = local & 1, use = local >> 1;
         if (use > 0 && !tc::wait_w(acc_empty + buf, (use - 1) & 1, abort_flag)) { record_timeout(); break; }
         tc::fence_after();
@@ -435,7 +536,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // Row `lane` of a 64B-swizzled 32 x 32 box: 16-byte piece q sits at q ^ ((lane / 2) % 4).
     const int swz = (lane >> 1) & 3;
     int local = 0;
-    for (int tile = pair; tile < tiles; tile += pairs, ++local) {
+    int norm_block = -1;   // row block whose statistics nr holds
+    float2 nr = make_float2(0.f, 1.f);
+    for (int k = 0; k < t_count; ++k, ++local) {
+      const int tile = t_first + k * t_step;
       const int m0 = (tile / n_tiles) * PM + (int)rank * BM, n0 = (tile % n_tiles) * BN;
       const int buf = local & 1, use = local >> 1;
       const int row0 = m0 + quarter * 32, row = row0 + lane;
@@ -456,8 +560,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       }
+      if constexpr (LN_FOLD) {
+        if (group < CHUNKS && tile / n_tiles != norm_block) {
+          nr = row_norm(ep, row, M);
+          norm_block = tile / n_tiles;
+        }
+      }
       Operands ops;
-      if (group < CHUNKS) prefetch32<EPI, !STAGED>(ep, N, row, n0 + group * 32, ops);
+      if (group < CHUNKS) prefetch32<E, !STAGED>(ep, N, row, n0 + group * 32, ops);
       if (!tc::wait(acc_full + buf, use & 1, abort_flag)) { record_timeout(); break; }
       tc::fence_after();
       bool ok = true;
@@ -465,7 +575,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int j = 0; j < MINE; ++j) {
         const int chunk = group + 4 * j;
         if (chunk < CHUNKS) {
-          if (j > 0) prefetch32<EPI, !STAGED>(ep, N, row, n0 + chunk * 32, ops);
+          if (j > 0) prefetch32<E, !STAGED>(ep, N, row, n0 + chunk * 32, ops);
           uint32_t acc[32];
           tc::ld32(taddr + chunk * 32, acc);
           tc::wait_ld();
@@ -477,7 +587,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               for (int q = 0; q < 4; ++q) ops.res[q] = rb[q ^ swz];
             }
             float y[32];
-            epilogue_math<EPI>(ep, row, n0 + chunk * 32, acc, ops, y);
+            float* vs = v_stage + ws * 32;
+            if constexpr (LN_FOLD) {
+              __syncwarp();   // the previous chunk's reads of vs are done
+              vs[lane] = ops.v;
+              __syncwarp();
+            }
+            epilogue_math<E>(ep, row, n0 + chunk * 32, acc, ops, nr, y, LN_FOLD ? vs : nullptr);
+            if constexpr (LN_STATS) chunk_stats(ep, M, row, n0 + chunk * 32, y);
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               rb[q ^ swz] = make_uint4(tc::pack_bf16x2(y[8 * q], y[8 * q + 1]), tc::pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
@@ -490,7 +607,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               tc::bulk_commit();
             }
           } else {
-            if (row < M) epilogue32<EPI>(ep, out, N, row, n0 + chunk * 32, acc, ops);
+            float* vs = v_stage + ws * 32;
+            if constexpr (LN_FOLD) {
+              __syncwarp();
+              vs[lane] = ops.v;
+              __syncwarp();
+            }
+            if (row < M) epilogue32<E>(ep, out, M, N, row, n0 + chunk * 32, acc, ops, nr, LN_FOLD ? vs : nullptr);
           }
         }
       }
@@ -511,7 +634,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 template <int BN, int STAGES>
 constexpr size_t pair_smem_bytes() {
   return 1024 + STAGES * (A_BYTES + (size_t)(BN / 2) * BK * 2) + (size_t)kEpilogueWarps * 2 * BOX +
-         (2 * STAGES + 4 + 2 * kEpilogueWarps) * 8 + 16;
+         (2 * STAGES + 4 + 2 * kEpilogueWarps) * 8 + 16 + kEpilogueWarps * 32 * 4;
 }
 
 template <int BN, int STAGES, int EPI>
@@ -707,8 +830,9 @@ static int make_box_map(CUtensorMap* map, const void* ptr, int rows, int cols) {
   return SVX_OK;
 }
 
-template <int EPI>
+template <int E>
 static int run_epi(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream) {
+  constexpr int EPI = E & 7;
   if (plan.pair_bn && M % PM == 0) {
     CUtensorMap o{}, r{};
     if (EPI != SVX_EPI_CLASS_MAJOR) {
@@ -719,26 +843,38 @@ static int run_epi(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& 
       }
       if (rc) return rc;
     }
-    return launch_pair_epi<EPI>(plan.a, plan.b_half, o, r, plan.pair_bn, out, M, plan.N, plan.K, ep, stream);
+    return launch_pair_epi<E>(plan.a, plan.b_half, o, r, plan.pair_bn, out, M, plan.N, plan.K, ep, stream);
   }
-  return launch_epi<EPI>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
+  return launch_epi<E>(plan.a, plan.b, plan.bn, out, M, plan.N, plan.K, ep, stream);
 }
 
 int gemm_run(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream) {
   SVX_REQUIRE(M > 0 && M <= plan.M && M % BM == 0, "gemm: run rows must be a multiple of 128 within the plan");
-  switch (ep.epilogue) {
+  // The LayerNorm fold is built for the linears that follow a LayerNorm (bias, GELU, RoPE, class-major epilogues),
+  // the row statistics for the residual epilogues that produce the normalised streams.
+  const bool fold = ep.ln_stats_in != nullptr, stats = ep.ln_stats_out != nullptr;
+  SVX_REQUIRE(!fold || (ep.ln_u && ep.ln_v && ep.ln_chunks > 0 && plan.K == 32 * ep.ln_chunks),
+              "gemm: the LayerNorm fold needs u, v and K / 32 statistics per row");
+  switch (ep.epilogue | (fold ? kFold : 0) | (stats ? kStats : 0)) {
     case SVX_EPI_BIAS: return run_epi<SVX_EPI_BIAS>(plan, M, out, ep, stream);
     case SVX_EPI_BIAS_GELU: return run_epi<SVX_EPI_BIAS_GELU>(plan, M, out, ep, stream);
     case SVX_EPI_GATE_RESIDUAL: return run_epi<SVX_EPI_GATE_RESIDUAL>(plan, M, out, ep, stream);
     case SVX_EPI_RESIDUAL: return run_epi<SVX_EPI_RESIDUAL>(plan, M, out, ep, stream);
     case SVX_EPI_ROPE: return run_epi<SVX_EPI_ROPE>(plan, M, out, ep, stream);
     case SVX_EPI_CLASS_MAJOR: return run_epi<SVX_EPI_CLASS_MAJOR>(plan, M, out, ep, stream);
-    default: return fail(SVX_ERR_INVALID, "gemm: unknown epilogue");
+    case SVX_EPI_BIAS | kFold: return run_epi<SVX_EPI_BIAS | kFold>(plan, M, out, ep, stream);
+    case SVX_EPI_BIAS_GELU | kFold: return run_epi<SVX_EPI_BIAS_GELU | kFold>(plan, M, out, ep, stream);
+    case SVX_EPI_ROPE | kFold: return run_epi<SVX_EPI_ROPE | kFold>(plan, M, out, ep, stream);
+    case SVX_EPI_CLASS_MAJOR | kFold: return run_epi<SVX_EPI_CLASS_MAJOR | kFold>(plan, M, out, ep, stream);
+    case SVX_EPI_GATE_RESIDUAL | kStats: return run_epi<SVX_EPI_GATE_RESIDUAL | kStats>(plan, M, out, ep, stream);
+    case SVX_EPI_RESIDUAL | kStats: return run_epi<SVX_EPI_RESIDUAL | kStats>(plan, M, out, ep, stream);
+    default:
+      return fail(SVX_ERR_INVALID, "gemm: unknown epilogue, or a LayerNorm fold / row statistics it does not take");
   }
 }
 
-int epi_from_args(const svx_epilogue_args* e, EpiParams* ep, int N) {
-  SVX_REQUIRE(e && e->bias, "gemm: epilogue needs a bias");
+int epi_from_args(const svx_epilogue_args* e, EpiParams* ep, int N, int K) {
+  SVX_REQUIRE(e && (e->bias || e->ln_stats_in), "gemm: epilogue needs a bias (or the LayerNorm fold's u and v)");
   *ep = EpiParams{};
   ep->epilogue = e->epilogue;
   ep->bias = e->bias;
@@ -751,6 +887,21 @@ int epi_from_args(const svx_epilogue_args* e, EpiParams* ep, int N) {
   ep->head_dim = e->head_dim;
   ep->classes = e->classes;
   ep->height = e->height; ep->depth = e->depth; ep->width = e->width; ep->patch = e->patch;
+  ep->ln_stats_in = reinterpret_cast<const float2*>(e->ln_stats_in);
+  ep->ln_u = e->ln_u;
+  ep->ln_v = e->ln_v;
+  ep->ln_chunks = K / 32;
+  ep->ln_inv_chunks = K >= 32 ? 32.f / (float)K : 0.f;
+  ep->ln_eps = e->ln_eps;
+  ep->ln_stats_out = reinterpret_cast<float2*>(e->ln_stats_out);
+  if (e->ln_stats_in)
+    SVX_REQUIRE(e->ln_u && e->ln_v && K % 32 == 0 && (reinterpret_cast<uintptr_t>(e->ln_u) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(e->ln_v) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(e->ln_stats_in) & 7) == 0,
+                "gemm: the LayerNorm fold needs K % 32 == 0, 16-byte aligned u and v, 8-byte aligned statistics");
+  if (e->ln_stats_out)
+    SVX_REQUIRE(e->epilogue != SVX_EPI_CLASS_MAJOR && (reinterpret_cast<uintptr_t>(e->ln_stats_out) & 7) == 0,
+                "gemm: row statistics need a row-major output and an 8-byte aligned buffer");
   if (e->epilogue == SVX_EPI_GATE_RESIDUAL) SVX_REQUIRE(e->gate && e->residual, "gemm: gated residual needs gate+res");
   if (e->epilogue == SVX_EPI_RESIDUAL) SVX_REQUIRE(e->residual, "gemm: residual epilogue needs the residual");
   if (e->epilogue == SVX_EPI_ROPE)
@@ -772,7 +923,7 @@ extern "C" int svx_gemm(const uint16_t* A, const uint16_t* W, uint16_t* out, int
                         const svx_epilogue_args* epi, void* stream) {
   SVX_REQUIRE(A && W && out, "svx_gemm: null operand");
   EpiParams ep;
-  int rc = epi_from_args(epi, &ep, N);
+  int rc = epi_from_args(epi, &ep, N, K);
   if (rc) return rc;
   GemmPlan plan;
   rc = gemm_plan(&plan, A, W, M, N, K, 0);

@@ -164,6 +164,19 @@ def rope_tables(positions, head_dim):
             phase.cos().to(torch.bfloat16).reshape(n, -1).contiguous())
 
 
+def fold_layernorm(weight, bias, one_plus_scale=None, shift=None):
+    """The LayerNorm + AdaLN modulate before a linear, folded into it (`svx_epilogue_args` ln_*): the linear then
+    takes the raw residual stream x and computes r (x W'^T - mu u) + v, with mu, r the row's LayerNorm statistics.
+    W' = bf16(W (1 + scale)) (exact fp32 product of two bf16 values, rounded once), u = sum_k W'[n, k] (bf16: its
+    term is scaled by mu / sigma), v = b + W shift (float64 sums, fp32). Without scale/shift (LayerNorm without
+    affine) W' = W and v = b."""
+    w = weight.float()
+    folded = weight if one_plus_scale is None else (w * one_plus_scale.float()[None, :]).to(torch.bfloat16)
+    u = folded.double().sum(1)
+    v = bias.double() + (w.double() @ shift.double() if shift is not None else 0.)
+    return folded.contiguous(), u.to(torch.bfloat16).contiguous(), v.float().contiguous()
+
+
 class PreparedModel:
     """Device-resident bf16 weights and precomputed constants of one model (one per GPU)."""
 
@@ -199,12 +212,14 @@ class PreparedModel:
         head_w = sd['backbone.class_head.weight'].reshape(64, v, cfg.d).transpose(0, 1).reshape(64 * v, cfg.d)
         self.head_w = head_w.to(torch.bfloat16).contiguous()
         self.head_b = sd['backbone.class_head.bias'].reshape(64, v).t().reshape(-1).to(torch.bfloat16).contiguous()
+        self.head_fold = fold_layernorm(self.head_w, self.head_b, self.final_ops, self.final_shift)
         self.cross = []
         for j in range(len(cfg.layer_indices)):
             self.cross.append({n: _bf16(sd[f'cross.{j}.{n}'], dev) for n in
                                ('query.weight', 'query.bias', 'proj.weight', 'proj.bias')} |
                               {'zero.weight': _bf16(sd[f'zero.{j}.weight'], dev),
                                'zero.bias': _bf16(sd[f'zero.{j}.bias'], dev)})
+            self.cross[j]['query_fold'] = fold_layernorm(self.cross[j]['query.weight'], self.cross[j]['query.bias'])
         self.zero_yadd = torch.zeros((cfg.patches, cfg.d), device=dev, dtype=torch.bfloat16)
         if cfg.layer_indices:
             self.table_l1, self.bias_l1 = self._table('l1_patch')
@@ -224,6 +239,8 @@ class PreparedModel:
              ('attn.qkv.weight', 'attn.qkv.bias', 'attn.proj.weight', 'attn.proj.bias', 'mlp.0.weight', 'mlp.0.bias',
               'mlp.2.weight', 'mlp.2.bias')}
         w.update(shift1=s1, ops1=(1 + c1).contiguous(), gate1=g1, shift2=s2, ops2=(1 + c2).contiguous(), gate2=g2)
+        w['qkv_fold'] = fold_layernorm(w['attn.qkv.weight'], w['attn.qkv.bias'], w['ops1'], w['shift1'])
+        w['fc1_fold'] = fold_layernorm(w['mlp.0.weight'], w['mlp.0.bias'], w['ops2'], w['shift2'])
         return w
 
     def _y_embed(self, prefix, y):
@@ -403,18 +420,23 @@ class Engine:
         self.ws = {n: torch.zeros((rows, w), **bf) for n, w in
                    (('xb', cfg.d), ('xc', cfg.d), ('h', cfg.d), ('qkv', 3 * cfg.d), ('attn', cfg.d), ('mlp', cfg.mlp),
                     ('qx', cfg.d), ('ax', cfg.d))}
+        # row statistics of the residual streams for the folded LayerNorms: chunk-major [d/32][n*patches] (mean, M2)
+        self.stats = {n: torch.zeros((cfg.d // 32, rows, 2), device=dev, dtype=torch.float32) for n in ('b', 'c')}
         p = lambda t: t.data_ptr()
 
         def block(w):
-            return _lib.BlockWeights(p(w['attn.qkv.weight']), p(w['attn.qkv.bias']), p(w['attn.proj.weight']),
-                                     p(w['attn.proj.bias']), p(w['mlp.0.weight']), p(w['mlp.0.bias']),
+            (qkv_w, qkv_u, qkv_v), (fc1_w, fc1_u, fc1_v) = w['qkv_fold'], w['fc1_fold']
+            return _lib.BlockWeights(p(qkv_w), p(w['attn.qkv.bias']), p(w['attn.proj.weight']),
+                                     p(w['attn.proj.bias']), p(fc1_w), p(w['mlp.0.bias']),
                                      p(w['mlp.2.weight']), p(w['mlp.2.bias']), p(w['shift1']), p(w['ops1']),
-                                     p(w['gate1']), p(w['shift2']), p(w['ops2']), p(w['gate2']))
+                                     p(w['gate1']), p(w['shift2']), p(w['ops2']), p(w['gate2']),
+                                     p(qkv_u), p(qkv_v), p(fc1_u), p(fc1_v))
         self._backbone = (_lib.BlockWeights * cfg.depth)(*[block(w) for w in model.backbone])
         self._control = (_lib.BlockWeights * max(1, n_control))(*[block(w) for w in model.control])
         self._cross = (_lib.CrossWeights * max(1, n_control))(*[
             _lib.CrossWeights(p(c['query.weight']), p(c['query.bias']), p(c['proj.weight']), p(c['proj.bias']),
-                              p(c['zero.weight']), p(c['zero.bias']), p(k), p(v))
+                              p(c['zero.weight']), p(c['zero.bias']), p(k), p(v), p(c['query_fold'][1]),
+                              p(c['query_fold'][2]))
             for c, (k, v) in zip(model.cross, self.kv)])
         self._layer_index = (ctypes.c_int32 * max(1, n_control))(*cfg.layer_indices)
         y, z, x = cfg.voxel_shape
@@ -422,11 +444,12 @@ class Engine:
                                          self.key_capacity, n_control, self._layer_index)
         self._weights = _lib.EngineWeights(
             p(model.table_b), p(model.bias_b), p(model.yadd_b), p(model.table_c), p(model.bias_c), p(model.yadd_c),
-            self._backbone, self._control, self._cross, p(model.final_shift), p(model.final_ops), p(model.head_w),
-            p(model.head_b), p(model.rope_sin), p(model.rope_cos), p(model.cross_sin), p(model.cross_cos),
-            p(self.lengths))
+            self._backbone, self._control, self._cross, p(model.final_shift), p(model.final_ops),
+            p(model.head_fold[0]), p(model.head_b), p(model.rope_sin), p(model.rope_cos), p(model.cross_sin),
+            p(model.cross_cos), p(self.lengths), p(model.head_fold[1]), p(model.head_fold[2]))
         self._workspace = _lib.EngineWorkspace(*[p(self.ws[n]) for n in
-                                                 ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp', 'qx', 'ax')])
+                                                 ('xb', 'xc', 'h', 'qkv', 'attn', 'mlp', 'qx', 'ax')],
+                                               p(self.stats['b']), p(self.stats['c']))
         handle = ctypes.c_void_p()
         check(_lib.load().svx_engine_create(ctypes.byref(self._config), ctypes.byref(self._weights),
                                             ctypes.byref(self._workspace), ctypes.byref(handle)), 'svx_engine_create')

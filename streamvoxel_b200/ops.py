@@ -153,7 +153,9 @@ def ease_finish(tokens, last, finish, air_token):
 
 
 def patch_embed(tokens, classes, table_b, bias_b, add_b, table_c=None, bias_c=None, add_c=None, out_b=None,
-                out_c=None):
+                out_c=None, stats_b=None, stats_c=None):
+    """Patch-4 token embed of both branches; stats_b / stats_c (optional fp32 [d/32, rows, 2]) receive each output
+    row's 32-column chunk statistics (mean, M2), chunk-major, for the LayerNorm fold of the next linear."""
     s, height, depth, width = tokens.shape
     d = table_b.shape[1]
     patches = (height // 4) * (depth // 4) * (width // 4)
@@ -163,7 +165,7 @@ def patch_embed(tokens, classes, table_b, bias_b, add_b, table_c=None, bias_c=No
         out_c = torch.empty((s * patches, d), device=tokens.device, dtype=torch.bfloat16)
     check(_lib.load().svx_patch_embed(ptr(tokens), s, height, depth, width, 4, classes, d, ptr(table_b), ptr(bias_b),
                                       ptr(add_b), ptr(out_b), ptr(table_c), ptr(bias_c), ptr(add_c), ptr(out_c),
-                                      stream_ptr()), 'svx_patch_embed')
+                                      ptr(stats_b), ptr(stats_c), stream_ptr()), 'svx_patch_embed')
     return out_b, out_c
 
 
@@ -177,8 +179,10 @@ def layernorm_modulate(x, eps=1e-6, one_plus_scale=None, shift=None, out=None):
 
 
 def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None, rope=None, rope_cols=0,
-         rows_per_slot=0, head_dim=96, classes=0, geometry=(0, 0, 0)):
-    """out = epilogue(a @ w.T + bias) on the tcgen05 GEMM. a [M,K], w [N,K], bias [N] bf16."""
+         rows_per_slot=0, head_dim=96, classes=0, geometry=(0, 0, 0), ln=None, stats_out=None):
+    """out = epilogue(a @ w.T + bias) on the tcgen05 GEMM. a [M,K], w [N,K], bias [N] bf16.
+    ln = (stats [K/32, M, 2] fp32, u [N] bf16, v [N] fp32, eps): the LayerNorm folded in, out = epilogue(r (acc - mu u) + v)
+    with w the modulated weights; stats_out: fp32 [N/32, M, 2] chunk statistics of the bf16 output rows."""
     m, k = a.shape
     n = w.shape[0]
     for t in (a, w, bias):
@@ -192,6 +196,13 @@ def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None,
                              rope_sin=ptr(rope[0] if rope else None).value, rope_cos=ptr(rope[1] if rope else None).value,
                              rope_cols=rope_cols, rows_per_slot=rows_per_slot, head_dim=head_dim, classes=classes,
                              height=geometry[0], depth=geometry[1], width=geometry[2], patch=4)
+    if ln is not None:
+        stats, u, v, eps = ln
+        assert stats.dtype == v.dtype == torch.float32 and u.dtype == torch.bfloat16
+        args.ln_stats_in, args.ln_u, args.ln_v, args.ln_eps = ptr(stats).value, ptr(u).value, ptr(v).value, eps
+    if stats_out is not None:
+        assert stats_out.dtype == torch.float32
+        args.ln_stats_out = ptr(stats_out).value
     check(_lib.load().svx_gemm(ptr(a), ptr(w), ptr(out), m, n, k, ctypes.byref(args), stream_ptr()), 'svx_gemm')
     return out
 

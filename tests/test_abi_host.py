@@ -45,8 +45,10 @@ def test_invalid_arguments_are_rejected_before_any_launch(lib):
 def test_ctypes_structs_match_the_c_layout():
     from streamvoxel_b200 import _lib, ops
     assert ctypes.sizeof(_lib.StepParams) == 32 == ops.STEP_DTYPE.itemsize
-    assert _lib.EpilogueArgs.bias.offset == 8 and ctypes.sizeof(_lib.EpilogueArgs) == 8 + 5 * 8 + 8 * 4
-    assert ctypes.sizeof(_lib.BlockWeights) == 14 * 8 and ctypes.sizeof(_lib.CrossWeights) == 8 * 8
+    assert _lib.EpilogueArgs.bias.offset == 8 and ctypes.sizeof(_lib.EpilogueArgs) == 8 + 5 * 8 + 8 * 4 + 5 * 8
+    assert _lib.EpilogueArgs.ln_stats_in.offset == 80 and _lib.EpilogueArgs.ln_stats_out.offset == 112
+    assert ctypes.sizeof(_lib.BlockWeights) == 18 * 8 and ctypes.sizeof(_lib.CrossWeights) == 10 * 8
+    assert ctypes.sizeof(_lib.EngineWorkspace) == 10 * 8 and ctypes.sizeof(_lib.EngineWeights) == 20 * 8
     assert _lib.EngineConfig.layer_index.offset == 48
 
 

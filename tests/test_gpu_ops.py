@@ -445,3 +445,78 @@ def test_eval_select_full_size_matches_oracle(ops, seed):
         assert int(count[s]) == n and np.array_equal(index[s, :n].cpu().numpy(), np.flatnonzero(want[s]))
         assert (index[s, n:] == -1).all() and int(status[s]) == 0
         assert np.array_equal(commit[s].cpu().numpy() == 3, want[s])
+
+
+def _chunk_stats(x):
+    """(mean, M2) of every 32-column chunk of the rows of x, chunk-major [K/32, M, 2], in float64."""
+    c = x.double().reshape(x.shape[0], -1, 32)
+    mean = c.mean(-1)
+    return torch.stack((mean, ((c - mean[..., None]) ** 2).sum(-1)), -1).transpose(0, 1)
+
+
+def test_patch_embed_writes_row_statistics(ops):
+    torch.manual_seed(16)
+    classes, d = 31, 192
+    table = (torch.randn(((classes + 1) * 64, d)) * 0.05).bfloat16().cuda()
+    bias = (torch.randn(d) * 0.1 + 0.3).bfloat16().cuda()
+    add = (torch.randn((256, d)) * 0.1).bfloat16().cuda()
+    tokens = torch.randint(0, classes + 1, (2, 64, 16, 16)).to(torch.int16).cuda()
+    stats_b = torch.zeros((d // 32, 512, 2), device='cuda')
+    stats_c = torch.zeros_like(stats_b)
+    out_b, out_c = ops.patch_embed(tokens, classes, table, bias, add, table, bias, add, stats_b=stats_b,
+                                   stats_c=stats_c)
+    want = _chunk_stats(out_b.float())
+    torch.testing.assert_close(stats_b.double(), want, atol=1e-5, rtol=1e-5)
+    assert torch.equal(stats_b, stats_c)
+
+
+@pytest.mark.parametrize('epilogue', ['bias', 'gelu', 'rope', 'class_major'])
+def test_gemm_layernorm_fold_matches_layernorm_then_linear(ops, epilogue):
+    """A residual GEMM writes its output rows' chunk statistics; the next linear takes the raw rows with the LayerNorm
+    + AdaLN modulate folded in (W' = W (1 + scale), r (acc - mu u) + v) and matches LayerNorm -> modulate -> linear
+    in fp32 within 1e-2 abs + 1e-2 rel."""
+    from streamvoxel_b200 import _lib
+    from streamvoxel_b200.model import fold_layernorm
+    torch.manual_seed(17)
+    m, k = 1024, 768
+    n = {'bias': 768, 'gelu': 3072, 'rope': 2304, 'class_major': 64 * 5}[epilogue]
+    res = (torch.randn((m, k), device='cuda') * 0.8 + 0.2).bfloat16()
+    a = (torch.randn((m, k), device='cuda') * 0.5).bfloat16()
+    wr = (torch.randn((k, k), device='cuda') * 0.03).bfloat16()
+    br = (torch.randn(k, device='cuda') * 0.1).bfloat16()
+    x = res.clone()
+    stats = torch.full((k // 32, m, 2), float('nan'), device='cuda')
+    ops.gemm(a, wr, br, _lib.EPI_RESIDUAL, out=x, residual=x, stats_out=stats)
+    torch.testing.assert_close(stats.double(), _chunk_stats(x.float()), atol=1e-5, rtol=1e-5)
+    w = (torch.randn((n, k), device='cuda') * 0.03).bfloat16()
+    b = (torch.randn(n, device='cuda') * 0.1).bfloat16()
+    ops_ = (1 + torch.randn(k, device='cuda') * 0.2).bfloat16()
+    shift = (torch.randn(k, device='cuda') * 0.2).bfloat16()
+    wf, u, v = fold_layernorm(w, b, ops_, shift)
+    h = torch.nn.functional.layer_norm(x.float(), (k,), eps=1e-6) * ops_.float() + shift.float()
+    y = h @ w.float().t() + b.float()
+    kwargs = {}
+    if epilogue == 'gelu':
+        kind, want = _lib.EPI_BIAS_GELU, torch.nn.functional.gelu(y)
+    elif epilogue == 'rope':
+        theta = torch.rand((1024, 48), device='cuda') * 6.2831853
+        sin, cos = theta.sin().bfloat16(), theta.cos().bfloat16()
+        kind, kwargs = _lib.EPI_ROPE, dict(rope=(sin, cos), rope_cols=2 * k, rows_per_slot=1024)
+        want = None   # compared against the unfolded GEMM on the same LayerNorm output below
+    elif epilogue == 'class_major':
+        kind, kwargs = _lib.EPI_CLASS_MAJOR, dict(rows_per_slot=1024, classes=5, geometry=(256, 16, 16))
+        want = None
+    else:
+        kind, want = _lib.EPI_BIAS, y
+    got = ops.gemm(x, wf, b, kind, ln=(stats, u, v, 1e-6), **kwargs)
+    if want is None:   # the same epilogue without the fold, on the bf16 LayerNorm output
+        want = ops.gemm(h.bfloat16(), w, b, kind, **kwargs)
+    if epilogue == 'rope':
+        # RoPE rounds a*cos, b*sin and their difference to bf16: a one-ulp difference of its inputs (the fold rounds W',
+        # the unfolded path rounds h) flips a product's rounding now and then, up to one ulp of the product (0.03 at
+        # magnitude 4) where the difference cancels. Allowed: 0.1% of the elements outside the bound, none past 0.0625.
+        diff = (got.float() - want.float()).abs()
+        outside = diff > 1e-2 + 1e-2 * want.float().abs()
+        assert outside.float().mean().item() <= 1e-3 and diff.max().item() <= 0.0625
+    else:
+        torch.testing.assert_close(got.float(), want.float(), atol=1e-2, rtol=1e-2)
