@@ -216,7 +216,7 @@ SVX_API int svx_attention(const uint16_t* q, int64_t q_row_stride, const uint16_
                           const int32_t* lengths, int slots, int heads, int queries, int keys, uint16_t* out,
                           const int32_t* plan, int plan_ctas, void* stream);
 /* Work-unit assignment for svx_attention (plan, device copy) on plan_ctas CTAs. A unit is two 128-query tiles of one
- * (slot, head); units go longest first to the least-loaded CTA (cost: key tiles + 1), which balances slots of unequal
+ * (slot, head); units go longest first to the least-loaded CTA (cost: key tiles + 2), which balances slots of unequal
  * key lengths. plan = [G + 1 offsets][units natural ids (slot*heads + head)*pairs + pair], G = min(ctas, units).
  * The plan affects only which CTA computes a unit, never the result: a plan built for other lengths stays correct.
  * lengths: host array [slots] or NULL (all `keys`). plan_ints returns the ints a plan takes (0: bad shape).

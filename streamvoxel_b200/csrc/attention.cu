@@ -481,14 +481,15 @@ int attention_plan(const int32_t* const* lengths, const int* keys, int problems,
   const int pairs = (queries / TQ + 1) / 2, per_slot = heads * pairs, per_prob = slots * per_slot;
   const int units = problems * per_prob;
   const int G = std::min(ctas, units);
-  // Cost of a unit in quarter key tiles: its tiles plus one tile of per-unit work (Q load, ring fill, epilogue);
+  // Cost of a unit in quarter key tiles: its tiles plus two tiles of per-unit work (Q load, ring fill, epilogue; the
+  // joint launch measured on B200 at the bench's lengths: 1 tile 176.3 us, 2 tiles 173.1, 3-6 tiles the same as 2);
   // a unit without keys only writes zeros.
   std::vector<int64_t> cost(units);
   for (int u = 0; u < units; ++u) {
     const int pb = u / per_prob, slot = (u % per_prob) / per_slot;
     const int len = lengths && lengths[pb] ? std::max(0, std::min(lengths[pb][slot], keys[pb])) : keys[pb];
     const int tiles = (len + TK - 1) / TK;
-    cost[u] = tiles ? 4 * (int64_t)tiles + 4 : 1;
+    cost[u] = tiles ? 4 * (int64_t)tiles + 8 : 1;
   }
   std::vector<int> order(units);
   for (int u = 0; u < units; ++u) order[u] = u;

@@ -120,7 +120,7 @@ def test_attention_plan_partitions_units_longest_first(lib, lengths, heads, quer
     assert offsets[0] == 0 and offsets[-1] == units and all(a <= b for a, b in zip(offsets, offsets[1:]))
     assert sorted(ids) == list(range(units))
     lens = [keys] * slots if lengths is None else lengths
-    cost = [(4 * t + 4 if t else 1) for t in ((lens[u // (heads * pairs)] + 95) // 96 for u in range(units))]
+    cost = [(4 * t + 8 if t else 1) for t in ((lens[u // (heads * pairs)] + 95) // 96 for u in range(units))]
     loads = [sum(cost[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
     assert max(max(cost), -(-sum(cost) // grid)) <= max(loads) <= _lpt_makespan(cost, grid)
     for c in range(grid):   # each CTA's units longest first
@@ -137,25 +137,26 @@ def test_attention_plan_rejects_bad_shapes_and_small_buffers(lib):
 
 def test_attention_plan_balances_the_bench_lengths(lib):
     """For the bench's eight slots the boustrophedon order gives a makespan of 125 key tiles (+2 units) against an
-    average of 96.4; the plan reaches 104 quarter-tile-costed units of work within 6% of the average."""
+    average of 96.4; the plan's makespan (key tiles + 2 per unit) stays within 9% of its average (the longest unit
+    alone is 102)."""
     from streamvoxel_b200 import ops
     lengths = [2368, 3392, 2368, 9536, 4416, 4416, 6464, 9536]
     plan, grid = ops.attention_plan(lengths, 8, 8, 1024, 9600, 148)
     offsets, ids = plan[:grid + 1].tolist(), plan[grid + 1:].tolist()
-    tiles = [(lengths[u // 32] + 95) // 96 + 1 for u in range(256)]
+    tiles = [(lengths[u // 32] + 95) // 96 + 2 for u in range(256)]
     loads = [sum(tiles[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
-    assert max(loads) <= 104 and sum(loads) / grid > 98
+    assert max(loads) <= 1.09 * sum(loads) / grid
 
 
 def test_attention_multi_plan_covers_both_problems(lib):
     """The joint plan of a cross-attention (bench lengths) and a self-attention assigns all 512 units once, problem
-    0 first in the numbering, and balances better than the two launches' makespans added (104 + 24 unit costs)."""
+    0 first in the numbering, and balances better than the two launches' makespans added (108 + 26 unit costs)."""
     from streamvoxel_b200 import ops
     lengths = [2368, 3392, 2368, 9536, 4416, 4416, 6464, 9536]
     plan, grid = ops.attention_multi_plan([(lengths, 9600), (None, 1024)], 8, 8, 1024, 148)
     offsets, ids = plan[:grid + 1].tolist(), plan[grid + 1:].tolist()
     assert grid == 148 and sorted(ids) == list(range(512))
-    tiles = [((lengths[u // 32] if u < 256 else 1024) + 95) // 96 + 1 for u in range(512)]
+    tiles = [((lengths[u // 32] if u < 256 else 1024) + 95) // 96 + 2 for u in range(512)]
     loads = [sum(tiles[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
-    assert max(loads) < 104 + 24
+    assert max(loads) < 108 + 26 and sum(loads) / grid > 0.93 * max(loads)
     assert lib.svx_attention_multi_plan_ints(3, 8, 8, 1024, 148) == 0
