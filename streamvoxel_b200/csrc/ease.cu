@@ -242,6 +242,27 @@ struct BlockGeom {
   }
 };
 
+// Non-deferred (nt) and selectable (lg) voxels of 4^3 block j: one 32-bit load of `last` and one 64-bit load of the
+// tokens per 4-voxel x-row (a row starts at a multiple of 4 voxels; the entry points check the alignment).
+__device__ __forceinline__ void block_counts(const BlockGeom& g, const uint8_t* lst, const int16_t* tok, int mask_id,
+                                             int j, int& nt, int& lg) {
+  nt = 0;
+  lg = 0;
+#pragma unroll 4
+  for (int r = 0; r < 16; ++r) {
+    const int n = g.voxel(j, r * 4);
+    const uint32_t l4 = *reinterpret_cast<const uint32_t*>(lst + n);
+    const uint2 t4 = *reinterpret_cast<const uint2*>(tok + n);
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      const bool nl = ((l4 >> (8 * x)) & 0xFFu) == 0;
+      const int16_t t = (int16_t)(((x < 2 ? t4.x : t4.y) >> (16 * (x & 1))) & 0xFFFFu);
+      nt += nl;
+      lg += nl && t == mask_id;
+    }
+  }
+}
+
 // Per-block quota (`block_quota.py:24-30` / `fast_ops.py:451-463`): float64 apportioning of the step goal over
 // blocks, the remainder to the blocks with the largest fractional part (seeded order `pos` breaks ties).
 __global__ void __launch_bounds__(kSelectThreads) ease_quota_kernel(const int16_t* __restrict__ tokens,
@@ -264,8 +285,8 @@ __global__ void __launch_bounds__(kSelectThreads) ease_quota_kernel(const int16_
   const int16_t* tok = tokens + (int64_t)slot * voxels;
   const uint8_t* lst = last + (int64_t)slot * voxels;
   if (j < g.blocks && p.k > 0) {
-    int ntot = 0;
-    for (int i = 0; i < 64; ++i) ntot += !lst[g.voxel(j, i)];
+    int ntot = 0, unused = 0;
+    block_counts(g, lst, tok, mask_id, j, ntot, unused);
     double ideal = p.frac * (double)ntot;
     base = (long long)floor(ideal + 1e-9);
     key = -(ideal - (double)base) * 1e6 + (double)pos[(int64_t)slot * g.blocks + j];
@@ -299,12 +320,7 @@ __global__ void __launch_bounds__(kSelectThreads) ease_quota_kernel(const int16_
   if (j < g.blocks && p.k > 0) {
     const int block = ids[j];
     int lg = 0, nt = 0;
-    for (int i = 0; i < 64; ++i) {
-      int n = g.voxel(block, i);
-      bool nl = !lst[n];
-      nt += nl;
-      lg += nl && tok[n] == mask_id;
-    }
+    block_counts(g, lst, tok, mask_id, block, nt, lg);
     long long b = (long long)floor(p.frac * (double)nt + 1e-9);
     long long target = b + (j < extra ? 1 : 0);
     long long q = target - (nt - lg);
@@ -368,111 +384,6 @@ __device__ __forceinline__ uint64_t order_key(float score, int n) {
   return (uint64_t(u) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(n));
 }
 
-// Global trim / top-up (`block_quota.py:34-37`, `top_mask` `:4-12`) when the clamped block quotas miss k, then the
-// ascending compaction of the chosen voxels (`nonzero_static`, `fast_ops.py:548`) and the quota check (`:540`).
-// The fix-up is a radix select over the 64-bit key (score order, then lower voxel index first).
-__global__ void __launch_bounds__(kSelectThreads) ease_fixup_compact_kernel(
-    const float* __restrict__ scores, const int16_t* __restrict__ tokens, const uint8_t* __restrict__ last,
-    const svx_step_params* __restrict__ params, int voxels, int mask_id, uint8_t* __restrict__ chosen,
-    int32_t* __restrict__ got, int32_t* __restrict__ index_out, int index_capacity, int32_t* __restrict__ chosen_count,
-    uint32_t* __restrict__ status) {
-  const int slot = blockIdx.x;
-  const int t = threadIdx.x;
-  const int64_t off = (int64_t)slot * voxels;
-  const int k = params[slot].k;
-  const int have = got[slot];
-  __shared__ uint32_t hist[256];
-  __shared__ unsigned long long prefix, prefix_mask;
-  __shared__ int remaining, candidates;
-  __shared__ int scan[kSelectThreads];
-  if (k > 0 && have != k) {
-    const bool trim = have > k;  // trim: keep the best k of the chosen; top-up: add the best k-have of the rest
-    if (t == 0) { prefix = 0; prefix_mask = 0; remaining = trim ? k : k - have; candidates = 0; }
-    __syncthreads();
-    int mine = 0;
-    for (int n = t; n < voxels; n += blockDim.x) {
-      bool sel = !last[off + n] && tokens[off + n] == mask_id;
-      bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
-      mine += cand;
-    }
-    atomicAdd(&candidates, mine);
-    __syncthreads();
-    const bool take_all = remaining >= candidates;
-    if (!take_all && remaining > 0) {
-      for (int shift = 56; shift >= 0; shift -= 8) {
-        for (int i = t; i < 256; i += blockDim.x) hist[i] = 0;
-        __syncthreads();
-        for (int n = t; n < voxels; n += blockDim.x) {
-          bool sel = !last[off + n] && tokens[off + n] == mask_id;
-          bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
-          if (!cand) continue;
-          uint64_t key = order_key(scores[off + n], n);
-          if ((key & prefix_mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-        }
-        __syncthreads();
-        if (t == 0) {
-          int acc = 0;
-          for (int d = 255; d >= 0; --d) {
-            int c = (int)hist[d];
-            if (acc + c >= remaining) {
-              remaining -= acc;
-              prefix |= (unsigned long long)d << shift;
-              prefix_mask |= 255ull << shift;
-              break;
-            }
-            acc += c;
-          }
-        }
-        __syncthreads();
-      }
-    }
-    // prefix is now the key of the remaining-th best candidate; candidates at or above it are taken.
-    for (int n = t; n < voxels; n += blockDim.x) {
-      bool sel = !last[off + n] && tokens[off + n] == mask_id;
-      bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
-      bool take = cand && (take_all || (remaining > 0 && order_key(scores[off + n], n) >= prefix));
-      if (trim && cand && !take) chosen[off + n] = 0;
-      if (!trim && take) chosen[off + n] = 1;
-    }
-    __syncthreads();
-  }
-  // Ascending compaction: thread t owns voxels [t*per, (t+1)*per).
-  const int per = (voxels + blockDim.x - 1) / blockDim.x;
-  const int lo = min(voxels, t * per), hi = min(voxels, lo + per);
-  int count = 0;
-  bool bad = false;
-  for (int n = lo; n < hi; ++n) {
-    if (chosen[off + n]) {
-      ++count;
-      bad |= last[off + n] || tokens[off + n] != mask_id;
-    }
-  }
-  scan[t] = count;
-  __syncthreads();
-  for (int s = 1; s < (int)blockDim.x; s <<= 1) {  // Hillis-Steele inclusive scan
-    int v = t >= s ? scan[t - s] : 0;
-    __syncthreads();
-    scan[t] += v;
-    __syncthreads();
-  }
-  int w = scan[t] - count;
-  for (int n = lo; n < hi; ++n)
-    if (chosen[off + n]) {
-      if (w < index_capacity) index_out[(int64_t)slot * index_capacity + w] = n;
-      ++w;
-    }
-  const int total = scan[blockDim.x - 1];
-  for (int i = total + t; i < index_capacity; i += blockDim.x) index_out[(int64_t)slot * index_capacity + i] = -1;
-  bad = __syncthreads_or(bad);
-  if (t == 0) {
-    chosen_count[slot] = total;
-    got[slot] = total;
-    if ((bad || total != k) && status) atomicOr(status + slot, SVX_STATUS_QUOTA_MISSED);
-  }
-}
-
-// ----------------------------------------------------------------------------------------------- eval selection
-
 // Radix select over a 64-bit order key inside one CTA: the key of the c-th best candidate (c >= 1; with fewer than
 // c candidates 0, so that every candidate is at or above it). Keys are unique (the voxel index is in the low word),
 // so exactly min(c, candidates) candidates have key >= the result. 8-bit digits from the top; a digit whose bucket
@@ -519,6 +430,126 @@ __device__ uint64_t cta_select_key(int voxels, int c, Cand cand, Key key, uint32
   __syncthreads();
   return result;
 }
+
+// Global trim / top-up (`block_quota.py:34-37`, `top_mask` `:4-12`) when the clamped block quotas miss k, then the
+// ascending compaction of the chosen voxels (`nonzero_static`, `fast_ops.py:548`) and the quota check (`:540`).
+// The fix-up is a radix select over the 64-bit key (score order, then lower voxel index first).
+__global__ void __launch_bounds__(kSelectThreads) ease_fixup_compact_kernel(
+    const float* __restrict__ scores, const int16_t* __restrict__ tokens, const uint8_t* __restrict__ last,
+    const svx_step_params* __restrict__ params, int voxels, int mask_id, uint8_t* __restrict__ chosen,
+    int32_t* __restrict__ got, int32_t* __restrict__ index_out, int index_capacity, int32_t* __restrict__ chosen_count,
+    uint32_t* __restrict__ status) {
+  const int slot = blockIdx.x;
+  const int t = threadIdx.x;
+  const int64_t off = (int64_t)slot * voxels;
+  const int k = params[slot].k;
+  const int have = got[slot];
+  __shared__ uint32_t hist[256];
+  __shared__ unsigned long long prefix, sel_sh[4];
+  __shared__ int remaining, candidates;
+  __shared__ int scan[kSelectThreads];
+  if (k > 0 && have != k) {
+    const bool trim = have > k;  // trim: keep the best k of the chosen; top-up: add the best k-have of the rest
+    if (t == 0) { prefix = 0; remaining = trim ? k : k - have; candidates = 0; }
+    __syncthreads();
+    int mine = 0;
+    for (int n = t; n < voxels; n += blockDim.x) {
+      bool sel = !last[off + n] && tokens[off + n] == mask_id;
+      bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
+      mine += cand;
+    }
+    atomicAdd(&candidates, mine);
+    __syncthreads();
+    const bool take_all = remaining >= candidates;
+    if (!take_all && remaining > 0) {
+      auto cand = [&](int n) {
+        const bool sel = !last[off + n] && tokens[off + n] == mask_id;
+        return trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
+      };
+      auto key = [&](int n) { return order_key(scores[off + n], n); };
+      const uint64_t thr = cta_select_key(voxels, remaining, cand, key, hist, sel_sh);
+      if (t == 0) prefix = thr;
+      __syncthreads();
+    }
+    // prefix is now the key of the remaining-th best candidate; candidates at or above it are taken.
+    for (int n = t; n < voxels; n += blockDim.x) {
+      bool sel = !last[off + n] && tokens[off + n] == mask_id;
+      bool cand = trim ? (bool)chosen[off + n] : (sel && !chosen[off + n]);
+      bool take = cand && (take_all || (remaining > 0 && order_key(scores[off + n], n) >= prefix));
+      if (trim && cand && !take) chosen[off + n] = 0;
+      if (!trim && take) chosen[off + n] = 1;
+    }
+    __syncthreads();
+  }
+  // Ascending compaction: thread t owns voxels [t*per, (t+1)*per), read 16 flags per load when per % 16 == 0.
+  const int per = (voxels + blockDim.x - 1) / blockDim.x;
+  const int lo = min(voxels, t * per), hi = min(voxels, lo + per);
+  const bool wide = per % 16 == 0 && voxels % per == 0 && (reinterpret_cast<uintptr_t>(chosen + off) & 15) == 0;
+  int count = 0;
+  bool bad = false;
+  if (wide) {
+    for (int n0 = lo; n0 < hi; n0 += 16) {
+      const uint4 c = *reinterpret_cast<const uint4*>(chosen + off + n0);
+      if (!(c.x | c.y | c.z | c.w)) continue;
+      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        count += (int)((w[q] * 0x01010101u) >> 24);   // flags are 0 or 1
+        for (int b = 0; b < 4; ++b)
+          if ((w[q] >> (8 * b)) & 0xFFu) {
+            const int n = n0 + 4 * q + b;
+            bad |= last[off + n] || tokens[off + n] != mask_id;
+          }
+      }
+    }
+  } else {
+    for (int n = lo; n < hi; ++n) {
+      if (chosen[off + n]) {
+        ++count;
+        bad |= last[off + n] || tokens[off + n] != mask_id;
+      }
+    }
+  }
+  scan[t] = count;
+  __syncthreads();
+  for (int s = 1; s < (int)blockDim.x; s <<= 1) {  // Hillis-Steele inclusive scan
+    int v = t >= s ? scan[t - s] : 0;
+    __syncthreads();
+    scan[t] += v;
+    __syncthreads();
+  }
+  int w = scan[t] - count;
+  if (wide) {
+    for (int n0 = lo; n0 < hi && count; n0 += 16) {
+      const uint4 c = *reinterpret_cast<const uint4*>(chosen + off + n0);
+      if (!(c.x | c.y | c.z | c.w)) continue;
+      const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        for (int b = 0; b < 4; ++b)
+          if ((wd[q] >> (8 * b)) & 0xFFu) {
+            if (w < index_capacity) index_out[(int64_t)slot * index_capacity + w] = n0 + 4 * q + b;
+            ++w;
+          }
+    }
+  } else {
+    for (int n = lo; n < hi; ++n)
+      if (chosen[off + n]) {
+        if (w < index_capacity) index_out[(int64_t)slot * index_capacity + w] = n;
+        ++w;
+      }
+  }
+  const int total = scan[blockDim.x - 1];
+  for (int i = total + t; i < index_capacity; i += blockDim.x) index_out[(int64_t)slot * index_capacity + i] = -1;
+  bad = __syncthreads_or(bad);
+  if (t == 0) {
+    chosen_count[slot] = total;
+    got[slot] = total;
+    if ((bad || total != k) && status) atomicOr(status + slot, SVX_STATUS_QUOTA_MISSED);
+  }
+}
+
+// ----------------------------------------------------------------------------------------------- eval selection
 
 // The evaluation decoders' selections (`streamvoxel/eval/samplers.py:23-64`), one CTA per slot over the masked voxels
 // (tokens == mask_id): RANDOM/ENTROPY = top_mask of the draw / the score (`block_quota.py:4-12`: largest first, lower
@@ -905,6 +936,8 @@ extern "C" int svx_ease_select(const float* scores, const int16_t* tokens, const
   SVX_REQUIRE(scores && tokens && last && pos && params && chosen && index_out && chosen_count && workspace &&
                   slots > 0 && index_capacity > 0,
               "svx_ease_select: bad arguments");
+  SVX_REQUIRE((reinterpret_cast<uintptr_t>(tokens) & 7) == 0 && (reinterpret_cast<uintptr_t>(last) & 3) == 0,
+              "svx_ease_select: tokens must be 8-byte and last 4-byte aligned");
   cudaStream_t s = as_stream(stream);
   int32_t* quota = static_cast<int32_t*>(workspace);
   int32_t* got = quota + (size_t)slots * g.blocks;
