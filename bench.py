@@ -256,7 +256,8 @@ def algorithmic_bytes(name, cfg, lengths):
 
 
 def time_kernels(cfg, forward, batch, lengths):
-    """Average launch duration of each kernel class of the step at the step's shapes (CUDA events, 20 launches)."""
+    """Average launch duration of each kernel class of the step at the step's shapes (CUDA events around a replayed
+    CUDA graph of 20 launches)."""
     from streamvoxel_b200 import ops, _lib
     dev = forward.device
     rows, d, heads = SLOTS * cfg.patches, cfg.d, cfg.heads
@@ -268,14 +269,27 @@ def time_kernels(cfg, forward, batch, lengths):
     tables = m.rope_sin, m.rope_cos
 
     def clock(fn, reps=20):
-        fn()
-        torch.cuda.synchronize()
+        """Device time per launch: `reps` launches captured in one CUDA graph and replayed (as the step runs them), so
+        that host-side launch cost (ctypes, tensor-map encoding) does not set a floor under short kernels."""
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+            fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(dev)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(reps):
-            fn()
+        graph.replay()
         b.record()
         b.synchronize()
+        del graph
         return a.elapsed_time(b) / reps * 1e-3
 
     mean_len = float(np.mean(lengths))

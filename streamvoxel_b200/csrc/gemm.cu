@@ -172,6 +172,23 @@ __device__ __forceinline__ void chunk_stats(const EpiParams& ep, int M, int row,
   ep.ln_stats_out[(int64_t)(n / 32) * M + row] = make_float2(mean, m2);   // chunk-major [N / 32][M]
 }
 
+// The same statistics from the 16 packed bf16 pairs the epilogue stores (unpacking is exact and takes no conversion).
+__device__ __forceinline__ void chunk_stats_packed(const EpiParams& ep, int M, int row, int n,
+                                                   const uint32_t (&pk)[16]) {
+  float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) s = __fadd2_rn(s, unpack2(pk[j]));
+  const float mean = (s.x + s.y) * (1.f / 32.f);
+  const float2 nm = make_float2(-mean, -mean);
+  float2 m2 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float2 d = __fadd2_rn(unpack2(pk[j]), nm);
+    m2 = __ffma2_rn(d, d, m2);
+  }
+  ep.ln_stats_out[(int64_t)(n / 32) * M + row] = make_float2(mean, m2.x + m2.y);
+}
+
 // Epilogue arithmetic of one row x 32 columns [n, n+32) of the tile; acc holds fp32 accumulators, o the bias, gate,
 // RoPE table and residual words of the row; nr the row's (mean, 1/std) when the LayerNorm is folded in.
 // vs: the warp's 32 v values of this chunk in shared memory (LayerNorm fold; nullptr: read them from global memory).
@@ -594,12 +611,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               __syncwarp();
             }
             epilogue_math<E>(ep, row, n0 + chunk * 32, acc, ops, nr, y, LN_FOLD ? vs : nullptr);
-            if constexpr (LN_STATS) chunk_stats(ep, M, row, n0 + chunk * 32, y);
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pk[j] = tc::pack_bf16x2(y[2 * j], y[2 * j + 1]);
+            if constexpr (LN_STATS) chunk_stats_packed(ep, M, row, n0 + chunk * 32, pk);
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              rb[q ^ swz] = make_uint4(tc::pack_bf16x2(y[8 * q], y[8 * q + 1]), tc::pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
-                                       tc::pack_bf16x2(y[8 * q + 4], y[8 * q + 5]),
-                                       tc::pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+              rb[q ^ swz] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
             tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) {
