@@ -192,10 +192,10 @@ typedef struct {
   /* LayerNorm fold (bias, GELU, RoPE, class-major epilogues): A holds the raw rows x and W the modulated weights
    * W'[n][k] = W[n][k] (1 + scale[k]); out = epilogue(r (acc - mu u[n]) + v[n]) with mu, r = 1/sqrt(var + ln_eps)
    * of each A row from ln_stats_in ([K/32][M] (mean, M2) pairs of its 32-column chunks, chunk-major),
-   * u[n] = sum_k W'[n][k] (bf16), v[n] = b[n] + sum_k W[n][k] shift[k] (fp32). Replaces LayerNorm + modulate +
-   * linear (`unconditional_md4_timefree.py:12-13,53-63`). */
+   * u[n] = sum_k W'[n][k], v[n] = b[n] + sum_k W[n][k] shift[k] (fp32). Replaces LayerNorm + modulate + linear
+   * (`unconditional_md4_timefree.py:12-13,53-63`). */
   const float* ln_stats_in;  /* NULL: out = epilogue(acc + b) */
-  const uint16_t* ln_u;
+  const float* ln_u;
   const float* ln_v;
   float ln_eps;
   float* ln_stats_out;       /* optional (residual epilogues) [N/32][M] (mean, M2) of the bf16 output rows' chunks */
@@ -254,18 +254,14 @@ typedef struct {
   const uint16_t *qkv_w, *qkv_b, *proj_w, *proj_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
   const uint16_t *shift1, *one_plus_scale1, *gate1, *shift2, *one_plus_scale2, *gate2;
   /* LayerNorm fold of the two linears that follow a LayerNorm (see svx_epilogue_args): qkv_w and fc1_w hold the
-   * modulated weights W (1 + scale), u = their row sums (bf16 [N]), v = b + W shift (fp32 [N]). */
-  const uint16_t *qkv_u;
-  const float *qkv_v;
-  const uint16_t *fc1_u;
-  const float *fc1_v;
+   * modulated weights W (1 + scale), u = their row sums, v = b + W shift (fp32 [N]). */
+  const float *qkv_u, *qkv_v, *fc1_u, *fc1_v;
 } svx_block_weights;
 
 typedef struct {
   const uint16_t *query_w, *query_b, *proj_w, *proj_b, *zero_w, *zero_b;
   const uint16_t *k, *v;     /* packed cached K/V of this layer: [slots][heads][key_capacity][96] bf16, RoPE applied */
-  const uint16_t* query_u;   /* LayerNorm fold of the query linear (no affine): row sums of W (bf16), v = b (fp32) */
-  const float* query_v;
+  const float *query_u, *query_v; /* LayerNorm fold of the query linear (no affine): row sums of W, v = b (fp32) */
 } svx_cross_weights;
 
 typedef struct {
@@ -285,8 +281,7 @@ typedef struct {
   const uint16_t *rope_sin, *rope_cos;          /* self-attention RoPE tables [patches][48] */
   const uint16_t *cross_sin, *cross_cos;        /* cross-attention query RoPE tables [patches][48] */
   const int32_t* lengths;                       /* [slots] valid packed keys per slot (device) */
-  const uint16_t* head_u;                       /* LayerNorm fold of the head: head_w = W (1 + final scale) */
-  const float* head_v;
+  const float *head_u, *head_v;                 /* LayerNorm fold of the head: head_w = W (1 + final scale) */
 } svx_engine_weights;
 
 typedef struct {

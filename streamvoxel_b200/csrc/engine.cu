@@ -72,7 +72,7 @@ float2* stats_of(const svx_engine& E, const uint16_t* x) {
 }
 
 // The LayerNorm (eps 1e-6, `unconditional_md4_timefree.py:53-54`) of x folded into a linear's epilogue.
-void fold(EpiParams& e, const svx_engine& E, const uint16_t* x, const uint16_t* u, const float* v) {
+void fold(EpiParams& e, const svx_engine& E, const uint16_t* x, const float* u, const float* v) {
   e.ln_stats_in = stats_of(E, x);
   e.ln_u = u;
   e.ln_v = v;

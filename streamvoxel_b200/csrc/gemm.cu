@@ -88,10 +88,10 @@ __device__ __forceinline__ void unpack8(uint4 raw, float* v) {
 
 // Operands an epilogue chunk reads from global memory, fetched before the accumulator is ready (bf16, packed).
 struct Operands {
-  uint4 bias[4];    // bias | u (LayerNorm fold, bf16)
+  uint4 bias[4];
   uint4 extra[4];   // gate (GATE_RESIDUAL) | sin, cos (ROPE: 2 + 2)
   uint4 res[4];     // residual row slice (GATE_RESIDUAL, RESIDUAL)
-  float v;          // LayerNorm fold: v[n + lane], staged through shared memory for the whole warp
+  float u, v;       // LayerNorm fold: u[n + lane], v[n + lane], staged through shared memory for the whole warp
 };
 
 // GLOBAL_RES = false: the residual comes from a staging box in shared memory instead.
@@ -99,10 +99,8 @@ template <int E, bool GLOBAL_RES = true>
 __device__ __forceinline__ void prefetch32(const EpiParams& ep, int N, int row, int n, Operands& o) {
   constexpr int EPI = E & 7;
   [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
-  if constexpr (LN_FOLD) {   // u (bf16) and v (fp32) in place of the bias, which v holds
-    const uint4* u = reinterpret_cast<const uint4*>(ep.ln_u + n);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o.bias[i] = __ldg(u + i);
+  if constexpr (LN_FOLD) {   // this lane's u and v in place of the bias, which v holds
+    o.u = __ldg(ep.ln_u + n + lane_id());
     o.v = __ldg(ep.ln_v + n + lane_id());
   } else {
     const uint4* b = reinterpret_cast<const uint4*>(ep.bias + n);
@@ -191,26 +189,28 @@ __device__ __forceinline__ void chunk_stats_packed(const EpiParams& ep, int M, i
 
 // Epilogue arithmetic of one row x 32 columns [n, n+32) of the tile; acc holds fp32 accumulators, o the bias, gate,
 // RoPE table and residual words of the row; nr the row's (mean, 1/std) when the LayerNorm is folded in.
-// vs: the warp's 32 v values of this chunk in shared memory (LayerNorm fold; nullptr: read them from global memory).
+// uv: the warp's 32 u then 32 v values of this chunk in shared memory (LayerNorm fold; nullptr: read them from
+// global memory).
 template <int E>
 __device__ __forceinline__ void epilogue_math(const EpiParams& ep, int row, int n, const uint32_t (&acc)[32],
                                               const Operands& o, float2 nr, float (&y)[32],
-                                              const float* vs = nullptr) {
+                                              const float* uv = nullptr) {
   constexpr int EPI = E & 7;
   [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
   if constexpr (LN_FOLD) {
     const float2 ra = make_float2(nr.y, nr.y), rb = make_float2(-nr.x * nr.y, -nr.x * nr.y);
-    const uint32_t* uw = reinterpret_cast<const uint32_t*>(o.bias);
-    const float4* vp = reinterpret_cast<const float4*>(vs ? vs : ep.ln_v + n);
+    const float4* up = reinterpret_cast<const float4*>(uv ? uv : ep.ln_u + n);
+    const float4* vp = reinterpret_cast<const float4*>(uv ? uv + 32 : ep.ln_v + n);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const float4 vq = vp[q];
+      const float4 uq = up[q], vq = vp[q];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int j = 2 * q + h;
+        const float2 u2 = h ? make_float2(uq.z, uq.w) : make_float2(uq.x, uq.y);
         const float2 v2 = h ? make_float2(vq.z, vq.w) : make_float2(vq.x, vq.y);
         const float2 a = make_float2(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1]));
-        const float2 v = round2(__ffma2_rn(a, ra, __ffma2_rn(rb, unpack2(uw[j]), v2)));
+        const float2 v = round2(__ffma2_rn(a, ra, __ffma2_rn(rb, u2, v2)));
         y[2 * j] = v.x;
         y[2 * j + 1] = v.y;
       }
@@ -265,11 +265,11 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, int row, int 
 template <int E>
 __device__ __forceinline__ void epilogue32(const EpiParams& ep, uint16_t* out, int M, int N, int row, int n,
                                            const uint32_t (&acc)[32], const Operands& o, float2 nr,
-                                           const float* vs = nullptr) {
+                                           const float* uv = nullptr) {
   constexpr int EPI = E & 7;
   [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
   float y[32];
-  epilogue_math<E>(ep, row, n, acc, o, nr, y, vs);
+  epilogue_math<E>(ep, row, n, acc, o, nr, y, uv);
   if constexpr (LN_STATS && EPI != SVX_EPI_CLASS_MAJOR) chunk_stats(ep, M, row, n, y);
   if constexpr (EPI == SVX_EPI_CLASS_MAJOR) {
     // W rows are ordered n = v * 64 + o, so the 32 columns are one class v and offsets o..o+31 of one patch.
@@ -458,7 +458,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* res_full = acc_empty + 2;                              // per epilogue warp and box
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2 * kEpilogueWarps);
   volatile uint32_t* abort_flag = tmem_slot + 1;
-  float* v_stage = reinterpret_cast<float*>(tmem_slot + 4);       // LayerNorm fold: 32 v values per epilogue warp
+  float* uv_stage = reinterpret_cast<float*>(tmem_slot + 4);      // LayerNorm fold: 32 u + 32 v per epilogue warp
 
   const int warp = warp_id(), lane = lane_id();
   const uint32_t rank = tc::cluster_rank();
@@ -604,13 +604,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               for (int q = 0; q < 4; ++q) ops.res[q] = rb[q ^ swz];
             }
             float y[32];
-            float* vs = v_stage + ws * 32;
+            float* uv = uv_stage + ws * 64;
             if constexpr (LN_FOLD) {
-              __syncwarp();   // the previous chunk's reads of vs are done
-              vs[lane] = ops.v;
+              __syncwarp();   // the previous chunk's reads of uv are done
+              uv[lane] = ops.u;
+              uv[32 + lane] = ops.v;
               __syncwarp();
             }
-            epilogue_math<E>(ep, row, n0 + chunk * 32, acc, ops, nr, y, LN_FOLD ? vs : nullptr);
+            epilogue_math<E>(ep, row, n0 + chunk * 32, acc, ops, nr, y, LN_FOLD ? uv : nullptr);
             uint32_t pk[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) pk[j] = tc::pack_bf16x2(y[2 * j], y[2 * j + 1]);
@@ -625,13 +626,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               tc::bulk_commit();
             }
           } else {
-            float* vs = v_stage + ws * 32;
+            float* uv = uv_stage + ws * 64;
             if constexpr (LN_FOLD) {
               __syncwarp();
-              vs[lane] = ops.v;
+              uv[lane] = ops.u;
+              uv[32 + lane] = ops.v;
               __syncwarp();
             }
-            if (row < M) epilogue32<E>(ep, out, M, N, row, n0 + chunk * 32, acc, ops, nr, LN_FOLD ? vs : nullptr);
+            if (row < M) epilogue32<E>(ep, out, M, N, row, n0 + chunk * 32, acc, ops, nr, LN_FOLD ? uv : nullptr);
           }
         }
       }
@@ -652,7 +654,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 template <int BN, int STAGES>
 constexpr size_t pair_smem_bytes() {
   return 1024 + STAGES * (A_BYTES + (size_t)(BN / 2) * BK * 2) + (size_t)kEpilogueWarps * 2 * BOX +
-         (2 * STAGES + 4 + 2 * kEpilogueWarps) * 8 + 16 + kEpilogueWarps * 32 * 4;
+         (2 * STAGES + 4 + 2 * kEpilogueWarps) * 8 + 16 + kEpilogueWarps * 64 * 4;
 }
 
 template <int BN, int STAGES, int EPI>

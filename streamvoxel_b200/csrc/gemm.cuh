@@ -20,7 +20,7 @@ struct EpiParams {
   // W the modulated weights W'[n][k] = W[n][k] (1 + scale[k]), u[n] = sum_k W'[n][k], v[n] = b[n] + sum_k W[n][k]
   // shift[k]), so that no LayerNorm kernel runs between a residual GEMM and the next linear.
   const float2* ln_stats_in;   // [ln_chunks][M] (mean, M2) of the input rows' 32-column chunks (chunk-major)
-  const uint16_t* ln_u;        // [N] bf16 (its term is scaled by mu / sigma, so bf16 suffices)
+  const float* ln_u;           // [N] fp32
   const float* ln_v;           // [N] fp32
   int ln_chunks;
   float ln_inv_chunks;         // 1 / ln_chunks

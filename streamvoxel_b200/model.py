@@ -167,14 +167,13 @@ def rope_tables(positions, head_dim):
 def fold_layernorm(weight, bias, one_plus_scale=None, shift=None):
     """The LayerNorm + AdaLN modulate before a linear, folded into it (`svx_epilogue_args` ln_*): the linear then
     takes the raw residual stream x and computes r (x W'^T - mu u) + v, with mu, r the row's LayerNorm statistics.
-    W' = bf16(W (1 + scale)) (exact fp32 product of two bf16 values, rounded once), u = sum_k W'[n, k] (bf16: its
-    term is scaled by mu / sigma), v = b + W shift (float64 sums, fp32). Without scale/shift (LayerNorm without
-    affine) W' = W and v = b."""
+    W' = bf16(W (1 + scale)) (exact fp32 product of two bf16 values, rounded once), u = sum_k W'[n, k],
+    v = b + W shift (float64 sums, fp32). Without scale/shift (LayerNorm without affine) W' = W and v = b."""
     w = weight.float()
     folded = weight if one_plus_scale is None else (w * one_plus_scale.float()[None, :]).to(torch.bfloat16)
     u = folded.double().sum(1)
     v = bias.double() + (w.double() @ shift.double() if shift is not None else 0.)
-    return folded.contiguous(), u.to(torch.bfloat16).contiguous(), v.float().contiguous()
+    return folded.contiguous(), u.float().contiguous(), v.float().contiguous()
 
 
 class PreparedModel:

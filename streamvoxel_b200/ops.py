@@ -181,7 +181,7 @@ def layernorm_modulate(x, eps=1e-6, one_plus_scale=None, shift=None, out=None):
 def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None, rope=None, rope_cols=0,
          rows_per_slot=0, head_dim=96, classes=0, geometry=(0, 0, 0), ln=None, stats_out=None):
     """out = epilogue(a @ w.T + bias) on the tcgen05 GEMM. a [M,K], w [N,K], bias [N] bf16.
-    ln = (stats [K/32, M, 2] fp32, u [N] bf16, v [N] fp32, eps): the LayerNorm folded in, out = epilogue(r (acc - mu u) + v)
+    ln = (stats [K/32, M, 2] fp32, u [N], v [N] fp32, eps): the LayerNorm folded in, out = epilogue(r (acc - mu u) + v)
     with w the modulated weights; stats_out: fp32 [N/32, M, 2] chunk statistics of the bf16 output rows."""
     m, k = a.shape
     n = w.shape[0]
@@ -198,7 +198,7 @@ def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None,
                              height=geometry[0], depth=geometry[1], width=geometry[2], patch=4)
     if ln is not None:
         stats, u, v, eps = ln
-        assert stats.dtype == v.dtype == torch.float32 and u.dtype == torch.bfloat16
+        assert stats.dtype == u.dtype == v.dtype == torch.float32
         args.ln_stats_in, args.ln_u, args.ln_v, args.ln_eps = ptr(stats).value, ptr(u).value, ptr(v).value, eps
     if stats_out is not None:
         assert stats_out.dtype == torch.float32

@@ -75,6 +75,26 @@ def test_small_forward_matches_oracle_per_slot():
         _assert_logits(got[i], want)
 
 
+def test_wide_forward_matches_oracle_per_slot():
+    """The BASELINE config-5 width (d = 1152, 12 heads x 96, MLP 4608): 36 row-statistics chunks per LayerNorm fold,
+    18-block K loops, 12-head attention plans; two backbone layers, both fed by control layers."""
+    from streamvoxel_b200 import model as sm, synth
+    cfg = sm.small_test_config(d=1152, heads=12, mlp=4608, depth=2, layer_indices=(0, 1))
+    engine, sd, spec = _engine(cfg, 2, std=0.02, l1_cap=3, l2_cap=8)
+    tokens = []
+    for i, k in enumerate((1, 3)):
+        engine.load_slot(i, synth.item(300 + i, spec, k=k, far=8))
+        t, _ = synth.target_tokens(400 + i, spec)
+        tokens.append(t)
+    engine.wait_loads()
+    engine.tokens.copy_(torch.from_numpy(np.stack(tokens)).cuda())
+    got = engine.eager(torch.ones(2)).float().cpu()
+    for i in range(2):
+        want = om.control_forward(sd, torch.from_numpy(tokens[i][None]).long(), _kv_of_slot(engine, i),
+                                  _cfg_dict(cfg), bf16=True)[0]
+        _assert_logits(got[i], want)
+
+
 def test_graph_replay_equals_eager_and_buckets_agree():
     from streamvoxel_b200 import model as sm, synth
     cfg = sm.small_test_config()
