@@ -2,10 +2,11 @@
 
     python -m streamvoxel_b200.profile_case <case> [--launches N]
 
-Cases: attention_cross, attention_joint (cross + self in one launch), attention_self, gemm_fc1, gemm_qkv, gemm_dxd, gemm_head, ease_scores, ease_mark,
-ease_select, ease_sample, patch_embed (both branches; tokens uniform over the 257 ids, the gather's worst case). Inputs are seeded random tensors with the bench's shapes (8 slots, d=768, 8 heads x 96, V=256,
-65536 voxels, packed keys of k = 0..7 L1 tiles); every case's working set is larger than the 126 MB L2 except the
-selection. Prints the mean launch time measured with CUDA events.
+Cases: attention_cross, attention_joint (cross + self in one launch), attention_self, gemm_fc1, gemm_fc1_fold (the
+LayerNorm folded in, as the engine runs fc1), gemm_qkv, gemm_dxd, gemm_head, ease_scores, ease_mark, ease_select,
+ease_sample, patch_embed (both branches; tokens uniform over the 257 ids, the gather's worst case). Inputs are seeded
+random tensors with the bench's shapes (8 slots, d=768, 8 heads x 96, V=256, 65536 voxels, packed keys of k = 0..7
+L1 tiles); every case's working set is larger than the 126 MB L2 except the GEMMs' and the selection. Prints the mean launch time measured with CUDA events.
 """
 from __future__ import annotations
 
@@ -43,6 +44,11 @@ def cases():
          (('qkv', (3 * D, D)), ('fc1', (MLP, D)), ('dxd', (D, D)), ('head', (64 * V, D)))}
     b = {n: rnd(t.shape[0], s=0.02) for n, t in w.items()}
     gate = rnd(D, s=0.1)
+    from streamvoxel_b200.model import fold_layernorm
+    fc1_fold = fold_layernorm(w['fc1'], b['fc1'], (1 + rnd(D, s=0.1).float()).bfloat16(), rnd(D, s=0.1))
+    hc = h.double().reshape(rows, D // 32, 32)
+    h_stats = torch.stack((hc.mean(-1), ((hc - hc.mean(-1, keepdim=True)) ** 2).sum(-1)), -1).transpose(0, 1)
+    h_stats = h_stats.float().contiguous()
     logits = rnd(SLOTS, V, 256, 16, 16, s=2.0)
     sin = rnd(PATCHES, 48)
     cos = rnd(PATCHES, 48)
@@ -75,6 +81,9 @@ def cases():
                                                  kv_row_stride=3 * D, out=out),
                            4.0 * SLOTS * HEADS * PATCHES * PATCHES * 96),
         'gemm_fc1': (lambda: ops.gemm(h, w['fc1'], b['fc1'], _lib.EPI_BIAS_GELU, out=mlp), 2.0 * rows * D * MLP),
+        # fc1 as the engine runs it: the LayerNorm + modulate folded in (raw rows h, their chunk statistics)
+        'gemm_fc1_fold': (lambda: ops.gemm(h, fc1_fold[0], b['fc1'], _lib.EPI_BIAS_GELU, out=mlp,
+                                           ln=(h_stats, *fc1_fold[1:], 1e-6)), 2.0 * rows * D * MLP),
         'gemm_qkv': (lambda: ops.gemm(h, w['qkv'], b['qkv'], _lib.EPI_ROPE, out=qkv, rope=(sin, cos),
                                       rope_cols=2 * D, rows_per_slot=PATCHES), 2.0 * rows * D * 3 * D),
         'gemm_dxd': (lambda: ops.gemm(h, w['dxd'], b['dxd'], _lib.EPI_GATE_RESIDUAL, out=out, gate=gate,
