@@ -160,3 +160,44 @@ def test_attention_multi_plan_covers_both_problems(lib):
     loads = [sum(tiles[u] for u in ids[offsets[c]:offsets[c + 1]]) for c in range(grid)]
     assert max(loads) < 108 + 26 and sum(loads) / grid > 0.93 * max(loads)
     assert lib.svx_attention_multi_plan_ints(3, 8, 8, 1024, 148) == 0
+
+
+def test_layernorm_fold_algebra_matches_layernorm_then_linear():
+    """The host half of the LayerNorm fold: with W' = fold_layernorm(W, b, 1 + scale, shift), the epilogue formula
+    r (x W'^T - mu u) + v equals LayerNorm -> modulate -> linear (float64, up to the bf16 rounding of W')."""
+    from streamvoxel_b200.model import fold_layernorm
+    g = torch.Generator().manual_seed(3)
+    m, k, n = 64, 768, 96
+    x = torch.randn((m, k), generator=g, dtype=torch.float64) * 0.7 + 0.3
+    w = (torch.randn((n, k), generator=g) * 0.03).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    ops_ = (1 + torch.randn(k, generator=g) * 0.2).to(torch.bfloat16)
+    shift = (torch.randn(k, generator=g) * 0.2).to(torch.bfloat16)
+    wf, u, v = fold_layernorm(w, b, ops_, shift)
+    assert wf.dtype == torch.bfloat16 and u.dtype == v.dtype == torch.float32
+    mu = x.mean(1, keepdim=True)
+    r = 1 / torch.sqrt(x.var(1, unbiased=False, keepdim=True) + 1e-6)
+    got = r * (x @ wf.double().t() - mu * u.double()) + v.double()
+    want = ((x - mu) * r * ops_.double() + shift.double()) @ w.double().t() + b.double()
+    torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)   # W' rounded to bf16 (as h is, unfolded)
+    exact = r * (x @ (w.double() * ops_.double()).t() - mu * (w.double() * ops_.double()).sum(1)) + v.double()
+    torch.testing.assert_close(exact, want, atol=1e-9, rtol=1e-9)   # the identity itself is exact
+    wf0, u0, v0 = fold_layernorm(w, b)   # LayerNorm without affine
+    assert torch.equal(wf0, w) and torch.equal(v0, b.float())
+
+
+def test_row_statistics_merge_restated():
+    """The kernels' chunk statistics and their merge, restated in numpy: per 32-column chunk (mean, M2); the row's mean
+    and variance from shifted sums about the first chunk's mean (`row_norm` in gemm.cu) equal the two-pass values,
+    also when the row's mean is far larger than its spread."""
+    rng = np.random.default_rng(5)
+    for offset in (0.0, 50.0):
+        x = (rng.standard_normal((16, 768)) * 0.5 + offset).astype(np.float32)
+        c = x.reshape(16, 24, 32).astype(np.float64)
+        mean_c, m2_c = c.mean(-1), ((c - c.mean(-1, keepdims=True)) ** 2).sum(-1)
+        d = mean_c - mean_c[:, :1]
+        dm = d.sum(1) / 24
+        mean = mean_c[:, 0] + dm
+        var = (m2_c + 32 * d * d).sum(1) / 768 - dm * dm
+        np.testing.assert_allclose(mean, x.astype(np.float64).mean(1), rtol=1e-12, atol=1e-12)
+        np.testing.assert_allclose(var, x.astype(np.float64).var(1), rtol=1e-9)
