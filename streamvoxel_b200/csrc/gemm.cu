@@ -798,9 +798,10 @@ static int pick_bn(int M, int N) {
 }
 
 // Tile width for CTA pairs (256-row tiles, 74 pairs on 148 SMs). A tile's main loop is bound by its products, which
-// scale with BN, plus a per-tile cost of about 32 columns' worth (epilogue tail, accumulator hand-off): the cost of a
-// width is (rounds of tiles over the pairs) x (BN + 32); the wider tile on ties. Measured on B200 at M = 8192:
-// BN = 128 never beat 256; 192 fills the pairs better when N is 768 or 3072.
+// scale with BN, plus a per-tile cost (epilogue, accumulator hand-off) that the fused epilogues (LayerNorm fold, row
+// statistics, RoPE, GELU) make worth about 200 columns: the cost of a width is (rounds of tiles over the pairs) x
+// (BN + 200); the wider tile on ties. Measured on B200 at M = 8192 with the engine's epilogues (us, BN 256/192/128):
+// qkv 36.5/42.2/43.7, fc1 43.8/44.8/54.6, fc2 43.4/35.9/46.0, d x d 19.0/17.0/19.6, head 187.0/-/240.0.
 static int pick_pair_bn(int M, int N) {
   int sms = 148;
   int device = 0;
@@ -811,7 +812,7 @@ static int pick_pair_bn(int M, int N) {
   for (int bn : {256, 192, 128}) {
     if (N % bn) continue;
     const long tiles = (long)(N / bn) * (M / PM);
-    const long cost = ((tiles + pairs - 1) / pairs) * (bn + 32);
+    const long cost = ((tiles + pairs - 1) / pairs) * (bn + 200);
     if (!best || cost < best_cost) { best = bn; best_cost = cost; }
   }
   return best;
