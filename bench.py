@@ -169,7 +169,6 @@ def run_device_steps(batch, steps, seeds):
     (committed voxels, kernel launches, marking forwards). Each forward of a window is credited with an equal share of
     the window's voxels (its column commits them all: solid steps plus the deferred low-entropy-last voxels at finish):
     exact for whole windows, and the steady-state rate when the timed region ends inside a window."""
-    from streamvoxel_b200.stream.batch import EASE_LAUNCHES
     committed = launches = markings = 0
     per_step = batch.launches()
     done = 0

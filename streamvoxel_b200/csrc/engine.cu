@@ -105,7 +105,7 @@ int run_block_qkv(const svx_engine& E, const svx_block_weights& bw, const GemmPl
 // The second half, after the attention: x += g1 proj(attn); x += g2 fc2(GELU(fc1(modulate(LN(x))))).
 int run_block_rest(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
                    cudaStream_t s) {
-  const int d = E.cfg.d, rows = n * E.patches;
+  const int rows = n * E.patches;
   const svx_engine_workspace& ws = E.ws;
   int rc;
   EpiParams e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);

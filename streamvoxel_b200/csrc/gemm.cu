@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            uint16_t* __restrict__ out, int M, int N, int K,
                                                            const EpiParams ep) {
-  constexpr int EPI = E & 7;
+  [[maybe_unused]] constexpr int EPI = E & 7;
   [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
   constexpr uint32_t B_BYTES = BN * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
@@ -518,8 +518,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = tc::instr_desc(PM, BN);
       int it = 0, local = 0;
       bool ok = true;
-      for (int k = 0; ok && k < t_count; ++k, ++local) {
-        const int tile = t_first + k * t_step;
+      for (int k = 0; ok && k < t_count; ++k, ++local) {   // the tiles' order is the producer's; only their count
         const int buf = local & 1, use = local >> 1;
         if (use > 0 && !tc::wait_w(acc_empty + buf, (use - 1) & 1, abort_flag)) { record_timeout(); break; }
         tc::fence_after();
@@ -614,7 +613,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             epilogue_math<E>(ep, row, n0 + chunk * 32, acc, ops, nr, y, LN_FOLD ? uv : nullptr);
             uint32_t pk[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) pk[j] = tc::pack_bf16x2(y[2 * j], y[2 * j + 1]);
+            for (int w = 0; w < 16; ++w) pk[w] = tc::pack_bf16x2(y[2 * w], y[2 * w + 1]);
             if constexpr (LN_STATS) chunk_stats_packed(ep, M, row, n0 + chunk * 32, pk);
 #pragma unroll
             for (int q = 0; q < 4; ++q)

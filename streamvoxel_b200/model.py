@@ -16,7 +16,7 @@ The per-step forward then runs entirely in libsvx (`svx_engine_forward`).
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass, field, replace
+from dataclasses import dataclass, replace
 
 import numpy as np
 import torch

@@ -4,7 +4,6 @@ import os
 import tempfile
 
 import numpy as np
-import pytest
 import torch.multiprocessing as mp
 
 from streamvoxel_b200.stream import expand, scheduler as sch

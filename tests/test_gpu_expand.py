@@ -1,6 +1,5 @@
 """The world-expansion driver through the real engine (small model): windows conditioned on committed columns via
 `make_item`, sampled by the whole-step graph, committed and re-admitted until the region is full."""
-import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
