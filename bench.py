@@ -32,6 +32,7 @@ METRIC = 'committed voxels/s per B200 (8 slots)'
 UNIT = 'voxels/s'
 SLOTS, L1_CAP, L2_CAP, CAP = 8, 8, 81, 32
 WORKLOAD = 'config2: DiT-B/4 (d=768, 8x96 heads, 12 layers, V=256) + 12-layer ControlNet, 8 slots, bf16, cached K/V'
+BYTE_KERNELS = ('ease_scores', 'patch_embed')   # memory-bound: rates in GB/s, left out of the step's FLOPs
 
 
 def parse():
@@ -332,6 +333,13 @@ def time_kernels(cfg, forward, batch, lengths):
                             4.0 * SLOTS * heads * cfg.patches * mean_len * 96 + self_flops, 12),
         'ease_scores': (lambda: ops.ease_scores(forward.logits, batch.status, out=batch.scores),
                         float(forward.logits.numel() * 2 + batch.scores.numel() * 4), 1),
+        # both branches' embed of the slots' current tokens with the first LayerNorms' chunk statistics; bytes: tokens
+        # in, y-embeddings in, rows and statistics out (the 2 x 25 MB tables are gathered from L2)
+        'patch_embed': (lambda: ops.patch_embed(forward.tokens, cfg.classes, m.table_b, m.bias_b, m.yadd_b, m.table_c,
+                                                m.bias_c, m.yadd_c, out_b=ws['xb'], out_c=ws['xc'], stats_b=stats,
+                                                stats_c=forward.engine.stats['c']),
+                        float(forward.tokens.numel() * 2 + 2 * cfg.patches * d * 2 + 2 * rows * d * 2
+                              + 2 * (d // 32) * rows * 8), 1),
     }
     out = {}
     for name, (fn, work, count) in kernels.items():
@@ -431,7 +439,7 @@ def main_ours(args):
         os.path.join(ROOT, 'MEASURED_PEAKS.json')) else {}
     dominant = max(kernels, key=lambda k: kernels[k]['share_seconds'])
     kd = kernels[dominant]
-    if dominant.startswith('ease'):
+    if dominant in BYTE_KERNELS:
         peak, unit, bound, src = peaks.get('hbm_gbs', 6650.0), 'GB/s', 'hbm', 'measured' if peaks else 'fallback'
         achieved = kd['work'] / kd['seconds'] / 1e9
     else:
@@ -442,7 +450,7 @@ def main_ours(args):
     if dominant in MEASURED_TRAFFIC:
         measured, captured_alg = MEASURED_TRAFFIC[dominant]
         traffic = measured * algorithmic_bytes(dominant, cfg, lengths) / captured_alg
-    step_flops = sum(k['work'] * k['per_step'] for n, k in kernels.items() if not n.startswith('ease'))
+    step_flops = sum(k['work'] * k['per_step'] for n, k in kernels.items() if n not in BYTE_KERNELS)
     cpu = cpu_baseline(cfg, sd, lengths, args.cpu_sample)
     steps_per_s = args.steps / seconds
     line = dict(
@@ -463,7 +471,7 @@ def main_ours(args):
                       algorithmic=f"{kd['work']:.4g} {'bytes' if bound == 'hbm' else 'FLOP'} per launch"),
         step_tflops=step_flops / (seconds / args.steps) / 1e12,
         kernels={k: dict(us=v['seconds'] * 1e6, per_step=v['per_step'],
-                         rate=(v['work'] / v['seconds'] / (1e9 if k.startswith('ease') else 1e12)))
+                         rate=(v['work'] / v['seconds'] / (1e9 if k in BYTE_KERNELS else 1e12)))
                  for k, v in kernels.items()},
         cpu_baseline=cpu, clocks=clocks.summary())
     print(json.dumps(line), flush=True)

@@ -7,13 +7,19 @@
 namespace svx {
 namespace {
 
-__device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 raw) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    acc[2 * j] += __uint_as_float(w[j] << 16);
-    acc[2 * j + 1] += __uint_as_float(w[j] & 0xFFFF0000u);
-  }
+// acc[j] += bf16 element j of the 16 bytes (element 2i in the low half of word i), each add the fp32 add of the
+// exactly widened bf16 value, rounded to nearest even. sm_100's mixed-precision add (`add.rn.f32.bf16`) takes the bf16
+// half straight from the packed word: one instruction per element instead of a shift or mask plus an fp32 add, which
+// takes ~15% off the embed, whose time does not follow the bytes it gathers (all-MASK columns, whose 64 rows repeat in
+// every patch, take as long as random ones; skipping repeated rows did not help).
+__device__ __forceinline__ void add_bf16x8(float (&a)[8], uint4 r) {
+  asm("{\n\t.reg .b16 l0, h0, l1, h1, l2, h2, l3, h3;\n\t"
+      "mov.b32 {l0, h0}, %8;\n\tmov.b32 {l1, h1}, %9;\n\tmov.b32 {l2, h2}, %10;\n\tmov.b32 {l3, h3}, %11;\n\t"
+      "add.rn.f32.bf16 %0, l0, %0;\n\tadd.rn.f32.bf16 %1, h0, %1;\n\tadd.rn.f32.bf16 %2, l1, %2;\n\t"
+      "add.rn.f32.bf16 %3, h1, %3;\n\tadd.rn.f32.bf16 %4, l2, %4;\n\tadd.rn.f32.bf16 %5, h2, %5;\n\t"
+      "add.rn.f32.bf16 %6, l3, %6;\n\tadd.rn.f32.bf16 %7, h3, %7;\n\t}"
+      : "+f"(a[0]), "+f"(a[1]), "+f"(a[2]), "+f"(a[3]), "+f"(a[4]), "+f"(a[5]), "+f"(a[6]), "+f"(a[7])
+      : "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w));
 }
 
 __device__ __forceinline__ void unpack_bf16x8(uint4 raw, float (&v)[8]) {
@@ -38,22 +44,23 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float (&v)[8]) {
 // buffers it also writes (mean, M2) of every 32-column chunk of the bf16 output row (four adjacent lanes), chunk-major
 // ([d/32][rows]), the statistics the first LayerNorm of each branch takes from the GEMM that follows.
 __global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int height, int depth, int width, int classes,
-                                   int d, const uint16_t* __restrict__ table_b, const uint16_t* __restrict__ bias_b,
-                                   const uint16_t* __restrict__ add_b, uint16_t* __restrict__ out_b,
-                                   const uint16_t* __restrict__ table_c, const uint16_t* __restrict__ bias_c,
-                                   const uint16_t* __restrict__ add_c, uint16_t* __restrict__ out_c,
-                                   float2* __restrict__ stats_b, float2* __restrict__ stats_c) {
+                                   int d, int total_rows, const uint16_t* __restrict__ table_b,
+                                   const uint16_t* __restrict__ bias_b, const uint16_t* __restrict__ add_b,
+                                   uint16_t* __restrict__ out_b, const uint16_t* __restrict__ table_c,
+                                   const uint16_t* __restrict__ bias_c, const uint16_t* __restrict__ add_c,
+                                   uint16_t* __restrict__ out_c, float2* __restrict__ stats_b,
+                                   float2* __restrict__ stats_c) {
   constexpr int P = 4, P3 = 64;
   grid_launch_dependents();
   grid_dependency_wait();
   const int gz = depth / P, gx = width / P;
   const int patches = (height / P) * gz * gx;
   const int row = blockIdx.x;  // slot * patches + p
-  const int slot = row / patches, p = row % patches;
-  const int py = p / (gz * gx), pz = (p / gx) % gz, px = p % gx;
   __shared__ int rows[P3];
-  if (threadIdx.x < P3) {
-    const int o = threadIdx.x, oy = o >> 4, oz = (o >> 2) & 3, ox = o & 3;
+  for (int o = threadIdx.x; o < P3; o += blockDim.x) {
+    const int slot = row / patches, p = row % patches;
+    const int py = p / (gz * gx), pz = (p / gx) % gz, px = p % gx;
+    const int oy = o >> 4, oz = (o >> 2) & 3, ox = o & 3;
     const int64_t voxel = (((int64_t)slot * height + py * P + oy) * depth + pz * P + oz) * width + px * P + ox;
     int t = tokens[voxel];
     t = t < 0 ? 0 : (t > classes ? classes : t);  // out-of-vocabulary ids clamp instead of reading out of bounds
@@ -63,14 +70,14 @@ __global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int heigh
   const int c0 = threadIdx.x * 8;
   if (c0 >= d) return;
   for (int branch = 0; branch < 2; ++branch) {
-    const uint16_t* table = branch ? table_c : table_b;
-    if (!table) continue;
+    if (!(branch ? table_c : table_b)) continue;
+    const uint16_t* table = (branch ? table_c : table_b) + c0;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
-    for (int o = 0; o < P3; ++o) add_bf16x8(acc, *reinterpret_cast<const uint4*>(table + (int64_t)rows[o] * d + c0));
+    for (int o = 0; o < P3; ++o) add_bf16x8(acc, *reinterpret_cast<const uint4*>(table + (int64_t)rows[o] * d));
     float bias[8], add[8];
     unpack_bf16x8(*reinterpret_cast<const uint4*>((branch ? bias_c : bias_b) + c0), bias);
-    unpack_bf16x8(*reinterpret_cast<const uint4*>((branch ? add_c : add_b) + (int64_t)p * d + c0), add);
+    unpack_bf16x8(*reinterpret_cast<const uint4*>((branch ? add_c : add_b) + (int64_t)(row % patches) * d + c0), add);
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = round_bf16(round_bf16(round_bf16(acc[j]) + bias[j]) + add[j]);
     *reinterpret_cast<uint4*>((branch ? out_c : out_b) + (int64_t)row * d + c0) = pack_bf16x8(acc);
@@ -88,7 +95,7 @@ __global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int heigh
       for (int j = 0; j < 8; ++j) m2 = fmaf(acc[j] - mean, acc[j] - mean, m2);
       m2 += __shfl_xor_sync(group, m2, 1);
       m2 += __shfl_xor_sync(group, m2, 2);
-      if ((threadIdx.x & 3) == 0) stats[(int64_t)(threadIdx.x / 4) * gridDim.x + row] = make_float2(mean, m2);
+      if ((threadIdx.x & 3) == 0) stats[(int64_t)(threadIdx.x / 4) * total_rows + row] = make_float2(mean, m2);
     }
   }
 }
@@ -164,8 +171,9 @@ int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int
   int threads = ((d / 8 + 31) / 32) * 32;
   if (threads < 64) threads = 64;
   return launch_dependent("patch_embed_kernel", patch_embed_kernel, dim3(slots * patches), dim3(threads), 0, stream,
-                          tokens, height, depth, width, classes, d, table_b, bias_b, add_b, out_b, table_c, bias_c,
-                          add_c, out_c, reinterpret_cast<float2*>(stats_b), reinterpret_cast<float2*>(stats_c));
+                          tokens, height, depth, width, classes, d, slots * patches, table_b, bias_b, add_b, out_b,
+                          table_c, bias_c, add_c, out_c, reinterpret_cast<float2*>(stats_b),
+                          reinterpret_cast<float2*>(stats_c));
 }
 
 int layernorm_run(const uint16_t* x, int rows, int d, float eps, const uint16_t* ops, const uint16_t* shift,

@@ -470,6 +470,56 @@ def test_patch_embed_writes_row_statistics(ops):
     assert torch.equal(stats_b, stats_c)
 
 
+def _embed_sequential(tokens, table, bias, add, classes):
+    """The embed in the kernel's arithmetic: fp32 sum over the 64 offsets in order o = 0..63, then bf16(bf16(bf16(sum)
+    + bias) + add[p]), ids clamped to [0, classes]."""
+    s, h, dz, w = tokens.shape
+    t = tokens.long().clamp(0, classes).reshape(s, h // 4, 4, dz // 4, 4, w // 4, 4)
+    rows = t.permute(0, 1, 3, 5, 2, 4, 6).reshape(-1, 64) * 64 + torch.arange(64)
+    tab = table.float()
+    acc = torch.zeros((len(rows), table.shape[1]))
+    for o in range(64):
+        acc = acc + tab[rows[:, o]]
+    return _bf16(_bf16(_bf16(acc) + bias.float()) + add.float().repeat(s, 1))
+
+
+@pytest.mark.parametrize('shape,tokens', [((3, 4, 8, 4), 'random'), ((1, 4, 4, 12), 'random'),
+                                          ((3, 8, 8, 4), 'terrain'), ((2, 64, 16, 16), 'terrain'),
+                                          ((2, 64, 16, 16), 'mask'), ((5, 4, 8, 4), 'out_of_range')])
+def test_patch_embed_bit_exact_sequential_sum(ops, shape, tokens):
+    """The embed (fp32 sum of 64 bf16 table rows with sm_100's mixed-precision adds) is bit-exact against the
+    sequential fp32 sum: odd row counts (6, 3 and 10 rows), terrain-like columns (air above a height, a few ids below,
+    MASK with probability r), all-MASK columns and out-of-vocabulary ids (clamped); the chunk statistics follow the same
+    rows."""
+    g = torch.Generator().manual_seed(sum(shape) + len(tokens))
+    classes, d = 40, 128
+    s, h, dz, w = shape
+    if tokens == 'random':
+        t = torch.randint(0, classes + 1, shape, generator=g)
+    elif tokens == 'terrain':
+        height = torch.randint(h // 4, 3 * h // 4, (s, 1, dz, w), generator=g)
+        y = torch.arange(h)[None, :, None, None]
+        t = torch.where(y < height, torch.randint(1, 5, shape, generator=g), 0)
+        r = torch.rand((s, 1, 1, 1), generator=g)
+        t = torch.where(torch.rand(shape, generator=g) < r, classes, t)
+    elif tokens == 'mask':
+        t = torch.full(shape, classes)
+    else:
+        t = torch.randint(-3, classes + 4, shape, generator=g)
+    table = (torch.randn(((classes + 1) * 64, d), generator=g) * 0.05).bfloat16()
+    bias = (torch.randn(d, generator=g) * 0.1).bfloat16()
+    patches = (h // 4) * (dz // 4) * (w // 4)
+    add = (torch.randn((patches, d), generator=g) * 0.1).bfloat16()
+    want = _embed_sequential(t, table, bias, add, classes)
+    rows = s * patches
+    stats_b = torch.zeros((d // 32, rows, 2), device='cuda')
+    out_b, out_c = ops.patch_embed(t.to(torch.int16).cuda(), classes, table.cuda(), bias.cuda(), add.cuda(),
+                                   table.cuda(), bias.cuda(), add.cuda(), stats_b=stats_b)
+    assert torch.equal(out_b.float().cpu(), want)
+    assert torch.equal(out_b, out_c)
+    torch.testing.assert_close(stats_b.double().cpu(), _chunk_stats(want), atol=1e-5, rtol=1e-5)
+
+
 @pytest.mark.parametrize('epilogue', ['bias', 'gelu', 'rope', 'class_major'])
 def test_gemm_layernorm_fold_matches_layernorm_then_linear(ops, epilogue):
     """A residual GEMM writes its output rows' chunk statistics; the next linear takes the raw rows with the LayerNorm
