@@ -166,6 +166,14 @@ SVX_API int svx_patch_embed(const int16_t* tokens, int slots, int height, int de
 SVX_API int svx_layernorm_modulate(const uint16_t* x, int rows, int d, float eps, const uint16_t* one_plus_scale,
                                    const uint16_t* shift, uint16_t* out, void* stream);
 
+/* The condition encoder's LayerNorms (`streaming_controlnet.py:142-158` `_encode_columns`: `l2_norm` (affine, eps 1e-5)
+ * then GELU before the 4^3 down-conv; `:158,167-168,217-218`: + type + size embeddings, then `context_norm` (no
+ * affine, eps 1e-6)), in fp32: out = bf16(g(LN(x + pre) * weight + bias)), g = GELU(erf) when gelu != 0. pre [d] fp32
+ * (16-byte aligned), weight/bias [d] fp32, each may be NULL (weight and bias together). x,out [rows][d] bf16, 16-byte
+ * aligned, out may be x; d % 8 == 0, d <= 1536. Replaces `F.layer_norm` / `F.gelu` of `FastSlotForward.encode` (`fast_ops.py:228-239`). */
+SVX_API int svx_layernorm_affine(const uint16_t* x, int rows, int d, float eps, const float* pre,
+                                 const float* weight, const float* bias, int gelu, uint16_t* out, void* stream);
+
 /* Epilogues of svx_gemm. out = f(acc + bias) with acc = A[M,K] . W[N,K]^T in fp32, every step rounded to bf16 as
  * eager autocast rounds it (`streamvoxel/models/unconditional_md4_timefree.py:37-63`). */
 typedef enum {

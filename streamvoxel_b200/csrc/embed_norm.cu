@@ -160,6 +160,79 @@ __global__ void layernorm_modulate_kernel(const uint16_t* __restrict__ x, int ro
   }
 }
 
+// LayerNorm of the condition encoder (`streamvoxel/models/streaming_controlnet.py:142-158,160-169,218`) in fp32:
+// v = x + pre (pre: the fp32 type + size embeddings, `:158,217`; optional), y = (v - mean) * rstd, then
+// y * weight + bias (fp32 affine of `l2_norm`, `:147`; optional) and GELU(erf) (`:147`; optional), stored bf16
+// (the cast the next linear or conv makes under autocast). One warp per row, as above; a warp reads its whole row
+// before it writes, so out may be x (in place).
+template <int PER>
+__global__ void layernorm_affine_kernel(const uint16_t* x, int rows, int d, float eps, const float* __restrict__ pre,
+                                        const float* __restrict__ weight, const float* __restrict__ bias, int gelu,
+                                        uint16_t* out) {
+  grid_launch_dependents();
+  grid_dependency_wait();
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (row >= rows) return;
+  const int lane = lane_id();
+  const int chunks = d >> 3;
+  const uint16_t* src = x + (int64_t)row * d;
+  float v[PER][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = i * 32 + lane;
+    if (c < chunks) {
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(src + c * 8), v[i]);
+      if (pre) {
+        const float4 a = *reinterpret_cast<const float4*>(pre + c * 8);
+        const float4 b = *reinterpret_cast<const float4*>(pre + c * 8 + 4);
+        v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
+        v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[i][j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / d;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    if (i * 32 + lane < chunks) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float c = v[i][j] - mean;
+        var += c * c;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float rstd = rsqrtf(var / d + eps);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = i * 32 + lane;
+    if (c >= chunks) continue;
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = (v[i][j] - mean) * rstd;
+    if (weight) {
+      const float w[8] = {weight[c * 8], weight[c * 8 + 1], weight[c * 8 + 2], weight[c * 8 + 3],
+                          weight[c * 8 + 4], weight[c * 8 + 5], weight[c * 8 + 6], weight[c * 8 + 7]};
+      const float b[8] = {bias[c * 8], bias[c * 8 + 1], bias[c * 8 + 2], bias[c * 8 + 3],
+                          bias[c * 8 + 4], bias[c * 8 + 5], bias[c * 8 + 6], bias[c * 8 + 7]};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = fmaf(y[j], w[j], b[j]);
+    }
+    if (gelu) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = 0.5f * y[j] * (1.f + erff(y[j] * 0.7071067811865476f));
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)row * d + c * 8) = pack_bf16x8(y);
+  }
+}
+
 }  // namespace
 
 int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int width, int classes, int d,
@@ -193,6 +266,18 @@ int layernorm_run(const uint16_t* x, int rows, int d, float eps, const uint16_t*
   }
 }
 
+int layernorm_affine_run(const uint16_t* x, int rows, int d, float eps, const float* pre, const float* weight,
+                         const float* bias, int gelu, uint16_t* out, cudaStream_t stream) {
+  using Kernel = void (*)(const uint16_t*, int, int, float, const float*, const float*, const float*, int, uint16_t*);
+  static const Kernel kernels[] = {layernorm_affine_kernel<1>, layernorm_affine_kernel<2>, layernorm_affine_kernel<3>,
+                                   layernorm_affine_kernel<4>, layernorm_affine_kernel<5>, layernorm_affine_kernel<6>};
+  const int per = (d / 8 + 31) / 32;
+  if (per < 1 || per > 6) return fail(SVX_ERR_INVALID, "layernorm_affine: d must be at most 1536");
+  const int warps = 8;
+  return launch_dependent("layernorm_affine_kernel", kernels[per - 1], dim3((rows + warps - 1) / warps),
+                          dim3(warps * 32), 0, stream, x, rows, d, eps, pre, weight, bias, gelu, out);
+}
+
 }  // namespace svx
 
 using namespace svx;
@@ -218,4 +303,15 @@ extern "C" int svx_layernorm_modulate(const uint16_t* x, int rows, int d, float 
   SVX_REQUIRE((one_plus_scale == nullptr) == (shift == nullptr), "svx_layernorm_modulate: scale and shift go together");
   SVX_REQUIRE(d % 8 == 0 && d <= 1536, "svx_layernorm_modulate: d must be a multiple of 8, at most 1536");
   return layernorm_run(x, rows, d, eps, one_plus_scale, shift, out, as_stream(stream));
+}
+
+extern "C" int svx_layernorm_affine(const uint16_t* x, int rows, int d, float eps, const float* pre,
+                                    const float* weight, const float* bias, int gelu, uint16_t* out, void* stream) {
+  SVX_REQUIRE(x && out && rows > 0, "svx_layernorm_affine: bad arguments");
+  SVX_REQUIRE((weight == nullptr) == (bias == nullptr), "svx_layernorm_affine: weight and bias go together");
+  SVX_REQUIRE(d % 8 == 0 && d <= 1536, "svx_layernorm_affine: d must be a multiple of 8, at most 1536");
+  SVX_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                reinterpret_cast<uintptr_t>(pre)) & 15) == 0,
+              "svx_layernorm_affine: x, out and pre must be 16-byte aligned");
+  return layernorm_affine_run(x, rows, d, eps, pre, weight, bias, gelu, out, as_stream(stream));
 }

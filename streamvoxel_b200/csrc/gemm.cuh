@@ -61,5 +61,7 @@ int patch_embed_run(const int16_t* tokens, int slots, int height, int depth, int
                     float* stats_b, float* stats_c, cudaStream_t stream);
 int layernorm_run(const uint16_t* x, int rows, int d, float eps, const uint16_t* ops, const uint16_t* shift,
                   uint16_t* out, cudaStream_t stream);
+int layernorm_affine_run(const uint16_t* x, int rows, int d, float eps, const float* pre, const float* weight,
+                         const float* bias, int gelu, uint16_t* out, cudaStream_t stream);
 
 }  // namespace svx

@@ -223,6 +223,17 @@ class PreparedModel:
         if cfg.layer_indices:
             self.table_l1, self.bias_l1 = self._table('l1_patch')
             self.table_l2, self.bias_l2 = self._table('l2_patch')
+            # the column encoder's constants: l2_norm's fp32 affine, the 4^3 down-conv as a [d, 64 d] GEMM weight in
+            # (ky, kz, kx, d_in) order, its bias (bf16, added to the bf16 conv output), and each level's type + size
+            # embeddings summed in fp32 (added before context_norm)
+            self.l2_norm_w = sd['l2_norm.weight'].contiguous()
+            self.l2_norm_b = sd['l2_norm.bias'].contiguous()
+            self.l2_down_w = sd['l2_down.weight'].permute(0, 2, 3, 4, 1).reshape(cfg.d, -1).to(torch.bfloat16)
+            self.l2_down_w = self.l2_down_w.contiguous()
+            self.l2_down_b = sd['l2_down.bias'].to(torch.bfloat16)
+            self.level_embed = [(sd['type_embed.weight'][i] + sd['size_embed.weight'][i]).contiguous() for i in (0, 1)]
+            self.zero_bias = torch.zeros(cfg.d, device=dev, dtype=torch.bfloat16)
+            self._down_bias_rows = self.l2_down_b[None].expand(256, cfg.d).contiguous()
         self.kv_weight = [_bf16(sd[f'cross.{j}.key_value.weight'], dev) for j in range(len(cfg.layer_indices))]
         self.kv_bias = [_bf16(sd[f'cross.{j}.key_value.bias'], dev) for j in range(len(cfg.layer_indices))]
 
@@ -269,14 +280,14 @@ class PreparedModel:
                 prefix = cache.tokens(l2_keys, l2_blocks, self._l2_prefix)
             else:
                 prefix = self._l2_prefix(np.asarray(l2_blocks))
-            l1 = F.layer_norm(self._encode_columns(np.asarray(l1_blocks), 0).float(), (cfg.d,), eps=1e-6)
+            l1 = self._encode_columns(np.asarray(l1_blocks), 0)
             bio, bio_positions = self._biome(torch.as_tensor(np.asarray(biomes), device=dev).long(), bio_pos)
-            local = torch.cat((l1.flatten(0, 1), bio), 0)
+            local = torch.cat((l1.flatten(0, 1), bio.to(torch.bfloat16)), 0)
             local_positions = torch.cat((pos1.reshape(-1, 3), bio_positions), 0)
         # Every layer's key_value linear over all condition tokens at once (prefix rows, then local rows): the bf16
         # input autocast would cast, one tcgen05 GEMM per layer with the bias and the axial RoPE of the K half fused
         # in its epilogue (the same bf16 rounding points as `F.linear` then `AxialRoPE`), tables built once.
-        tokens = torch.cat((prefix.to(torch.bfloat16), local.float().to(torch.bfloat16)), 0)
+        tokens = torch.cat((prefix, local), 0)
         positions = torch.cat((pos2, local_positions.float()), 0)
         n = len(tokens)
         rows = -(-n // 256) * 256
@@ -295,30 +306,42 @@ class PreparedModel:
         return layers
 
     def _l2_prefix(self, blocks):
-        """Encoded prefix tokens of L2 columns [n, H, T, T] -> [n * 16, d] bf16 (the cast the key_value linear makes)."""
-        with torch.autocast('cuda', dtype=torch.bfloat16):
-            l2 = self._encode_columns(blocks, 1).flatten(0, 1)
-            return F.layer_norm(l2.float(), (self.cfg.d,), eps=1e-6).to(torch.bfloat16)
+        """Encoded prefix tokens of L2 columns [n, H, T, T] -> [n * H / 16, d] bf16 (the cast the key_value linear
+        makes)."""
+        return self._encode_columns(blocks, 1).flatten(0, 1)
 
     def _encode_columns(self, tokens, level):
-        """`_encode_columns` (`streaming_controlnet.py:142-158`): one-hot conv patchify (the gather kernel), for L2 then
-        LayerNorm (affine) -> GELU -> 4^3 down-conv; plus the type and size embeddings (fp32 parameters)."""
-        cfg, dev, sd = self.cfg, self.device, self.sd
+        """`_encode_columns` (`streaming_controlnet.py:142-158`) and `context_norm` (`:167-168`) on libsvx kernels:
+        the one-hot conv patchify (the gather kernel); for L2 `l2_norm` + GELU (`svx_layernorm_affine`, fp32) and the
+        4^3 stride-4 down-conv as one GEMM: the 64 patches under an output token are 64 consecutive rows of the
+        patchified column (patch order y, z, x with 4 x 4 patches per y), so A is the [n H/16, 64 d] view and W the
+        conv weight in (ky, kz, kx, d_in) order; the conv's bias is added to its bf16 output in bf16 (the separate
+        bias add of the conv under autocast) by the residual epilogue over rows of the bias. Then the type + size
+        embeddings and the no-affine LayerNorm (`svx_layernorm_affine` with `pre`; the two fp32 embeddings summed
+        once, not added one after the other). Returns [n, count, d] bf16."""
+        cfg, dev = self.cfg, self.device
+        height, tile = cfg.voxel_shape[0], cfg.voxel_shape[1]
+        count = (height // 16) if level else cfg.patches
         if len(tokens) == 0:
-            count = (tokens.shape[1] // (16 if level else 4)) * (1 if level else 16) if tokens.ndim == 4 else 0
-            return torch.zeros((0, count, cfg.d), device=dev)
+            return torch.zeros((0, count, cfg.d), device=dev, dtype=torch.bfloat16)
         t = torch.as_tensor(tokens, device=dev).to(torch.int16).contiguous()
         table, bias = (self.table_l1, self.bias_l1) if level == 0 else (self.table_l2, self.bias_l2)
-        x, _ = ops.patch_embed(t, cfg.classes, table, bias, self.zero_yadd)
         n = len(t)
-        x = x.reshape(n, cfg.patches, cfg.d)
-        if level:
-            x = F.gelu(F.layer_norm(x.float(), (cfg.d,), sd['l2_norm.weight'], sd['l2_norm.bias'], 1e-5))
-            h, w = cfg.voxel_shape[0] // 4, cfg.voxel_shape[1] // 4
-            grid = x.reshape(n, h, w, w, cfg.d).permute(0, 4, 1, 2, 3)
-            x = F.conv3d(grid, sd['l2_down.weight'], None, stride=4)
-            x = (x + sd['l2_down.bias'].to(x.dtype)[:, None, None, None]).flatten(2).transpose(1, 2)
-        return x + sd['type_embed.weight'][level] + sd['size_embed.weight'][level]
+        if not level:
+            x, _ = ops.patch_embed(t, cfg.classes, table, bias, self.zero_yadd)
+            return ops.layernorm_affine(x, 1e-6, pre=self.level_embed[0]).view(n, count, cfg.d)
+        if tile != 16:
+            raise ValueError('the L2 down-conv takes 16-wide columns (one output token per 4 patch layers)')
+        rows = n * count
+        padded = -(-rows // 256) * 256
+        grid = torch.zeros((padded * 64, cfg.d), device=dev, dtype=torch.bfloat16)
+        x, _ = ops.patch_embed(t, cfg.classes, table, bias, self.zero_yadd, out_b=grid[:rows * 64])
+        ops.layernorm_affine(x, 1e-5, weight=self.l2_norm_w, bias=self.l2_norm_b, gelu=True, out=x)
+        if len(self._down_bias_rows) < padded:
+            self._down_bias_rows = self.l2_down_b[None].expand(padded, cfg.d).contiguous()
+        down = ops.gemm(grid.view(padded, 64 * cfg.d), self.l2_down_w, self.zero_bias, _lib.EPI_RESIDUAL,
+                        residual=self._down_bias_rows[:padded])
+        return ops.layernorm_affine(down[:rows], 1e-6, pre=self.level_embed[1]).view(n, count, cfg.d)
 
     def _biome(self, biomes, bio_positions):
         """`_biome_condition` (`streaming_controlnet.py:196-219`)."""

@@ -178,6 +178,17 @@ def layernorm_modulate(x, eps=1e-6, one_plus_scale=None, shift=None, out=None):
     return out
 
 
+def layernorm_affine(x, eps, pre=None, weight=None, bias=None, gelu=False, out=None):
+    """bf16(g(LN(x + pre) * weight + bias)) in fp32 (the condition encoder's LayerNorms; g = GELU(erf) with gelu).
+    x [rows, d] bf16; pre, weight, bias [d] fp32 or None."""
+    rows, d = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    check(_lib.load().svx_layernorm_affine(ptr(x), rows, d, float(eps), ptr(pre), ptr(weight), ptr(bias), int(gelu),
+                                           ptr(out), stream_ptr()), 'svx_layernorm_affine')
+    return out
+
+
 def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None, rope=None, rope_cols=0,
          rows_per_slot=0, head_dim=96, classes=0, geometry=(0, 0, 0), ln=None, stats_out=None):
     """out = epilogue(a @ w.T + bias) on the tcgen05 GEMM. a [M,K], w [N,K], bias [N] bf16.

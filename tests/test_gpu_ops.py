@@ -368,6 +368,27 @@ def test_layernorm_modulate(ops):
         torch.testing.assert_close(got, _bf16(ln), atol=1e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize('d', [192, 768])
+def test_layernorm_affine_matches_torch(ops, d):
+    """The condition encoder's LayerNorms on `svx_layernorm_affine`: l2_norm (fp32 affine, eps 1e-5) + GELU(erf), and
+    + type/size embeddings then the no-affine context_norm (eps 1e-6), against torch fp32 rounded once to bf16; in
+    place (out = x) as the encoder runs it."""
+    F = torch.nn.functional
+    torch.manual_seed(21)
+    rows = 300
+    x = (torch.randn((rows, d), device='cuda') * 0.7 + 0.1).bfloat16()
+    w = torch.randn(d, device='cuda') * 0.5 + 1
+    b = torch.randn(d, device='cuda') * 0.2
+    pre = torch.randn(d, device='cuda') * 0.3
+    got = ops.layernorm_affine(x, 1e-5, weight=w, bias=b, gelu=True).float()
+    torch.testing.assert_close(got, _bf16(F.gelu(F.layer_norm(x.float(), (d,), w, b, 1e-5))), atol=1e-2, rtol=1e-2)
+    got = ops.layernorm_affine(x, 1e-6, pre=pre).float()
+    torch.testing.assert_close(got, _bf16(F.layer_norm(x.float() + pre, (d,), eps=1e-6)), atol=1e-2, rtol=1e-2)
+    y = x.clone()
+    ops.layernorm_affine(y, 1e-6, pre=pre, out=y)
+    assert torch.equal(y.float(), got)
+
+
 def test_patch_embed_matches_gather(ops):
     from oracle import model as om
     from oracle.model import Precision
