@@ -215,6 +215,15 @@ typedef struct {
 SVX_API int svx_gemm(const uint16_t* A, const uint16_t* W, uint16_t* out, int M, int N, int K,
                      const svx_epilogue_args* epi, void* stream);
 
+/* Two independent gated-residual GEMMs with row statistics (epilogue SVX_EPI_GATE_RESIDUAL, ln_stats_out set, no
+ * LayerNorm fold) of the same M, N, K in one launch: out_i = bf16(res_i + bf16(gate_i[n] bf16(A_i W_i^T + b_i))).
+ * M % 256 == 0. A gate of ones gives the plain residual of SVX_EPI_RESIDUAL bit for bit. The engine runs a control
+ * layer's cross-attention projection (`streaming_controlnet.py:61`) with its backbone block's attention projection
+ * (`unconditional_md4_timefree.py:62`) this way: both follow the joint attention launch. */
+SVX_API int svx_gemm_group(const uint16_t* A0, const uint16_t* W0, uint16_t* out0, const svx_epilogue_args* epi0,
+                           const uint16_t* A1, const uint16_t* W1, uint16_t* out1, const svx_epilogue_args* epi1,
+                           int M, int N, int K, void* stream);
+
 /* Non-causal attention, head_dim 96, per (slot, head): out = softmax(Q K^T / sqrt(96)) V over keys < length[slot].
  * Q rows: q + (slot*queries + i)*q_row_stride + head*96; K/V: kv + slot*kv_slot_stride + head*kv_head_stride +
  * key*kv_row_stride. out [slot*queries + i][heads*96]. lengths == NULL: every slot has `keys` keys.

@@ -103,6 +103,8 @@ _SIGNATURES = {
     'svx_layernorm_modulate': (c_int, [c_ptr, c_int, c_int, ctypes.c_float, c_ptr, c_ptr, c_ptr, c_ptr]),
     'svx_layernorm_affine': (c_int, [c_ptr, c_int, c_int, ctypes.c_float, c_ptr, c_ptr, c_ptr, c_int, c_ptr, c_ptr]),
     'svx_gemm': (c_int, [c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, ctypes.POINTER(EpilogueArgs), c_ptr]),
+    'svx_gemm_group': (c_int, [c_ptr, c_ptr, c_ptr, ctypes.POINTER(EpilogueArgs), c_ptr, c_ptr, c_ptr,
+                               ctypes.POINTER(EpilogueArgs), c_int, c_int, c_int, c_ptr]),
     'svx_attention': (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_int, c_int, c_int, c_int,
                               c_ptr, c_ptr, c_int, c_ptr]),
     'svx_attention_plan_ints': (c_int, [c_int, c_int, c_int, c_int]),

@@ -34,8 +34,12 @@ struct svx_engine {
   int32_t* plan_dev = nullptr;
   int plan_stride = 0, plan_ctas = 0;
   std::vector<int32_t> plan_host;
+  // bf16 ones [d]: the gate that makes the cross projection's plain residual a gated one, so that it runs in one
+  // launch with the backbone's attention projection (svx::gemm_run_group)
+  uint16_t* ones = nullptr;
   ~svx_engine() {
     if (plan_dev) cudaFree(plan_dev);
+    if (ones) cudaFree(ones);
   }
 };
 
@@ -102,21 +106,33 @@ int run_block_qkv(const svx_engine& E, const svx_block_weights& bw, const GemmPl
   return gemm_run(plans[0], rows, ws.qkv, e, s);
 }
 
-// The second half, after the attention: x += g1 proj(attn); x += g2 fc2(GELU(fc1(modulate(LN(x))))).
-int run_block_rest(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
-                   cudaStream_t s) {
+// x += g1 proj(attn), with the row statistics of the new x.
+EpiParams proj_epi(const svx_engine& E, const svx_block_weights& bw, uint16_t* x) {
+  EpiParams e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);
+  e.gate = bw.gate1; e.residual = x; e.ln_stats_out = stats_of(E, x);
+  return e;
+}
+
+// The MLP half: x += g2 fc2(GELU(fc1(modulate(LN(x))))).
+int run_block_mlp(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
+                  cudaStream_t s) {
   const int rows = n * E.patches;
   const svx_engine_workspace& ws = E.ws;
   int rc;
-  EpiParams e = epi(SVX_EPI_GATE_RESIDUAL, bw.proj_b);
-  e.gate = bw.gate1; e.residual = x; e.ln_stats_out = stats_of(E, x);
-  if ((rc = gemm_run(plans[1], rows, x, e, s))) return rc;
-  e = epi(SVX_EPI_BIAS_GELU, bw.fc1_b);
+  EpiParams e = epi(SVX_EPI_BIAS_GELU, bw.fc1_b);
   fold(e, E, x, bw.fc1_u, bw.fc1_v);
   if ((rc = gemm_run(plans[2], rows, ws.mlp, e, s))) return rc;
   e = epi(SVX_EPI_GATE_RESIDUAL, bw.fc2_b);
   e.gate = bw.gate2; e.residual = x; e.ln_stats_out = stats_of(E, x);
   return gemm_run(plans[3], rows, x, e, s);
+}
+
+// The second half, after the attention: x += g1 proj(attn), then the MLP half.
+int run_block_rest(const svx_engine& E, const svx_block_weights& bw, const GemmPlan* plans, uint16_t* x, int n,
+                   cudaStream_t s) {
+  int rc;
+  if ((rc = gemm_run(plans[1], n * E.patches, x, proj_epi(E, bw, x), s))) return rc;
+  return run_block_mlp(E, bw, plans, x, n, s);
 }
 
 // One time-free AdaLN block on x (`UnconditionalBlock.forward`, `unconditional_md4_timefree.py:60-63`).
@@ -154,10 +170,17 @@ int run_control_layer(const svx_engine& E, int i, int j, int n, cudaStream_t s) 
   const int units = 2 * n * E.cfg.heads * ((E.patches / 128 + 1) / 2);
   const int32_t* plan = E.plan_dev + (size_t)(n - 1) * E.plan_stride;
   if ((rc = attention_launch(both, 2, n, E.cfg.heads, E.patches, plan, std::min(E.plan_ctas, units), s))) return rc;
-  e = epi(SVX_EPI_RESIDUAL, cw.proj_b);
-  e.residual = ws.xc; e.ln_stats_out = stats_of(E, ws.xc);
-  if ((rc = gemm_run(cp[5], rows, ws.xc, e, s))) return rc;
-  if ((rc = run_block_rest(E, E.backbone[i], bp, ws.xb, n, s))) return rc;
+  // c += proj(ax) (a residual: its gate is ones) and b += g1 proj(attn) in one launch, then block_b's MLP half
+  e = epi(SVX_EPI_GATE_RESIDUAL, cw.proj_b);
+  e.gate = E.ones; e.residual = ws.xc; e.ln_stats_out = stats_of(E, ws.xc);
+  if (rows % 256 == 0) {
+    rc = gemm_run_group(cp[5], ws.xc, e, bp[1], ws.xb, proj_epi(E, E.backbone[i], ws.xb), rows, s);
+  } else {
+    rc = gemm_run(cp[5], rows, ws.xc, e, s);
+    if (!rc) rc = gemm_run(bp[1], rows, ws.xb, proj_epi(E, E.backbone[i], ws.xb), s);
+  }
+  if (rc) return rc;
+  if ((rc = run_block_mlp(E, E.backbone[i], bp, ws.xb, n, s))) return rc;
   e = epi(SVX_EPI_RESIDUAL, cw.zero_b);
   e.residual = ws.xb; e.ln_stats_out = stats_of(E, ws.xb);
   return gemm_run(cp[6], rows, ws.xb, e, s);
@@ -251,6 +274,10 @@ extern "C" int svx_engine_create(const svx_engine_config* config, const svx_engi
       if (!rc && err == cudaSuccess)
         err = cudaMemcpy(e->plan_dev, e->plan_host.data(), e->plan_host.size() * sizeof(int32_t),
                          cudaMemcpyHostToDevice);
+      const std::vector<uint16_t> ones((size_t)c.d, 0x3F80);   // bf16 1.0
+      if (!rc && err == cudaSuccess) err = cudaMalloc(&e->ones, ones.size() * sizeof(uint16_t));
+      if (!rc && err == cudaSuccess)
+        err = cudaMemcpy(e->ones, ones.data(), ones.size() * sizeof(uint16_t), cudaMemcpyHostToDevice);
     }
     if (!rc && err != cudaSuccess) rc = fail(SVX_ERR_CUDA, cudaGetErrorString(err));
   }
@@ -303,7 +330,9 @@ extern "C" int svx_engine_set_lengths(svx_engine* E, const int32_t* lengths, voi
 extern "C" int svx_engine_launches(const svx_engine* E, int n) {
   if (!E || n < 1) return 0;
   const int per_block = 5;   // qkv, attention, proj, fc1, fc2 (LayerNorms folded into qkv and fc1)
-  const int per_cross = 3;   // query, proj, zero (its attention shares the backbone block's launch)
+  // query, zero (+ proj when it cannot share the backbone projection's launch); the attention shares the backbone
+  // block's launch
+  const int per_cross = (n * E->patches) % 256 == 0 ? 2 : 3;
   return 1 + E->cfg.depth_layers * per_block + E->cfg.n_control * (per_block + per_cross) + 1;
 }
 

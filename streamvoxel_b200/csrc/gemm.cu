@@ -28,8 +28,9 @@ constexpr int kThreads = 640;  // warps 0-1 producer/MMA, 2-3 idle, 4-19 epilogu
 constexpr int kEpilogueWarps = 16;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 // Kernel variants: the epilogue (svx_epilogue, bits 0-2) | kFold (LayerNorm folded into this GEMM's epilogue) |
-// kStats (row statistics for the next LayerNorm written by this epilogue).
-constexpr int kFold = 8, kStats = 16;
+// kStats (row statistics for the next LayerNorm written by this epilogue) | kGroup (two independent problems of the
+// same shape in one launch: the second problem's tiles follow the first's, with their own operands and epilogue).
+constexpr int kFold = 8, kStats = 16, kGroup = 32;
 
 __device__ __forceinline__ void record_timeout() { atomicOr(&g_svx_timeouts, SVX_STATUS_WAIT_TIMEOUT); }
 
@@ -439,9 +440,13 @@ template <int BN, int STAGES, int E>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
-                     uint16_t* __restrict__ out, int M, int N, int K, const EpiParams ep) {
+                     uint16_t* __restrict__ out, int M, int N, int K, const __grid_constant__ EpiParams ep,
+                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                     const __grid_constant__ CUtensorMap tmO2, const __grid_constant__ CUtensorMap tmR2,
+                     const __grid_constant__ EpiParams ep2) {
   constexpr int EPI = E & 7;
   [[maybe_unused]] constexpr bool LN_FOLD = (E & kFold) != 0, LN_STATS = (E & kStats) != 0;
+  constexpr bool GROUP = (E & kGroup) != 0;   // tiles [per, 2 per) are the second problem's (tmA2 ... ep2)
   constexpr uint32_t HB_BYTES = (BN / 2) * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;   // allocations are powers of two
   constexpr bool STAGED = EPI != SVX_EPI_CLASS_MAJOR;
@@ -465,7 +470,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
   const int kblocks = K / BK;
   const int n_tiles = N / BN;
-  const int tiles = (M / PM) * n_tiles;
+  const int per = (M / PM) * n_tiles;
+  const int tiles = GROUP ? 2 * per : per;
   // Tiles of this pair: round-robin (tile = pair + k * pairs), or, with the LayerNorm fold, a contiguous run, so that
   // consecutive tiles share their rows and the rows' statistics are merged once per row block (same makespan).
   int t_first = pair, t_step = pairs, t_count = tiles > pair ? (tiles - pair + pairs - 1) / pairs : 0;
@@ -487,6 +493,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc::prefetch_map(&tmB);
     if (STAGED) tc::prefetch_map(&tmO);
     if (RES) tc::prefetch_map(&tmR);
+    if (GROUP) {
+      tc::prefetch_map(&tmA2);
+      tc::prefetch_map(&tmB2);
+      if (STAGED) tc::prefetch_map(&tmO2);
+      if (RES) tc::prefetch_map(&tmR2);
+    }
   }
   if (warp == 1) tc::tmem_alloc_pair(tmem_slot, TMEM_COLS);
   tc::fence_before();
@@ -505,13 +517,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int k = 0; ok && k < t_count; ++k) {
         const int tile = t_first + k * t_step;
-        const int m0 = (tile / n_tiles) * PM + (int)rank * BM, n0 = (tile % n_tiles) * BN + (int)rank * (BN / 2);
+        const bool second = GROUP && tile >= per;
+        const int lt = second ? tile - per : tile;
+        const CUtensorMap* map_a = second ? &tmA2 : &tmA;
+        const CUtensorMap* map_b = second ? &tmB2 : &tmB;
+        const int m0 = (lt / n_tiles) * PM + (int)rank * BM, n0 = (lt % n_tiles) * BN + (int)rank * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES, round = it / STAGES;
           if (round > 0 && !tc::wait_w(empty + s, (round - 1) & 1, abort_flag)) { record_timeout(); ok = false; break; }
           if (rank == 0) tc::expect_tx_w(full + s, 2 * (A_BYTES + HB_BYTES));
-          tc::tma_load_2d_pair_w(a_s + s * A_BYTES, &tmA, kb * BK, m0, full0 + 8 * s);
-          tc::tma_load_2d_pair_w(b_s + s * HB_BYTES, &tmB, kb * BK, n0, full0 + 8 * s);
+          tc::tma_load_2d_pair_w(a_s + s * A_BYTES, map_a, kb * BK, m0, full0 + 8 * s);
+          tc::tma_load_2d_pair_w(b_s + s * HB_BYTES, map_b, kb * BK, n0, full0 + 8 * s);
         }
       }
     } else if (warp == 1 && rank == 0) {
@@ -556,7 +572,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     float2 nr = make_float2(0.f, 1.f);
     for (int k = 0; k < t_count; ++k, ++local) {
       const int tile = t_first + k * t_step;
-      const int m0 = (tile / n_tiles) * PM + (int)rank * BM, n0 = (tile % n_tiles) * BN;
+      const bool second = GROUP && tile >= per;
+      const int lt = second ? tile - per : tile;
+      const EpiParams& e = second ? ep2 : ep;
+      const CUtensorMap* map_o = second ? &tmO2 : &tmO;
+      const CUtensorMap* map_r = second ? &tmR2 : &tmR;
+      const int m0 = (lt / n_tiles) * PM + (int)rank * BM, n0 = (lt % n_tiles) * BN;
       const int buf = local & 1, use = local >> 1;
       const int row0 = m0 + quarter * 32, row = row0 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN);
@@ -569,7 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               const int chunk = group + 4 * j;
               if (chunk < CHUNKS) {
                 mbar_expect_tx(res_full + 2 * ws + j, BOX);
-                tc::tma_load_2d(wbox + j * BOX, &tmR, n0 + chunk * 32, row0, res_full + 2 * ws + j);
+                tc::tma_load_2d(wbox + j * BOX, map_r, n0 + chunk * 32, row0, res_full + 2 * ws + j);
               }
             }
           }
@@ -577,13 +598,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
       }
       if constexpr (LN_FOLD) {
-        if (group < CHUNKS && tile / n_tiles != norm_block) {
-          nr = row_norm(ep, row, M);
-          norm_block = tile / n_tiles;
+        if (group < CHUNKS && lt / n_tiles != norm_block) {
+          nr = row_norm(e, row, M);
+          norm_block = lt / n_tiles;
         }
       }
       Operands ops;
-      if (group < CHUNKS) prefetch32<E, !STAGED>(ep, N, row, n0 + group * 32, ops);
+      if (group < CHUNKS) prefetch32<E, !STAGED>(e, N, row, n0 + group * 32, ops);
       if (!tc::wait(acc_full + buf, use & 1, abort_flag)) { record_timeout(); break; }
       tc::fence_after();
       bool ok = true;
@@ -591,7 +612,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int j = 0; j < MINE; ++j) {
         const int chunk = group + 4 * j;
         if (chunk < CHUNKS) {
-          if (j > 0) prefetch32<E, !STAGED>(ep, N, row, n0 + chunk * 32, ops);
+          if (j > 0) prefetch32<E, !STAGED>(e, N, row, n0 + chunk * 32, ops);
           uint32_t acc[32];
           tc::ld32(taddr + chunk * 32, acc);
           tc::wait_ld();
@@ -610,18 +631,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               uv[32 + lane] = ops.v;
               __syncwarp();
             }
-            epilogue_math<E>(ep, row, n0 + chunk * 32, acc, ops, nr, y, LN_FOLD ? uv : nullptr);
+            epilogue_math<E>(e, row, n0 + chunk * 32, acc, ops, nr, y, LN_FOLD ? uv : nullptr);
             uint32_t pk[16];
 #pragma unroll
             for (int w = 0; w < 16; ++w) pk[w] = tc::pack_bf16x2(y[2 * w], y[2 * w + 1]);
-            if constexpr (LN_STATS) chunk_stats_packed(ep, M, row, n0 + chunk * 32, pk);
+            if constexpr (LN_STATS) chunk_stats_packed(e, M, row, n0 + chunk * 32, pk);
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               rb[q ^ swz] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
             tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tc::tma_store_2d(&tmO, n0 + chunk * 32, row0, wbox + j * BOX);
+              tc::tma_store_2d(map_o, n0 + chunk * 32, row0, wbox + j * BOX);
               tc::bulk_commit();
             }
           } else {
@@ -632,7 +653,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               uv[32 + lane] = ops.v;
               __syncwarp();
             }
-            if (row < M) epilogue32<E>(ep, out, M, N, row, n0 + chunk * 32, acc, ops, nr, LN_FOLD ? uv : nullptr);
+            if (row < M) epilogue32<E>(e, out, M, N, row, n0 + chunk * 32, acc, ops, nr, LN_FOLD ? uv : nullptr);
           }
         }
       }
@@ -656,9 +677,13 @@ constexpr size_t pair_smem_bytes() {
          (2 * STAGES + 4 + 2 * kEpilogueWarps) * 8 + 16 + kEpilogueWarps * 64 * 4;
 }
 
+// One launch of the pair kernel; with kGroup in EPI, a second problem of the same M, N, K (a2 ... ep2) whose tiles
+// follow the first's (without it the second set repeats the first and is not read).
 template <int BN, int STAGES, int EPI>
 int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const CUtensorMap& r,
-                     uint16_t* out, int M, int N, int K, const EpiParams& ep, cudaStream_t stream) {
+                     uint16_t* out, int M, int N, int K, const EpiParams& ep, cudaStream_t stream,
+                     const CUtensorMap* a2 = nullptr, const CUtensorMap* b2 = nullptr, const CUtensorMap* o2 = nullptr,
+                     const CUtensorMap* r2 = nullptr, const EpiParams* ep2 = nullptr) {
   constexpr size_t bytes = pair_smem_bytes<BN, STAGES>();
   static int max_pairs = 0;
   if (!max_pairs) {
@@ -673,10 +698,11 @@ int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
     SVX_REQUIRE(clusters > 0, "gemm: no CTA pair fits on this device");
     max_pairs = clusters;
   }
-  const int tiles = (N / BN) * (M / PM);
+  const int tiles = (N / BN) * (M / PM) * ((EPI & kGroup) ? 2 : 1);
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   return launch_dependent("gemm_pair_kernel", gemm_pair_kernel<BN, STAGES, EPI>, dim3(2 * pairs), dim3(kThreads),
-                          bytes, stream, a, b, o, r, out, M, N, K, ep);
+                          bytes, stream, a, b, o, r, out, M, N, K, ep, a2 ? *a2 : a, b2 ? *b2 : b, o2 ? *o2 : o,
+                          r2 ? *r2 : r, ep2 ? *ep2 : ep);
 }
 
 template <int BN, int STAGES>
@@ -893,6 +919,36 @@ int gemm_run(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cu
   }
 }
 
+// Two independent gated-residual GEMMs with row statistics (E = GATE_RESIDUAL | kStats) of the same shape in one
+// CTA-pair launch: one launch's fixed cost and tail instead of two. Both plans must take the same pair tile width.
+int gemm_run_group(const GemmPlan& p0, uint16_t* out0, const EpiParams& e0, const GemmPlan& p1, uint16_t* out1,
+                   const EpiParams& e1, int M, cudaStream_t stream) {
+  SVX_REQUIRE(M > 0 && M % PM == 0 && M <= p0.M && M <= p1.M,
+              "gemm group: rows must be a multiple of 256 within both plans");
+  SVX_REQUIRE(p0.N == p1.N && p0.K == p1.K && p0.pair_bn && p0.pair_bn == p1.pair_bn,
+              "gemm group: both problems need the same N, K and pair tile width");
+  for (const EpiParams* e : {&e0, &e1})
+    SVX_REQUIRE(e->epilogue == SVX_EPI_GATE_RESIDUAL && e->bias && e->gate && e->residual && e->ln_stats_out &&
+                    !e->ln_stats_in,
+                "gemm group: both problems are gated residuals with row statistics (no LayerNorm fold)");
+  CUtensorMap o0{}, r0{}, o1{}, r1{};
+  int rc = make_box_map(&o0, out0, M, p0.N);
+  if (!rc) rc = make_box_map(&r0, e0.residual, M, p0.N);
+  if (!rc) rc = make_box_map(&o1, out1, M, p1.N);
+  if (!rc) rc = make_box_map(&r1, e1.residual, M, p1.N);
+  if (rc) return rc;
+  constexpr int E = SVX_EPI_GATE_RESIDUAL | kStats | kGroup;
+  switch (p0.pair_bn) {
+    case 256: return launch_pair_tile<256, 4, E>(p0.a, p0.b_half, o0, r0, out0, M, p0.N, p0.K, e0, stream, &p1.a,
+                                                 &p1.b_half, &o1, &r1, &e1);
+    case 192: return launch_pair_tile<192, 5, E>(p0.a, p0.b_half, o0, r0, out0, M, p0.N, p0.K, e0, stream, &p1.a,
+                                                 &p1.b_half, &o1, &r1, &e1);
+    case 128: return launch_pair_tile<128, 5, E>(p0.a, p0.b_half, o0, r0, out0, M, p0.N, p0.K, e0, stream, &p1.a,
+                                                 &p1.b_half, &o1, &r1, &e1);
+    default: return fail(SVX_ERR_INVALID, "gemm group: pair tile width must be 128, 192 or 256");
+  }
+}
+
 int epi_from_args(const svx_epilogue_args* e, EpiParams* ep, int N, int K) {
   SVX_REQUIRE(e && (e->bias || e->ln_stats_in), "gemm: epilogue needs a bias (or the LayerNorm fold's u and v)");
   *ep = EpiParams{};
@@ -949,6 +1005,21 @@ extern "C" int svx_gemm(const uint16_t* A, const uint16_t* W, uint16_t* out, int
   rc = gemm_plan(&plan, A, W, M, N, K, 0);
   if (rc) return rc;
   return gemm_run(plan, M, out, ep, as_stream(stream));
+}
+
+extern "C" int svx_gemm_group(const uint16_t* A0, const uint16_t* W0, uint16_t* out0, const svx_epilogue_args* epi0,
+                              const uint16_t* A1, const uint16_t* W1, uint16_t* out1, const svx_epilogue_args* epi1,
+                              int M, int N, int K, void* stream) {
+  SVX_REQUIRE(A0 && W0 && out0 && A1 && W1 && out1, "svx_gemm_group: null operand");
+  EpiParams e0, e1;
+  int rc = epi_from_args(epi0, &e0, N, K);
+  if (!rc) rc = epi_from_args(epi1, &e1, N, K);
+  if (rc) return rc;
+  GemmPlan p0, p1;
+  rc = gemm_plan(&p0, A0, W0, M, N, K, 0);
+  if (!rc) rc = gemm_plan(&p1, A1, W1, M, N, K, 0);
+  if (rc) return rc;
+  return gemm_run_group(p0, out0, e0, p1, out1, e1, M, as_stream(stream));
 }
 
 extern "C" uint32_t svx_wait_timeouts(void) {

@@ -37,6 +37,8 @@ struct GemmPlan {
 
 int gemm_plan(GemmPlan* plan, const uint16_t* A, const uint16_t* W, int M, int N, int K, int bn);
 int gemm_run(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cudaStream_t stream);
+int gemm_run_group(const GemmPlan& p0, uint16_t* out0, const EpiParams& e0, const GemmPlan& p1, uint16_t* out1,
+                   const EpiParams& e1, int M, cudaStream_t stream);
 // 3-D bf16 tensor map (inner, groups, rows), box (box_inner, 1, box_rows), 128B swizzle (box_inner 64) or 64B swizzle
 // (box_inner 32); elements past `inner` read 0.
 int make_map_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t groups, uint64_t rows,

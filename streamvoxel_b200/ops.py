@@ -218,6 +218,32 @@ def gemm(a, w, bias, epilogue=_lib.EPI_BIAS, out=None, gate=None, residual=None,
     return out
 
 
+def gemm_group(problems):
+    """Two gated-residual GEMMs with row statistics in one launch (`svx_gemm_group`): problems = two dicts with a, w,
+    bias, gate, residual, stats_out (and optional out); out_i = bf16(res_i + bf16(gate_i bf16(a_i w_i^T + bias_i))).
+    Returns the two outputs."""
+    outs, args = [], []
+    for p in problems:
+        m, k = p['a'].shape
+        n = p['w'].shape[0]
+        for t in (p['a'], p['w'], p['bias'], p['gate'], p['residual']):
+            assert t.dtype == torch.bfloat16 and t.is_contiguous()
+        assert p['stats_out'].dtype == torch.float32
+        out = p.get('out')
+        if out is None:
+            out = torch.empty((m, n), device=p['a'].device, dtype=torch.bfloat16)
+        outs.append(out)
+        args.append(_lib.EpilogueArgs(epilogue=_lib.EPI_GATE_RESIDUAL, bias=p['bias'].data_ptr(),
+                                      gate=p['gate'].data_ptr(), residual=p['residual'].data_ptr(),
+                                      ln_stats_out=p['stats_out'].data_ptr(), patch=4))
+    (m, k), n = problems[0]['a'].shape, problems[0]['w'].shape[0]
+    assert problems[1]['a'].shape == (m, k) and problems[1]['w'].shape == (n, k)
+    check(_lib.load().svx_gemm_group(ptr(problems[0]['a']), ptr(problems[0]['w']), ptr(outs[0]), ctypes.byref(args[0]),
+                                     ptr(problems[1]['a']), ptr(problems[1]['w']), ptr(outs[1]), ctypes.byref(args[1]),
+                                     m, n, k, stream_ptr()), 'svx_gemm_group')
+    return outs
+
+
 def attention_plan(lengths, slots, heads, queries, keys, ctas, device=None):
     """Work-unit plan of `svx_attention_plan` for host key lengths (sequence or None) on `ctas` CTAs. Returns the
     int32 plan (on `device`, or a host tensor) and the CTA count the launch must use."""

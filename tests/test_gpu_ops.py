@@ -541,6 +541,29 @@ def test_patch_embed_bit_exact_sequential_sum(ops, shape, tokens):
     torch.testing.assert_close(stats_b.double().cpu(), _chunk_stats(want), atol=1e-5, rtol=1e-5)
 
 
+@pytest.mark.parametrize('m', [256, 2048, 8192])
+def test_gemm_group_equals_two_launches(ops, m):
+    """`svx_gemm_group` (two gated-residual GEMMs with row statistics in one launch, as the engine runs a control
+    layer's cross projection with its backbone block's attention projection) equals the two launches bit for bit,
+    outputs and statistics; a gate of ones gives the plain residual epilogue exactly."""
+    from streamvoxel_b200 import _lib
+    torch.manual_seed(23)
+    d = 768
+    a = [(torch.randn((m, d), device='cuda') * 0.5).bfloat16() for _ in range(2)]
+    w = [(torch.randn((d, d), device='cuda') * 0.03).bfloat16() for _ in range(2)]
+    b = [(torch.randn(d, device='cuda') * 0.1).bfloat16() for _ in range(2)]
+    res = [torch.randn((m, d), device='cuda').bfloat16() for _ in range(2)]
+    gate = (torch.randn(d, device='cuda') * 0.5).bfloat16()
+    ones = torch.ones(d, device='cuda', dtype=torch.bfloat16)
+    stats = [torch.zeros((d // 32, m, 2), device='cuda') for _ in range(4)]
+    want0 = ops.gemm(a[0], w[0], b[0], _lib.EPI_GATE_RESIDUAL, gate=gate, residual=res[0], stats_out=stats[0])
+    want1 = ops.gemm(a[1], w[1], b[1], _lib.EPI_RESIDUAL, residual=res[1], stats_out=stats[1])
+    got0, got1 = ops.gemm_group([dict(a=a[0], w=w[0], bias=b[0], gate=gate, residual=res[0], stats_out=stats[2]),
+                                 dict(a=a[1], w=w[1], bias=b[1], gate=ones, residual=res[1], stats_out=stats[3])])
+    assert torch.equal(got0, want0) and torch.equal(got1, want1)
+    assert torch.equal(stats[2], stats[0]) and torch.equal(stats[3], stats[1])
+
+
 @pytest.mark.parametrize('epilogue', ['bias', 'gelu', 'rope', 'class_major'])
 def test_gemm_layernorm_fold_matches_layernorm_then_linear(ops, epilogue):
     """A residual GEMM writes its output rows' chunk statistics; the next linear takes the raw rows with the LayerNorm
