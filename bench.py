@@ -267,6 +267,7 @@ def time_kernels(cfg, forward, batch, lengths):
     k0, v0 = forward.engine.kv[0]
     stats = forward.engine.stats['b']
     tables = m.rope_sin, m.rope_cos
+    ones = torch.ones(d, device=dev, dtype=torch.bfloat16)
 
     def clock(fn, reps=20):
         """Device time per launch: `reps` launches captured in one CUDA graph and replayed (as the step runs them), so
@@ -318,7 +319,14 @@ def time_kernels(cfg, forward, batch, lengths):
         'gemm_dxd': (lambda: ops.gemm(ws['attn'], bw['attn.proj.weight'], bw['attn.proj.bias'],
                                       _lib.EPI_GATE_RESIDUAL, out=ws['xb'], gate=bw['gate1'], residual=ws['xb'],
                                       stats_out=stats),
-                     2.0 * rows * d * d, 24 + 3 * 12),
+                     2.0 * rows * d * d, 3 * 12),   # control proj, cross query, zero
+        # a control layer's cross projection (gate of ones: the plain residual) with its backbone block's attention
+        # projection in one launch, as the engine runs them
+        'gemm_dxd_group': (lambda: ops.gemm_group([
+            dict(a=ws['ax'], w=cw['proj.weight'], bias=cw['proj.bias'], gate=ones, residual=ws['xc'],
+                 stats_out=forward.engine.stats['c'], out=ws['xc']),
+            dict(a=ws['attn'], w=bw['attn.proj.weight'], bias=bw['attn.proj.bias'], gate=bw['gate1'], residual=ws['xb'],
+                 stats_out=stats, out=ws['xb'])]), 2 * 2.0 * rows * d * d, 12),
         'gemm_head': (lambda: ops.gemm(ws['xb'], m.head_fold[0], m.head_b, _lib.EPI_CLASS_MAJOR, out=forward.logits,
                                        rows_per_slot=cfg.patches, classes=cfg.classes, geometry=cfg.voxel_shape,
                                        ln=(stats, *m.head_fold[1:], 1e-6)),
