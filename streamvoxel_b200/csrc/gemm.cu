@@ -921,18 +921,24 @@ int gemm_run(const GemmPlan& plan, int M, uint16_t* out, const EpiParams& ep, cu
 
 // Two independent gated-residual GEMMs with row statistics (E = GATE_RESIDUAL | kStats) of the same shape in one
 // CTA-pair launch: one launch's fixed cost and tail instead of two. Both plans must take the same pair tile width.
-int gemm_run_group(const GemmPlan& p0, uint16_t* out0, const EpiParams& e0, const GemmPlan& p1, uint16_t* out1,
-                   const EpiParams& e1, int M, cudaStream_t stream) {
-  SVX_REQUIRE(M > 0 && M % PM == 0 && M <= p0.M && M <= p1.M,
-              "gemm group: rows must be a multiple of 256 within both plans");
-  SVX_REQUIRE(p0.N == p1.N && p0.K == p1.K && p0.pair_bn && p0.pair_bn == p1.pair_bn,
-              "gemm group: both problems need the same N, K and pair tile width");
+static int check_group(const EpiParams& e0, const EpiParams& e1, int M) {
+  SVX_REQUIRE(M > 0 && M % PM == 0, "gemm group: rows must be a positive multiple of 256");
   for (const EpiParams* e : {&e0, &e1})
     SVX_REQUIRE(e->epilogue == SVX_EPI_GATE_RESIDUAL && e->bias && e->gate && e->residual && e->ln_stats_out &&
                     !e->ln_stats_in,
                 "gemm group: both problems are gated residuals with row statistics (no LayerNorm fold)");
+  return SVX_OK;
+}
+
+int gemm_run_group(const GemmPlan& p0, uint16_t* out0, const EpiParams& e0, const GemmPlan& p1, uint16_t* out1,
+                   const EpiParams& e1, int M, cudaStream_t stream) {
+  int rc = check_group(e0, e1, M);
+  if (rc) return rc;
+  SVX_REQUIRE(M <= p0.M && M <= p1.M, "gemm group: rows beyond a plan");
+  SVX_REQUIRE(p0.N == p1.N && p0.K == p1.K && p0.pair_bn && p0.pair_bn == p1.pair_bn,
+              "gemm group: both problems need the same N, K and pair tile width");
   CUtensorMap o0{}, r0{}, o1{}, r1{};
-  int rc = make_box_map(&o0, out0, M, p0.N);
+  rc = make_box_map(&o0, out0, M, p0.N);
   if (!rc) rc = make_box_map(&r0, e0.residual, M, p0.N);
   if (!rc) rc = make_box_map(&o1, out1, M, p1.N);
   if (!rc) rc = make_box_map(&r1, e1.residual, M, p1.N);
@@ -1014,6 +1020,7 @@ extern "C" int svx_gemm_group(const uint16_t* A0, const uint16_t* W0, uint16_t* 
   EpiParams e0, e1;
   int rc = epi_from_args(epi0, &e0, N, K);
   if (!rc) rc = epi_from_args(epi1, &e1, N, K);
+  if (!rc) rc = check_group(e0, e1, M);   // before any CUDA call
   if (rc) return rc;
   GemmPlan p0, p1;
   rc = gemm_plan(&p0, A0, W0, M, N, K, 0);

@@ -176,6 +176,13 @@ def fold_layernorm(weight, bias, one_plus_scale=None, shift=None):
     return folded.contiguous(), u.float().contiguous(), v.float().contiguous()
 
 
+def down_conv_weight(weight):
+    """The 4^3 stride-4 Conv3d weight [d_out, d_in, 4, 4, 4] as the [d_out, 64 d_in] bf16 weight of the GEMM that
+    replaces it: an output token's 64 patches are consecutive patchified rows (patch order y, z, x over a 16-wide
+    column, 16 patches per y layer), so A is the [tokens, 64 d_in] view with k = (ky * 16 + kz * 4 + kx) * d_in + c."""
+    return weight.permute(0, 2, 3, 4, 1).reshape(weight.shape[0], -1).to(torch.bfloat16).contiguous()
+
+
 class PreparedModel:
     """Device-resident bf16 weights and precomputed constants of one model (one per GPU)."""
 
@@ -228,8 +235,7 @@ class PreparedModel:
             # embeddings summed in fp32 (added before context_norm)
             self.l2_norm_w = sd['l2_norm.weight'].contiguous()
             self.l2_norm_b = sd['l2_norm.bias'].contiguous()
-            self.l2_down_w = sd['l2_down.weight'].permute(0, 2, 3, 4, 1).reshape(cfg.d, -1).to(torch.bfloat16)
-            self.l2_down_w = self.l2_down_w.contiguous()
+            self.l2_down_w = down_conv_weight(sd['l2_down.weight'])
             self.l2_down_b = sd['l2_down.bias'].to(torch.bfloat16)
             self.level_embed = [(sd['type_embed.weight'][i] + sd['size_embed.weight'][i]).contiguous() for i in (0, 1)]
             self.zero_bias = torch.zeros(cfg.d, device=dev, dtype=torch.bfloat16)

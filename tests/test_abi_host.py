@@ -186,6 +186,34 @@ def test_layernorm_fold_algebra_matches_layernorm_then_linear():
     assert torch.equal(wf0, w) and torch.equal(v0, b.float())
 
 
+def test_down_conv_as_gemm_layout():
+    """The L2 down-conv of the condition encoder (`streaming_controlnet.py:148`, Conv3d 4^3 stride 4 over the
+    patchified column) equals the GEMM the encoder runs: the [n H/16, 64 d] view of the patchified rows times
+    `down_conv_weight` (float64, CPU)."""
+    from streamvoxel_b200.model import down_conv_weight
+    g = torch.Generator().manual_seed(5)
+    n, h, d = 3, 8, 16                                   # columns, patch layers (y), channels; 4 x 4 patches per layer
+    x = torch.randn((n * h * 16, d), generator=g, dtype=torch.float64)   # rows in patch order (y, z, x)
+    w = (torch.randn((d, d, 4, 4, 4), generator=g) * 0.1).to(torch.bfloat16).double()
+    grid = x.reshape(n, h, 4, 4, d).permute(0, 4, 1, 2, 3)
+    want = torch.nn.functional.conv3d(grid, w, None, stride=4).flatten(2).transpose(1, 2).reshape(-1, d)
+    got = x.view(n * h // 4, 64 * d) @ down_conv_weight(w).double().t()
+    torch.testing.assert_close(got, want, atol=1e-12, rtol=1e-12)
+
+
+def test_grouped_gemm_validates_before_any_launch(lib):
+    """`svx_gemm_group` takes two gated residuals with row statistics and 256-row multiples, checked on the host
+    before any CUDA call."""
+    from streamvoxel_b200 import _lib
+    fake = 1 << 20   # never dereferenced: the checks fail first
+    good = _lib.EpilogueArgs(epilogue=_lib.EPI_GATE_RESIDUAL, bias=fake, gate=fake, residual=fake, ln_stats_out=fake)
+    plain = _lib.EpilogueArgs(epilogue=_lib.EPI_RESIDUAL, bias=fake, residual=fake, ln_stats_out=fake)
+    p = ctypes.c_void_p(fake)
+    for a, b, m in ((good, plain, 256), (good, good, 384)):
+        status = lib.svx_gemm_group(p, p, p, ctypes.byref(a), p, p, p, ctypes.byref(b), m, 768, 768, None)
+        assert status == _lib.SVX_ERR_INVALID and b'gemm group' in lib.svx_last_error()
+
+
 def test_row_statistics_merge_restated():
     """The kernels' chunk statistics and their merge, restated in numpy: per 32-column chunk (mean, M2); the row's mean
     and variance from shifted sums about the first chunk's mean (`row_norm` in gemm.cu) equal the two-pass values,
