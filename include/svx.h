@@ -133,8 +133,10 @@ SVX_API int svx_eval_select(const float* scores, const float* draw, const int16_
 /* Categorical draw + token commit for the chosen voxels (`streamvoxel/stream/fast_ops.py:549-551`,
  * `streamvoxel/stream/slot.py:149-151`): p = softmax over classes in fp32, value = argmax(p / q).
  * noise != NULL (parity mode): q = noise[slot][i][classes] fp32, the exponential draws torch.multinomial takes from
- * the slot generator; the softmax reproduces torch's CUDA row softmax reduction order. noise == NULL (native mode):
- * q = -log(u) with u from Philox4x32-10 keyed by (params.seed, params.step, voxel, class).
+ * the slot generator; the softmax reproduces torch's CUDA row softmax reduction order. noise == NULL (native mode,
+ * the Gumbel-max form of the same draw): value = argmax x - log(-log u), u = (2 (w >> 9) + 1) 2^-24 from
+ * Philox4x32-10 keyed by (params.seed, params.step, voxel, class), both logarithms an atanh series evaluated in
+ * single-rounded fp32 operations, so a host restatement reproduces every value bit for bit.
  * Writes tokens[index] = value, values_out [slots][index_capacity] int16. */
 SVX_API int svx_ease_sample(const void* logits, int dtype, int slots, int classes, int voxels,
                             int64_t logit_slot_stride, const int32_t* index, const svx_step_params* params,

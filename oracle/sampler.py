@@ -227,7 +227,7 @@ def native_uniforms(seed, step, voxels, classes):
     """Uniforms in (0,1) of the native draw for `voxels` (flat YZX indexes) x `classes`, float32 [n, classes].
 
     Counter (class // 4, voxel, step, NATIVE_STREAM), key (seed low, seed high); output word class % 4;
-    u = ((word >> 8) + 0.5) * 2^-24, exactly representable in fp32."""
+    u = (2 (word >> 9) + 1) * 2^-24: odd multiples of 2^-24, exactly representable in fp32, never 0 or 1."""
     voxels = np.asarray(voxels, np.int64)
     groups = (classes + 3) // 4
     g = np.arange(groups, dtype=np.uint32)[None, :]
@@ -238,18 +238,46 @@ def native_uniforms(seed, step, voxels, classes):
                           np.full((len(voxels), groups), NATIVE_STREAM, np.uint32),
                           np.uint32(seed & 0xFFFFFFFF), np.uint32(seed >> 32))
     stacked = np.stack(words, -1).reshape(len(voxels), groups * 4)[:, :classes]
-    return (((stacked >> np.uint32(8)).astype(np.float32) + np.float32(0.5)) * np.float32(2.0 ** -24)).astype(np.float32)
+    odd = ((stacked >> np.uint32(9)) << np.uint32(1)) | np.uint32(1)
+    return (odd.astype(np.float32) * np.float32(2.0 ** -24)).astype(np.float32)
+
+
+# 1/11, 1/9, 1/7, 1/5, 1/3 and ln 2 rounded to the nearest fp32 value (the kernel writes the same hexadecimal literals)
+_SERIES = [np.float32(float.fromhex(h)) for h in ('0x1.745d18p-4', '0x1.c71c72p-4', '0x1.24924ap-3', '0x1.99999ap-3',
+                                                  '0x1.555556p-2')]
+_LN2 = np.float32(float.fromhex('0x1.62e430p-1'))
+
+
+def series_log(a):
+    """Natural log of positive normal fp32 values by the atanh series, with exactly the fp32 operations of the native
+    draw kernel's `series_log`: a = m 2^e with m in [sqrt(1/2), sqrt(2)), s = (m - 1) / (m + 1), z = s^2,
+    log a = e ln 2 + 2 s (1 + z (1/3 + z (1/5 + z (1/7 + z (1/9 + z/11))))), each operation rounded once to fp32."""
+    a = np.asarray(a, np.float32)
+    bits = a.view(np.int32)
+    e = (bits >> 23) - 127
+    mbits = (bits & 0x007FFFFF) | 0x3F800000
+    high = mbits > 0x3FB504F3
+    mbits = np.where(high, mbits - 0x00800000, mbits).astype(np.int32)
+    e = np.where(high, e + 1, e)
+    m = mbits.view(np.float32)
+    one = np.float32(1)
+    s = (m - one) / (m + one)
+    z = s * s
+    t = _SERIES[0]
+    for c in _SERIES[1:]:
+        t = c + z * t
+    t = one + z * t
+    return (e.astype(np.float32) * _LN2 + (np.float32(2) * s) * t).astype(np.float32)
 
 
 def native_sample(logits_cn, voxels, seed, step):
-    """Native (graph-capturable) draw: argmax_v exp(x_v - max) / E_v with E_v = -log(u_v), u from Philox.
-
-    Distributed as `multinomial(softmax(x), 1)` (exponential race); logits_cn is [C, n] fp32 for the voxels."""
+    """Native (graph-capturable) draw, Gumbel-max: argmax_v x_v - log(-log u_v) with `series_log` for both logs and
+    one fp32 subtraction, ties to the lower class; distributed as `multinomial(softmax(x), 1)`. Bit-exact with the
+    kernel given the same fp32 logits. logits_cn is [C, n] for the voxels."""
     x = np.asarray(logits_cn, np.float32).T
-    e = np.exp(x - x.max(1, keepdims=True))
     u = native_uniforms(seed, step, voxels, x.shape[1])
-    race = -np.log(u)
-    return (e / race).argmax(1).astype(np.int64)
+    key = (x - series_log(-series_log(u))).astype(np.float32)
+    return key.argmax(1).astype(np.int64)
 
 
 # ------------------------------------------------------------------------------------------------ the slot

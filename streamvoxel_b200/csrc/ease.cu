@@ -770,8 +770,37 @@ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32
 
 constexpr uint32_t kNativeStream = 0x53564F58u;
 
-// Native draw: argmax_v e^(x_v - max) / E_v, E_v = -log(u_v), u from Philox keyed by (seed, step, voxel, class).
-// Lane L owns class groups g = L, L+32, ... of 4 consecutive classes, so each Philox call feeds 4 classes.
+// Natural logarithm of a positive normal fp32 value from the atanh series: a = m 2^e with m in [sqrt(1/2), sqrt(2)),
+// log a = e ln 2 + 2 atanh(s), s = (m - 1) / (m + 1), atanh(s) = s (1 + z/3 + z^2/5 + ... + z^5/11), z = s^2
+// (|s| <= 0.1716, so the first omitted term is below 1e-10 relative). Every step is one IEEE round-to-nearest fp32
+// operation (the __f*_rn intrinsics are never contracted into FMAs), so a host restatement that performs the same
+// operations in the same order returns the same bits; that makes the native draw reproducible off the device.
+__device__ __forceinline__ float series_log(float a) {
+  int bits = __float_as_int(a);
+  int e = (bits >> 23) - 127;
+  int mbits = (bits & 0x007FFFFF) | 0x3F800000;
+  if (mbits > 0x3FB504F3) {  // m > sqrt(2): halve m
+    mbits -= 0x00800000;
+    e += 1;
+  }
+  const float m = __int_as_float(mbits);
+  const float s = __fdiv_rn(__fsub_rn(m, 1.f), __fadd_rn(m, 1.f));
+  const float z = __fmul_rn(s, s);
+  // 1/11, 1/9, 1/7, 1/5, 1/3 and ln 2, each the nearest fp32 value, written out in hexadecimal
+  float t = 0x1.745d18p-4f;
+  t = __fadd_rn(0x1.c71c72p-4f, __fmul_rn(z, t));
+  t = __fadd_rn(0x1.24924ap-3f, __fmul_rn(z, t));
+  t = __fadd_rn(0x1.99999ap-3f, __fmul_rn(z, t));
+  t = __fadd_rn(0x1.555556p-2f, __fmul_rn(z, t));
+  t = __fadd_rn(1.f, __fmul_rn(z, t));
+  return __fadd_rn(__fmul_rn((float)e, 0x1.62e430p-1f), __fmul_rn(__fmul_rn(2.f, s), t));
+}
+
+// Native draw (Gumbel-max): argmax_v x_v - log E_v with E_v = -log u_v, which is distributed as
+// multinomial(softmax(x), 1). u_v = (2 (w >> 9) + 1) 2^-24 (odd multiples of 2^-24, exactly representable, never 0
+// or 1) from Philox keyed by (seed, step, voxel, class); the logs are `series_log`, the subtraction one fp32 op, ties
+// go to the lower class. Lane L owns class groups g = L, L+32, ... of 4 consecutive classes, so each Philox call
+// feeds 4 classes.
 template <typename T>
 __global__ void ease_sample_native_kernel(const T* __restrict__ logits, int classes, int voxels, int64_t slot_stride,
                                           const int32_t* __restrict__ index, const svx_step_params* __restrict__ params,
@@ -787,13 +816,9 @@ __global__ void ease_sample_native_kernel(const T* __restrict__ logits, int clas
   if (n < 0) return;
   const T* col = logits + slot * slot_stride + n;
   const int groups = (classes + 3) >> 2;
-  float m = -INFINITY;
-  for (int c = lane; c < classes; c += 32) m = fmaxf(m, load_as_f32(col + (int64_t)c * voxels));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   float best = -INFINITY;
   int arg = 0x7fffffff;
-  bool nan = isnan(m);
+  bool nan = false;
   for (int g = lane; g < groups; g += 32) {
     uint32_t w[4] = {(uint32_t)g, (uint32_t)n, (uint32_t)p.step, kNativeStream};
     philox4x32_10(w, (uint32_t)p.seed, (uint32_t)(p.seed >> 32));
@@ -801,10 +826,10 @@ __global__ void ease_sample_native_kernel(const T* __restrict__ logits, int clas
     for (int j = 0; j < 4; ++j) {
       int c = g * 4 + j;
       if (c >= classes) break;
-      float u = ((float)(w[j] >> 8) + 0.5f) * 5.9604644775390625e-08f;  // 2^-24
-      float race = -logf(u);
-      float e = expf(load_as_f32(col + (int64_t)c * voxels) - m);
-      argmax_merge(best, arg, e / race, c);
+      const float u = (float)(((w[j] >> 9) << 1) | 1u) * 5.9604644775390625e-08f;  // 2^-24
+      const float x = load_as_f32(col + (int64_t)c * voxels);
+      nan |= isnan(x);
+      argmax_merge(best, arg, __fsub_rn(x, series_log(-series_log(u))), c);
     }
   }
 #pragma unroll
@@ -813,6 +838,7 @@ __global__ void ease_sample_native_kernel(const T* __restrict__ logits, int clas
     int a = __shfl_xor_sync(0xffffffffu, arg, o);
     argmax_merge(best, arg, b, a);
   }
+  nan = __any_sync(0xffffffffu, nan);
   if (lane == 0) {
     tokens[(int64_t)slot * voxels + n] = (int16_t)arg;
     values_out[(int64_t)slot * index_capacity + i] = (int16_t)arg;

@@ -147,19 +147,22 @@ def test_parity_sampling_equals_torch_multinomial(ops, classes):
     assert torch.equal(tokens[0, idx.long()].long(), want)
 
 
-def test_native_sampling_matches_oracle_rule(ops):
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_native_sampling_equals_oracle_bit_for_bit(ops, dtype):
+    """The native Gumbel-max draw (Philox + the atanh-series logs in single-rounded fp32) equals the oracle's
+    restatement for every chosen voxel, at full size (2048 of 65536 voxels, V = 256) and with V = 6."""
     torch.manual_seed(1)
-    classes, voxels, k = 256, 65536, 2048
-    logits = (torch.randn((1, classes, voxels), device='cuda') * 2).to(torch.bfloat16).contiguous()
-    idx = torch.sort(torch.randperm(voxels, device='cuda')[:k]).values.int()
-    tokens = torch.full((1, voxels), classes, dtype=torch.int16, device='cuda')
-    seed, step = 0x1234567890ABCDEF, 7
-    params = ops.step_params([(k, step, 0, 0.0, seed)], 'cuda')
-    values = ops.ease_sample(logits, idx[None].contiguous(), params, tokens)[0].cpu().numpy()
-    cols = logits[0].float().cpu().numpy()[:, idx.cpu().numpy()]
-    want = osm.native_sample(cols, idx.cpu().numpy(), seed, step)
-    agree = float((values == want).mean())
-    assert agree >= 0.999, agree
+    for classes, voxels, k in ((256, 65536, 2048), (6, 1024, 300)):
+        logits = (torch.randn((1, classes, voxels), device='cuda') * 2).to(dtype).contiguous()
+        idx = torch.sort(torch.randperm(voxels, device='cuda')[:k]).values.int()
+        tokens = torch.full((1, voxels), classes, dtype=torch.int16, device='cuda')
+        seed, step = 0x1234567890ABCDEF, 7
+        params = ops.step_params([(k, step, 0, 0.0, seed)], 'cuda')
+        values = ops.ease_sample(logits, idx[None].contiguous(), params, tokens)[0].cpu().numpy()
+        cols = logits[0].float().cpu().numpy()[:, idx.cpu().numpy()]
+        want = osm.native_sample(cols, idx.cpu().numpy(), seed, step)
+        assert np.array_equal(values, want), float((values == want).mean())
+        assert np.array_equal(tokens[0, idx.long()].cpu().numpy(), want)
 
 
 # ---------------------------------------------------------------------------------------------- forward ops

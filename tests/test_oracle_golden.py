@@ -172,3 +172,24 @@ def test_eval_decoders_match_reference_given_its_draws():
         keys = [str(k) for k in g[f'e{i}_event_keys']]
         got = np.asarray([[float(ev.get(k, np.nan)) for k in keys] for ev in events])
         np.testing.assert_array_equal(got, g[f'e{i}_events'])
+
+
+def test_series_log_and_native_draw():
+    """The native draw's logarithm (atanh series in single-rounded fp32) is within 4e-7 relative of log over the range
+    the draw uses, and the Gumbel-max draw is distributed as softmax(x): 400,000 draws of one 8-class row land within
+    five standard errors of p in every class."""
+    rng = np.random.default_rng(0)
+    a = rng.uniform(2.0 ** -25, 17.0, 200_000).astype(np.float32)
+    a = np.concatenate([a, np.float32(1) - np.arange(1, 64, dtype=np.float32) * np.float32(2.0 ** -24)])
+    got = osm.series_log(a).astype(np.float64)
+    want = np.log(a.astype(np.float64))
+    assert np.all(np.abs(got - want) <= 4e-7 * np.maximum(np.abs(want), 2.0 ** -24))
+    u = osm.native_uniforms(3, 1, np.arange(4096), 256)
+    assert u.min() > 0 and u.max() < 1 and np.all(np.mod(u * 2 ** 24, 2) == 1)
+    x = rng.normal(0, 1, (8, 1)).astype(np.float32)
+    n = 400_000
+    values = osm.native_sample(np.repeat(x, n, 1), np.arange(n), 9, 1)
+    p = np.exp(x[:, 0] - x.max())
+    p /= p.sum()
+    freq = np.bincount(values, minlength=8) / n
+    assert np.all(np.abs(freq - p) <= 5 * np.sqrt(p * (1 - p) / n))
