@@ -323,10 +323,11 @@ class Slot:
         committed = sum(self.quotas[:self.solid_calls]) if self.quotas else 0
         return actual_time((self.total - committed) / self.total)
 
-    def mark(self, logits):
-        """Marking forward, `slot.py:124-136`."""
+    def mark(self, logits, air=None):
+        """Marking forward, `slot.py:124-136`; `air` overrides the air probability (a test feed of the reference's
+        `softmax(0)[air].sum(0)` computed elsewhere)."""
         self.nfe += 1
-        air = air_probability(logits, self.air_ids)
+        air = air_probability(logits, self.air_ids) if air is None else np.asarray(air, np.float32)
         ones = np.ones(self.shape, bool)
         self.last = low_entropy_last_update(self.last, ones, air, ~ones, self.last_eps, False, True)
         self.last_count = int(self.last.sum())
@@ -347,12 +348,16 @@ class Slot:
             raise AssertionError('low-entropy-last solid step did not meet its quota')
         return chosen
 
-    def consume(self, logits, tokens, noise=None, native=False, scores=None):
-        """One forward (`slot.py:117-164`); `tokens` [Y,Z,X] is updated in place. Returns (record|None, commit|None)."""
+    def consume(self, logits, tokens, noise=None, native=False, scores=None, air=None, draw=None):
+        """One forward (`slot.py:117-164`); `tokens` [Y,Z,X] is updated in place. Returns (record|None, commit|None).
+
+        Test feeds: `scores` (the entropy), `air` (the marking probability), and `draw(positions) -> values`, which
+        replaces the categorical draw (for instance the reference's own `torch.multinomial` call on the device that
+        holds the logits and the slot generator); `logits` may then be None for solid steps."""
         if self.phase == 'idle':
             return None, None
         if self.phase == 'marking':
-            self.mark(logits)
+            self.mark(logits, air)
             if not self.quotas:
                 return self._finish(tokens), None
             return None, None
@@ -360,10 +365,13 @@ class Slot:
             return self._finish(tokens), None
         chosen = self.select(logits, tokens, scores)
         positions = np.flatnonzero(chosen)
-        columns = np.asarray(logits, np.float32).reshape(self.classes, -1)[:, positions]
-        if native:
+        if draw is not None:
+            values = np.asarray(draw(positions), np.int64)
+        elif native:
+            columns = np.asarray(logits, np.float32).reshape(self.classes, -1)[:, positions]
             values = native_sample(columns, positions, self.seed, self.nfe + 1)
         else:
+            columns = np.asarray(logits, np.float32).reshape(self.classes, -1)[:, positions]
             q = noise(len(positions), self.classes)
             values = categorical_from_noise(softmax0(columns).T, q)
         tokens.reshape(-1)[positions] = values

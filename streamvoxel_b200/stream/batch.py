@@ -6,6 +6,15 @@ Per-window work stays outside the graph, as in the reference: the block order (`
 window seed + 9173, `streamvoxel/stream/slot.py:97-99`), the marking forward's last mask and its count (one host read,
 `slot.py:130`) and the quartercos quota list. Slots that are marking, finished or idle take k = 0 in the step graph.
 
+Two draws (`sampling`):
+* 'native' -- the Gumbel-max draw on counter-based Philox keyed by (slot seed, step, voxel, class): nothing outside
+  the graph, reproducible bit for bit by a host restatement;
+* 'parity' -- the reference's draw: each solid step's exponential noise is drawn from the slot's own torch generator
+  (seeded with the window seed, the call `torch.multinomial(p, 1, generator)` makes, `streamvoxel/stream/slot.py:150`)
+  into a static device buffer before the graph replays, and the graph's draw takes argmax(softmax(x) / q) with torch's
+  row-softmax order, so every commit equals the reference slot's given the same logits. The noise fill is a device
+  kernel per solid slot, enqueued before the replay; the host does not wait for it.
+
 Two drivers:
 * `step()` -- one forward for every armed slot with the host bookkeeping of `consume_batch`: per-step scalars copied
   H2D from pinned memory, commits copied D2H and returned (the worker-facing path, one host wait per forward);
@@ -18,17 +27,21 @@ import numpy as np
 import torch
 
 from streamvoxel_b200 import ops
-from streamvoxel_b200.sampling import low_entropy_last_quotas
+from streamvoxel_b200.sampling import counts, low_entropy_last_quotas
 
 EASE_LAUNCHES = 5   # scores, quota, block select, fix-up/compaction, sample
 
 
 class SlotBatch:
-    def __init__(self, forward, *, air_ids=(0,), air_token=0, last_eps=1e-4, block_size=4, sampling='native'):
-        if sampling != 'native':
-            raise ValueError('the whole-step graph draws with the native counter-based sampler')
+    def __init__(self, forward, *, air_ids=(0,), air_token=0, last_eps=1e-4, block_size=4, sampling='native',
+                 min_cap=32):
+        """`min_cap`: the smallest window cap `arm` accepts in parity mode; it sizes the static noise buffer (the
+        largest quota of a cap-step quartercos schedule, times the classes, per slot)."""
+        if sampling not in ('native', 'parity'):
+            raise ValueError('sampling must be native or parity')
         if block_size != 4:
             raise ValueError('the selection kernel implements 4^3 blocks')
+        self.sampling = sampling
         self.forward = forward
         self.device = forward.device
         self.slots = forward.batch
@@ -54,6 +67,12 @@ class SlotBatch:
         self.host_values = torch.zeros((b, self.total), dtype=torch.int16, pin_memory=True)
         self.host_small = torch.zeros(2 * b, dtype=torch.int32, pin_memory=True)
         self.state = [dict(phase='idle') for _ in range(b)]
+        self.noise = None
+        self.generators = [None] * b
+        if sampling == 'parity':
+            self.min_cap = int(min_cap)
+            self.noise_capacity = max(counts(self.total, self.min_cap, 'quartercos'))
+            self.noise = torch.ones((b, self.noise_capacity, self.classes), dtype=torch.float32, device=dev)
         self.graph = None
         self._capture()
 
@@ -64,7 +83,8 @@ class SlotBatch:
         ops.ease_select(self.scores, self.forward.tokens, self.last, self.pos, self.params, self.classes, self.total,
                         chosen=self.chosen, index=self.index, count=self.count, status=self.status,
                         workspace=self.workspace)
-        ops.ease_sample(logits, self.index, self.params, self.forward.tokens, values=self.values, status=self.status)
+        ops.ease_sample(logits, self.index, self.params, self.forward.tokens, noise=self.noise, values=self.values,
+                        status=self.status)
 
     def _device_step(self):
         self.forward._call(self.slots)
@@ -90,16 +110,24 @@ class SlotBatch:
         return self.forward.engine.launches(self.slots) + EASE_LAUNCHES
 
     # -- windows
-    def arm(self, slot, seed, cap, item=None, target=()):
-        """Start a window in `slot` (`LowEntropyLastSlot.arm`, `slot.py:86-103`); `item` loads its conditions."""
+    def arm(self, slot, seed, cap, item=None, target=(), *, order=None):
+        """Start a window in `slot` (`LowEntropyLastSlot.arm`, `slot.py:86-103`); `item` loads its conditions.
+        `order` replaces the block permutation drawn from Generator(seed + 9173)."""
+        if self.sampling == 'parity' and int(cap) < self.min_cap:
+            raise ValueError(f'cap {cap} is below min_cap {self.min_cap}, which sized the parity noise buffer')
         if item is not None:
             self.forward.load_slot(slot, item)
             self.forward.wait_loads()
         else:
             self.forward.tokens[slot].fill_(self.classes)
-        g = torch.Generator(device=self.device).manual_seed(int(seed) + 9173)
-        order = torch.randperm(self.blocks, device=self.device, generator=g)
+        if order is None:
+            g = torch.Generator(device=self.device).manual_seed(int(seed) + 9173)
+            order = torch.randperm(self.blocks, device=self.device, generator=g)
+        else:
+            order = torch.as_tensor(order, dtype=torch.long, device=self.device)
         self.pos[slot, order] = torch.arange(self.blocks, device=self.device, dtype=torch.int32)
+        if self.sampling == 'parity':
+            self.generators[slot] = torch.Generator(device=self.device).manual_seed(int(seed))
         self.last[slot].zero_()
         self.state[slot] = dict(phase='marking', seed=int(seed), cap=int(cap), target=tuple(target), nfe=0,
                                 solid_calls=0, quotas=None, last_count=0)
@@ -159,6 +187,18 @@ class SlotBatch:
         return dict(target=st['target'], seed=st['seed'], cap=st['cap'], nfe=st['nfe'], actual=st['solid_calls'],
                     last_count=st['last_count'], last_frac=st['last_count'] / self.total)
 
+    def _draw_noise(self, rows):
+        """Parity mode: each solid slot's exponential draws for this step, from its generator, into the static
+        buffer (the same generator call and shape as `torch.multinomial(p[k, C], 1, generator)`)."""
+        if self.sampling != 'parity':
+            return
+        for i, row in enumerate(rows):
+            k = row[0]
+            if k > self.noise_capacity:
+                raise ValueError(f'quota {k} exceeds the parity noise capacity {self.noise_capacity}')
+            if k:
+                self.noise[i, :k].exponential_(generator=self.generators[i])
+
     def step(self):
         """One forward for every armed slot with its EASE step; returns {slot: (record|None, commit|None)}."""
         marking = [i for i, st in enumerate(self.state) if st['phase'] == 'marking']
@@ -167,6 +207,7 @@ class SlotBatch:
         self.params_host.copy_(self._pack(rows))
         self.params.copy_(self.params_host, non_blocking=True)
         self.status.zero_()
+        self._draw_noise(rows)
         self.graph.replay()
         self._mark(marking)
         kmax = max([r[0] for r in rows] + [0])
@@ -210,9 +251,11 @@ class SlotBatch:
             counts = self.last_count.tolist()
             self._after_mark(range(self.slots), counts)
             steps = max(len(st['quotas']) for st in self.state)
-            staged = []
+            staged, row_list = [], []
             for s in range(steps):
-                staged.append(self._pack(self._rows()))
+                rows = self._rows()
+                staged.append(self._pack(rows))
+                row_list.append(rows)
                 for st in self.state:
                     if st['solid_calls'] < len(st['quotas']):
                         st['solid_calls'] += 1
@@ -220,6 +263,7 @@ class SlotBatch:
             table = torch.stack(staged).to(dev, non_blocking=False)
             for s in range(steps):
                 self.params.copy_(table[s])
+                self._draw_noise(row_list[s])
                 self.graph.replay()
             for i in range(self.slots):
                 self._finish(i)

@@ -7,7 +7,8 @@
 * `FastLowEntropyLastSlot` (`fast_ops.py:481-581`): the reference slot whose marking, selection, draw and commit run
   in libsvx. `sampling='parity'` takes the categorical draw's exponential noise from the slot's torch generator (the
   same call `torch.multinomial` makes), so commits equal the reference's given the same logits; `sampling='native'`
-  draws with counter-based Philox on the device (no generator, fully graph-capturable).
+  draws with counter-based Philox on the device (Gumbel-max, no generator, fully graph-capturable, reproduced bit for
+  bit by the host restatement in the oracle).
 * `SelectGraphs` (`fast_ops.py:584-623`) and `consume_batch` (`fast_ops.py:626-642`): per-(bucket, slot) captured
   selection and one host wait per forward.
 """
@@ -212,16 +213,23 @@ class LowEntropyLastSlot:
     def idle(self):
         return self.phase == 'idle'
 
-    def arm(self, seed, cap, target):
-        """`slot.py:86-103`: block order from Generator(seed + 9173), sample generator on seed."""
+    def arm(self, seed, cap, target, *, order=None):
+        """`slot.py:86-103`: block order from Generator(seed + 9173), sample generator on seed. `order` replaces the
+        block permutation (for a caller that replays a window whose order another device drew: `torch.randperm`
+        gives different permutations on the CPU and on CUDA for the same seed)."""
         self.phase = 'marking'
         self.seed, self.cap, self.target = int(seed), int(cap), tuple(target)
         self.nfe = self.actual = self.solid_calls = 0
         self.quotas = None
         self.last_count = 0
         blocks = self.total // self.block_size ** 3
-        order_rng = torch.Generator(device=self.device).manual_seed(self.seed + 9173)
-        self.order = torch.randperm(blocks, device=self.device, generator=order_rng)
+        if order is None:
+            order_rng = torch.Generator(device=self.device).manual_seed(self.seed + 9173)
+            self.order = torch.randperm(blocks, device=self.device, generator=order_rng)
+        else:
+            self.order = torch.as_tensor(order, dtype=torch.long, device=self.device)
+            if sorted(self.order.tolist()) != list(range(blocks)):
+                raise ValueError(f'order must be a permutation of the {blocks} blocks')
         self.generator = torch.Generator(device=self.device).manual_seed(self.seed)
         self.step_map = torch.zeros(self.shape, dtype=torch.int16)
         self.values = torch.full(self.shape, -1, dtype=torch.int16)
@@ -245,6 +253,9 @@ class FastLowEntropyLastSlot(LowEntropyLastSlot):
 
     def __init__(self, *args, entropy='torch', sampling='parity', **kwargs):
         super().__init__(*args, **kwargs)
+        # Parity mode: a callable (k, classes) -> fp32 device tensor [k, classes] that replaces the exponential draws
+        # from the slot generator (a replay of draws recorded elsewhere); None draws them from the generator.
+        self.noise_source = None
         if entropy not in ('torch', 'triton'):
             raise ValueError('entropy must be torch or triton')
         if sampling not in ('parity', 'native'):
@@ -269,10 +280,15 @@ class FastLowEntropyLastSlot(LowEntropyLastSlot):
         self.workspace = ops.select_workspace(1, self.total, dev)
         self._host = torch.empty(2 * self.total + 1, dtype=torch.int32, pin_memory=True)
 
-    def arm(self, seed, cap, target):
-        super().arm(seed, cap, target)
+    def arm(self, seed, cap, target, *, order=None):
+        super().arm(seed, cap, target, order=order)
         self.last_static.zero_()
         self.pos[0, self.order] = torch.arange(len(self.order), device=self.device, dtype=torch.int32)
+
+    @property
+    def last(self):
+        """The deferred-voxel mask [Y, Z, X] bool on the device (the reference slot's `last`)."""
+        return self.last_static[0].bool()
 
     def stageable(self):
         return self.phase == 'solid' and self.quotas is not None and self.solid_calls < len(self.quotas)
@@ -315,7 +331,10 @@ class FastLowEntropyLastSlot(LowEntropyLastSlot):
         else:
             graph.replay()
         noise = None
-        if self.sampling == 'parity':
+        if self.sampling == 'parity' and self.noise_source is not None:
+            noise = torch.as_tensor(self.noise_source(k, self.classes), dtype=torch.float32,
+                                    device=self.device).reshape(1, k, self.classes).contiguous()
+        elif self.sampling == 'parity':
             # The exponential draws torch.multinomial(probabilities, 1, generator) makes (`slot.py:150`).
             noise = torch.empty((1, k, self.classes), device=self.device).exponential_(generator=self.generator)
         ops.ease_sample(logits[None], self.index, self.params, tokens[None], noise=noise, values=self.values_dev,
@@ -387,19 +406,21 @@ class SelectGraphs:
         current = torch.cuda.current_stream(device)
         warm = torch.cuda.Stream(device=device)
         warm.wait_stream(current)
-        with torch.cuda.stream(warm):
+        with torch.cuda.stream(warm), torch.inference_mode():
             for size, out in engine.outputs.items():
                 for i in range(size):
                     slots[i].select(out[i], engine.tokens[i])
         current.wait_stream(warm)
         torch.cuda.synchronize(device)
         stream = torch.cuda.Stream(device=device)
-        for size, out in sorted(engine.outputs.items()):
-            for i in range(size):
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph, stream=stream, capture_error_mode='thread_local'):
-                    slots[i].select(out[i], engine.tokens[i])
-                self.graphs[size, i] = graph
+        pool = torch.cuda.graph_pool_handle()   # one memory pool for every (bucket, slot) capture
+        with torch.inference_mode():
+            for size, out in sorted(engine.outputs.items()):
+                for i in range(size):
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, pool=pool, stream=stream, capture_error_mode='thread_local'):
+                        slots[i].select(out[i], engine.tokens[i])
+                    self.graphs[size, i] = graph
         for slot in slots:
             slot.chosen.zero_()
             slot.status.zero_()

@@ -26,6 +26,59 @@ def test_decode_low_entropy_last_completes_and_is_deterministic():
     assert np.array_equal(tokens, again['compact']) and np.array_equal(steps, again['commit_step'])
 
 
+def test_decode_low_entropy_last_equals_reference_slot():
+    """Config-1 parity: `decode_low_entropy_last` (`streamvoxel/eval/samplers.py:118-134`) on the small time-free model
+    equals the reference slot driven over the same forwards (each step's logits from our engine, the block order and
+    the multinomial draws from CUDA generators on the same seeds, the selection given the kernel's scores): tokens,
+    commit steps, nfe and last_count."""
+    from reference_slot import ReferenceSlot
+    from streamvoxel_b200 import model as sm, ops
+    from streamvoxel_b200.decode import UnconditionalForward, decode_low_entropy_last
+    cfg = sm.small_test_config(layer_indices=())
+    forward = UnconditionalForward(cfg, sm.synthetic_state_dict(cfg, seed=4, std=0.05))
+    shape, classes, seed = cfg.voxel_shape, cfg.classes, 21
+    spec = dict(air_ids=(0,), air_token=0, last_eps=1e-4, block_size=4, steps=12)
+    recorded = []
+
+    def recording(tokens, t):
+        out = forward(tokens, t)
+        recorded.append(out[0].clone())
+        return out
+
+    result, info = decode_low_entropy_last(recording, spec, seed, 'cuda', shape, classes)
+    blocks = int(np.prod(shape)) // 64
+    order = torch.randperm(blocks, device='cuda', generator=torch.Generator(device='cuda').manual_seed(seed + 9173))
+    ref = ReferenceSlot(shape, classes, last_eps=spec['last_eps'])
+    ref.arm(seed, spec['steps'], (), order.cpu().numpy())
+    tokens = np.full(shape, classes, np.int64)
+    record = None
+    for logits in recorded:
+        assert record is None
+        scores = ops.ease_scores(logits[None].contiguous())[0].cpu().numpy()
+        record, _ = ref.consume(logits, tokens, scores)
+    assert record is not None and info['nfe'] == record['nfe'] == len(recorded)
+    assert info['last_count'] == record['last_count']
+    assert np.array_equal(result['compact'], tokens)
+    assert np.array_equal(result['commit_step'], record['step_map'])
+
+
+@pytest.mark.slow
+def test_decode_low_entropy_last_full_size():
+    """BASELINE config 1 at full size: the time-free DiT-B/4 (d = 768, 8 x 96 heads, 12 layers, V = 256) decodes one
+    all-MASK column, cap 32, seed 0, on one B200; reports NFE and wall time."""
+    from streamvoxel_b200 import model as sm
+    from streamvoxel_b200.decode import UnconditionalForward, decode_low_entropy_last
+    from streamvoxel_b200.sampling import low_entropy_last_quotas
+    cfg = sm.dit_b4_unconditional()
+    forward = UnconditionalForward(cfg, sm.synthetic_state_dict(cfg, seed=0))
+    spec = dict(air_ids=(0,), air_token=0, last_eps=1e-4, block_size=4, steps=32)
+    decode_low_entropy_last(forward, spec, 1, 'cuda', cfg.voxel_shape, cfg.classes)   # warm-up
+    result, info = decode_low_entropy_last(forward, spec, 0, 'cuda', cfg.voxel_shape, cfg.classes)
+    print(f"config 1: nfe {info['nfe']}, last_count {info['last_count']}, {info['seconds'] * 1e3:.1f} ms per column")
+    assert info['nfe'] == 1 + len(low_entropy_last_quotas(65536, 32, info['last_count'], 'quartercos'))
+    assert result['compact'].max() < cfg.classes and result['commit_step'].min() >= 1
+
+
 def _eval_fixture_module():
     import importlib.util
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden', 'make_golden.py')
