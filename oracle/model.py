@@ -278,6 +278,14 @@ def encode_kv(sd, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes, cfg, bf16=False):
     """Packed per-layer cross K/V of one item: `encode_item` `streamvoxel/stream/engine.py:75-84` followed by
     `prefix_kv` (`streaming_controlnet.py:171-176`) and `local_kv` (`streamvoxel/stream/fast_ops.py:90-95`),
     prefix keys first (`fast_ops.py:228-239`). Returns [(k, v)] per control layer, each [1,H,L,D]."""
+    prefix_kv, (local_kv, _, _) = encode_condition(sd, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes, cfg, bf16)
+    return [(torch.cat((pk, lk), 2), torch.cat((pv, lv), 2)) for (pk, pv), (lk, lv) in zip(prefix_kv, local_kv)]
+
+
+def encode_condition(sd, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes, cfg, bf16=False):
+    """The pieces `engine.unpadded_logits` hands the model (`streamvoxel/stream/engine.py:75-102`): per control layer
+    the prefix (k, v) [1,H,P,D] (keys rotated), and (local K/V per layer, the local condition tokens [1,L,d], their
+    key positions [1,L,3])."""
     p = Precision(bf16)
     height, tile, classes, heads = cfg['voxel_shape'][0], cfg['voxel_shape'][1], cfg['num_classes'], cfg['num_heads']
     pos1, pos2, bio_pos = build_group(l1_xz, l2_xz, height, tile)
@@ -289,7 +297,7 @@ def encode_kv(sd, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes, cfg, bf16=False):
     local = torch.cat((l1.flatten(0, 1)[None], bio), 1)
     local_positions = torch.cat((pos1.reshape(1, -1, 3), bio_positions), 1)
     d = l2.shape[-1] if len(l2) else local.shape[-1]
-    layers = []
+    layers, locals_ = [], []
     for j in range(len(cfg['layer_indices'])):
         w, bias = sd[f'cross.{j}.key_value.weight'], sd[f'cross.{j}.key_value.bias']
         freq = rope_frequencies(d // heads)
@@ -297,7 +305,6 @@ def encode_kv(sd, l1_blocks, l1_xz, l2_blocks, l2_xz, biomes, cfg, bf16=False):
         def kv(value, positions):
             k, v = p.linear(value, w, bias).reshape(value.shape[0], value.shape[1], 2, heads, d // heads).unbind(2)
             return rope(k.transpose(1, 2), positions, freq, p), v.transpose(1, 2)
-        pk, pv = kv(prefix[None], pos2[None])
-        lk, lv = kv(local, local_positions)
-        layers.append((torch.cat((pk, lk), 2), torch.cat((pv, lv), 2)))
-    return layers
+        layers.append(kv(prefix[None], pos2[None]))
+        locals_.append(kv(local, local_positions))
+    return layers, (locals_, local, local_positions)

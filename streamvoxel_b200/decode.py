@@ -28,6 +28,8 @@ class UnconditionalForward:
 
     def __init__(self, cfg, state_dict, device='cuda'):
         from streamvoxel_b200.model import Engine, PreparedModel
+        if cfg.layer_indices:
+            raise ValueError('UnconditionalForward runs the backbone alone (layer_indices=())')
         self.cfg, self.device = cfg, torch.device(device)
         self.engine = Engine(PreparedModel(cfg, state_dict, self.device), 1, 0)
         self.logits = torch.empty((1, cfg.classes, *cfg.voxel_shape), dtype=torch.bfloat16, device=self.device)

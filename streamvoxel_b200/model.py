@@ -290,16 +290,21 @@ class PreparedModel:
             bio, bio_positions = self._biome(torch.as_tensor(np.asarray(biomes), device=dev).long(), bio_pos)
             local = torch.cat((l1.flatten(0, 1), bio.to(torch.bfloat16)), 0)
             local_positions = torch.cat((pos1.reshape(-1, 3), bio_positions), 0)
-        # Every layer's key_value linear over all condition tokens at once (prefix rows, then local rows): the bf16
-        # input autocast would cast, one tcgen05 GEMM per layer with the bias and the axial RoPE of the K half fused
-        # in its epilogue (the same bf16 rounding points as `F.linear` then `AxialRoPE`), tables built once.
-        tokens = torch.cat((prefix, local), 0)
-        positions = torch.cat((pos2, local_positions.float()), 0)
+        # Every layer's key_value linear over all condition tokens at once (prefix rows, then local rows).
+        return self.key_values(torch.cat((prefix, local), 0), torch.cat((pos2, local_positions.float()), 0))
+
+    @torch.no_grad()
+    def key_values(self, tokens, positions):
+        """Per control layer (k, v), each [heads, n, 96] bf16, of n encoded condition tokens [n, d] at key positions
+        [n, 3]: `RotaryCrossAttention.encode_kv` (`streaming_controlnet.py:31-35`) = the key_value linear on the bf16
+        input autocast would cast, then the axial RoPE of the keys. One tcgen05 GEMM per layer with the bias and the
+        RoPE fused in its epilogue (the same bf16 rounding points as `F.linear` then `AxialRoPE`), tables built once."""
+        cfg, dev = self.cfg, self.device
         n = len(tokens)
         rows = -(-n // 256) * 256
         padded = torch.zeros((rows, cfg.d), device=dev, dtype=torch.bfloat16)
-        padded[:n] = tokens
-        phase = (positions.float()[..., None] * rope_frequencies(96).to(dev)).reshape(n, 48)
+        padded[:n] = tokens.to(device=dev, dtype=torch.bfloat16)
+        phase = (positions.to(dev).float()[..., None] * rope_frequencies(96).to(dev)).reshape(n, 48)
         sin = torch.zeros((rows, 48), device=dev, dtype=torch.bfloat16)
         cos = torch.zeros((rows, 48), device=dev, dtype=torch.bfloat16)
         sin[:n], cos[:n] = phase.sin().to(torch.bfloat16), phase.cos().to(torch.bfloat16)

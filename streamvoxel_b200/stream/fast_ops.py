@@ -20,7 +20,8 @@ import numpy as np
 import torch
 
 from streamvoxel_b200 import _lib, ops
-from streamvoxel_b200.model import Engine, ModelConfig, PreparedModel
+from streamvoxel_b200.model import Engine
+from streamvoxel_b200.modules import prepared_model
 from streamvoxel_b200.sampling import actual_time, low_entropy_last_quotas
 from streamvoxel_b200.stream.condition import probe_item
 
@@ -49,9 +50,9 @@ class FastSlotForward:
             raise ValueError("compile must be False, True or 'emulate'")
         self.device = torch.device(device)
         _lib.require_device(self.device)
-        if not isinstance(model, PreparedModel):
-            cfg, state_dict = model
-            model = PreparedModel(cfg, state_dict, self.device)
+        # a reference CompactStreamingControlNet (as `worker.py:272` passes it), a (ModelConfig, state dict) pair or a
+        # PreparedModel
+        model = prepared_model(model, self.device)
         self.model, self.spec = model, spec
         self.l2_cache = None   # created on the first item that names its L2 columns (`Item.l2_keys`)
         cfg = model.cfg
