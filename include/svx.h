@@ -8,6 +8,9 @@
  *     The library allocates no device memory; it keeps TMA descriptors in host memory.
  *   - Work is enqueued on the given cudaStream_t (passed as void*); nothing synchronises the host, so every call
  *     is capturable in a CUDA graph (after one warm-up call that configures each kernel's shared memory).
+ *   - Per-device settings (each kernel's shared-memory opt-in, occupancy, the no-allocation scratch address) are
+ *     made on the first call with that device current and kept for the life of the process: cudaDeviceReset, or
+ *     releasing and re-creating a device's primary context, is not supported while the library is loaded.
  *   - Logit layout is the reference's: class-major [slot][V][Y][Z][X] (`streamvoxel/stream/fast_ops.py:307`).
  *   - Tokens are int16 [slot][Y][Z][X]; the mask token id equals V (`streamvoxel/stream/condition.py:25`).
  *
@@ -92,8 +95,8 @@ SVX_API int svx_ease_select(const float* scores, const int16_t* tokens, const ui
  * while it is running, cannot hand svx_ease_select a workspace; this variant takes none. Its scratch is a fixed
  * array compiled into the library (262,400 bytes, held on every GPU that loads the library until the process exits),
  * so it accepts at most 64 slots and 1024 4^3 blocks per column and returns SVX_ERR_INVALID beyond that. The first call
- * on each device looks the array's device address up (cudaGetSymbolAddress); make that first call before any stream
- * capture. Every call uses the same array: calls whose kernels overlap on the GPU (other streams, other host threads)
+ * on each device looks the array's device address up (cudaGetSymbolAddress) and keeps it for the life of the process
+ * (no device reset, see the conventions above); make that first call before any stream capture. Every call uses the same array: calls whose kernels overlap on the GPU (other streams, other host threads)
  * race and must be serialised by the caller. The kernels overwrite all scratch they read on every call. Outputs,
  * inputs and errors are those of svx_ease_select. */
 SVX_API int svx_ease_select_noalloc(const float* scores, const int16_t* tokens, const uint8_t* last, const int32_t* pos,

@@ -581,17 +581,14 @@ int attention_launch(const svx_attention_problem* probs, int problems, int slots
     if (rc) return rc;
     prm.pr[pb] = AttnProblem{keys, per_prob, kv_mode, a.lengths, a.out};
   }
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice<int> sms_per_device;
+  int sms = 0;
+  const int rc = sms_per_device.get(&sms, [](int device, int* count) -> int {
     SVX_CHECK_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-    configured = true;
-  }
-  static int sms = 0;
-  if (!sms) {
-    int device = 0;
-    SVX_CHECK_CUDA(cudaGetDevice(&device));
-    SVX_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
-  }
+    SVX_CHECK_CUDA(cudaDeviceGetAttribute(count, cudaDevAttrMultiProcessorCount, device));
+    return SVX_OK;
+  });
+  if (rc) return rc;
   SVX_REQUIRE(!plan || (plan_ctas >= 1 && plan_ctas <= units), "attention: a plan needs 1 <= ctas <= units");
   const int grid = plan ? plan_ctas : (units < sms ? units : sms);
   return launch_dependent("attention_tc_kernel", attention_tc_kernel, dim3(grid), dim3(kThreads), kSmem, stream,

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <atomic>
+#include <mutex>
 #include <string>
 #include <utility>
 
@@ -29,6 +31,42 @@ int fail(int status, const std::string& text);
 
 // Launch error of the kernel just enqueued (configuration errors only; no host sync).
 int launch_status(const char* what);
+
+// A value set up once per device: a kernel's dynamic shared-memory opt-in (cudaFuncSetAttribute) belongs to the
+// device's primary context, and occupancy, SM counts and symbol addresses are per device. `get` runs
+// configure(device, &value) on the first call made with each device current (under a lock, so first calls from
+// several host threads configure a device once) and returns the stored value afterwards. The values live for the
+// process: after cudaDeviceReset, or once the primary context has been released and created again, they are stale,
+// so the library does not support either while it is loaded.
+constexpr int kMaxDevices = 64;
+
+template <typename T>
+class PerDevice {
+ public:
+  template <typename F>
+  int get(T* value, F&& configure) {
+    int device = 0;
+    SVX_CHECK_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kMaxDevices) return fail(SVX_ERR_INVALID, "device index beyond the per-device tables");
+    if (!ready_[device].load(std::memory_order_acquire)) {
+      std::lock_guard<std::mutex> lock(mutex_);
+      if (!ready_[device].load(std::memory_order_relaxed)) {
+        T v{};
+        const int rc = configure(device, &v);
+        if (rc) return rc;
+        values_[device] = v;
+        ready_[device].store(true, std::memory_order_release);
+      }
+    }
+    *value = values_[device];
+    return SVX_OK;
+  }
+
+ private:
+  std::mutex mutex_;
+  std::atomic<bool> ready_[kMaxDevices] = {};
+  T values_[kMaxDevices] = {};
+};
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -920,8 +920,10 @@ extern "C" int svx_ease_scores(const void* logits, int dtype, int slots, int cla
 extern "C" int svx_ease_mark(const void* logits, int dtype, int slots, int classes, int height, int depth, int width,
                              int64_t logit_slot_stride, const int32_t* air_ids, int n_air, double last_eps,
                              uint8_t* last, int32_t* last_count, void* stream) {
+  SVX_REQUIRE(height > 0 && depth > 0 && width > 0 && (int64_t)height * depth * width <= INT32_MAX,
+              "svx_ease_mark: the column must hold between 1 and 2^31 - 1 voxels");
   const int voxels = height * depth * width;
-  SVX_REQUIRE(logits && last && last_count && air_ids && n_air > 0 && slots > 0 && voxels > 0,
+  SVX_REQUIRE(logits && last && last_count && air_ids && n_air > 0 && slots > 0,
               "svx_ease_mark: bad arguments");
   SVX_REQUIRE(aligned16(logits), "svx_ease_mark: logits must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
@@ -956,6 +958,8 @@ extern "C" int svx_ease_select(const float* scores, const int16_t* tokens, const
   SVX_REQUIRE(block == 4, "svx_ease_select: only 4^3 blocks are implemented");
   SVX_REQUIRE(height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 && height > 0 && depth > 0 && width > 0,
               "svx_ease_select: shape must be a positive multiple of 4");
+  SVX_REQUIRE((int64_t)height * depth * width <= (int64_t)kSelectThreads * 64,
+              "svx_ease_select: at most 1024 blocks per column");
   const int voxels = height * depth * width;
   BlockGeom g{height, depth, width, depth / 4, width / 4, voxels / 64};
   SVX_REQUIRE(g.blocks <= kSelectThreads, "svx_ease_select: at most 1024 blocks per column");
@@ -990,6 +994,8 @@ extern "C" int svx_eval_select(const float* scores, const float* draw, const int
               "svx_eval_select: bad arguments (scores, draw and pos are required whatever the mode)");
   SVX_REQUIRE(height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 && height > 0 && depth > 0 && width > 0,
               "svx_eval_select: the column must tile by 4^3 blocks");
+  SVX_REQUIRE((int64_t)height * depth * width <= (int64_t)kSelectThreads * 64,
+              "svx_eval_select: at most 1024 blocks per column");
   BlockGeom g{height, depth, width, depth / 4, width / 4, (height / 4) * (depth / 4) * (width / 4)};
   SVX_REQUIRE(g.blocks <= kSelectThreads, "svx_eval_select: at most 1024 blocks per column");
   ease_eval_select_kernel<<<slots, kSelectThreads, 0, as_stream(stream)>>>(
@@ -1091,7 +1097,6 @@ namespace svx {
 namespace {
 constexpr int kNoAllocMaxSlots = 64;
 constexpr int kNoAllocMaxBlocks = kSelectThreads;  // 4^3 blocks per column, as svx_ease_select allows
-constexpr int kNoAllocMaxDevices = 64;
 }  // namespace
 }  // namespace svx
 
@@ -1101,25 +1106,18 @@ static __device__ __align__(256) int32_t g_select_scratch[svx::kNoAllocMaxSlots 
 
 namespace svx {
 namespace {
-std::mutex g_scratch_mutex;
-void* g_scratch_address[kNoAllocMaxDevices] = {};
+PerDevice<void*> g_scratch_address;
 
-// Device address of g_select_scratch on the current device, looked up once per device. In host code the array's name
-// only stands in for the symbol; a kernel must be given the address cudaGetSymbolAddress returns.
+// Device address of g_select_scratch on the current device, looked up once per device (the address stays valid while
+// the device's primary context lives, which is why the library does not support a device reset). In host code the
+// array's name only stands in for the symbol; a kernel must be given the address cudaGetSymbolAddress returns.
 int scratch_address(void** out) {
-  int device = 0;
-  SVX_CHECK_CUDA(cudaGetDevice(&device));
-  if (device < 0 || device >= kNoAllocMaxDevices) return fail(SVX_ERR_INVALID, "svx_ease_select_noalloc: device index");
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_address[device]) {
-    void* address = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&address, g_select_scratch);
+  return g_scratch_address.get(out, [](int, void** address) -> int {
+    cudaError_t e = cudaGetSymbolAddress(address, g_select_scratch);
     if (e != cudaSuccess)
       return fail(SVX_ERR_CUDA, std::string("svx_ease_select_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-    g_scratch_address[device] = address;
-  }
-  *out = g_scratch_address[device];
-  return SVX_OK;
+    return SVX_OK;
+  });
 }
 }  // namespace
 }  // namespace svx
@@ -1132,7 +1130,7 @@ extern "C" int svx_ease_select_noalloc(const float* scores, const int16_t* token
   SVX_REQUIRE(slots > 0 && slots <= kNoAllocMaxSlots,
               "svx_ease_select_noalloc: at most 64 slots per call (the fixed scratch holds 64 x 1025 int32)");
   SVX_REQUIRE(height > 0 && depth > 0 && width > 0 && height % 4 == 0 && depth % 4 == 0 && width % 4 == 0 &&
-                  (height / 4) * (depth / 4) * (width / 4) <= kNoAllocMaxBlocks,
+                  (int64_t)(height / 4) * (depth / 4) * (width / 4) <= kNoAllocMaxBlocks,
               "svx_ease_select_noalloc: at most 1024 4^3 blocks per column");
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);

@@ -685,19 +685,20 @@ int launch_pair_tile(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
                      const CUtensorMap* a2 = nullptr, const CUtensorMap* b2 = nullptr, const CUtensorMap* o2 = nullptr,
                      const CUtensorMap* r2 = nullptr, const EpiParams* ep2 = nullptr) {
   constexpr size_t bytes = pair_smem_bytes<BN, STAGES>();
-  static int max_pairs = 0;
-  if (!max_pairs) {
+  static PerDevice<int> pairs_per_device;
+  int max_pairs = 0;
+  const int rc = pairs_per_device.get(&max_pairs, [](int, int* clusters) -> int {
     SVX_CHECK_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, STAGES, EPI>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = bytes;
-    int clusters = 0;
-    SVX_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<BN, STAGES, EPI>, &cfg));
-    SVX_REQUIRE(clusters > 0, "gemm: no CTA pair fits on this device");
-    max_pairs = clusters;
-  }
+    SVX_CHECK_CUDA(cudaOccupancyMaxActiveClusters(clusters, gemm_pair_kernel<BN, STAGES, EPI>, &cfg));
+    SVX_REQUIRE(*clusters > 0, "gemm: no CTA pair fits on this device");
+    return SVX_OK;
+  });
+  if (rc) return rc;
   const int tiles = (N / BN) * (M / PM) * ((EPI & kGroup) ? 2 : 1);
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   return launch_dependent("gemm_pair_kernel", gemm_pair_kernel<BN, STAGES, EPI>, dim3(2 * pairs), dim3(kThreads),
@@ -714,15 +715,15 @@ template <int BN, int STAGES, int EPI>
 int launch_tile(const CUtensorMap& a, const CUtensorMap& b, uint16_t* out, int M, int N, int K, const EpiParams& ep,
                 cudaStream_t stream) {
   constexpr size_t bytes = smem_bytes<BN, STAGES>();
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice<int> sms_per_device;
+  int sms = 0;
+  const int rc = sms_per_device.get(&sms, [](int device, int* count) -> int {
     SVX_CHECK_CUDA(cudaFuncSetAttribute(gemm_kernel<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)bytes));
-    configured = true;
-  }
-  int device = 0, sms = 0;
-  SVX_CHECK_CUDA(cudaGetDevice(&device));
-  SVX_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    SVX_CHECK_CUDA(cudaDeviceGetAttribute(count, cudaDevAttrMultiProcessorCount, device));
+    return SVX_OK;
+  });
+  if (rc) return rc;
   const int tiles = (N / BN) * (M / BM);
   return launch_dependent("gemm_kernel", gemm_kernel<BN, STAGES, EPI>, dim3(tiles < sms ? tiles : sms), dim3(kThreads),
                           bytes, stream, a, b, out, M, N, K, ep);

@@ -5,8 +5,8 @@ Who needs it: a host that leaves every byte of device memory to another framewor
 allocate while it runs, has no workspace to pass; the no-allocation entry point keeps its scratch in a fixed array
 inside the library. This file is collected last so a run that stops at the first failure has run every other test.
 Both calls go through the C ABI with ctypes. Selection is index work, so the outputs must be equal (the tolerance of
-the other selection tests); two calls in a row with different inputs show that the shared scratch left by one call
-does not leak into the next.
+the other selection tests); calls in a row with different inputs, slot counts and column sizes show that the shared
+scratch left by one call does not leak into the next.
 """
 import ctypes
 
@@ -68,12 +68,16 @@ def _call(lib, case, out, workspace=None):
     return status
 
 
-def test_no_alloc_selection_equals_workspace_selection_twice():
+def test_no_alloc_selection_equals_workspace_selection_in_a_row():
     from streamvoxel_b200 import _lib, ops
     _lib.require_device()
     lib = _lib.load()
-    for seed, slots in ((11, 8), (12, 5)):   # second call: other inputs, fewer slots, scratch left from the first
-        case = _case(seed, slots)
+    # Calls in a row on the shared scratch: other inputs and fewer slots; then a smaller column (256 blocks, so the
+    # per-slot counters sit where the first calls left block quotas); then the largest call the scratch takes (64 slots
+    # of 1024 blocks).
+    for seed, slots, shape in ((11, 8, (256, 16, 16)), (12, 5, (256, 16, 16)), (13, 6, (64, 16, 16)),
+                               (14, 64, (256, 16, 16))):
+        case = _case(seed, slots, shape)
         want = _outputs(case)
         workspace = ops.select_workspace(slots, case['total'], 'cuda')
         assert _call(lib, case, want, workspace) == _lib.SVX_OK
@@ -94,4 +98,8 @@ def test_no_alloc_selection_rejects_sizes_beyond_its_scratch():
     assert status == _lib.SVX_ERR_INVALID and b'64 slots' in lib.svx_last_error()
     status = lib.svx_ease_select_noalloc(null, null, null, null, null, 1, 512, 16, 16, 4, 256, null, null, 1, null,
                                          null, null)
+    assert status == _lib.SVX_ERR_INVALID and b'1024' in lib.svx_last_error()
+    # 2^42 blocks: a 32-bit product would wrap to 0 and pass; the count is formed in 64 bits and rejected
+    status = lib.svx_ease_select_noalloc(null, null, null, null, null, 1, 1 << 20, 1 << 20, 1 << 8, 4, 256, null, null,
+                                         1, null, null, null)
     assert status == _lib.SVX_ERR_INVALID and b'1024' in lib.svx_last_error()
