@@ -146,21 +146,41 @@ class Clocks:
 
 # ------------------------------------------------------------------------------------------------ ours
 
-def build(device, seed=0):
-    from streamvoxel_b200 import model as sm, synth
-    from streamvoxel_b200.stream.batch import SlotBatch
+def bench_items(cfg, seed=0):
+    """The slots' synthetic windows (`synth.item`: k ~ U{0..8} L1 tiles, 80 L2 columns, the biome window) and their
+    packed key lengths (prefix L2 tokens + L1 tokens + biome tokens), the one length rule of both arms."""
+    from streamvoxel_b200 import synth
     from streamvoxel_b200.stream.condition import ModelSpec
+    spec = ModelSpec.of(cfg)
+    l1, l2, biome = cfg.condition_widths()
+    rng = np.random.default_rng(seed)
+    items = [synth.item(int(rng.integers(1 << 30)), spec) for _ in range(SLOTS)]
+    lengths = [len(it.l2_blocks) * l2 + len(it.l1_blocks) * l1 + biome for it in items]
+    return spec, items, lengths
+
+
+def bench_config(lengths, world):
+    """The workload description both arms print (the same dict, so the two lines name the same configuration)."""
+    return dict(workload=WORKLOAD, slots_per_gpu=SLOTS, cap=CAP, l1_cap=L1_CAP, l2_cap=L2_CAP,
+                packed_keys=[int(v) for v in lengths], mean_packed_keys=float(np.mean(lengths)),
+                committed_accounting=('each forward of a window credited with an equal share of the window\'s '
+                                      '65536 voxels (exact for whole windows; steady-state rate otherwise)'),
+                l2_policy='inputs larger than L2 (268 MB logits + 0.86 GB weights per step)',
+                parallelism=f'dp{world}: one engine per GPU, no collective on the data path')
+
+
+def build(device, seed=0):
+    from streamvoxel_b200 import model as sm
+    from streamvoxel_b200.stream.batch import SlotBatch
     from streamvoxel_b200.stream.fast_ops import FastSlotForward
     cfg = sm.dit_b4_control()
     sd = sm.synthetic_state_dict(cfg, seed=seed)
-    spec = ModelSpec.of(cfg)
+    spec, items, lengths = bench_items(cfg, seed)
     forward = FastSlotForward((cfg, sd), spec, device, SLOTS, L1_CAP, L2_CAP)
-    rng = np.random.default_rng(seed)
-    lengths = []
-    for i in range(SLOTS):
-        forward.load_slot(i, synth.item(int(rng.integers(1 << 30)), spec))
+    for i, item in enumerate(items):
+        forward.load_slot(i, item)
     forward.wait_loads()
-    lengths = forward.packed.lengths.tolist()
+    assert forward.packed.lengths.tolist() == lengths
     batch = SlotBatch(forward)
     return cfg, sd, forward, batch, lengths
 
@@ -358,15 +378,17 @@ def time_kernels(cfg, forward, batch, lengths):
 
 def cpu_baseline(cfg, sd, lengths, sample=1):
     """The reference's CPU path (oracle port: fp32 torch forward + numpy EASE step) on the host cores for `sample`
-    slot-forwards of the same workload (one slot, its own packed K/V length), in committed voxels/s."""
+    slot-forwards of the same workload (one slot at the mean packed K/V length of the bench's slots), in committed
+    voxels/s. Runs with no other process of the job alive (the GPU ranks have returned), on every core the process
+    may use."""
     from oracle import model as om
     from oracle import sampler as osm
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else (os.cpu_count() or 1)
     torch.set_num_threads(threads)
     cfgd = dict(num_classes=cfg.classes, voxel_shape=cfg.voxel_shape, patch_size=4, depth=cfg.depth,
                 num_heads=cfg.heads, y_range=cfg.y_range, layer_indices=list(cfg.layer_indices))
     rng = np.random.default_rng(1)
-    length = int(np.median(lengths))
+    length = int(round(float(np.mean(lengths))))
     kv = [(torch.randn(1, cfg.heads, length, 96), torch.randn(1, cfg.heads, length, 96)) for _ in cfg.layer_indices]
     tokens = torch.full((1, *cfg.voxel_shape), cfg.classes, dtype=torch.long)
     total = int(np.prod(cfg.voxel_shape))
@@ -388,6 +410,8 @@ def cpu_baseline(cfg, sd, lengths, sample=1):
 
 
 def main_ours(args):
+    """Time the step on this rank's GPU; returns (the JSON line without its CPU baseline, cfg, sd, lengths) on rank 0
+    and None elsewhere. Every rank takes the same collective steps in the same order."""
     rank, world, local = dist_env()
     if world > 1:
         import datetime
@@ -412,13 +436,13 @@ def main_ours(args):
             dist.barrier()
         torch.cuda.synchronize(device)
 
-    def max_over_ranks(x):
+    def gather(obj):
         if world == 1:
-            return x
+            return [obj]
         import torch.distributed as dist
-        t = torch.tensor([x], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clocks:
@@ -427,9 +451,7 @@ def main_ours(args):
         committed, launches, markings = run_device_steps(batch, args.steps, iter(seeds))
         stop.record()
         barrier()
-    seconds = max_over_ranks(start.elapsed_time(stop) * 1e-3)
-    total_committed = committed * world if world > 1 else committed
-    value = total_committed / seconds
+    own_seconds = start.elapsed_time(stop) * 1e-3
     # end to end through the public step API (host scalars in, commits out, host bookkeeping), same step count
     for i in range(batch.slots):
         batch.state[i] = dict(phase='idle')
@@ -438,11 +460,17 @@ def main_ours(args):
     e2e_committed, h2d, d2h = run_api_steps(batch, args.steps, iter(seeds[10_000:]))
     stop.record()
     barrier()
-    e2e_seconds = max_over_ranks(start.elapsed_time(stop) * 1e-3)
-    e2e_value = e2e_committed * world / e2e_seconds
+    own_e2e = start.elapsed_time(stop) * 1e-3
     kernels = time_kernels(cfg, forward, batch, lengths)
+    ranks = gather(dict(rank=rank, ms_per_step=own_seconds / args.steps * 1e3,
+                        e2e_ms_per_step=own_e2e / args.steps * 1e3, committed=committed, e2e_committed=e2e_committed,
+                        mean_packed_keys=float(np.mean(lengths)), clocks=clocks.summary()))
     if rank != 0:
-        return
+        return None
+    seconds = max(r['ms_per_step'] for r in ranks) * args.steps * 1e-3   # max over ranks
+    e2e_seconds = max(r['e2e_ms_per_step'] for r in ranks) * args.steps * 1e-3
+    value = sum(r['committed'] for r in ranks) / seconds
+    e2e_value = sum(r['e2e_committed'] for r in ranks) / e2e_seconds
     peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json'))) if os.path.exists(
         os.path.join(ROOT, 'MEASURED_PEAKS.json')) else {}
     dominant = max(kernels, key=lambda k: kernels[k]['share_seconds'])
@@ -459,18 +487,13 @@ def main_ours(args):
         measured, captured_alg = MEASURED_TRAFFIC[dominant]
         traffic = measured * algorithmic_bytes(dominant, cfg, lengths) / captured_alg
     step_flops = sum(k['work'] * k['per_step'] for n, k in kernels.items() if n not in BYTE_KERNELS)
-    cpu = cpu_baseline(cfg, sd, lengths, args.cpu_sample)
     steps_per_s = args.steps / seconds
     line = dict(
         metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=seconds / args.steps * 1e3, higher_is_better=True, scaling='weak', vs_baseline=None,
         dtype='bf16', data='synthetic (seeded world generator, random-init N(0,0.02) weights)',
-        config=dict(workload=WORKLOAD, slots_per_gpu=SLOTS, cap=CAP, l1_cap=L1_CAP, l2_cap=L2_CAP,
-                    mean_packed_keys=float(np.mean(lengths)), sampler='EASE native Philox draw',
-                    committed_accounting=('each forward of a window credited with an equal share of the window\'s '
-                                          '65536 voxels (exact for whole windows; steady-state rate otherwise)'),
-                    l2_policy='inputs larger than L2 (268 MB logits + 0.86 GB weights per step)',
-                    parallelism=f'{world} independent engines, no collective'),
+        config=bench_config(lengths, world),
+        sampler='EASE, native Gumbel-max Philox draw (bit-exact with its host restatement)',
         forwards_per_s=steps_per_s * world, marking_forwards=markings,
         e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d / args.steps, d2h_bytes_per_step=d2h / args.steps),
         gpu_launches=launches,
@@ -481,27 +504,33 @@ def main_ours(args):
         kernels={k: dict(us=v['seconds'] * 1e6, per_step=v['per_step'],
                          rate=(v['work'] / v['seconds'] / (1e9 if k in BYTE_KERNELS else 1e12)))
                  for k, v in kernels.items()},
-        cpu_baseline=cpu, clocks=clocks.summary())
-    print(json.dumps(line), flush=True)
+        clocks=clocks.summary(),
+        per_rank=[dict(rank=r['rank'], ms_per_step=r['ms_per_step'], e2e_ms_per_step=r['e2e_ms_per_step'],
+                       mean_packed_keys=r['mean_packed_keys'], sm_mhz=r['clocks'].get('sm_mhz'),
+                       reasons=r['clocks'].get('reasons')) for r in ranks])
+    return line, cfg, sd, lengths
 
 
 def main_reference(args):
+    """The reference's CPU path on the host cores (rank 0 only), on this arm's config, metric and unit: each step is one
+    bounded sample (one slot-forward of the config-2 model at the bench's mean packed key length + one EASE solid
+    step), at most 3 samples."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
     from streamvoxel_b200 import model as sm
     cfg = sm.dit_b4_control()
     sd = sm.synthetic_state_dict(cfg, seed=0)
-    lengths = [1280 + 1024 * 4 + 64]   # k = 4 L1 tiles + 80 L2 columns + 64 biome tokens (mean of k ~ U{0..8})
+    _, _, lengths = bench_items(cfg, 0)
+    steps = min(max(1, args.steps), 3)
     began = time.perf_counter()
-    result = cpu_baseline(cfg, sd, lengths, min(max(1, args.steps), 3))
+    result = cpu_baseline(cfg, sd, lengths, steps)
     seconds = time.perf_counter() - began
-    line = dict(metric=METRIC, value=result['value'], unit=UNIT, n_gpus=world, steps=args.steps,
-                warmup=args.warmup, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
-                data='synthetic', impl='reference',
-                config=dict(workload=WORKLOAD, sample=result['sample']),
-                cpu_baseline=result, e2e=dict(value=result['value'], unit=UNIT, h2d_bytes_per_step=0,
-                                              d2h_bytes_per_step=0), seconds=seconds)
+    line = dict(metric=METRIC, value=result['value'], unit=UNIT, n_gpus=world, steps=steps, warmup=0,
+                higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32', data='synthetic', impl='reference',
+                config=bench_config(lengths, world), cpu_baseline=result,
+                e2e=dict(value=result['value'], unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+                seconds=seconds)
     print(json.dumps(line), flush=True)
 
 
@@ -509,14 +538,24 @@ def main():
     args = parse()
     if args.impl == 'reference':
         main_reference(args)
-    else:
-        try:
-            main_ours(args)
-        finally:
-            import torch.distributed as dist
-            if dist.is_available() and dist.is_initialized():
-                dist.barrier()
-                dist.destroy_process_group()
+        return
+    result = None
+    try:
+        result = main_ours(args)
+    finally:
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
+    if result is None:
+        return
+    line, cfg, sd, lengths = result
+    # The CPU baseline runs after the process group is gone and the other ranks have returned, so no waiting rank
+    # spins on a host core while it is timed.
+    if line['n_gpus'] > 1:
+        time.sleep(2.0)
+    line['cpu_baseline'] = cpu_baseline(cfg, sd, lengths, args.cpu_sample)
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == '__main__':
