@@ -37,24 +37,27 @@ def _kv_of_slot(engine, slot):
             for k, v in engine.packed.kv]
 
 
-def _assert_logits(got, want, outlier_ppm=0.0):
-    """Every logit within ATOL + RTOL |want|; a full-size 24-block forward may leave `outlier_ppm` parts per million
-    of its logits up to twice that bound (chains of one-ulp bf16 differences between two valid bf16 forwards: the
-    oracle's and the kernels' rounding points agree, their accumulation orders do not)."""
+def _assert_logits(got, want, outlier_ppm=0.0, min_agree=0.99):
+    """Every logit within ATOL + RTOL |want|. A full-size 24-block forward may leave `outlier_ppm` parts per million of
+    its 16.7 M logits up to 1.5 times that bound: two bf16 forwards with identical rounding points that differ only in
+    fp32 accumulation order already reach 0.94 of the bound there (`tests/test_forward_noise_floor.py`), and the
+    kernels round the folded LayerNorm's weights where the oracle rounds the modulated activations.
+    Random-init logits have near-tied top classes, so bf16 noise alone flips some argmaxes (1.4% between the two
+    valid full-size forwards above); a gross error flips most."""
     d = (got - want).abs()
     bound = ATOL + RTOL * want.abs()
     bad = int((d > bound).sum())
-    print(f'logits: max |d| {float(d.max()):.4g}, mean |d| {float(d.mean()):.3g}, out of tolerance {bad} / {got.numel()}')
+    print(f'logits: max |d| {float(d.max()):.4g}, mean |d| {float(d.mean()):.3g}, out of tolerance {bad} / '
+          f'{got.numel()}, max |d| / bound {float((d / bound).max()):.3f}')
     if outlier_ppm == 0.0:
         torch.testing.assert_close(got, want, atol=ATOL, rtol=RTOL)
     else:
         assert bad <= outlier_ppm * 1e-6 * got.numel(), bad
-        assert bool((d <= 2 * bound).all()), float((d / bound).max())
+        assert bool((d <= 1.5 * bound).all()), float((d / bound).max())
     assert float((got - want).abs().mean()) <= 5e-3
-    # Random-init logits have near-tied top classes, so bf16 noise flips some argmaxes; a gross error flips most.
     agree = float((got.argmax(0) == want.argmax(0)).float().mean())
     print(f'argmax agreement {agree:.4f}')
-    assert agree >= 0.95, agree
+    assert agree >= min_agree, agree
 
 
 def test_small_forward_matches_oracle_per_slot():
@@ -143,7 +146,7 @@ def test_full_size_control_forward_matches_oracle():
     torch.set_num_threads(max(1, torch.get_num_threads()))
     want = om.control_forward(sd, torch.from_numpy(tokens[1:2]).long(), _kv_of_slot(engine, 1), _cfg_dict(cfg),
                               bf16=True)[0]
-    _assert_logits(got, want, outlier_ppm=1.0)
+    _assert_logits(got, want, outlier_ppm=1.0, min_agree=0.98)
 
 
 @pytest.mark.slow
@@ -161,4 +164,4 @@ def test_full_size_unconditional_forward_matches_oracle():
     logits = torch.empty((1, cfg.classes, *cfg.voxel_shape), dtype=torch.bfloat16, device='cuda')
     got = engine.forward(1, t, logits)[0].float().cpu()
     want = om.unconditional_forward(sd, torch.from_numpy(tokens[None]).long(), _cfg_dict(cfg), bf16=True)[0]
-    _assert_logits(got, want)
+    _assert_logits(got, want, min_agree=0.98)
