@@ -287,6 +287,41 @@ def model_cases():
     _save('control_tiny.npz', **out)
 
 
+def full_size_case():
+    """The reference's own fp32 forward of the BASELINE config-2 model (DiT-B/4, d = 768, 8 x 96 heads, V = 256, 12-layer
+    ControlNet) on the CPU: `engine.unpadded_logits` (`streamvoxel/stream/engine.py:87-102`) with the seeded
+    synthetic weights of `streamvoxel_b200.model.synthetic_state_dict(seed=0)` loaded into the reference module, one
+    synthetic window (k = 2 L1 tiles, 80 L2 columns, the biome window) and a partially masked target. Stored: the
+    logits of 512 seeded voxels (all 256 classes, fp32)."""
+    from streamvoxel.models.compact_controlnet import CompactStreamingControlNet
+    from streamvoxel.models.unconditional_md4_timefree import UnconditionalMD4DiT
+    from streamvoxel.stream.condition import Item, ModelSpec
+    from streamvoxel.stream.engine import install_slot_attention, unpadded_logits
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from streamvoxel_b200 import model as sm, synth
+    from streamvoxel_b200.stream.condition import ModelSpec as OurSpec
+    cfg = sm.dit_b4_control()
+    base = UnconditionalMD4DiT(num_classes=256, voxel_shape=(256, 16, 16), hidden_dim=768, depth=12, num_heads=8,
+                               time_free=True)
+    model = CompactStreamingControlNet(base, control_depth=12, control_hidden_dim=768, checkpointing=False,
+                                       biome_halo=4, biome_patch=4, biome_classes=16, struct_classes=0)
+    state = sm.synthetic_state_dict(cfg, seed=0)
+    missing, unexpected = model.load_state_dict(state, strict=False)
+    assert not unexpected and all(k not in state for k in missing)
+    model.eval().requires_grad_(False)
+    install_slot_attention(model)   # as FastSlotForward does before the reference numerical gate calls unpadded_logits
+    ours = synth.item(701, OurSpec.of(cfg), k=2)
+    item = Item(ours.id, ours.seed, ours.steps, ours.temperature, ours.l1_blocks, ours.l1_xz, ours.l2_blocks,
+                ours.l2_xz, ours.biomes, None)
+    spec = ModelSpec(height=256, tile=16, num_classes=256, biome_classes=16, biome_halo=4, y_origin=-64.)
+    tokens = torch.from_numpy(synth.target_tokens(801, OurSpec.of(cfg))[0][None]).long()
+    with torch.no_grad():
+        logits = unpadded_logits(model, item, spec, tokens, torch.ones(1))[0]
+    voxels = np.sort(np.random.default_rng(3).choice(65536, 512, replace=False))
+    _save('control_full.npz', voxels=voxels, logits=logits.reshape(256, -1)[:, voxels].numpy(),
+          tokens=tokens[0].numpy().astype(np.int16))
+
+
 # ---------------------------------------------------------------------------------------------- window admission
 
 def _blob(rng, n):
@@ -395,7 +430,8 @@ def wire_cases():
 
 CASES = dict(quota=lambda: quota_cases(), top_mask=lambda: top_mask_cases(), schedule=lambda: schedule_cases(),
              scores=lambda: score_cases(), slots=lambda: slot_cases(), models=lambda: model_cases(),
-             scheduler=lambda: scheduler_cases(), wire=lambda: wire_cases(), eval=lambda: eval_cases())
+             scheduler=lambda: scheduler_cases(), wire=lambda: wire_cases(), eval=lambda: eval_cases(),
+             full_size=lambda: full_size_case())
 
 
 def main():

@@ -3,6 +3,7 @@
 import os
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import model as om
@@ -193,3 +194,26 @@ def test_series_log_and_native_draw():
     p /= p.sum()
     freq = np.bincount(values, minlength=8) / n
     assert np.all(np.abs(freq - p) <= 5 * np.sqrt(p * (1 - p) / n))
+
+
+@pytest.mark.slow
+def test_full_size_forward_matches_reference_fp32():
+    """The oracle's fp32 encoder + forward of the full-size config-2 model equals the reference's own
+    `engine.unpadded_logits` (fixture `control_full.npz`: 512 voxels x 256 classes) within 1e-4."""
+    from streamvoxel_b200 import model as sm, synth
+    from streamvoxel_b200.stream.condition import ModelSpec
+    g = _load('control_full.npz')
+    cfg = sm.dit_b4_control()
+    sd = sm.synthetic_state_dict(cfg, seed=0)
+    spec = ModelSpec.of(cfg)
+    cfgd = dict(num_classes=cfg.classes, voxel_shape=cfg.voxel_shape, patch_size=4, depth=cfg.depth,
+                num_heads=cfg.heads, y_range=cfg.y_range, layer_indices=list(cfg.layer_indices),
+                biome_halo=cfg.biome_halo, biome_patch=cfg.biome_patch)
+    item = synth.item(701, spec, k=2)
+    tokens, _ = synth.target_tokens(801, spec)
+    assert np.array_equal(tokens, g['tokens'])
+    with torch.no_grad():
+        kv = om.encode_kv(sd, item.l1_blocks, item.l1_xz, item.l2_blocks, item.l2_xz, item.biomes, cfgd)
+        got = om.control_forward(sd, torch.from_numpy(tokens[None]).long(), kv, cfgd)[0]
+    torch.testing.assert_close(got.reshape(256, -1)[:, g['voxels']], torch.from_numpy(g['logits']), atol=1e-4,
+                               rtol=1e-4)
