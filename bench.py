@@ -30,8 +30,20 @@ sys.path.insert(0, ROOT)
 
 METRIC = 'committed voxels/s per B200 (8 slots)'
 UNIT = 'voxels/s'
-SLOTS, L1_CAP, L2_CAP, CAP = 8, 8, 81, 32
-WORKLOAD = 'config2: DiT-B/4 (d=768, 8x96 heads, 12 layers, V=256) + 12-layer ControlNet, 8 slots, bf16, cached K/V'
+L1_CAP, L2_CAP, CAP = 8, 81, 32
+WORKLOADS = {
+    'config2': (8, 'dit_b4_control',
+                'config2: DiT-B/4 (d=768, 8x96 heads, 12 layers, V=256) + 12-layer ControlNet, 8 slots, bf16, cached K/V'),
+    'config5': (16, 'dit_l4_control',
+                'config5: DiT-L/4-class (d=1152, 12x96 heads, 24 layers, MLP 4608, V=256) + 24-layer ControlNet, '
+                '16 slots, bf16, cached K/V'),
+}
+SLOTS, MODEL, WORKLOAD = WORKLOADS['config2']
+
+
+def model_config():
+    from streamvoxel_b200 import model as sm
+    return getattr(sm, MODEL)()
 BYTE_KERNELS = ('ease_scores', 'patch_embed')   # memory-bound: rates in GB/s, left out of the step's FLOPs
 
 
@@ -42,7 +54,12 @@ def parse():
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     p.add_argument('--cpu-sample', type=int, default=1, help='slot-forwards in the CPU baseline sample')
-    return p.parse_args()
+    p.add_argument('--workload', default='config2', choices=sorted(WORKLOADS),
+                   help='config2 (default, the metric\'s configuration) or config5 (the larger model, 16 slots)')
+    args = p.parse_args()
+    global SLOTS, MODEL, WORKLOAD
+    SLOTS, MODEL, WORKLOAD = WORKLOADS[args.workload]
+    return args
 
 
 def dist_env():
@@ -165,7 +182,7 @@ def bench_config(lengths, world):
                 packed_keys=[int(v) for v in lengths], mean_packed_keys=float(np.mean(lengths)),
                 committed_accounting=('each forward of a window credited with an equal share of the window\'s '
                                       '65536 voxels (exact for whole windows; steady-state rate otherwise)'),
-                l2_policy='inputs larger than L2 (268 MB logits + 0.86 GB weights per step)',
+                l2_policy='inputs larger than L2 (the step reads all weights and writes all logits: >= 1 GB)',
                 parallelism=f'dp{world}: one engine per GPU, no collective on the data path')
 
 
@@ -173,7 +190,7 @@ def build(device, seed=0):
     from streamvoxel_b200 import model as sm
     from streamvoxel_b200.stream.batch import SlotBatch
     from streamvoxel_b200.stream.fast_ops import FastSlotForward
-    cfg = sm.dit_b4_control()
+    cfg = model_config()
     sd = sm.synthetic_state_dict(cfg, seed=seed)
     spec, items, lengths = bench_items(cfg, seed)
     forward = FastSlotForward((cfg, sd), spec, device, SLOTS, L1_CAP, L2_CAP)
@@ -324,29 +341,30 @@ def time_kernels(cfg, forward, batch, lengths):
     self_ = dict(q=ws['qkv'], k=ws['qkv'][:, d:], v=ws['qkv'][:, 2 * d:], keys=cfg.patches, q_row_stride=3 * d,
                  kv_slot_stride=cfg.patches * 3 * d, kv_head_stride=96, kv_row_stride=3 * d, out=ws['attn'])
     self_flops = 4.0 * SLOTS * heads * cfg.patches * cfg.patches * 96
+    nc = len(cfg.layer_indices)   # control layers: each has a cross-attention, a joint launch and a projection group
     kernels = {
         # as the engine runs them: the LayerNorm folded into qkv / fc1 / head, row statistics from fc2 / proj / zero
         'gemm_qkv_rope': (lambda: ops.gemm(ws['xb'], bw['qkv_fold'][0], bw['attn.qkv.bias'], _lib.EPI_ROPE,
                                            out=ws['qkv'], rope=tables, rope_cols=2 * d, rows_per_slot=cfg.patches,
                                            ln=(stats, *bw['qkv_fold'][1:], 1e-6)),
-                          2.0 * rows * d * 3 * d, 24),
+                          2.0 * rows * d * 3 * d, 2 * cfg.depth),
         'gemm_fc1_gelu': (lambda: ops.gemm(ws['xb'], bw['fc1_fold'][0], bw['mlp.0.bias'], _lib.EPI_BIAS_GELU,
                                            out=ws['mlp'], ln=(stats, *bw['fc1_fold'][1:], 1e-6)),
-                          2.0 * rows * d * cfg.mlp, 24),
+                          2.0 * rows * d * cfg.mlp, 2 * cfg.depth),
         'gemm_fc2_gate': (lambda: ops.gemm(ws['mlp'], bw['mlp.2.weight'], bw['mlp.2.bias'], _lib.EPI_GATE_RESIDUAL,
                                            out=ws['xb'], gate=bw['gate2'], residual=ws['xb'], stats_out=stats),
-                          2.0 * rows * cfg.mlp * d, 24),
+                          2.0 * rows * cfg.mlp * d, 2 * cfg.depth),
         'gemm_dxd': (lambda: ops.gemm(ws['attn'], bw['attn.proj.weight'], bw['attn.proj.bias'],
                                       _lib.EPI_GATE_RESIDUAL, out=ws['xb'], gate=bw['gate1'], residual=ws['xb'],
                                       stats_out=stats),
-                     2.0 * rows * d * d, 3 * 12),   # control proj, cross query, zero
+                     2.0 * rows * d * d, 3 * nc),   # control proj, cross query, zero
         # a control layer's cross projection (gate of ones: the plain residual) with its backbone block's attention
         # projection in one launch, as the engine runs them
         'gemm_dxd_group': (lambda: ops.gemm_group([
             dict(a=ws['ax'], w=cw['proj.weight'], bias=cw['proj.bias'], gate=ones, residual=ws['xc'],
                  stats_out=forward.engine.stats['c'], out=ws['xc']),
             dict(a=ws['attn'], w=bw['attn.proj.weight'], bias=bw['attn.proj.bias'], gate=bw['gate1'], residual=ws['xb'],
-                 stats_out=stats, out=ws['xb'])]), 2 * 2.0 * rows * d * d, 12),
+                 stats_out=stats, out=ws['xb'])]), 2 * 2.0 * rows * d * d, nc),
         'gemm_head': (lambda: ops.gemm(ws['xb'], m.head_fold[0], m.head_b, _lib.EPI_CLASS_MAJOR, out=forward.logits,
                                        rows_per_slot=cfg.patches, classes=cfg.classes, geometry=cfg.voxel_shape,
                                        ln=(stats, *m.head_fold[1:], 1e-6)),
@@ -355,10 +373,10 @@ def time_kernels(cfg, forward, batch, lengths):
         'attention_self': (lambda: ops.attention(ws['qkv'], ws['qkv'][:, d:], ws['qkv'][:, 2 * d:], SLOTS, heads,
                                                  cfg.patches, cfg.patches, q_row_stride=3 * d,
                                                  kv_slot_stride=cfg.patches * 3 * d, kv_head_stride=96,
-                                                 kv_row_stride=3 * d, out=ws['attn']), self_flops, 12),
+                                                 kv_row_stride=3 * d, out=ws['attn']), self_flops, nc),
         # the cross-attention with the backbone's self-attention in one launch
         'attention_joint': (lambda: ops.attention_multi([cross, self_], SLOTS, heads, cfg.patches, plan),
-                            4.0 * SLOTS * heads * cfg.patches * mean_len * 96 + self_flops, 12),
+                            4.0 * SLOTS * heads * cfg.patches * mean_len * 96 + self_flops, nc),
         'ease_scores': (lambda: ops.ease_scores(forward.logits, batch.status, out=batch.scores),
                         float(forward.logits.numel() * 2 + batch.scores.numel() * 4), 1),
         # both branches' embed of the slots' current tokens with the first LayerNorms' chunk statistics; bytes: tokens
@@ -519,7 +537,7 @@ def main_reference(args):
     if rank != 0:
         return
     from streamvoxel_b200 import model as sm
-    cfg = sm.dit_b4_control()
+    cfg = model_config()
     sd = sm.synthetic_state_dict(cfg, seed=0)
     _, _, lengths = bench_items(cfg, 0)
     steps = min(max(1, args.steps), 3)

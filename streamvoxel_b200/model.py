@@ -69,6 +69,13 @@ def dit_b4_control():
     return ModelConfig()
 
 
+def dit_l4_control():
+    """the DiT-L/4-class backbone + a ControlNet of the same depth. d = 1024 cannot carry the axial
+    RoPE (head_dim must be a multiple of 6: 1024 has no factor 3), so the nearest buildable width with the same
+    96-wide heads: d = 1152, 12 heads x 96, MLP 4608, 24 layers, 24 control layers."""
+    return ModelConfig(d=1152, heads=12, depth=24, mlp=4608, layer_indices=tuple(range(24)))
+
+
 def dit_b4_unconditional():
     """the time-free DiT-B/4 alone (no ControlNet)."""
     return ModelConfig(layer_indices=())

@@ -190,3 +190,22 @@ def test_full_size_forward_against_reference_fp32_logits():
     print(f'vs reference fp32: max |d| {float(d.max()):.4g}, mean |d| {float(d.mean()):.4g}, max |d| / bound '
           f'{ratio:.3f}, argmax agreement {agree:.4f}')
     assert float(d.mean()) <= 1.4 * 0.0044 and ratio <= 2.0 and agree >= 0.97
+
+
+@pytest.mark.slow
+def test_full_size_config5_forward_matches_oracle():
+    """BASELINE config 5 model at full size: the DiT-L/4-class backbone (d = 1152, 12 x 96 heads, 24 layers, MLP 4608)
+    + 24-layer ControlNet, slot 1 of a 2-slot batch (k = 3 L1 tiles, 80 L2 columns, the biome window), against the
+    oracle's bf16-rounding forward: 48 blocks and 24 cross-attentions, the same allowance as the config-2 model."""
+    from streamvoxel_b200 import model as sm, synth
+    cfg = sm.dit_l4_control()
+    engine, sd, spec = _engine(cfg, 2, l1_cap=8, l2_cap=81)
+    engine.load_slot(0, synth.item(710, spec, k=6))
+    engine.load_slot(1, synth.item(711, spec, k=3))
+    engine.wait_loads()
+    tokens = np.stack([synth.target_tokens(810 + i, spec)[0] for i in range(2)])
+    engine.tokens.copy_(torch.from_numpy(tokens).cuda())
+    got = engine.replay(torch.ones(2))[1].float().cpu()
+    want = om.control_forward(sd, torch.from_numpy(tokens[1:2]).long(), _kv_of_slot(engine, 1), _cfg_dict(cfg),
+                              bf16=True)[0]
+    _assert_logits(got, want, outlier_ppm=1.0, min_agree=0.98)
