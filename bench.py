@@ -34,6 +34,9 @@ L1_CAP, L2_CAP, CAP = 8, 81, 32
 WORKLOADS = {
     'config2': (8, 'dit_b4_control',
                 'config2: DiT-B/4 (d=768, 8x96 heads, 12 layers, V=256) + 12-layer ControlNet, 8 slots, bf16, cached K/V'),
+    'config4': (8, 'dit_b4_control',
+                'config4: streaming expansion 32^2 -> 64^2 columns (3072 windows), DiT-B/4 + 12-layer ControlNet, '
+                '8 slots per GPU, cap 32, Chebyshev >= 2 admission, whole step in one CUDA graph'),
     'config5': (16, 'dit_l4_control',
                 'config5: DiT-L/4-class (d=1152, 12x96 heads, 24 layers, MLP 4608, V=256) + 24-layer ControlNet, '
                 '16 slots, bf16, cached K/V'),
@@ -55,7 +58,10 @@ def parse():
     p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     p.add_argument('--cpu-sample', type=int, default=1, help='slot-forwards in the CPU baseline sample')
     p.add_argument('--workload', default='config2', choices=sorted(WORKLOADS),
-                   help='config2 (default, the metric\'s configuration) or config5 (the larger model, 16 slots)')
+                   help='config2 (default, the metric\'s configuration), config4 (the streaming expansion) or '
+                        'config5 (the larger model, 16 slots)')
+    p.add_argument('--side0', type=int, default=32, help='config4: side of the committed start square (columns)')
+    p.add_argument('--side1', type=int, default=64, help='config4: side of the target region (columns)')
     args = p.parse_args()
     global SLOTS, MODEL, WORKLOAD
     SLOTS, MODEL, WORKLOAD = WORKLOADS[args.workload]
@@ -552,6 +558,78 @@ def main_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def main_expand(args):
+    """a committed side0^2 start region grown to side1^2 columns through the public engine API
+    (`SlotBatch`, window admission, per-window condition encoding, commits), one engine per GPU; the ranks exchange
+    finished columns on the host (a gloo group). The timed region is the whole expansion (CUDA events on each rank,
+    max over ranks); `value` = committed voxels of all ranks / that time. Returns the JSON line on rank 0."""
+    rank, world, local = dist_env()
+    group = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=600))
+        group = dist.new_group(backend='gloo', timeout=datetime.timedelta(seconds=600))
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    from streamvoxel_b200 import _lib
+    from streamvoxel_b200.stream import expand
+    _lib.require_device(device)
+    cfg, sd, forward, batch, lengths = build(device, seed=0)
+    run_api_steps(batch, max(3, args.warmup), iter(range(10_000, 20_000)))   # warm-up through the step API
+    for i in range(batch.slots):
+        batch.state[i] = dict(phase='idle')
+    committed, region, biomes, player = expand.start_region(11, args.side0, args.side1, forward.spec,
+                                                            classes=cfg.classes)
+    exp = expand.Expansion(committed, biomes, forward.spec, player, region, ranks=world, slots=SLOTS, l2_cap=L2_CAP)
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        barrier()
+        start.record()
+        stats = expand.run(batch, exp, rank, group=group)
+        stop.record()
+        barrier()
+    seconds = start.elapsed_time(stop) * 1e-3
+    ranks = expand.host_exchange(dict(rank=rank, seconds=seconds, stats=stats, digest=exp.digest(),
+                                      clocks=clocks.summary()), group)
+    if rank != 0:
+        return None
+    wall = max(r['seconds'] for r in ranks)
+    voxels = sum(r['stats']['committed_voxels'] for r in ranks)
+    forwards = sum(r['stats']['forwards'] for r in ranks)
+    windows = sum(r['stats']['windows'] for r in ranks)
+    config = dict(workload=WORKLOAD, slots_per_gpu=SLOTS, cap=CAP, l1_cap=L1_CAP, l2_cap=L2_CAP, side0=args.side0,
+                  side1=args.side1, admission='pick_window order around the player at the region centre, Chebyshev >= 2',
+                  l2_policy='inputs larger than L2 (the step reads all weights and writes all logits: >= 1 GB)',
+                  parallelism=f'dp{world}: one engine per GPU, finished columns exchanged on the host (gloo)')
+    per_step_h2d = batch.params_host.numel()
+    line = dict(metric=METRIC, value=voxels / wall, unit=UNIT, n_gpus=world, steps=forwards, warmup=args.warmup,
+                ms_per_step=wall / max(1, forwards / world) * 1e3, higher_is_better=True, scaling='strong',
+                vs_baseline=None, dtype='bf16', data='synthetic (seeded world generator, random-init N(0,0.02) weights)',
+                config=config, windows=windows, committed_voxels=voxels, seconds=wall,
+                replicas_agree=len({r['digest'] for r in ranks}) == 1,
+                e2e=dict(value=voxels / wall, unit=UNIT, h2d_bytes_per_step=per_step_h2d,
+                         d2h_bytes_per_step=None,
+                         note='the expansion is timed end to end through the public API (item building, encoding, '
+                              'steps, commits, host exchange): value and e2e are the same measurement'),
+                gpu_launches=forwards * batch.launches(),
+                clocks=clocks.summary(),
+                per_rank=[dict(rank=r['rank'], seconds=r['seconds'], sm_mhz=r['clocks'].get('sm_mhz'),
+                               reasons=r['clocks'].get('reasons'),
+                               **{k: (round(v, 3) if isinstance(v, float) else v) for k, v in r['stats'].items()})
+                          for r in ranks])
+    return line
+
+
 def main():
     args = parse()
     if args.impl == 'reference':
@@ -559,13 +637,16 @@ def main():
         return
     result = None
     try:
-        result = main_ours(args)
+        result = main_expand(args) if args.workload == 'config4' else main_ours(args)
     finally:
         import torch.distributed as dist
         if dist.is_available() and dist.is_initialized():
             dist.barrier()
             dist.destroy_process_group()
     if result is None:
+        return
+    if args.workload == 'config4':
+        print(json.dumps(result), flush=True)
         return
     line, cfg, sd, lengths = result
     # The CPU baseline runs after the process group is gone and the other ranks have returned, so no waiting rank

@@ -133,11 +133,15 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
     finishes is published as a frame packet carrying its whole cell (global ids through `raw_map`) followed by its
     `window_commit` packet, as the reference's worker does without progressive frames."""
     slot_cell = [None] * engine.slots
-    stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0)
+    stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0, step_seconds=0.0,
+                 item_seconds=0.0, arm_seconds=0.0, exchange_seconds=0.0)
+    clock = time.perf_counter
     for _ in range(max_rounds):
         finished = []
         if any(c is not None for c in slot_cell):
+            t = clock()
             results = engine.step()
+            stats['step_seconds'] += clock() - t
             stats['forwards'] += 1
             for i, (record, _commit) in results.items():
                 if record is not None and slot_cell[i] is not None:
@@ -148,17 +152,23 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
                     stats['windows'] += 1
                     stats['committed_voxels'] += int(tokens.size)
                     slot_cell[i] = None
-        t0 = time.perf_counter()
+        t0 = clock()
         free_slots = [i for i, c in enumerate(slot_cell) if c is None]
         gathered = host_exchange((finished, len(free_slots)), group)
+        stats['exchange_seconds'] += clock() - t0
         for commits, _ in gathered:
             expansion.apply(commits)
         picks = expansion.admit([n for _, n in gathered])
         for cell in picks[rank]:
             i = free_slots.pop(0)
-            engine.arm(i, expansion.seed(cell), expansion.cap, item=expansion.item(cell), target=cell)
+            t = clock()
+            item = expansion.item(cell)
+            t1 = clock()
+            engine.arm(i, expansion.seed(cell), expansion.cap, item=item, target=cell)
+            stats['item_seconds'] += t1 - t
+            stats['arm_seconds'] += clock() - t1
             slot_cell[i] = cell
-        stats['admission_seconds'] += time.perf_counter() - t0
+        stats['admission_seconds'] += clock() - t0
         stats['rounds'] += 1
         if expansion.done:
             break
