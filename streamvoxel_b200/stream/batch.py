@@ -69,6 +69,7 @@ class SlotBatch:
         self.state = [dict(phase='idle') for _ in range(b)]
         self.noise = None
         self.generators = [None] * b
+        self._inflight = None   # (marking, rows, solid, slots in the step, event) of a launched, uncollected step
         if sampling == 'parity':
             self.min_cap = int(min_cap)
             self.noise_capacity = max(counts(self.total, self.min_cap, 'quartercos'))
@@ -110,14 +111,20 @@ class SlotBatch:
         return self.forward.engine.launches(self.slots) + EASE_LAUNCHES
 
     # -- windows
-    def arm(self, slot, seed, cap, item=None, target=(), *, order=None):
+    def arm(self, slot, seed, cap, item=None, target=(), *, order=None, wait=True):
         """Start a window in `slot` (`LowEntropyLastSlot.arm`, `slot.py:86-103`); `item` loads its conditions.
-        `order` replaces the block permutation drawn from Generator(seed + 9173)."""
+        `order` replaces the block permutation drawn from Generator(seed + 9173). With `wait=False` the condition
+        encode stays on the engine's side stream, joined by the next `launch` (the reference's `load_slot` then
+        `wait_loads` before the replay, `streamvoxel/stream/fast_ops.py:252-264`): a slot may be armed while another
+        step is in flight, since the side stream first waits for the work already enqueued."""
         if self.sampling == 'parity' and int(cap) < self.min_cap:
             raise ValueError(f'cap {cap} is below min_cap {self.min_cap}, which sized the parity noise buffer')
+        if self._inflight is not None and slot in self._inflight[3]:
+            raise ValueError(f'slot {slot} takes part in the step in flight; collect it first')
         if item is not None:
             self.forward.load_slot(slot, item)
-            self.forward.wait_loads()
+            if wait:
+                self.forward.wait_loads()
         else:
             self.forward.tokens[slot].fill_(self.classes)
         if order is None:
@@ -201,6 +208,15 @@ class SlotBatch:
 
     def step(self):
         """One forward for every armed slot with its EASE step; returns {slot: (record|None, commit|None)}."""
+        self.launch()
+        return self.collect()
+
+    def launch(self):
+        """Enqueue one step (the step graph, the marking launches and the D2H copies of its results) without waiting
+        for it; `collect` waits and does the host bookkeeping. Between the two the host may arm idle slots."""
+        if self._inflight is not None:
+            raise RuntimeError('a step is already in flight; collect it first')
+        self.forward.wait_loads()
         marking = [i for i, st in enumerate(self.state) if st['phase'] == 'marking']
         rows = self._rows()
         solid = [i for i, r in enumerate(rows) if r[0] > 0]
@@ -216,7 +232,17 @@ class SlotBatch:
             self.host_values[:, :kmax].copy_(self.values[:, :kmax], non_blocking=True)
         self.host_small[:self.slots].copy_(self.status, non_blocking=True)
         self.host_small[self.slots:].copy_(self.last_count, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
+        event = torch.cuda.Event()
+        event.record(torch.cuda.current_stream(self.device))
+        self._inflight = (marking, rows, solid, set(marking) | set(solid), event)
+
+    def collect(self):
+        """Wait for the launched step and book its commits; returns {slot: (record|None, commit|None)}."""
+        if self._inflight is None:
+            raise RuntimeError('no step in flight')
+        marking, rows, solid, _, event = self._inflight
+        self._inflight = None
+        event.synchronize()
         results = {}
         for i in self._after_mark(marking, self.host_small[self.slots:].tolist()):
             results[i] = (self._finish(i), None)

@@ -127,11 +127,20 @@ def host_exchange(obj, group=None):
     return out
 
 
-def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=None, raw_map=None):
+def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=None, raw_map=None, pipelined=None):
     """Drive `engine` (a `SlotBatch`, or any object with `slots`, `arm`, `step` and `column`) until the region is
     committed. Returns statistics of this rank. With a `publisher` (`wire.Publisher`), every window this rank
     finishes is published as a frame packet carrying its whole cell (global ids through `raw_map`) followed by its
-    `window_commit` packet, as the reference's worker does without progressive frames."""
+    `window_commit` packet, as the reference's worker does without progressive frames.
+
+    Pipelined (the default for an engine with `launch`/`collect`): the windows admitted after a step are built and
+    armed while the next step runs on the GPU (their condition encode joins before the step after), so the host's
+    admission work overlaps the device; a slot whose window finished sits out one step."""
+    if pipelined is None:
+        pipelined = hasattr(engine, 'launch') and hasattr(engine, 'collect')
+    if pipelined:
+        return _run_pipelined(engine, expansion, rank, group=group, max_rounds=max_rounds, publisher=publisher,
+                              raw_map=raw_map)
     slot_cell = [None] * engine.slots
     stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0, step_seconds=0.0,
                  item_seconds=0.0, arm_seconds=0.0, exchange_seconds=0.0)
@@ -168,6 +177,65 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
             stats['item_seconds'] += t1 - t
             stats['arm_seconds'] += clock() - t1
             slot_cell[i] = cell
+        stats['admission_seconds'] += clock() - t0
+        stats['rounds'] += 1
+        if expansion.done:
+            break
+        if not expansion.inflight:
+            raise RuntimeError('expansion blocked: no window in flight and none admissible')
+    stats['blocked_admissions'] = expansion.blocked_admissions
+    return stats
+
+
+def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw_map):
+    """`run` with the admission of step t's finished windows overlapping step t + 1 on the device."""
+    slot_cell = [None] * engine.slots
+    to_arm = []   # (slot, cell) admitted after the last collect, armed while the next step runs
+    stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0, step_seconds=0.0,
+                 item_seconds=0.0, arm_seconds=0.0, exchange_seconds=0.0, collect_wait_seconds=0.0, pipelined=True)
+    clock = time.perf_counter
+    for _ in range(max_rounds):
+        running = [i for i, c in enumerate(slot_cell) if c is not None and all(i != s for s, _ in to_arm)]
+        launched = False
+        if running:
+            t = clock()
+            engine.launch()
+            stats['step_seconds'] += clock() - t
+            launched = True
+        for i, cell in to_arm:   # host work that overlaps the step in flight
+            t = clock()
+            item = expansion.item(cell)
+            t1 = clock()
+            engine.arm(i, expansion.seed(cell), expansion.cap, item=item, target=cell, wait=False)
+            stats['item_seconds'] += t1 - t
+            stats['arm_seconds'] += clock() - t1
+        to_arm = []
+        finished = []
+        if launched:
+            t = clock()
+            results = engine.collect()
+            stats['collect_wait_seconds'] += clock() - t
+            stats['forwards'] += 1
+            for i, (record, _commit) in results.items():
+                if record is not None and slot_cell[i] is not None:
+                    tokens = engine.column(i)
+                    finished.append((slot_cell[i], tokens))
+                    if publisher is not None:
+                        _publish(publisher, record, slot_cell[i], tokens, i, rank, expansion.ranks, raw_map)
+                    stats['windows'] += 1
+                    stats['committed_voxels'] += int(tokens.size)
+                    slot_cell[i] = None
+        t0 = clock()
+        free_slots = [i for i, c in enumerate(slot_cell) if c is None]
+        gathered = host_exchange((finished, len(free_slots)), group)
+        stats['exchange_seconds'] += clock() - t0
+        for commits, _ in gathered:
+            expansion.apply(commits)
+        picks = expansion.admit([n for _, n in gathered])
+        for cell in picks[rank]:
+            i = free_slots.pop(0)
+            slot_cell[i] = cell
+            to_arm.append((i, cell))
         stats['admission_seconds'] += clock() - t0
         stats['rounds'] += 1
         if expansion.done:

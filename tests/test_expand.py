@@ -38,6 +38,29 @@ class FakeEngine:
         return np.random.default_rng(self.seeds[i]).integers(0, 32, (64, 16, 16)).astype(np.int16)
 
 
+class PipelinedFakeEngine(FakeEngine):
+    """`FakeEngine` with the `launch` / `collect` split: arming a slot of the step in flight is an error, and a
+    window armed after `launch` takes its first forward in the next step."""
+
+    def __init__(self, slots, steps=3):
+        super().__init__(slots, steps)
+        self.inflight = None
+
+    def arm(self, slot, seed, cap, item=None, target=(), wait=True):
+        assert self.inflight is None or slot not in self.inflight
+        super().arm(slot, seed, cap, item, target)
+
+    def launch(self):
+        assert self.inflight is None
+        self.inflight = {i for i in range(self.slots) if self.left[i]}
+        self.pending = super().step()
+
+    def collect(self):
+        assert self.inflight is not None
+        self.inflight = None
+        return self.pending
+
+
 class CheckedExpansion(expand.Expansion):
     def admit(self, free):
         before = set(self.committed)
@@ -85,6 +108,17 @@ def test_single_rank_expansion_commits_the_region():
     assert exp.done and not exp.inflight
     assert stats['windows'] == 100 - 16 and len(exp.committed) == 100
     assert all(l1 >= 1 for _, l1, _ in engine.armed)
+
+
+def test_pipelined_expansion_commits_the_same_world():
+    """Admission overlapping the step in flight (`launch` / arm idle slots / `collect`) commits every window once
+    and the same columns as the serial driver."""
+    serial, _, _ = _run(1, 4)
+    exp = _setup(1, 4)
+    engine = PipelinedFakeEngine(4)
+    stats = expand.run(engine, exp, 0)
+    assert stats['pipelined'] and exp.done and not exp.inflight
+    assert stats['windows'] == 100 - 16 and exp.digest() == serial.digest()
 
 
 def _worker(rank, world, port, path):
