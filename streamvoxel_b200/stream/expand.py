@@ -190,31 +190,41 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
 def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw_map):
     """`run` with the admission of step t's finished windows overlapping step t + 1 on the device."""
     slot_cell = [None] * engine.slots
-    to_arm = []   # (slot, cell) admitted after the last collect, armed while the next step runs
+    to_arm = []   # (slot, cell) admitted, not yet armed: armed while a step runs, as many as fit in its duration
     stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0, step_seconds=0.0,
-                 item_seconds=0.0, arm_seconds=0.0, exchange_seconds=0.0, collect_wait_seconds=0.0, pipelined=True)
+                 item_seconds=0.0, arm_seconds=0.0, exchange_seconds=0.0, collect_wait_seconds=0.0, pipelined=True,
+                 deferred_arms=0)
     clock = time.perf_counter
+    step_time = 0.0   # running estimate of one step's wall time (launch to collected)
     for _ in range(max_rounds):
-        running = [i for i, c in enumerate(slot_cell) if c is not None and all(i != s for s, _ in to_arm)]
+        waiting = {s for s, _ in to_arm}
+        running = [i for i, c in enumerate(slot_cell) if c is not None and i not in waiting]
         launched = False
+        began = clock()
         if running:
-            t = clock()
             engine.launch()
-            stats['step_seconds'] += clock() - t
+            stats['step_seconds'] += clock() - began
             launched = True
-        for i, cell in to_arm:   # host work that overlaps the step in flight
+        # Host work that overlaps the step in flight: arm the admitted windows while the step still runs (at least
+        # one per step; all of them when nothing runs), so a burst of finishing windows does not idle the device.
+        armed = 0
+        while to_arm and (not launched or armed == 0 or clock() - began < 0.8 * step_time):
+            i, cell = to_arm.pop(0)
             t = clock()
             item = expansion.item(cell)
             t1 = clock()
             engine.arm(i, expansion.seed(cell), expansion.cap, item=item, target=cell, wait=False)
             stats['item_seconds'] += t1 - t
             stats['arm_seconds'] += clock() - t1
-        to_arm = []
+            armed += 1
+        stats['deferred_arms'] += len(to_arm)
         finished = []
         if launched:
             t = clock()
             results = engine.collect()
             stats['collect_wait_seconds'] += clock() - t
+            elapsed = clock() - began
+            step_time = elapsed if step_time == 0.0 else 0.9 * step_time + 0.1 * elapsed
             stats['forwards'] += 1
             for i, (record, _commit) in results.items():
                 if record is not None and slot_cell[i] is not None:
