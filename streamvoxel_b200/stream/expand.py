@@ -222,9 +222,11 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
         if launched:
             t = clock()
             results = engine.collect()
-            stats['collect_wait_seconds'] += clock() - t
-            elapsed = clock() - began
-            step_time = elapsed if step_time == 0.0 else 0.9 * step_time + 0.1 * elapsed
+            wait = clock() - t
+            stats['collect_wait_seconds'] += wait
+            if wait > 1e-4:   # the device, not the host's arming, set this step's duration
+                elapsed = clock() - began
+                step_time = elapsed if step_time == 0.0 else 0.9 * step_time + 0.1 * elapsed
             stats['forwards'] += 1
             for i, (record, _commit) in results.items():
                 if record is not None and slot_cell[i] is not None:
