@@ -11,6 +11,9 @@ input/output fixtures to `tests/golden/*.npz`; `tests/test_oracle_golden.py` che
 * `sampler`  - EASE sampler: entropy, 4^3 block-quota selection, low-entropy-last marking, quartercos quotas,
                the categorical draw rule, Philox4x32-10, and a whole-window slot.
 * `eval_samplers` - the evaluation decoders (random / entropy / mixed / block selections, every schedule).
-* `model`    - time-free DiT + compact ControlNet forward (fp32 torch on the CPU, optional bf16 rounding points).
-* `synth`    - seeded synthetic columns, conditions and logits with the BASELINE shapes.
+* `model`    - time-free DiT + compact ControlNet forward (fp32 torch on the CPU, optional bf16 rounding points)
+               and the condition encoder.
+
+The seeded synthetic inputs (columns, conditions, logits with the BASELINE shapes) are the product's own
+`streamvoxel_b200.synth`, shared by the tests, the bench and the oracle checks.
 """
