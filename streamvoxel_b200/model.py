@@ -362,34 +362,75 @@ class PreparedModel:
         return ops.layernorm_affine(down[:rows], 1e-6, pre=self.level_embed[1]).view(n, count, cfg.d)
 
     def _biome(self, biomes, bio_positions):
-        """`_biome_condition` (`streaming_controlnet.py:196-219`)."""
-        cfg, sd = self.cfg, self.sd
+        """`_biome_condition` (`streaming_controlnet.py:196-219`) on libsvx kernels: the biome embedding rows gathered
+        (bf16, the cast autocast makes for the down-conv), the p^3 stride-p down-conv as one GEMM over the gathered
+        rows with its bf16 bias add in the residual epilogue, then the type + size embeddings and the no-affine
+        LayerNorm (`svx_layernorm_affine` with `pre`). The division by the window fraction of a padded block
+        (1, 1/2 or 1/4 for p = 4: always a power of two) is applied to the gathered rows and to the bias rows, which is
+        exact and commutes with every bf16 rounding, so the result equals bf16(bf16(conv) + bias) / fraction. The
+        pooled key positions depend only on the window geometry and are computed once. Returns (values [T, d] bf16,
+        positions [T, 3])."""
+        cfg, dev = self.cfg, self.device
         height = cfg.voxel_shape[0]
-        if cfg.biome_halo == 16 and cfg.biome_patch == 1:
-            values = F.embedding(biomes.reshape(-1), sd['biome_embed.weight'])
-            positions = bio_positions
-        else:
-            labels = biomes.reshape(1, height // 4, 12, 12)
-            positions = bio_positions.reshape(1, height // 4, 12, 12, 3)
+        if not hasattr(self, '_biome_plan'):
+            self._biome_plan = self._plan_biome(bio_positions)
+        index, scale, positions, bias_rows, tokens = self._biome_plan
+        labels = biomes.reshape(-1)
+        if cfg.biome_halo != 16 or cfg.biome_patch != 1:
+            labels = biomes.reshape(height // 4, 12, 12)
             if cfg.biome_halo == 4:
-                labels, positions = labels[:, :, 3:9, 3:9], positions[:, :, 3:9, 3:9]
-            values = F.embedding(labels, sd['biome_embed.weight']).permute(0, 4, 1, 2, 3)
-            p = cfg.biome_patch
-            if p > 1:
-                pad = (-labels.shape[-1]) % p
-                mask = values.new_ones((1, 1, height // 4, labels.shape[-2], labels.shape[-1]))
-                fraction = F.avg_pool3d(F.pad(mask, (0, pad, 0, pad)), p, p)
-                down = F.conv3d(F.pad(values, (0, pad, 0, pad)), sd['biome_down.weight'], None, stride=p)
-                down = down + sd['biome_down.bias'].to(down.dtype)[:, None, None, None]
-                values = down / fraction
-                coords = F.avg_pool3d(F.pad(positions.permute(0, 4, 1, 2, 3), (0, pad, 0, pad)), p, p) / fraction
-                positions = coords.flatten(2).transpose(1, 2)[0]
-            else:
-                positions = positions.reshape(-1, 3)
-            values = values.flatten(2).transpose(1, 2)[0]
-        size = sd['biome_size8'] if cfg.biome_patch == 2 else sd['size_embed.weight'][int(cfg.biome_patch == 4)]
-        values = values + sd['type_embed.weight'][2] + size
-        return F.layer_norm(values.float(), (cfg.d,), eps=1e-6), positions
+                labels = labels[:, 3:9, 3:9]
+            labels = labels.reshape(-1)
+        # padded grid cells point at the zero row appended to the table
+        padded = torch.cat((labels, labels.new_full((1,), cfg.biome_classes)))
+        rows = self._biome_table[padded[index]]                     # [T or rows, p^3, d] bf16
+        if cfg.biome_patch == 1:
+            x = rows.reshape(tokens, cfg.d)
+        else:
+            p3 = cfg.biome_patch ** 3
+            a = (rows * scale[:, None, None]).reshape(-1, p3 * cfg.d).contiguous()
+            x = ops.gemm(a, self._biome_down_w, self.zero_bias, _lib.EPI_RESIDUAL, residual=bias_rows)[:tokens]
+        return ops.layernorm_affine(x.contiguous(), 1e-6, pre=self._biome_pre), positions
+
+    def _plan_biome(self, bio_positions):
+        """Constants of the biome branch (window geometry only): the gather index of every down-conv input row, the
+        1/fraction scale per output token, the pooled key positions and the bias rows (bias / fraction, bf16)."""
+        cfg, dev, sd = self.cfg, self.device, self.sd
+        height, p = cfg.voxel_shape[0], cfg.biome_patch
+        table = torch.cat((sd['biome_embed.weight'], torch.zeros((1, cfg.d), device=dev)), 0)
+        self._biome_table = table.to(torch.bfloat16)
+        size = sd['biome_size8'] if p == 2 else sd['size_embed.weight'][int(p == 4)]
+        self._biome_pre = (sd['type_embed.weight'][2] + size).contiguous()
+        if cfg.biome_halo == 16 and p == 1:
+            n = bio_positions.reshape(-1, 3).shape[0]
+            return torch.arange(n, device=dev), None, bio_positions.reshape(-1, 3), None, n
+        side = 6 if cfg.biome_halo == 4 else 12
+        positions = bio_positions.reshape(height // 4, 12, 12, 3)
+        if cfg.biome_halo == 4:
+            positions = positions[:, 3:9, 3:9]
+        if p == 1:
+            n = height // 4 * side * side
+            return torch.arange(n, device=dev), None, positions.reshape(-1, 3), None, n
+        pad = (-side) % p
+        grid = side + pad
+        cells = torch.arange(height // 4 * side * side, device=dev).reshape(height // 4, side, side)
+        cells = F.pad(cells, (0, pad, 0, pad), value=height // 4 * side * side)   # the zero row
+        gy, gz = height // 4 // p, grid // p
+        blocks = cells.reshape(gy, p, gz, p, gz, p).permute(0, 2, 4, 1, 3, 5).reshape(gy * gz * gz, p ** 3)
+        valid = F.pad(torch.ones((1, 1, height // 4, side, side), device=dev), (0, pad, 0, pad))
+        fraction = F.avg_pool3d(valid, p, p).reshape(-1)
+        coords = F.avg_pool3d(F.pad(positions.permute(3, 0, 1, 2)[None], (0, pad, 0, pad)), p, p)[0]
+        pooled = (coords / fraction.reshape(gy, gz, gz)[None]).reshape(3, -1).t().contiguous()
+        tokens = len(blocks)
+        rows = -(-tokens // 256) * 256
+        index = torch.full((rows, p ** 3), height // 4 * side * side, device=dev, dtype=torch.long)
+        index[:tokens] = blocks
+        scale = torch.ones(rows, device=dev)
+        scale[:tokens] = 1.0 / fraction
+        self._biome_down_w = down_conv_weight(sd['biome_down.weight'])
+        bias = sd['biome_down.bias'].to(torch.bfloat16).float()
+        bias_rows = (bias[None] * scale[:, None]).to(torch.bfloat16).contiguous()
+        return index, scale.to(torch.bfloat16), pooled, bias_rows, tokens
 
 
 class L2TokenCache:
