@@ -446,7 +446,11 @@ class L2TokenCache:
         self.hits += len(keys) - len(missing)
         self.misses += len(missing)
         if missing:
-            fresh = encode(np.asarray(blocks)[missing])
+            try:   # an array or a lazy column stack copies only the columns asked for
+                picked = np.asarray(blocks[missing])
+            except TypeError:   # a list of tiles
+                picked = np.asarray(blocks)[missing]
+            fresh = encode(picked)
             per = len(fresh) // len(missing)
             for n, i in enumerate(missing):
                 self.entries[keys[i]] = fresh[n * per:(n + 1) * per]

@@ -16,7 +16,7 @@ import time
 
 import numpy as np
 
-from .scheduler import make_item, member_shares, separated, window_seed
+from .scheduler import fast_item, member_shares, separated, window_seed
 
 
 class Expansion:
@@ -92,7 +92,8 @@ class Expansion:
         return picks
 
     def item(self, cell):
-        return make_item(self.committed, cell, self.biomes, self.spec, self.world, self.cap, self.l2_cap)
+        """The window's `Item` (`make_item`'s result; L2 tiles stacked lazily, see `scheduler.fast_item`)."""
+        return fast_item(self.committed, cell, self.biomes, self.spec, self.world, self.cap, self.l2_cap)
 
     def seed(self, cell):
         return window_seed(self.world, *cell)

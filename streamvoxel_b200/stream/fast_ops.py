@@ -94,7 +94,7 @@ class FastSlotForward:
             self.l2_cache = L2TokenCache()
         layers = self.model.encode_item(item.l1_blocks, item.l1_xz, item.l2_blocks, item.l2_xz, item.biomes,
                                         l2_keys=keys, cache=self.l2_cache)
-        prefix = len(np.asarray(item.l2_blocks)) * self.l2_tokens
+        prefix = len(item.l2_blocks) * self.l2_tokens
         if prefix > self.prefix_len or layers[0][0].shape[1] - prefix > self.local_len:
             raise ValueError('Condition exceeds the slot capacity')
         return layers

@@ -125,6 +125,72 @@ def biome_volume(biomes, z, x, spec):
     return out
 
 
+def nearest_cells(cells, target, count):
+    """The `count` committed cells nearest to `target` by (squared distance, cell), as `make_item` picks its L2 tiles
+    (`scheduler.py:114`), found by growing a square around the target instead of sorting the whole snapshot: once
+    the square of radius r holds at least `count` cells within distance r, every cell at or below the count-th
+    distance lies inside it (ties included), so sorting the square's cells gives the same answer."""
+    z, x = target
+    total = len(cells)
+    r = max(1, int((count / 3.0) ** 0.5))
+    while True:
+        box = [(a, b) for a in range(z - r, z + r + 1) for b in range(x - r, x + r + 1) if (a, b) in cells]
+        within = sum(1 for a, b in box if (a - z) ** 2 + (b - x) ** 2 <= r * r)
+        if within >= count or len(box) == total:
+            box.sort(key=lambda c: ((c[0] - z) ** 2 + (c[1] - x) ** 2, c))
+            return box[:count]
+        r += 1
+
+
+class ColumnStack:
+    """The L2 tiles of an item as a lazy stack over the committed snapshot: `len`, fancy indexing (`stack[[i, j]]`)
+    and `np.asarray` give what the stacked [n, H, T, T] array would, but only the columns asked for are copied (the
+    encoder asks only for columns its L2 cache has not seen)."""
+
+    def __init__(self, cells, keys, shape):
+        self.cells, self.keys, self.shape_one = cells, list(keys), tuple(shape)
+
+    def __len__(self):
+        return len(self.keys)
+
+    @property
+    def shape(self):
+        return (len(self.keys),) + self.shape_one
+
+    def __getitem__(self, index):
+        picks = np.arange(len(self.keys))[index]
+        if np.ndim(picks) == 0:
+            return np.asarray(self.cells[self.keys[int(picks)]], np.int16)
+        if len(picks) == 0:
+            return np.zeros((0,) + self.shape_one, np.int16)
+        return np.stack([np.asarray(self.cells[self.keys[int(i)]], np.int16) for i in picks])
+
+    def __array__(self, dtype=None, copy=None):
+        out = self[np.arange(len(self.keys))]
+        return out if dtype is None else out.astype(dtype)
+
+
+def fast_item(cells, target, biomes, spec, world, cap, l2_cap):
+    """`make_item` with the same result for a driver that builds an item per window from a large snapshot: the L2
+    cells by `nearest_cells` and the L2 tiles as a `ColumnStack` (the L1 tiles, positions, seed and biome crop are
+    built exactly as `make_item` builds them)."""
+    z, x = target
+    if target in cells:
+        raise ValueError('Target already committed')
+    near = sorted((a, b) for a in (z - 1, z, z + 1) for b in (x - 1, x, x + 1) if (a, b) != target and (a, b) in cells)
+    if not near:
+        raise ValueError('Target has no committed neighbor')
+    far = sorted(nearest_cells(cells, target, l2_cap))
+    shape = (spec.height, spec.tile, spec.tile)
+    l1 = np.stack([np.asarray(cells[c], np.int16) for c in near])
+    if l1.shape[1:] != shape:
+        raise ValueError('Condition tile has the wrong shape')
+    return Item(id=f'{z}_{x}', seed=window_seed(world, z, x), steps=int(cap), temperature=1.0,
+                l1_blocks=l1, l1_xz=_relative_xz(near, z, x), l2_blocks=ColumnStack(cells, far, shape),
+                l2_xz=_relative_xz(far, z, x), biomes=biome_volume(biomes, z, x, spec), known=None,
+                l2_keys=[(world,) + c for c in far])
+
+
 def _relative_xz(cells, z, x):
     return np.asarray([[(b - x) * 16, (a - z) * 16] for a, b in cells], np.int64).reshape(-1, 2)
 

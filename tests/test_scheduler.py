@@ -68,3 +68,31 @@ def test_admission_properties():
             shares = [sch.rank_share(batch, ranks, r) for r in range(ranks)]
             assert sum(shares) == batch and shares == sorted(shares, reverse=True)
             assert [sch.member_shares(batch, [(r, 99, 1) for r in range(ranks)])[r] for r in range(ranks)] == shares
+
+
+def test_fast_item_equals_make_item():
+    """The expansion driver's item (`fast_item`: L2 cells by a growing square, L2 tiles stacked lazily) is the
+    reference rule's item (`make_item`) field for field, on random committed blobs and targets."""
+    from streamvoxel_b200.stream.condition import ModelSpec
+    from streamvoxel_b200.stream.scheduler import fast_item, make_item, ready_cells
+    spec = ModelSpec(height=16, tile=16, num_classes=8, biome_classes=16, biome_halo=4, y_origin=-64.0)
+    rng = np.random.default_rng(3)
+    biomes = rng.integers(0, 16, (4, 66, 66)).astype(np.int64)
+    for case in range(40):
+        cells, z, x = set(), 0, 0
+        for _ in range(int(rng.integers(1, 200))):
+            cells.add((z, x))
+            dz, dx = ((1, 0), (-1, 0), (0, 1), (0, -1))[int(rng.integers(0, 4))]
+            z, x = z + dz, x + dx
+        snapshot = {c: rng.integers(0, 9, (16, 16, 16)).astype(np.int16) for c in cells}
+        frontier = sorted(ready_cells(cells))
+        target = frontier[int(rng.integers(0, len(frontier)))]
+        cap = int(rng.choice([1, 5, 12, 81]))
+        want = make_item(snapshot, target, biomes, spec, 7, 32, cap)
+        got = fast_item(snapshot, target, biomes, spec, 7, 32, cap)
+        assert got.l2_keys == want.l2_keys and got.seed == want.seed and got.id == want.id
+        for name in ('l1_blocks', 'l1_xz', 'l2_xz', 'biomes'):
+            assert np.array_equal(getattr(got, name), getattr(want, name)), (case, name)
+        assert np.array_equal(np.asarray(got.l2_blocks), want.l2_blocks) and len(got.l2_blocks) == len(want.l2_blocks)
+        pick = [i for i in range(len(want.l2_blocks)) if i % 2]
+        assert np.array_equal(got.l2_blocks[pick], want.l2_blocks[pick])
