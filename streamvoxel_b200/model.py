@@ -147,6 +147,15 @@ def synthetic_state_dict(cfg, seed=0, std=0.02):
     return sd
 
 
+def to_device(array, device, dtype=None):
+    """A host array on `device` without blocking the host: staged in pinned memory and copied asynchronously on the
+    current stream (a copy from pageable memory would first wait for all work already queued on that stream)."""
+    host = torch.from_numpy(np.ascontiguousarray(array)) if isinstance(array, np.ndarray) else torch.as_tensor(array)
+    if dtype is not None:
+        host = host.to(dtype)
+    return host.pin_memory().to(device, non_blocking=True)
+
+
 def _bf16(t, device):
     return t.detach().to(device=device, dtype=torch.float32).to(torch.bfloat16).contiguous()
 
@@ -294,7 +303,7 @@ class PreparedModel:
             else:
                 prefix = self._l2_prefix(np.asarray(l2_blocks))
             l1 = self._encode_columns(np.asarray(l1_blocks), 0)
-            bio, bio_positions = self._biome(torch.as_tensor(np.asarray(biomes), device=dev).long(), bio_pos)
+            bio, bio_positions = self._biome(to_device(np.asarray(biomes, np.int64), dev), bio_pos)
             local = torch.cat((l1.flatten(0, 1), bio.to(torch.bfloat16)), 0)
             local_positions = torch.cat((pos1.reshape(-1, 3), bio_positions), 0)
         # Every layer's key_value linear over all condition tokens at once (prefix rows, then local rows).
@@ -311,7 +320,9 @@ class PreparedModel:
         rows = -(-n // 256) * 256
         padded = torch.zeros((rows, cfg.d), device=dev, dtype=torch.bfloat16)
         padded[:n] = tokens.to(device=dev, dtype=torch.bfloat16)
-        phase = (positions.to(dev).float()[..., None] * rope_frequencies(96).to(dev)).reshape(n, 48)
+        if not hasattr(self, '_key_freq'):
+            self._key_freq = rope_frequencies(96).to(dev)
+        phase = (positions.to(dev).float()[..., None] * self._key_freq).reshape(n, 48)
         sin = torch.zeros((rows, 48), device=dev, dtype=torch.bfloat16)
         cos = torch.zeros((rows, 48), device=dev, dtype=torch.bfloat16)
         sin[:n], cos[:n] = phase.sin().to(torch.bfloat16), phase.cos().to(torch.bfloat16)
@@ -342,7 +353,7 @@ class PreparedModel:
         count = (height // 16) if level else cfg.patches
         if len(tokens) == 0:
             return torch.zeros((0, count, cfg.d), device=dev, dtype=torch.bfloat16)
-        t = torch.as_tensor(tokens, device=dev).to(torch.int16).contiguous()
+        t = to_device(np.asarray(tokens, np.int16), dev)
         table, bias = (self.table_l1, self.bias_l1) if level == 0 else (self.table_l2, self.bias_l2)
         n = len(t)
         if not level:
@@ -485,7 +496,7 @@ def _group_positions(l1_xz, l2_xz, height, tile, device):
     pos1 = (_centers((height // 4, tile // 4, tile // 4), 4)[None] + offsets(l1_xz)[:, None]) / 4
     pos2 = ((_centers((height // 16, 1, 1), 16)[None] + offsets(l2_xz)[:, None]) / 4).reshape(-1, 3)
     bio = (_centers((height // 4, 12, 12), 4) + np.asarray([-tile, 0, -tile], np.float32)) / 4
-    return (torch.from_numpy(pos1).to(device), torch.from_numpy(pos2).to(device), torch.from_numpy(bio).to(device))
+    return to_device(pos1, device), to_device(pos2, device), to_device(bio, device)
 
 
 class Engine:
@@ -502,6 +513,7 @@ class Engine:
                     torch.zeros((self.slots, cfg.heads, self.key_capacity, 96), **bf)) for _ in range(n_control)]
         self.lengths = torch.zeros(self.slots, dtype=torch.int32, device=dev)
         self.host_lengths = (ctypes.c_int32 * self.slots)()
+        self.pending_lengths = {}
         self.ws = {n: torch.zeros((rows, w), **bf) for n, w in
                    (('xb', cfg.d), ('xc', cfg.d), ('h', cfg.d), ('qkv', 3 * cfg.d), ('attn', cfg.d), ('mlp', cfg.mlp),
                     ('qx', cfg.d), ('ax', cfg.d))}
@@ -540,8 +552,10 @@ class Engine:
                                             ctypes.byref(self._workspace), ctypes.byref(handle)), 'svx_engine_create')
         self.handle = handle
 
-    def write_slot(self, index, layers):
-        """Copy one window's packed K/V into slot `index` (`FastSlotForward._write`, `fast_ops.py:241-250`)."""
+    def write_slot(self, index, layers, defer=False):
+        """Copy one window's packed K/V into slot `index` (`FastSlotForward._write`, `fast_ops.py:241-250`). With
+        `defer`, the slot's key length (and the attention work plans built from the lengths) is applied later by
+        `apply_lengths`, on the stream that runs the forward."""
         length = layers[0][0].shape[1]
         if length > self.key_capacity:
             raise ValueError('Condition exceeds the captured capacity')
@@ -550,8 +564,19 @@ class Engine:
             sv[index, :, :length].copy_(v)
             sk[index, :, length:].zero_()
             sv[index, :, length:].zero_()
-        self.lengths[index] = length
-        self.host_lengths[index] = length
+        self.pending_lengths[index] = length
+        if not defer:
+            self.apply_lengths()
+
+    def apply_lengths(self):
+        """Set the pending slot key lengths on the current stream and rebuild the attention plans (their copy to the
+        device waits for the work queued on this stream, so run it where no step is in flight)."""
+        if not self.pending_lengths:
+            return
+        for index, length in self.pending_lengths.items():
+            self.lengths[index] = length
+            self.host_lengths[index] = length
+        self.pending_lengths = {}
         check(_lib.load().svx_engine_set_lengths(self.handle, self.host_lengths, _lib.stream_ptr(None)),
               'svx_engine_set_lengths')
 

@@ -57,7 +57,8 @@ def ease_scores(logits, status=None, out=None):
 
 
 def ease_mark(logits, air_ids, last_eps, last=None, last_count=None):
-    """Marking forward: per-column top run of voxels with P(air) > 1 - eps. Returns (last uint8, last_count int32)."""
+    """Marking forward: per-column top run of voxels with P(air) > 1 - eps. Returns (last uint8, last_count int32).
+    air_ids: a sequence of ids, or an int32 device tensor of them (no host-to-device copy per call)."""
     s, c, voxels, stride = _slots_view(logits)
     height, depth, width = logits.shape[2:]
     dev = logits.device
@@ -65,9 +66,13 @@ def ease_mark(logits, air_ids, last_eps, last=None, last_count=None):
         last = torch.empty((s, height, depth, width), device=dev, dtype=torch.uint8)
     if last_count is None:
         last_count = torch.empty(s, device=dev, dtype=torch.int32)
-    air = torch.as_tensor(list(air_ids), dtype=torch.int32, device=dev)
+    if isinstance(air_ids, torch.Tensor) and air_ids.is_cuda:
+        air = air_ids
+        assert air.dtype == torch.int32 and air.is_contiguous()
+    else:
+        air = torch.as_tensor(list(air_ids), dtype=torch.int32, device=dev)
     check(_lib.load().svx_ease_mark(ptr(logits), _dtype_code(logits), s, c, height, depth, width, stride, ptr(air),
-                                    len(air_ids), float(last_eps), ptr(last), ptr(last_count), stream_ptr()),
+                                    len(air), float(last_eps), ptr(last), ptr(last_count), stream_ptr()),
           'svx_ease_mark')
     return last, last_count
 

@@ -51,6 +51,7 @@ class SlotBatch:
         self.air_ids, self.air_token, self.last_eps = tuple(air_ids), int(air_token), float(last_eps)
         dev, b = self.device, self.slots
         self.blocks = self.total // 64
+        self.air_dev = torch.as_tensor(self.air_ids, dtype=torch.int32, device=dev)
         self.params = torch.zeros(b * ops.STEP_DTYPE.itemsize, dtype=torch.uint8, device=dev)
         self.params_host = torch.zeros(b * ops.STEP_DTYPE.itemsize, dtype=torch.uint8, pin_memory=True)
         self.pos = torch.zeros((b, self.blocks), dtype=torch.int32, device=dev)
@@ -166,7 +167,7 @@ class SlotBatch:
             while n < len(slots) and slots[n] == slots[0] + n:
                 n += 1
             lo, hi = slots[0], slots[0] + n
-            ops.ease_mark(logits[lo:hi], self.air_ids, self.last_eps, last=self.last[lo:hi],
+            ops.ease_mark(logits[lo:hi], self.air_dev, self.last_eps, last=self.last[lo:hi],
                           last_count=self.last_count[lo:hi])
             slots = slots[n:]
 

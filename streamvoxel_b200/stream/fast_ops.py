@@ -100,14 +100,20 @@ class FastSlotForward:
         return layers
 
     def load_slot(self, index, item):
-        """Encode + copy on the side stream; `wait_loads` joins it before the next replay (`fast_ops.py:252-260`)."""
+        """Encode + copy on the side stream; `wait_loads` joins it before the next replay (`fast_ops.py:252-260`).
+        The encode reads only the item and the weights, so it starts at once (its host inputs go through pinned
+        memory, and the host never waits for a step in flight); the copy into the slot's K/V rows and tokens waits
+        for the work already queued on the caller's stream, and the slot's key length is applied by `wait_loads`."""
+        with torch.cuda.stream(self.side):
+            layers = self.encode(item)
         self.side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self.side):
-            self.engine.write_slot(index, self.encode(item))
+            self.engine.write_slot(index, layers, defer=True)
             self.tokens[index].fill_(self.classes)
 
     def wait_loads(self):
         torch.cuda.current_stream(self.device).wait_stream(self.side)
+        self.engine.apply_lengths()
 
     def clear_tokens(self):
         self.wait_loads()
@@ -267,6 +273,7 @@ class FastLowEntropyLastSlot(LowEntropyLastSlot):
         self.entropy_name, self.sampling = entropy, sampling
         dev = self.device
         blocks = self.total // 64
+        self.air_dev = torch.as_tensor(self.air_ids, dtype=torch.int32, device=dev)
         self.last_static = torch.zeros((1, *self.shape), dtype=torch.uint8, device=dev)
         self.last_count_dev = torch.zeros(1, dtype=torch.int32, device=dev)
         self.pos = torch.zeros((1, blocks), dtype=torch.int32, device=dev)
@@ -297,7 +304,7 @@ class FastLowEntropyLastSlot(LowEntropyLastSlot):
     def mark(self, logits):
         """Marking forward (`slot.py:124-136`): the last mask on the device, one host read of its count."""
         self.nfe += 1
-        ops.ease_mark(logits[None], self.air_ids, self.last_eps, last=self.last_static, last_count=self.last_count_dev)
+        ops.ease_mark(logits[None], self.air_dev, self.last_eps, last=self.last_static, last_count=self.last_count_dev)
         self.last_count = int(self.last_count_dev.item())
         self.quotas = low_entropy_last_quotas(self.total, self.cap, self.last_count, 'quartercos')
         self.phase = 'solid'
