@@ -64,8 +64,11 @@ class SlotBatch:
         self.status = torch.zeros(b, dtype=torch.int32, device=dev)
         self.values = torch.zeros((b, self.total), dtype=torch.int16, device=dev)
         self.workspace = ops.select_workspace(b, self.total, dev)
-        self.host_index = torch.zeros((b, self.total), dtype=torch.int32, pin_memory=True)
-        self.host_values = torch.zeros((b, self.total), dtype=torch.int16, pin_memory=True)
+        # Flat pinned staging for the commits: a step's [slots, kmax] copy lands in the first slots * kmax entries as
+        # one contiguous block (a strided pinned destination would make the copy wait on the host).
+        self.host_index_flat = torch.zeros(b * self.total, dtype=torch.int32, pin_memory=True)
+        self.host_values_flat = torch.zeros(b * self.total, dtype=torch.int16, pin_memory=True)
+        self.host_index = self.host_values = None   # [slots, kmax] views of the step in flight
         self.host_small = torch.zeros(2 * b, dtype=torch.int32, pin_memory=True)
         self.state = [dict(phase='idle') for _ in range(b)]
         self.noise = None
@@ -229,8 +232,10 @@ class SlotBatch:
         self._mark(marking)
         kmax = max([r[0] for r in rows] + [0])
         if kmax:
-            self.host_index[:, :kmax].copy_(self.index[:, :kmax], non_blocking=True)
-            self.host_values[:, :kmax].copy_(self.values[:, :kmax], non_blocking=True)
+            self.host_index = self.host_index_flat[:self.slots * kmax].view(self.slots, kmax)
+            self.host_values = self.host_values_flat[:self.slots * kmax].view(self.slots, kmax)
+            self.host_index.copy_(self.index[:, :kmax], non_blocking=True)
+            self.host_values.copy_(self.values[:, :kmax], non_blocking=True)
         self.host_small[:self.slots].copy_(self.status, non_blocking=True)
         self.host_small[self.slots:].copy_(self.last_count, non_blocking=True)
         event = torch.cuda.Event()
