@@ -8,7 +8,8 @@ float64 accumulation (each rounded to bf16 at the same points). This pins the ba
 tolerance (`tests/test_gpu_engine.py`): the bound sits at the noise floor of bf16 forwards, so a one-ppm allowance
 there measures the kernels, not a defect.
 """
-import numpy as np
+import os
+
 import pytest
 import torch
 import torch.nn.functional as F
@@ -31,19 +32,26 @@ class _Float64Accumulation(om.Precision):
         return ((p.float().bfloat16().double() @ v) / p.sum(-1, keepdim=True)).to(torch.bfloat16).float()
 
 
+CONFIG5 = pytest.mark.skipif(not os.environ.get('SVX_NOISE_FLOOR_CONFIG5'),
+                             reason='the config-5 floor takes minutes on the CPU; set SVX_NOISE_FLOOR_CONFIG5=1')
+
+
 @pytest.mark.slow
-def test_two_valid_bf16_forwards_differ_near_the_bound(monkeypatch):
+@pytest.mark.parametrize('name', ['config2', pytest.param('config5', marks=CONFIG5)])
+def test_two_valid_bf16_forwards_differ_near_the_bound(monkeypatch, name):
+    """config 2 (the engine's full-size test window, k = 2) and config 5 (d = 1152, 24 + 24 layers; window k = 3)."""
     from streamvoxel_b200 import model as sm, synth
     from streamvoxel_b200.stream.condition import ModelSpec
-    cfg = sm.dit_b4_control()
+    cfg = sm.dit_b4_control() if name == 'config2' else sm.dit_l4_control()
     sd = sm.synthetic_state_dict(cfg, seed=0)
     spec = ModelSpec.of(cfg)
     cfgd = dict(num_classes=cfg.classes, voxel_shape=cfg.voxel_shape, patch_size=4, depth=cfg.depth,
                 num_heads=cfg.heads, y_range=cfg.y_range, layer_indices=list(cfg.layer_indices),
                 biome_halo=cfg.biome_halo, biome_patch=cfg.biome_patch)
-    item = synth.item(701, spec, k=2)
+    item = synth.item(701, spec, k=2) if name == 'config2' else synth.item(711, spec, k=3)
     kv = om.encode_kv(sd, item.l1_blocks, item.l1_xz, item.l2_blocks, item.l2_xz, item.biomes, cfgd, bf16=True)
-    tokens = torch.from_numpy(synth.target_tokens(801, spec)[0][None]).long()
+    target = 801 if name == 'config2' else 811
+    tokens = torch.from_numpy(synth.target_tokens(target, spec)[0][None]).long()
     with torch.no_grad():
         fp32 = om.control_forward(sd, tokens, kv, cfgd, bf16=True)[0]
         monkeypatch.setattr(om, 'Precision', _Float64Accumulation)
