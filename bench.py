@@ -592,6 +592,7 @@ def main_expand(args):
         torch.cuda.synchronize(device)
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    batch.timing, batch.device_seconds = True, 0.0
     with Clocks(local) as clocks:
         barrier()
         start.record()
@@ -599,6 +600,7 @@ def main_expand(args):
         stop.record()
         barrier()
     seconds = start.elapsed_time(stop) * 1e-3
+    stats['step_device_seconds'] = batch.device_seconds   # the step graphs' own device time (the rest: gaps)
     ranks = expand.host_exchange(dict(rank=rank, seconds=seconds, stats=stats, digest=exp.digest(),
                                       clocks=clocks.summary()), group)
     if rank != 0:

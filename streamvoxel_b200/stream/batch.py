@@ -74,6 +74,8 @@ class SlotBatch:
         self.noise = None
         self.generators = [None] * b
         self._inflight = None   # (marking, rows, solid, slots in the step, event) of a launched, uncollected step
+        # device time of the steps (step graph + marking), accumulated by `collect` when `timing` is on
+        self.timing, self.device_seconds, self._timing_events = False, 0.0, None
         if sampling == 'parity':
             self.min_cap = int(min_cap)
             self.noise_capacity = max(counts(self.total, self.min_cap, 'quartercos'))
@@ -228,8 +230,13 @@ class SlotBatch:
         self.params.copy_(self.params_host, non_blocking=True)
         self.status.zero_()
         self._draw_noise(rows)
+        if self.timing:
+            self._timing_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            self._timing_events[0].record()
         self.graph.replay()
         self._mark(marking)
+        if self.timing:
+            self._timing_events[1].record()
         kmax = max([r[0] for r in rows] + [0])
         if kmax:
             self.host_index = self.host_index_flat[:self.slots * kmax].view(self.slots, kmax)
@@ -249,6 +256,9 @@ class SlotBatch:
         marking, rows, solid, _, event = self._inflight
         self._inflight = None
         event.synchronize()
+        if self.timing and self._timing_events is not None:
+            self.device_seconds += self._timing_events[0].elapsed_time(self._timing_events[1]) * 1e-3
+            self._timing_events = None
         results = {}
         for i in self._after_mark(marking, self.host_small[self.slots:].tolist()):
             results[i] = (self._finish(i), None)
