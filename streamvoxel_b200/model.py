@@ -559,11 +559,12 @@ class Engine:
         length = layers[0][0].shape[1]
         if length > self.key_capacity:
             raise ValueError('Condition exceeds the captured capacity')
+        # Rows past the length are left as they are: the attention kernel loads only the tiles that hold the slot's
+        # keys and gives the keys past its length in the last tile a zero weight, so stale (finite) rows there never
+        # reach an output.
         for (sk, sv), (k, v) in zip(self.kv, layers):
             sk[index, :, :length].copy_(k)
             sv[index, :, :length].copy_(v)
-            sk[index, :, length:].zero_()
-            sv[index, :, length:].zero_()
         self.pending_lengths[index] = length
         if not defer:
             self.apply_lengths()

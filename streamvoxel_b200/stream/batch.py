@@ -192,6 +192,21 @@ class SlotBatch:
         """The slot's tokens as a host int16 array [Y, Z, X] (a finished window's committed column)."""
         return self.forward.tokens[slot].cpu().numpy().astype(np.int16, copy=True)
 
+    def column_async(self, slot):
+        """Enqueue the copy of the slot's tokens to pinned host memory; returns a callable that waits for that copy
+        only (not for work enqueued after it) and returns the column as `column` does."""
+        if not hasattr(self, '_column_host'):
+            self._column_host = torch.empty((self.slots, *self.shape), dtype=torch.int16, pin_memory=True)
+        host = self._column_host[slot]
+        host.copy_(self.forward.tokens[slot], non_blocking=True)
+        event = torch.cuda.Event()
+        event.record(torch.cuda.current_stream(self.device))
+
+        def result():
+            event.synchronize()
+            return host.numpy().astype(np.int16, copy=True)
+        return result
+
     def _finish(self, i):
         """`_finish` (`slot.py:166-176`): deferred voxels take air_token; returns the window record."""
         st = self.state[i]

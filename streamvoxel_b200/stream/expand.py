@@ -189,14 +189,19 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
 
 
 def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw_map):
-    """`run` with the admission of step t's finished windows overlapping step t + 1 on the device."""
+    """`run` with the host's admission work overlapping the device. One round: launch the next step at once (the
+    slots of windows that finished in the previous step sit it out), then -- while it runs -- read the finished
+    windows' columns (copies enqueued before the launch), exchange and commit them, admit new windows and arm them
+    into the free slots (as many as fit in the step's duration), then collect the step."""
     slot_cell = [None] * engine.slots
-    to_arm = []   # (slot, cell) admitted, not yet armed: armed while a step runs, as many as fit in its duration
+    to_arm = []      # (slot, cell) admitted, not yet armed
+    pending = []     # (cell, record, slot, column reader) of windows the last collect finished
     stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0, step_seconds=0.0,
                  item_seconds=0.0, arm_seconds=0.0, exchange_seconds=0.0, collect_wait_seconds=0.0, pipelined=True,
                  deferred_arms=0)
     clock = time.perf_counter
     step_time = 0.0   # running estimate of one step's wall time (launch to collected)
+    read_async = hasattr(engine, 'column_async')
     for _ in range(max_rounds):
         waiting = {s for s, _ in to_arm}
         running = [i for i, c in enumerate(slot_cell) if c is not None and i not in waiting]
@@ -206,39 +211,16 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
             engine.launch()
             stats['step_seconds'] += clock() - began
             launched = True
-        # Host work that overlaps the step in flight: arm the admitted windows while the step still runs (at least
-        # one per step; all of them when nothing runs), so a burst of finishing windows does not idle the device.
-        armed = 0
-        while to_arm and (not launched or armed == 0 or clock() - began < 0.8 * step_time):
-            i, cell = to_arm.pop(0)
-            t = clock()
-            item = expansion.item(cell)
-            t1 = clock()
-            engine.arm(i, expansion.seed(cell), expansion.cap, item=item, target=cell, wait=False)
-            stats['item_seconds'] += t1 - t
-            stats['arm_seconds'] += clock() - t1
-            armed += 1
-        stats['deferred_arms'] += len(to_arm)
-        finished = []
-        if launched:
-            t = clock()
-            results = engine.collect()
-            wait = clock() - t
-            stats['collect_wait_seconds'] += wait
-            if wait > 1e-4:   # the device, not the host's arming, set this step's duration
-                elapsed = clock() - began
-                step_time = elapsed if step_time == 0.0 else 0.9 * step_time + 0.1 * elapsed
-            stats['forwards'] += 1
-            for i, (record, _commit) in results.items():
-                if record is not None and slot_cell[i] is not None:
-                    tokens = engine.column(i)
-                    finished.append((slot_cell[i], tokens))
-                    if publisher is not None:
-                        _publish(publisher, record, slot_cell[i], tokens, i, rank, expansion.ranks, raw_map)
-                    stats['windows'] += 1
-                    stats['committed_voxels'] += int(tokens.size)
-                    slot_cell[i] = None
         t0 = clock()
+        finished = []
+        for cell, record, slot, read in pending:
+            tokens = read()
+            finished.append((cell, tokens))
+            if publisher is not None:
+                _publish(publisher, record, cell, tokens, slot, rank, expansion.ranks, raw_map)
+            stats['windows'] += 1
+            stats['committed_voxels'] += int(tokens.size)
+        pending = []
         free_slots = [i for i, c in enumerate(slot_cell) if c is None]
         gathered = host_exchange((finished, len(free_slots)), group)
         stats['exchange_seconds'] += clock() - t0
@@ -250,10 +232,41 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
             slot_cell[i] = cell
             to_arm.append((i, cell))
         stats['admission_seconds'] += clock() - t0
+        # Arm while the step still runs (at least one per step; all of them when nothing runs), so a burst of finishing
+        # windows does not idle the device.
+        armed = 0
+        while to_arm and (not launched or armed == 0 or clock() - began < 0.8 * step_time):
+            i, cell = to_arm.pop(0)
+            t = clock()
+            item = expansion.item(cell)
+            t1 = clock()
+            engine.arm(i, expansion.seed(cell), expansion.cap, item=item, target=cell, wait=False)
+            stats['item_seconds'] += t1 - t
+            stats['arm_seconds'] += clock() - t1
+            armed += 1
+        stats['deferred_arms'] += len(to_arm)
+        if launched:
+            t = clock()
+            results = engine.collect()
+            wait = clock() - t
+            stats['collect_wait_seconds'] += wait
+            if wait > 1e-4:   # the device, not the host's arming, set this step's duration
+                elapsed = clock() - began
+                step_time = elapsed if step_time == 0.0 else 0.9 * step_time + 0.1 * elapsed
+            stats['forwards'] += 1
+            for i, (record, _commit) in results.items():
+                if record is not None and slot_cell[i] is not None:
+                    if read_async:
+                        read = engine.column_async(i)
+                    else:
+                        column = engine.column(i)
+                        read = (lambda column=column: column)
+                    pending.append((slot_cell[i], record, i, read))
+                    slot_cell[i] = None
         stats['rounds'] += 1
-        if expansion.done:
+        if expansion.done and not pending:
             break
-        if not expansion.inflight:
+        if not expansion.inflight and not pending and not to_arm:
             raise RuntimeError('expansion blocked: no window in flight and none admissible')
     stats['blocked_admissions'] = expansion.blocked_admissions
     return stats
