@@ -23,6 +23,8 @@ Two drivers:
 """
 from __future__ import annotations
 
+from collections import deque
+
 import numpy as np
 import torch
 
@@ -54,6 +56,7 @@ class SlotBatch:
         self.air_dev = torch.as_tensor(self.air_ids, dtype=torch.int32, device=dev)
         self.params = torch.zeros(b * ops.STEP_DTYPE.itemsize, dtype=torch.uint8, device=dev)
         self.params_host = torch.zeros(b * ops.STEP_DTYPE.itemsize, dtype=torch.uint8, pin_memory=True)
+        self.params_host_sets = [torch.zeros_like(self.params_host).pin_memory() for _ in range(2)]
         self.pos = torch.zeros((b, self.blocks), dtype=torch.int32, device=dev)
         self.last = torch.zeros((b, *self.shape), dtype=torch.uint8, device=dev)
         self.last_count = torch.zeros(b, dtype=torch.int32, device=dev)
@@ -64,16 +67,17 @@ class SlotBatch:
         self.status = torch.zeros(b, dtype=torch.int32, device=dev)
         self.values = torch.zeros((b, self.total), dtype=torch.int16, device=dev)
         self.workspace = ops.select_workspace(b, self.total, dev)
-        # Flat pinned staging for the commits: a step's [slots, kmax] copy lands in the first slots * kmax entries as
-        # one contiguous block (a strided pinned destination would make the copy wait on the host).
-        self.host_index_flat = torch.zeros(b * self.total, dtype=torch.int32, pin_memory=True)
-        self.host_values_flat = torch.zeros(b * self.total, dtype=torch.int16, pin_memory=True)
-        self.host_index = self.host_values = None   # [slots, kmax] views of the step in flight
-        self.host_small = torch.zeros(2 * b, dtype=torch.int32, pin_memory=True)
+        # Flat pinned staging for the commits, one set per step that may be in flight: a step's [slots, kmax] copy
+        # lands in the first slots * kmax entries as one contiguous block (a strided pinned destination would make the
+        # copy wait on the host).
+        self.host_index_flat = [torch.zeros(b * self.total, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self.host_values_flat = [torch.zeros(b * self.total, dtype=torch.int16, pin_memory=True) for _ in range(2)]
+        self.host_small_sets = [torch.zeros(2 * b, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         self.state = [dict(phase='idle') for _ in range(b)]
         self.noise = None
         self.generators = [None] * b
-        self._inflight = None   # (marking, rows, solid, slots in the step, event) of a launched, uncollected step
+        self._queue = deque()   # launched, uncollected steps, oldest first (at most `depth`)
+        self._launches = 0
         # device time of the steps (step graph + marking), accumulated by `collect` when `timing` is on
         self.timing, self.device_seconds, self._timing_events = False, 0.0, None
         if sampling == 'parity':
@@ -125,8 +129,8 @@ class SlotBatch:
         step is in flight, since the side stream first waits for the work already enqueued."""
         if self.sampling == 'parity' and int(cap) < self.min_cap:
             raise ValueError(f'cap {cap} is below min_cap {self.min_cap}, which sized the parity noise buffer')
-        if self._inflight is not None and slot in self._inflight[3]:
-            raise ValueError(f'slot {slot} takes part in the step in flight; collect it first')
+        if any(slot in entry['slots'] for entry in self._queue):
+            raise ValueError(f'slot {slot} takes part in a step in flight; collect it first')
         if item is not None:
             self.forward.load_slot(slot, item)
             if wait:
@@ -142,7 +146,7 @@ class SlotBatch:
         if self.sampling == 'parity':
             self.generators[slot] = torch.Generator(device=self.device).manual_seed(int(seed))
         self.last[slot].zero_()
-        self.state[slot] = dict(phase='marking', seed=int(seed), cap=int(cap), target=tuple(target), nfe=0,
+        self.state[slot] = dict(phase='marking', seed=int(seed), cap=int(cap), target=tuple(target), nfe=0, launched=0, nfe_launched=0,
                                 solid_calls=0, quotas=None, last_count=0)
 
     def _rows(self):
@@ -181,6 +185,7 @@ class SlotBatch:
         for i in marking:
             st = self.state[i]
             st['nfe'] += 1
+            st['nfe_launched'] = max(st.get('nfe_launched', 0), st['nfe'])
             st['last_count'] = int(counts[i])
             st['quotas'] = low_entropy_last_quotas(self.total, st['cap'], st['last_count'], 'quartercos')
             st['phase'] = 'solid'
@@ -232,61 +237,103 @@ class SlotBatch:
         self.launch()
         return self.collect()
 
+    depth = 2   # steps that may be in flight at once
+
+    @property
+    def in_flight(self):
+        return len(self._queue)
+
+    def runnable(self):
+        """Whether a step launched now would give some slot a forward (a marking or a solid step)."""
+        return any(st['phase'] == 'marking' or (st['phase'] == 'solid' and st['launched'] < len(st['quotas']))
+                   for st in self.state)
+
+    def _rows_ahead(self):
+        """Per-slot scalars of the next step to launch: solid steps are counted when launched, so a step can be
+        launched while the previous one is still in flight (the schedule of a window is known once it is marked)."""
+        rows = []
+        for st in self.state:
+            if st['phase'] == 'solid' and st['launched'] < len(st['quotas']):
+                k = st['quotas'][st['launched']]
+                committed = sum(st['quotas'][:st['launched']])
+                frac = (committed + k) / (self.total - st['last_count'])
+                rows.append((k, st['nfe_launched'] + 1, committed, frac, st['seed']))
+            else:
+                rows.append((0, 0, 0, 0.0, 0))
+        return rows
+
     def launch(self):
         """Enqueue one step (the step graph, the marking launches and the D2H copies of its results) without waiting
-        for it; `collect` waits and does the host bookkeeping. Between the two the host may arm idle slots."""
-        if self._inflight is not None:
-            raise RuntimeError('a step is already in flight; collect it first')
+        for it; `collect` waits for the oldest step and does its host bookkeeping. Up to `depth` steps may be in flight:
+        a slot whose window was marked in a step still in flight takes no forward in later steps until that step is
+        collected (its quotas come from the marking), and a window whose last solid step is in flight takes none."""
+        if len(self._queue) >= self.depth:
+            raise RuntimeError(f'{self.depth} steps are already in flight; collect one first')
         self.forward.wait_loads()
         marking = [i for i, st in enumerate(self.state) if st['phase'] == 'marking']
-        rows = self._rows()
+        rows = self._rows_ahead()
         solid = [i for i, r in enumerate(rows) if r[0] > 0]
-        self.params_host.copy_(self._pack(rows))
-        self.params.copy_(self.params_host, non_blocking=True)
+        for i in marking:
+            self.state[i]['phase'] = 'marking_sent'
+            self.state[i]['nfe_launched'] += 1
+        for i in solid:
+            self.state[i]['launched'] += 1
+            self.state[i]['nfe_launched'] += 1
+        buf = self._launches % 2
+        self._launches += 1
+        # one pinned source per step in flight: the H2D copy reads it when the stream reaches it
+        params_host = self.params_host_sets[buf]
+        params_host.copy_(self._pack(rows))
+        self.params.copy_(params_host, non_blocking=True)
         self.status.zero_()
         self._draw_noise(rows)
+        timing = None
         if self.timing:
-            self._timing_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            self._timing_events[0].record()
+            timing = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            timing[0].record()
         self.graph.replay()
         self._mark(marking)
         if self.timing:
-            self._timing_events[1].record()
+            timing[1].record()
         kmax = max([r[0] for r in rows] + [0])
+        host_index = host_values = None
         if kmax:
-            self.host_index = self.host_index_flat[:self.slots * kmax].view(self.slots, kmax)
-            self.host_values = self.host_values_flat[:self.slots * kmax].view(self.slots, kmax)
-            self.host_index.copy_(self.index[:, :kmax], non_blocking=True)
-            self.host_values.copy_(self.values[:, :kmax], non_blocking=True)
-        self.host_small[:self.slots].copy_(self.status, non_blocking=True)
-        self.host_small[self.slots:].copy_(self.last_count, non_blocking=True)
+            host_index = self.host_index_flat[buf][:self.slots * kmax].view(self.slots, kmax)
+            host_values = self.host_values_flat[buf][:self.slots * kmax].view(self.slots, kmax)
+            host_index.copy_(self.index[:, :kmax], non_blocking=True)
+            host_values.copy_(self.values[:, :kmax], non_blocking=True)
+        host_small = self.host_small_sets[buf]
+        host_small[:self.slots].copy_(self.status, non_blocking=True)
+        host_small[self.slots:].copy_(self.last_count, non_blocking=True)
         event = torch.cuda.Event()
         event.record(torch.cuda.current_stream(self.device))
-        self._inflight = (marking, rows, solid, set(marking) | set(solid), event)
+        self._queue.append(dict(marking=marking, rows=rows, solid=solid, slots=set(marking) | set(solid), event=event,
+                                index=host_index, values=host_values, small=host_small, timing=timing))
+        # the params buffer is read by this step's graph; the next launch's H2D copy is queued after it
 
     def collect(self):
-        """Wait for the launched step and book its commits; returns {slot: (record|None, commit|None)}."""
-        if self._inflight is None:
+        """Wait for the oldest launched step and book its commits; returns {slot: (record|None, commit|None)}."""
+        if not self._queue:
             raise RuntimeError('no step in flight')
-        marking, rows, solid, _, event = self._inflight
-        self._inflight = None
-        event.synchronize()
-        if self.timing and self._timing_events is not None:
-            self.device_seconds += self._timing_events[0].elapsed_time(self._timing_events[1]) * 1e-3
-            self._timing_events = None
+        entry = self._queue.popleft()
+        marking, rows, solid = entry['marking'], entry['rows'], entry['solid']
+        entry['event'].synchronize()
+        if entry['timing'] is not None:
+            self.device_seconds += entry['timing'][0].elapsed_time(entry['timing'][1]) * 1e-3
+        small = entry['small']
         results = {}
-        for i in self._after_mark(marking, self.host_small[self.slots:].tolist()):
+        for i in self._after_mark(marking, small[self.slots:].tolist()):
             results[i] = (self._finish(i), None)
         for i in marking:
             results.setdefault(i, (None, None))
         for i in solid:
-            if int(self.host_small[i]) & 1:
+            if int(small[i]) & 1:
                 raise AssertionError('low-entropy-last solid step did not meet its quota')
             st = self.state[i]
             k = rows[i][0]
             st['solid_calls'] += 1
             st['nfe'] += 1
-            commit = dict(positions=self.host_index[i, :k].numpy().copy(), values=self.host_values[i, :k].numpy().copy(),
+            commit = dict(positions=entry['index'][i, :k].numpy().copy(), values=entry['values'][i, :k].numpy().copy(),
                           step=st['nfe'])
             record = self._finish(i) if st['solid_calls'] >= len(st['quotas']) else None
             results[i] = (record, commit)

@@ -202,15 +202,20 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
     clock = time.perf_counter
     step_time = 0.0   # running estimate of one step's wall time (launch to collected)
     read_async = hasattr(engine, 'column_async')
+    depth = getattr(engine, 'depth', 1)
     for _ in range(max_rounds):
-        waiting = {s for s, _ in to_arm}
-        running = [i for i, c in enumerate(slot_cell) if c is not None and i not in waiting]
-        launched = False
         began = clock()
-        if running:
-            engine.launch()
-            stats['step_seconds'] += clock() - began
-            launched = True
+        # keep up to `depth` steps in flight: the next step is queued before the host works on the last one's results
+        if hasattr(engine, 'runnable'):
+            while engine.in_flight < depth and engine.runnable():
+                engine.launch()
+            launched = engine.in_flight > 0
+        else:
+            waiting = {s for s, _ in to_arm}
+            launched = any(c is not None and i not in waiting for i, c in enumerate(slot_cell))
+            if launched:
+                engine.launch()
+        stats['step_seconds'] += clock() - began
         t0 = clock()
         finished = []
         for cell, record, slot, read in pending:

@@ -39,26 +39,42 @@ class FakeEngine:
 
 
 class PipelinedFakeEngine(FakeEngine):
-    """`FakeEngine` with the `launch` / `collect` split: arming a slot of the step in flight is an error, and a
-    window armed after `launch` takes its first forward in the next step."""
+    """`FakeEngine` with `launch` / `collect` and up to two steps in flight: a window's forwards are counted when
+    launched, arming a slot of a step in flight is an error, and a window armed while steps are in flight takes its
+    first forward in the next step launched."""
+    depth = 2
 
     def __init__(self, slots, steps=3):
         super().__init__(slots, steps)
-        self.inflight = None
+        self.to_launch = [0] * slots
+        self.queue = []
+
+    @property
+    def in_flight(self):
+        return len(self.queue)
+
+    def runnable(self):
+        return any(self.to_launch)
 
     def arm(self, slot, seed, cap, item=None, target=(), wait=True):
-        assert self.inflight is None or slot not in self.inflight
+        assert all(slot not in entry for entry in self.queue)
         super().arm(slot, seed, cap, item, target)
+        self.to_launch[slot] = self.steps
 
     def launch(self):
-        assert self.inflight is None
-        self.inflight = {i for i in range(self.slots) if self.left[i]}
-        self.pending = super().step()
+        assert len(self.queue) < self.depth
+        entry = [i for i in range(self.slots) if self.to_launch[i]]
+        for i in entry:
+            self.to_launch[i] -= 1
+        self.queue.append(entry)
 
     def collect(self):
-        assert self.inflight is not None
-        self.inflight = None
-        return self.pending
+        out = {}
+        for i in self.queue.pop(0):
+            self.left[i] -= 1
+            done = dict(target=self.targets[i], nfe=self.steps, last_frac=0.0, cap=32, actual=self.steps)
+            out[i] = (done if self.left[i] == 0 else None, None)
+        return out
 
 
 class CheckedExpansion(expand.Expansion):
@@ -111,8 +127,8 @@ def test_single_rank_expansion_commits_the_region():
 
 
 def test_pipelined_expansion_commits_the_same_world():
-    """Admission overlapping the step in flight (`launch` / arm idle slots / `collect`) commits every window once
-    and the same columns as the serial driver."""
+    """Admission overlapping the steps in flight (two launched ahead, arming idle slots, collecting the oldest)
+    commits every window once and the same columns as the serial driver."""
     serial, _, _ = _run(1, 4)
     exp = _setup(1, 4)
     engine = PipelinedFakeEngine(4)

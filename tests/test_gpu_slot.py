@@ -226,3 +226,39 @@ def test_slot_batch_windows_equal_reference_slot(sampling):
                     arm(i)
         step += 1
         assert step < 64
+
+
+@pytest.mark.parametrize('sampling', ['parity', 'native'])
+def test_slot_batch_two_steps_in_flight_equal_one(sampling):
+    """`SlotBatch` driven with two steps in flight (`launch` twice, then `collect` the oldest, re-arming finished
+    slots while a step runs) commits exactly what the one-step `step()` driver commits, window for window: a slot
+    sits out the steps it cannot take (marked but not yet collected, or finished), which changes no window's forwards."""
+    def run(two):
+        cfg, batch = _small_batch(sampling)
+        seeds = iter(range(900, 1000))
+        for i in range(batch.slots):
+            batch.arm(i, next(seeds), 8 + i, order=np.random.default_rng(i).permutation(batch.blocks))
+        commits, windows = {}, 0
+        while windows < 2 * batch.slots:
+            if two:
+                while batch.in_flight < batch.depth and batch.runnable():
+                    batch.launch()
+                results = batch.collect()
+            else:
+                results = batch.step()
+            for i, (record, commit) in results.items():
+                key = (i, batch.state[i].get('seed'))
+                if commit is not None:
+                    commits.setdefault(key, []).append((commit['step'], commit['positions'].tolist(),
+                                                        commit['values'].tolist()))
+                if record is not None:
+                    commits.setdefault((i, record['seed']), []).append(('done', batch.column(i).tobytes()))
+                    windows += 1
+                    if windows <= batch.slots:
+                        batch.arm(i, next(seeds) + 1000 * i, 8 + i,
+                                  order=np.random.default_rng(100 + i).permutation(batch.blocks))
+        while batch.in_flight:
+            batch.collect()
+        return commits
+
+    assert run(True) == run(False)
