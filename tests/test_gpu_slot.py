@@ -235,10 +235,9 @@ def test_slot_batch_two_steps_in_flight_equal_one(sampling):
     sits out the steps it cannot take (marked but not yet collected, or finished), which changes no window's forwards."""
     def run(two):
         cfg, batch = _small_batch(sampling)
-        seeds = iter(range(900, 1000))
         for i in range(batch.slots):
-            batch.arm(i, next(seeds), 8 + i, order=np.random.default_rng(i).permutation(batch.blocks))
-        commits, windows = {}, 0
+            batch.arm(i, 900 + 100 * i, 8 + i, order=np.random.default_rng(i).permutation(batch.blocks))
+        commits, windows, rearmed = {}, 0, set()
         while windows < 2 * batch.slots:
             if two:
                 while batch.in_flight < batch.depth and batch.runnable():
@@ -254,8 +253,9 @@ def test_slot_batch_two_steps_in_flight_equal_one(sampling):
                 if record is not None:
                     commits.setdefault((i, record['seed']), []).append(('done', batch.column(i).tobytes()))
                     windows += 1
-                    if windows <= batch.slots:
-                        batch.arm(i, next(seeds) + 1000 * i, 8 + i,
+                    if i not in rearmed:   # a second window per slot, its seed a function of the slot only
+                        rearmed.add(i)
+                        batch.arm(i, 901 + 100 * i, 8 + i,
                                   order=np.random.default_rng(100 + i).permutation(batch.blocks))
         while batch.in_flight:
             batch.collect()
