@@ -77,7 +77,8 @@ class FastSlotForward:
         probe = self.encode(probe_item(spec))
         for slot in range(self.batch):
             self.engine.write_slot(slot, probe)
-        self.side = torch.cuda.Stream(device=self.device)
+        self.side = torch.cuda.Stream(device=self.device)          # slot writes: ordered after the queued steps
+        self.encoder = torch.cuda.Stream(device=self.device)       # condition encodes: never wait for a step
         self.sizes = sorted({min(self.batch, 2 ** k) for k in range(self.batch.bit_length() + 1)})
         self.graphs, self.outputs = {}, {}
         self.graph_ok = False
@@ -100,13 +101,19 @@ class FastSlotForward:
         return layers
 
     def load_slot(self, index, item):
-        """Encode + copy on the side stream; `wait_loads` joins it before the next replay (`fast_ops.py:252-260`).
-        The encode reads only the item and the weights, so it starts at once (its host inputs go through pinned
-        memory, and the host never waits for a step in flight); the copy into the slot's K/V rows and tokens waits
-        for the work already queued on the caller's stream, and the slot's key length is applied by `wait_loads`."""
-        with torch.cuda.stream(self.side):
+        """Encode + copy off the caller's stream; `wait_loads` joins it before the next replay
+        (`fast_ops.py:252-260`). The encode reads only the item and the weights, so it runs on its own stream that
+        never waits for a step (its host inputs go through pinned memory: the host never waits either); the copy into
+        the slot's K/V rows and tokens runs on the side stream after the encode and after the work already queued on
+        the caller's stream, and the slot's key length is applied by `wait_loads`. Encodes of several slots therefore
+        queue back to back, not each behind the previous slot's copy."""
+        with torch.cuda.stream(self.encoder):
             layers = self.encode(item)
+        self.side.wait_stream(self.encoder)
         self.side.wait_stream(torch.cuda.current_stream(self.device))
+        for k, v in layers:   # made on the encoder stream, read on the side stream
+            k.record_stream(self.side)
+            v.record_stream(self.side)
         with torch.cuda.stream(self.side):
             self.engine.write_slot(index, layers, defer=True)
             self.tokens[index].fill_(self.classes)
