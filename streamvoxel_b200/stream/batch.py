@@ -146,8 +146,8 @@ class SlotBatch:
         if self.sampling == 'parity':
             self.generators[slot] = torch.Generator(device=self.device).manual_seed(int(seed))
         self.last[slot].zero_()
-        self.state[slot] = dict(phase='marking', seed=int(seed), cap=int(cap), target=tuple(target), nfe=0, launched=0, nfe_launched=0,
-                                solid_calls=0, quotas=None, last_count=0)
+        self.state[slot] = dict(phase='marking', seed=int(seed), cap=int(cap), target=tuple(target), nfe=0,
+                                solid_calls=0, quotas=None, last_count=0, launched=0, nfe_launched=0)
 
     def _rows(self):
         rows = []

@@ -198,7 +198,7 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
     pending = []     # (cell, record, slot, column reader) of windows the last collect finished
     stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0, step_seconds=0.0,
                  item_seconds=0.0, arm_seconds=0.0, exchange_seconds=0.0, collect_wait_seconds=0.0, pipelined=True,
-                 deferred_arms=0)
+                 deferred_arms=0, launched_ahead=0)
     clock = time.perf_counter
     step_time = 0.0   # running estimate of one step's wall time (launch to collected)
     read_async = hasattr(engine, 'column_async')
@@ -208,6 +208,7 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
         # keep up to `depth` steps in flight: the next step is queued before the host works on the last one's results
         if hasattr(engine, 'runnable'):
             while engine.in_flight < depth and engine.runnable():
+                stats['launched_ahead'] += engine.in_flight > 0
                 engine.launch()
             launched = engine.in_flight > 0
         else:
