@@ -58,3 +58,13 @@ def probe_item(spec):
     biomes = np.zeros((height // 4, 12, 12), np.int64)
     return Item('probe', 0, 1, 1.0, blocks, np.asarray([[-tile, 0]], np.int64), blocks.copy(),
                 np.asarray([[-2 * tile, 0]], np.int64), biomes, None)
+
+
+def largest_item(spec, l1_cap, l2_cap):
+    """An item with the most conditions a slot holds (`l1_cap` L1 tiles, `l2_cap` L2 columns), all-air columns."""
+    height, tile = spec.height, spec.tile
+    l1 = np.zeros((max(1, l1_cap), height, tile, tile), np.int16)
+    l2 = np.zeros((max(1, l2_cap), height, tile, tile), np.int16)
+    offsets = lambda n, r: np.asarray([[(i % 9 - 4) * tile, (i // 9 - r) * tile] for i in range(n)], np.int64)
+    return Item('largest', 0, 1, 1.0, l1, offsets(len(l1), 6), l2, offsets(len(l2), 4),
+                np.zeros((height // 4, 12, 12), np.int64), None)

@@ -23,7 +23,7 @@ from streamvoxel_b200 import _lib, ops
 from streamvoxel_b200.model import Engine
 from streamvoxel_b200.modules import prepared_model
 from streamvoxel_b200.sampling import actual_time, low_entropy_last_quotas
-from streamvoxel_b200.stream.condition import probe_item
+from streamvoxel_b200.stream.condition import largest_item, probe_item
 
 KEY_BLOCK = 128
 RECOMMENDED = dict(patchify='gather', attention='flex', compile='emulate')
@@ -79,6 +79,12 @@ class FastSlotForward:
             self.engine.write_slot(slot, probe)
         self.side = torch.cuda.Stream(device=self.device)          # slot writes: ordered after the queued steps
         self.encoder = torch.cuda.Stream(device=self.device)       # condition encodes: never wait for a step
+        # One encode of the largest condition the slots hold (l1_cap L1 tiles, l2_cap L2 columns), on the encoder
+        # stream, so that the memory pool already holds blocks of every size later encodes ask for: a device
+        # allocation while steps are queued would stall the device (it synchronises).
+        with torch.cuda.stream(self.encoder):
+            self.encode(largest_item(spec, self.l1_cap, self.l2_cap))
+        torch.cuda.synchronize(self.device)
         self.sizes = sorted({min(self.batch, 2 ** k) for k in range(self.batch.bit_length() + 1)})
         self.graphs, self.outputs = {}, {}
         self.graph_ok = False
