@@ -446,7 +446,10 @@ def main_ours(args):
     torch.cuda.set_device(device)
     from streamvoxel_b200 import _lib
     _lib.require_device(device)
-    cfg, sd, forward, batch, lengths = build(device, seed=rank)
+    # Weak scaling: every rank runs the same per-GPU workload (the same weights and the same eight windows'
+    # conditions, so the same packed key lengths as at N = 1); only the sampled windows' seeds differ by rank. With
+    # per-rank conditions the slowest rank's longer keys, not the GPUs, set the max-over-ranks time.
+    cfg, sd, forward, batch, lengths = build(device, seed=0)
     seeds = list(range(rank * 1_000_000, rank * 1_000_000 + 100_000))
     # warm-up: W forwards through the public step path
     run_api_steps(batch, max(3, args.warmup), iter(seeds[50_000:]))
