@@ -77,6 +77,10 @@ class SlotBatch:
         self.noise = None
         self.generators = [None] * b
         self._queue = deque()   # launched, uncollected steps, oldest first (at most `depth`)
+        # a finishing window's tokens and its deferred-voxel mask, copied to the host by the step that finishes it and
+        # by its marking step, so its committed column is ready when that step is collected
+        self._final_tokens = torch.zeros((b, *self.shape), dtype=torch.int16, pin_memory=True)
+        self._final_last = torch.zeros((b, *self.shape), dtype=torch.uint8, pin_memory=True)
         self._launches = 0
         # device time of the steps (step graph + marking), accumulated by `collect` when `timing` is on
         self.timing, self.device_seconds, self._timing_events = False, 0.0, None
@@ -295,6 +299,11 @@ class SlotBatch:
         self._mark(marking)
         if self.timing:
             timing[1].record()
+        for i in marking:
+            self._final_last[i].copy_(self.last[i], non_blocking=True)
+        finishing = [i for i in solid if self.state[i]['launched'] == len(self.state[i]['quotas'])]
+        for i in finishing:
+            self._final_tokens[i].copy_(self.forward.tokens[i], non_blocking=True)
         kmax = max([r[0] for r in rows] + [0])
         host_index = host_values = None
         if kmax:
@@ -308,7 +317,8 @@ class SlotBatch:
         event = torch.cuda.Event()
         event.record(torch.cuda.current_stream(self.device))
         self._queue.append(dict(marking=marking, rows=rows, solid=solid, slots=set(marking) | set(solid), event=event,
-                                index=host_index, values=host_values, small=host_small, timing=timing))
+                                index=host_index, values=host_values, small=host_small, timing=timing,
+                                finishing=set(finishing)))
         # the params buffer is read by this step's graph; the next launch's H2D copy is queued after it
 
     def collect(self):
@@ -323,7 +333,9 @@ class SlotBatch:
         small = entry['small']
         results = {}
         for i in self._after_mark(marking, small[self.slots:].tolist()):
-            results[i] = (self._finish(i), None)
+            record = self._finish(i)   # every voxel deferred: the column is all air
+            record['column'] = np.full(self.shape, self.air_token, np.int16)
+            results[i] = (record, None)
         for i in marking:
             results.setdefault(i, (None, None))
         for i in solid:
@@ -335,7 +347,13 @@ class SlotBatch:
             st['nfe'] += 1
             commit = dict(positions=entry['index'][i, :k].numpy().copy(), values=entry['values'][i, :k].numpy().copy(),
                           step=st['nfe'])
-            record = self._finish(i) if st['solid_calls'] >= len(st['quotas']) else None
+            record = None
+            if st['solid_calls'] >= len(st['quotas']):
+                record = self._finish(i)
+                if i in entry['finishing']:   # the committed column, deferred voxels as air, without a device wait
+                    column = self._final_tokens[i].numpy().copy()
+                    column[self._final_last[i].numpy().astype(bool)] = self.air_token
+                    record['column'] = column
             results[i] = (record, commit)
         return dict(sorted(results.items()))
 

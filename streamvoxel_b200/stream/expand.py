@@ -262,7 +262,9 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
             stats['forwards'] += 1
             for i, (record, _commit) in results.items():
                 if record is not None and slot_cell[i] is not None:
-                    if read_async:
+                    if 'column' in record:   # the engine copied it out with the step
+                        read = (lambda column=record['column']: column)
+                    elif read_async:
                         read = engine.column_async(i)
                     else:
                         column = engine.column(i)

@@ -220,6 +220,7 @@ def test_slot_batch_windows_equal_reference_slot(sampling):
                 for key in ('nfe', 'actual', 'last_count'):
                     assert record[key] == want_record[key], key
                 assert np.array_equal(batch.column(i), ref_tokens[i]), i
+                assert np.array_equal(record['column'], ref_tokens[i]), i   # staged by the finishing step
                 finished += 1
                 windows[i] += 1
                 if windows[i] < 2:
@@ -251,7 +252,8 @@ def test_slot_batch_two_steps_in_flight_equal_one(sampling):
                     commits.setdefault(key, []).append((commit['step'], commit['positions'].tolist(),
                                                         commit['values'].tolist()))
                 if record is not None:
-                    commits.setdefault((i, record['seed']), []).append(('done', batch.column(i).tobytes()))
+                    assert np.array_equal(record['column'], batch.column(i))
+                    commits.setdefault((i, record['seed']), []).append(('done', record['column'].tobytes()))
                     windows += 1
                     if i not in rearmed:   # a second window per slot, its seed a function of the slot only
                         rearmed.add(i)
