@@ -586,6 +586,10 @@ def main_expand(args):
     committed, region, biomes, player = expand.start_region(11, args.side0, args.side1, forward.spec,
                                                             classes=cfg.classes)
     exp = expand.Expansion(committed, biomes, forward.spec, player, region, ranks=world, slots=SLOTS, l2_cap=L2_CAP)
+    exchange = None   # one rank: nothing to exchange
+    if world > 1:     # finished columns and free slots over NCCL, on a stream of their own
+        import torch.distributed as dist
+        exchange = expand.DeviceExchange(dist.group.WORLD, SLOTS, forward.shape, device)
 
     def barrier():
         torch.cuda.synchronize(device)
@@ -599,7 +603,7 @@ def main_expand(args):
     with Clocks(local) as clocks:
         barrier()
         start.record()
-        stats = expand.run(batch, exp, rank, group=group)
+        stats = expand.run(batch, exp, rank, group=group, exchange=exchange)
         stop.record()
         barrier()
     seconds = start.elapsed_time(stop) * 1e-3
@@ -615,7 +619,7 @@ def main_expand(args):
     config = dict(workload=WORKLOAD, slots_per_gpu=SLOTS, cap=CAP, l1_cap=L1_CAP, l2_cap=L2_CAP, side0=args.side0,
                   side1=args.side1, admission='pick_window order around the player at the region centre, Chebyshev >= 2',
                   l2_policy='inputs larger than L2 (the step reads all weights and writes all logits: >= 1 GB)',
-                  parallelism=f'dp{world}: one engine per GPU, finished columns exchanged on the host (gloo)')
+                  parallelism=f'dp{world}: one engine per GPU, finished columns all-gathered over NCCL each round')
     per_step_h2d = batch.params_host.numel()
     line = dict(metric=METRIC, value=voxels / wall, unit=UNIT, n_gpus=world, steps=forwards, warmup=args.warmup,
                 ms_per_step=wall / max(1, forwards / world) * 1e3, higher_is_better=True, scaling='strong',

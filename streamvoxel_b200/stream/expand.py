@@ -128,19 +128,76 @@ def host_exchange(obj, group=None):
     return out
 
 
-def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=None, raw_map=None, pipelined=None):
+class DeviceExchange:
+    """`host_exchange` of (finished columns, free slots) over a device process group (NCCL): a fixed-size header per
+    rank (finished count, free slots, the finished cells) all-gathered every round, and the finished columns
+    all-gathered only in rounds where some rank finished one (every rank reads the same headers, so all take the same
+    collectives). The collectives run on a stream of their own, so they do not queue behind the steps in flight, and
+    only the columns that exist are copied back to the host. Returns what `host_exchange` returns."""
+
+    def __init__(self, group, slots, shape, device):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist, self.group = torch, dist, group
+        self.ranks = dist.get_world_size(group)
+        self.slots, self.shape = int(slots), tuple(shape)
+        width = 2 + 2 * self.slots
+        self.stream = torch.cuda.Stream(device=device)
+        self.header_host = torch.zeros(width, dtype=torch.int64, pin_memory=True)
+        self.header = torch.zeros(width, dtype=torch.int64, device=device)
+        self.headers = torch.zeros((self.ranks, width), dtype=torch.int64, device=device)
+        self.columns_host = torch.zeros((self.slots, *self.shape), dtype=torch.int16, pin_memory=True)
+        self.columns = torch.zeros((self.slots, *self.shape), dtype=torch.int16, device=device)
+        self.gathered = torch.zeros((self.ranks, self.slots, *self.shape), dtype=torch.int16, device=device)
+
+    def __call__(self, obj):
+        torch, dist = self.torch, self.dist
+        finished, free = obj
+        if len(finished) > self.slots:
+            raise ValueError('more finished windows than slots')
+        header = self.header_host
+        header.zero_()
+        header[0], header[1] = len(finished), int(free)
+        for j, (cell, column) in enumerate(finished):
+            header[2 + 2 * j], header[3 + 2 * j] = int(cell[0]), int(cell[1])
+            self.columns_host[j].copy_(torch.from_numpy(np.ascontiguousarray(column, np.int16)))
+        with torch.cuda.stream(self.stream):
+            self.header.copy_(header, non_blocking=True)
+            dist.all_gather_into_tensor(self.headers, self.header, group=self.group)
+            headers = self.headers.cpu().numpy()   # waits for this stream only
+            out = [([], int(h[1])) for h in headers]
+            if int(headers[:, 0].sum()):
+                if finished:
+                    self.columns[:len(finished)].copy_(self.columns_host[:len(finished)], non_blocking=True)
+                dist.all_gather_into_tensor(self.gathered.view(-1), self.columns.view(-1), group=self.group)
+                for r, h in enumerate(headers):
+                    count = int(h[0])
+                    if count:
+                        cols = self.gathered[r, :count].cpu().numpy()
+                        out[r] = ([((int(h[2 + 2 * j]), int(h[3 + 2 * j])), cols[j].copy()) for j in range(count)],
+                                  int(h[1]))
+        return out
+
+
+def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=None, raw_map=None, pipelined=None,
+        exchange=None):
     """Drive `engine` (a `SlotBatch`, or any object with `slots`, `arm`, `step` and `column`) until the region is
     committed. Returns statistics of this rank. With a `publisher` (`wire.Publisher`), every window this rank
     finishes is published as a frame packet carrying its whole cell (global ids through `raw_map`) followed by its
     `window_commit` packet, as the reference's worker does without progressive frames.
+
+    `exchange`: the callable that all-gathers (finished, free slots) between the ranks (default `host_exchange` over
+    `group`; `DeviceExchange` gathers over NCCL).
 
     Pipelined (the default for an engine with `launch`/`collect`): the windows admitted after a step are built and
     armed while the next step runs on the GPU (their condition encode joins before the step after), so the host's
     admission work overlaps the device; a slot whose window finished sits out one step."""
     if pipelined is None:
         pipelined = hasattr(engine, 'launch') and hasattr(engine, 'collect')
+    if exchange is None:
+        exchange = lambda obj: host_exchange(obj, group)
     if pipelined:
-        return _run_pipelined(engine, expansion, rank, group=group, max_rounds=max_rounds, publisher=publisher,
+        return _run_pipelined(engine, expansion, rank, exchange=exchange, max_rounds=max_rounds, publisher=publisher,
                               raw_map=raw_map)
     slot_cell = [None] * engine.slots
     stats = dict(rounds=0, forwards=0, windows=0, committed_voxels=0, admission_seconds=0.0, step_seconds=0.0,
@@ -164,7 +221,7 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
                     slot_cell[i] = None
         t0 = clock()
         free_slots = [i for i, c in enumerate(slot_cell) if c is None]
-        gathered = host_exchange((finished, len(free_slots)), group)
+        gathered = exchange((finished, len(free_slots)))
         stats['exchange_seconds'] += clock() - t0
         for commits, _ in gathered:
             expansion.apply(commits)
@@ -188,7 +245,7 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
     return stats
 
 
-def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw_map):
+def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, raw_map):
     """`run` with the host's admission work overlapping the device. One round: launch the next step at once (the
     slots of windows that finished in the previous step sit it out), then -- while it runs -- read the finished
     windows' columns (copies enqueued before the launch), exchange and commit them, admit new windows and arm them
@@ -228,7 +285,7 @@ def _run_pipelined(engine, expansion, rank, *, group, max_rounds, publisher, raw
             stats['committed_voxels'] += int(tokens.size)
         pending = []
         free_slots = [i for i, c in enumerate(slot_cell) if c is None]
-        gathered = host_exchange((finished, len(free_slots)), group)
+        gathered = exchange((finished, len(free_slots)))
         stats['exchange_seconds'] += clock() - t0
         for commits, _ in gathered:
             expansion.apply(commits)
