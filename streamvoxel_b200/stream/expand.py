@@ -136,19 +136,28 @@ class DeviceExchange:
     only the columns that exist are copied back to the host. Returns what `host_exchange` returns."""
 
     def __init__(self, group, slots, shape, device):
+        import contextlib
+
         import torch
         import torch.distributed as dist
         self.torch, self.dist, self.group = torch, dist, group
         self.ranks = dist.get_world_size(group)
         self.slots, self.shape = int(slots), tuple(shape)
         width = 2 + 2 * self.slots
-        self.stream = torch.cuda.Stream(device=device)
-        self.header_host = torch.zeros(width, dtype=torch.int64, pin_memory=True)
+        device = torch.device(device)
+        cuda = device.type == 'cuda'
+        # A CPU device (a gloo group) runs the same collectives on the calling thread; it is there for tests.
+        self.stream = torch.cuda.Stream(device=device) if cuda else None
+        self.context = (lambda: torch.cuda.stream(self.stream)) if cuda else contextlib.nullcontext
+        self.header_host = torch.zeros(width, dtype=torch.int64, pin_memory=cuda)
         self.header = torch.zeros(width, dtype=torch.int64, device=device)
         self.headers = torch.zeros((self.ranks, width), dtype=torch.int64, device=device)
-        self.columns_host = torch.zeros((self.slots, *self.shape), dtype=torch.int16, pin_memory=True)
+        self.columns_host = torch.zeros((self.slots, *self.shape), dtype=torch.int16, pin_memory=cuda)
         self.columns = torch.zeros((self.slots, *self.shape), dtype=torch.int16, device=device)
         self.gathered = torch.zeros((self.ranks, self.slots, *self.shape), dtype=torch.int16, device=device)
+        # NCCL has no 16-bit integer type: the columns travel as their bytes.
+        self.columns_bytes = self.columns.view(-1).view(torch.uint8)
+        self.gathered_bytes = self.gathered.view(-1).view(torch.uint8)
 
     def __call__(self, obj):
         torch, dist = self.torch, self.dist
@@ -161,15 +170,15 @@ class DeviceExchange:
         for j, (cell, column) in enumerate(finished):
             header[2 + 2 * j], header[3 + 2 * j] = int(cell[0]), int(cell[1])
             self.columns_host[j].copy_(torch.from_numpy(np.ascontiguousarray(column, np.int16)))
-        with torch.cuda.stream(self.stream):
+        with self.context():
             self.header.copy_(header, non_blocking=True)
-            dist.all_gather_into_tensor(self.headers, self.header, group=self.group)
+            dist.all_gather_into_tensor(self.headers.view(-1), self.header, group=self.group)
             headers = self.headers.cpu().numpy()   # waits for this stream only
             out = [([], int(h[1])) for h in headers]
             if int(headers[:, 0].sum()):
                 if finished:
                     self.columns[:len(finished)].copy_(self.columns_host[:len(finished)], non_blocking=True)
-                dist.all_gather_into_tensor(self.gathered.view(-1), self.columns.view(-1), group=self.group)
+                dist.all_gather_into_tensor(self.gathered_bytes, self.columns_bytes, group=self.group)
                 for r, h in enumerate(headers):
                     count = int(h[0])
                     if count:

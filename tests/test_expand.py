@@ -179,3 +179,10 @@ def test_published_packets_rebuild_the_committed_columns():
         np.testing.assert_array_equal(pos, np.flatnonzero(flat))
         np.testing.assert_array_equal(ids, flat[flat != 0])
     assert wire.unbatch(wire.batch_line(pub.packets[:10])) == pub.packets[:10]
+
+
+def test_device_exchange_two_gloo_ranks():
+    """`DeviceExchange`'s rounds (header every round, columns only when some rank finished) on two gloo ranks: the
+    same host logic the NCCL group runs on GPUs."""
+    from exchange_worker import check_rounds, run_two_ranks
+    check_rounds(run_two_ranks('gloo'))

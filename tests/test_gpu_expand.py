@@ -51,40 +51,11 @@ def test_l2_token_cache_gives_identical_keys_and_values():
     assert cache.hits > 0 and cache.misses <= len(committed)
 
 
-def _exchange_worker(rank, world, port, path):
-    import torch
-    import torch.distributed as dist
-    from streamvoxel_b200.stream.expand import DeviceExchange
-    torch.cuda.set_device(rank)
-    dist.init_process_group('nccl', init_method=f'tcp://127.0.0.1:{port}', rank=rank, world_size=world)
-    exchange = DeviceExchange(dist.group.WORLD, 4, (8, 4, 4), torch.device('cuda', rank))
-    rounds = []
-    for r in range(3):   # round 0: nobody finished; round 1: rank 1 finishes two windows; round 2: both finish one
-        finished = []
-        if (r == 1 and rank == 1) or r == 2:
-            finished = [((rank, r + j), np.full((8, 4, 4), 10 * rank + r + j, np.int16)) for j in range(1 if r == 2 else 2)]
-        rounds.append(exchange((finished, 3 - rank)))
-    with open(f'{path}.{rank}', 'w') as f:
-        f.write(repr([[(len(fin), free, [(c, int(col.sum())) for c, col in fin]) for fin, free in got] for got in rounds]))
-    dist.barrier()
-    dist.destroy_process_group()
-
-
 def test_device_exchange_two_ranks():
     """`DeviceExchange` (finished columns and free-slot counts all-gathered over NCCL) gives every rank the same
     rounds, including rounds where nobody or only one rank finished."""
-    import tempfile
     import torch
-    import torch.multiprocessing as mp
+    from exchange_worker import check_rounds, run_two_ranks
     if torch.cuda.device_count() < 2:
         pytest.skip('needs two GPUs')
-    port = 29700 + os.getpid() % 1000
-    with tempfile.TemporaryDirectory() as tmp:
-        path = os.path.join(tmp, 'x')
-        mp.start_processes(_exchange_worker, args=(2, port, path), nprocs=2, join=True, start_method='spawn')
-        seen = [open(f'{path}.{r}').read() for r in range(2)]
-    assert seen[0] == seen[1]
-    rounds = eval(seen[0])
-    assert rounds[0] == [(0, 3, []), (0, 2, [])]
-    assert rounds[1][0] == (0, 3, []) and rounds[1][1][0] == 2 and rounds[1][1][2][0] == ((1, 1), 11 * 128)
-    assert rounds[2][0][2] == [((0, 2), 2 * 128)] and rounds[2][1][2] == [((1, 2), 12 * 128)]
+    check_rounds(run_two_ranks('nccl'))
