@@ -220,10 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Register split: the load/MMA warpgroup keeps 64 per thread, the two softmax warpgroups take 216
-  // (128 x 64 + 256 x 216 <= 384 x 168, the launch's allocation).
+  // No register split between the roles: ptxas compiles every role within the launch's 168 registers a thread
+  // anyway, and a setmaxnreg decrease in the load/MMA branch made it spill values that the softmax reloads per tile.
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
     if (warp == 0) {   // Q and the K ring
       int T = 0, qn = 0;
       bool ok = true;
@@ -320,7 +319,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const __grid_
       tc::tmem_dealloc(*tmem_slot, TMEM_COLS);
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");
     const int i = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;

@@ -31,10 +31,18 @@ __device__ __forceinline__ void unpack_bf16x8(uint4 raw, float (&v)[8]) {
   }
 }
 
+// Two values rounded to bf16 (nearest even) and widened back: one paired conversion instead of two single ones.
+__device__ __forceinline__ float2 round_bf16_pair(float a, float b) {
+  return __bfloat1622float2(__floats2bfloat162_rn(a, b));
+}
+
 __device__ __forceinline__ uint4 pack_bf16x8(const float (&v)[8]) {
   uint32_t w[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) w[j] = (uint32_t)f32_to_bf16(v[2 * j]) | ((uint32_t)f32_to_bf16(v[2 * j + 1]) << 16);
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    w[j] = *reinterpret_cast<const uint32_t*>(&h);
+  }
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -79,7 +87,13 @@ __global__ void patch_embed_kernel(const int16_t* __restrict__ tokens, int heigh
     unpack_bf16x8(*reinterpret_cast<const uint4*>((branch ? bias_c : bias_b) + c0), bias);
     unpack_bf16x8(*reinterpret_cast<const uint4*>((branch ? add_c : add_b) + (int64_t)(row % patches) * d + c0), add);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = round_bf16(round_bf16(round_bf16(acc[j]) + bias[j]) + add[j]);
+    for (int j = 0; j < 8; j += 2) {
+      float2 r = round_bf16_pair(acc[j], acc[j + 1]);
+      r = round_bf16_pair(r.x + bias[j], r.y + bias[j + 1]);
+      r = round_bf16_pair(r.x + add[j], r.y + add[j + 1]);
+      acc[j] = r.x;
+      acc[j + 1] = r.y;
+    }
     *reinterpret_cast<uint4*>((branch ? out_c : out_b) + (int64_t)row * d + c0) = pack_bf16x8(acc);
     float2* stats = branch ? stats_c : stats_b;
     if (stats) {   // d % 32 == 0: the four lanes of a chunk are all active (lanes past d have returned)
