@@ -37,14 +37,6 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // Warp-collective forms (all 32 lanes call them converged; one elected lane performs the operation). Keeping the
 // issue loop warp-uniform lets the compiler hold descriptors and coordinates in uniform registers, which the tensor
 // core and TMA instructions take directly; issuing from a single divergent lane costs ~100 cycles per instruction.
-__device__ __forceinline__ void tma_load_2d_w(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n\t}"
-      ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_load_3d_w(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
                                               uint64_t* bar) {
   asm volatile(
@@ -98,26 +90,6 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t b
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
 }
 
-__device__ __forceinline__ void umma_w(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred e, p;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
-}
-
-// A operand from tensor memory (M=128 lanes, two bf16 per 32-bit column along K), B from shared memory.
-__device__ __forceinline__ void umma_ts_w(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred e, p;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc));
-}
-
 // Batched issue for attention tiles (warp-collective, one elect for the whole batch; descriptors advance by
 // constants, so the issuing warp spends a few instructions per product).
 // S = Q K^T over K = 96: four K-steps in the 128B-swizzled parts (qw, kw), two in the 64B-swizzled parts (qn, kn);
@@ -139,31 +111,6 @@ __device__ __forceinline__ void mma_qk96_w(uint32_t d, uint64_t qw, uint64_t kw,
       "add.s64 a, %3, 2;\n\tadd.s64 b, %4, 2;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, pt;\n\t}"
       ::"r"(d), "l"(qw), "l"(kw), "l"(qn), "l"(kn), "r"(idesc));
-}
-
-// O += P V over K = 128 keys: A = P in TMEM (8 columns per K-step), B = V MN-major 128B-swizzled (16 keys x 128 B =
-// 2048 bytes per K-step, +128 in descriptor units). `acc` = 0 starts O from the first product.
-__device__ __forceinline__ void mma_pv128_w(uint32_t d, uint32_t a, uint64_t v, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred e, p0, pt;\n\t.reg .b64 b;\n\t.reg .b32 t;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p0, %4, 0;\n\tsetp.eq.b32 pt, %3, %3;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
-      "add.s32 t, %1, 8;\n\tadd.s64 b, %2, 128;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
-      "add.s32 t, %1, 16;\n\tadd.s64 b, %2, 256;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
-      "add.s32 t, %1, 24;\n\tadd.s64 b, %2, 384;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
-      "add.s32 t, %1, 32;\n\tadd.s64 b, %2, 512;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
-      "add.s32 t, %1, 40;\n\tadd.s64 b, %2, 640;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
-      "add.s32 t, %1, 48;\n\tadd.s64 b, %2, 768;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t"
-      "add.s32 t, %1, 56;\n\tadd.s64 b, %2, 896;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t], b, %3, pt;\n\t}"
-      ::"r"(d), "r"(a), "l"(v), "r"(idesc), "r"(acc));
 }
 
 // O += P V over K = 96 keys: A = P in TMEM (8 columns per K-step; steps 0-3 at `a_lo`, steps 4-5 at `a_hi`), B = V
