@@ -429,8 +429,9 @@ def cpu_baseline(cfg, sd, lengths, sample=1):
     seconds = (time.perf_counter() - began) / sample
     per_forward = total / (1 + len(quotas))   # voxels a slot commits per forward, averaged over its window
     return dict(value=per_forward / seconds, unit=UNIT, cores=threads, kind='port',
-                sample=f'{sample} slot-forward(s) of the config-2 model (fp32, K/V length {length}) + one EASE solid '
-                       f'step on [256, 65536]; {seconds:.2f} s each; voxels/s = 65536/33 per slot-forward')
+                sample=f'{sample} slot-forward(s) of the bench model (d={cfg.d}, {cfg.depth} + '
+                       f'{len(cfg.layer_indices)} layers; fp32, K/V length {length}) + one EASE solid step on '
+                       f'[{cfg.classes}, 65536]; {seconds:.2f} s each; voxels/s = 65536/33 per slot-forward')
 
 
 def main_ours(args):
@@ -540,7 +541,7 @@ def main_ours(args):
 
 def main_reference(args):
     """The reference's CPU path on the host cores (rank 0 only), on this arm's config, metric and unit: each step is one
-    bounded sample (one slot-forward of the config-2 model at the bench's mean packed key length + one EASE solid
+    bounded sample (one slot-forward of the workload's model at the bench's mean packed key length + one EASE solid
     step), at most 3 samples."""
     rank, world, _ = dist_env()
     if rank != 0:
