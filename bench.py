@@ -252,19 +252,29 @@ def run_device_steps(batch, steps, seeds):
 
 
 def run_api_steps(batch, steps, seeds):
-    """Exactly `steps` forwards through `SlotBatch.step` (per-step H2D scalars, D2H commits, host bookkeeping); the
-    same per-forward share of each window's voxels as `run_device_steps`."""
+    """Exactly `steps` forwards through the SlotBatch API as a caller that overlaps its host work with the device
+    drives it: up to `SlotBatch.depth` steps in flight (`launch` queues a step with the H2D copy of its scalars from
+    pinned memory and the D2H copies of its commits; `collect` waits for the oldest and books them), finished windows
+    re-armed after their step is collected. The same per-forward share of each window's voxels as
+    `run_device_steps`."""
     committed = h2d = d2h = 0
     it = iter(seeds)
     for i in range(batch.slots):
         if batch.state[i]['phase'] == 'idle':
             batch.arm(i, next(it), CAP)
-    for _ in range(steps):
-        rows = batch._rows()
-        kmax = max([r[0] for r in rows] + [0])
-        h2d += batch.params_host.numel()
-        d2h += (2 * batch.slots) * 4 + (batch.slots * kmax * (4 + 2) if kmax else 0)
-        results = batch.step()
+    launched = collected = 0
+    while collected < steps:
+        while launched < steps and batch.in_flight < batch.depth and batch.runnable():
+            batch.launch()
+            rows = batch._queue[-1]['rows']
+            kmax = max([r[0] for r in rows] + [0])
+            h2d += batch.params_host.numel()
+            d2h += (2 * batch.slots) * 4 + (batch.slots * kmax * (4 + 2) if kmax else 0)
+            launched += 1
+        if not batch.in_flight:
+            raise RuntimeError('no slot can take a forward')   # every finished window is re-armed, so it cannot happen
+        results = batch.collect()
+        collected += 1
         for i, (record, commit) in results.items():
             if record is not None:
                 committed += batch.total   # a finished window committed its whole column
