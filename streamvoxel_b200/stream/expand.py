@@ -129,19 +129,11 @@ def host_exchange(obj, group=None):
 
 
 class DeviceExchange:
-    """`host_exchange` of (finished columns, free slots) over a device process group (NCCL), in two forms.
-
-    Called (`exchange(obj)`): a fixed-size header per rank (finished count, free slots, the finished cells)
-    all-gathered every round, and the finished columns all-gathered only in rounds where some rank finished one (every
-    rank reads the same headers, so all take the same collectives). Returns what `host_exchange` returns.
-
-    Started and finished (`start(obj)`, then `finish()` a round later, as `run` does with this exchange): one
-    all-gather per round of the header and all `slots` column buffers, enqueued on the exchange's stream and read back
-    a round later, so no rank waits for the others' current round (the round's admission uses the previous round's
-    reports; see `_run_pipelined`). Two buffer sets alternate between the rounds in flight.
-
-    The collectives run on a stream of their own, so they do not queue behind the steps in flight, and only the
-    columns that exist are copied back to the host."""
+    """`host_exchange` of (finished columns, free slots) over a device process group (NCCL): a fixed-size header per
+    rank (finished count, free slots, the finished cells) all-gathered every round, and the finished columns
+    all-gathered only in rounds where some rank finished one (every rank reads the same headers, so all take the same
+    collectives). The collectives run on a stream of their own, so they do not queue behind the steps in flight, and
+    only the columns that exist are copied back to the host. Returns what `host_exchange` returns."""
 
     def __init__(self, group, slots, shape, device):
         import contextlib
@@ -151,45 +143,35 @@ class DeviceExchange:
         self.torch, self.dist, self.group = torch, dist, group
         self.ranks = dist.get_world_size(group)
         self.slots, self.shape = int(slots), tuple(shape)
-        self.width = 2 + 2 * self.slots
+        width = 2 + 2 * self.slots
         device = torch.device(device)
         cuda = device.type == 'cuda'
-        self.device = device
         # A CPU device (a gloo group) runs the same collectives on the calling thread; it is there for tests.
         self.stream = torch.cuda.Stream(device=device) if cuda else None
         self.context = (lambda: torch.cuda.stream(self.stream)) if cuda else contextlib.nullcontext
-        self.header_host = torch.zeros(self.width, dtype=torch.int64, pin_memory=cuda)
-        self.header = torch.zeros(self.width, dtype=torch.int64, device=device)
-        self.headers = torch.zeros((self.ranks, self.width), dtype=torch.int64, device=device)
+        self.header_host = torch.zeros(width, dtype=torch.int64, pin_memory=cuda)
+        self.header = torch.zeros(width, dtype=torch.int64, device=device)
+        self.headers = torch.zeros((self.ranks, width), dtype=torch.int64, device=device)
         self.columns_host = torch.zeros((self.slots, *self.shape), dtype=torch.int16, pin_memory=cuda)
         self.columns = torch.zeros((self.slots, *self.shape), dtype=torch.int16, device=device)
         self.gathered = torch.zeros((self.ranks, self.slots, *self.shape), dtype=torch.int16, device=device)
         # NCCL has no 16-bit integer type: the columns travel as their bytes.
         self.columns_bytes = self.columns.view(-1).view(torch.uint8)
         self.gathered_bytes = self.gathered.view(-1).view(torch.uint8)
-        # the started form: per buffer set, one record of header bytes then the columns, per rank
-        self.record_bytes = self.width * 8 + self.columns.numel() * 2
-        self.sets = None
-        self.in_flight = []   # (set index, event) of started exchanges, oldest first
-        self.rounds = 0
 
-    def _pack(self, obj, header, columns):
-        torch = self.torch
+    def __call__(self, obj):
+        torch, dist = self.torch, self.dist
         finished, free = obj
         if len(finished) > self.slots:
             raise ValueError('more finished windows than slots')
+        header = self.header_host
         header.zero_()
         header[0], header[1] = len(finished), int(free)
         for j, (cell, column) in enumerate(finished):
             header[2 + 2 * j], header[3 + 2 * j] = int(cell[0]), int(cell[1])
-            columns[j].copy_(torch.from_numpy(np.ascontiguousarray(column, np.int16)))
-
-    def __call__(self, obj):
-        torch, dist = self.torch, self.dist
-        finished, _ = obj
-        self._pack(obj, self.header_host, self.columns_host)
+            self.columns_host[j].copy_(torch.from_numpy(np.ascontiguousarray(column, np.int16)))
         with self.context():
-            self.header.copy_(self.header_host, non_blocking=True)
+            self.header.copy_(header, non_blocking=True)
             dist.all_gather_into_tensor(self.headers.view(-1), self.header, group=self.group)
             headers = self.headers.cpu().numpy()   # waits for this stream only
             out = [([], int(h[1])) for h in headers]
@@ -203,54 +185,6 @@ class DeviceExchange:
                         cols = self.gathered[r, :count].cpu().numpy()
                         out[r] = ([((int(h[2 + 2 * j]), int(h[3 + 2 * j])), cols[j].copy()) for j in range(count)],
                                   int(h[1]))
-        return out
-
-    def _set(self, k):
-        torch = self.torch
-        if self.sets is None:
-            cuda = self.device.type == 'cuda'
-            self.sets = [dict(host=torch.zeros(self.record_bytes, dtype=torch.uint8, pin_memory=cuda),
-                              send=torch.zeros(self.record_bytes, dtype=torch.uint8, device=self.device),
-                              recv=torch.zeros(self.ranks * self.record_bytes, dtype=torch.uint8, device=self.device))
-                         for _ in range(2)]
-        return self.sets[k]
-
-    def start(self, obj):
-        """Enqueue this round's exchange of (finished columns, free slots); `finish` returns it."""
-        torch, dist = self.torch, self.dist
-        if len(self.in_flight) >= 2:
-            raise RuntimeError('two exchanges are already in flight; finish one first')
-        k = self.rounds % 2
-        self.rounds += 1
-        buf = self._set(k)
-        header = buf['host'][:self.width * 8].view(torch.int64)
-        columns = buf['host'][self.width * 8:].view(torch.int16).view(self.slots, *self.shape)
-        self._pack(obj, header, columns)
-        with self.context():
-            buf['send'].copy_(buf['host'], non_blocking=True)
-            dist.all_gather_into_tensor(buf['recv'], buf['send'], group=self.group)
-            event = torch.cuda.Event() if self.stream is not None else None
-            if event is not None:
-                event.record(self.stream)
-        self.in_flight.append((k, event))
-
-    def finish(self):
-        """The oldest started exchange: [(finished [(cell, column)], free slots)] per rank, as `host_exchange`."""
-        torch = self.torch
-        k, event = self.in_flight.pop(0)
-        buf = self._set(k)
-        if event is not None:
-            event.synchronize()
-        recv = buf['recv'].view(self.ranks, self.record_bytes)
-        headers = recv[:, :self.width * 8].contiguous().view(torch.int64).view(self.ranks, self.width).cpu().numpy()
-        out = []
-        for r, h in enumerate(headers):
-            count = int(h[0])
-            finished = []
-            if count:
-                cols = recv[r, self.width * 8:].view(torch.int16).view(self.slots, *self.shape)[:count].cpu().numpy()
-                finished = [((int(h[2 + 2 * j]), int(h[3 + 2 * j])), cols[j].copy()) for j in range(count)]
-            out.append((finished, int(h[1])))
         return out
 
 
@@ -324,13 +258,7 @@ def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, 
     """`run` with the host's admission work overlapping the device. One round: launch the next step at once (the
     slots of windows that finished in the previous step sit it out), then -- while it runs -- read the finished
     windows' columns (copies enqueued before the launch), exchange and commit them, admit new windows and arm them
-    into the free slots (as many as fit in the step's duration), then collect the step.
-
-    With an exchange that has `start` / `finish` (`DeviceExchange`), the exchange runs a round behind: a round applies
-    and admits from the reports every rank started in the previous round, then starts its own report (the columns it
-    read, and its free slots after this round's admissions), so no rank waits for the others' current round. Every
-    rank applies the same reports in the same round, so the replicas stay identical; a rank's reported free slots can
-    only grow before the report is used (collects free slots, only admissions take them), so no slot is given twice."""
+    into the free slots (as many as fit in the step's duration), then collect the step."""
     slot_cell = [None] * engine.slots
     to_arm = []      # (slot, cell) admitted, not yet armed
     pending = []     # (cell, record, slot, column reader) of windows the last collect finished
@@ -341,10 +269,6 @@ def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, 
     step_time = 0.0   # running estimate of one step's wall time (launch to collected)
     read_async = hasattr(engine, 'column_async')
     depth = getattr(engine, 'depth', 1)
-    lagged = hasattr(exchange, 'start') and hasattr(exchange, 'finish')
-    stalled = 0
-    if lagged:   # before the first report: every rank has all its slots free
-        previous = [([], engine.slots) for _ in range(expansion.ranks)]
     for _ in range(max_rounds):
         began = clock()
         # keep up to `depth` steps in flight: the next step is queued before the host works on the last one's results
@@ -370,10 +294,7 @@ def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, 
             stats['committed_voxels'] += int(tokens.size)
         pending = []
         free_slots = [i for i, c in enumerate(slot_cell) if c is None]
-        if lagged:
-            gathered = exchange.finish() if exchange.in_flight else previous
-        else:
-            gathered = exchange((finished, len(free_slots)))
+        gathered = exchange((finished, len(free_slots)))
         stats['exchange_seconds'] += clock() - t0
         for commits, _ in gathered:
             expansion.apply(commits)
@@ -382,10 +303,6 @@ def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, 
             i = free_slots.pop(0)
             slot_cell[i] = cell
             to_arm.append((i, cell))
-        if lagged:
-            t1 = clock()
-            exchange.start((finished, len(free_slots)))
-            stats['exchange_seconds'] += clock() - t1
         stats['admission_seconds'] += clock() - t0
         # Arm while the step still runs (at least one per step; all of them when nothing runs), so a burst of finishing
         # windows does not idle the device.
@@ -421,16 +338,10 @@ def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, 
                     pending.append((slot_cell[i], record, i, read))
                     slot_cell[i] = None
         stats['rounds'] += 1
-        if expansion.done and not pending:   # every rank applies the same reports, so all stop in this round
+        if expansion.done and not pending:
             break
-        # nothing running, read or waiting to be armed: with the lagged exchange, reports still on their way may free
-        # cells for a round or two
-        stalled = stalled + 1 if not expansion.inflight and not pending and not to_arm else 0
-        if stalled > (2 if lagged else 0):
+        if not expansion.inflight and not pending and not to_arm:
             raise RuntimeError('expansion blocked: no window in flight and none admissible')
-    if lagged:
-        while exchange.in_flight:   # the last round's reports (no commits once the region is done)
-            exchange.finish()
     stats['blocked_admissions'] = expansion.blocked_admissions
     return stats
 

@@ -186,31 +186,3 @@ def test_device_exchange_two_gloo_ranks():
     same host logic the NCCL group runs on GPUs."""
     from exchange_worker import check_rounds, run_two_ranks
     check_rounds(run_two_ranks('gloo'))
-
-
-def _lagged_worker(rank, world, port, path):
-    import torch.distributed as dist
-    dist.init_process_group('gloo', init_method=f'tcp://127.0.0.1:{port}', rank=rank, world_size=world)
-    exp = _setup(world, 3)
-    engine = PipelinedFakeEngine(3)
-    exchange = expand.DeviceExchange(dist.group.WORLD, 3, (SPEC.height, SPEC.tile, SPEC.tile), 'cpu')
-    stats = expand.run(engine, exp, rank, exchange=exchange)
-    with open(f'{path}.{rank}', 'w') as f:
-        f.write(f"{exp.digest()} {stats['windows']} {len(exp.committed)} {int(exp.done)} {len(exchange.in_flight)}")
-    dist.barrier()
-    dist.destroy_process_group()
-
-
-def test_lagged_exchange_keeps_identical_replicas():
-    """The exchange a round behind (`DeviceExchange.start` / `finish` on a gloo group): both ranks apply the same
-    reports in the same rounds, commit the whole region once and end with identical replicas -- the same world as one
-    rank, since a column depends on its window seed only."""
-    single, _, _ = _run(1, 6)
-    port = 29600 + os.getpid() % 2000
-    with tempfile.TemporaryDirectory() as tmp:
-        path = os.path.join(tmp, 'out')
-        mp.start_processes(_lagged_worker, args=(2, port, path), nprocs=2, join=True, start_method='spawn')
-        rows = [open(f'{path}.{r}').read().split() for r in range(2)]
-    assert rows[0][0] == rows[1][0] == single.digest()
-    assert int(rows[0][1]) + int(rows[1][1]) == 100 - 16 and int(rows[0][1]) > 0 and int(rows[1][1]) > 0
-    assert all(r[2] == '100' and r[3] == '1' and r[4] == '0' for r in rows)
