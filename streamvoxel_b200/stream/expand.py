@@ -362,9 +362,59 @@ def start_region(seed, side0, side1, spec, classes=None):
     return committed, region, biomes, player
 
 
+class _StandInEngine:
+    """A slot batch whose windows take `forwards` steps and commit nothing (for `simulate`): `launch` / `collect` with
+    two steps in flight, as `SlotBatch` runs them."""
+    depth = 2
+
+    def __init__(self, slots, forwards, shape):
+        self.slots, self.forwards, self.shape = slots, forwards, shape
+        self.left = [0] * slots
+        self.to_launch = [0] * slots
+        self.targets = [None] * slots
+        self.queue = []
+
+    @property
+    def in_flight(self):
+        return len(self.queue)
+
+    def runnable(self):
+        return any(self.to_launch)
+
+    def arm(self, slot, seed, cap, item=None, target=(), wait=True):
+        self.left[slot] = self.to_launch[slot] = self.forwards
+        self.targets[slot] = target
+
+    def launch(self):
+        entry = [i for i in range(self.slots) if self.to_launch[i]]
+        for i in entry:
+            self.to_launch[i] -= 1
+        self.queue.append(entry)
+
+    def collect(self):
+        out = {}
+        for i in self.queue.pop(0):
+            self.left[i] -= 1
+            record = dict(target=self.targets[i], column=np.zeros(self.shape, np.int16)) if self.left[i] == 0 else None
+            out[i] = (record, None)
+        return out
+
+
+def simulate(side0, side1, spec, slots, forwards=33, seed=11):
+    """The steps an expansion of the side0^2 -> side1^2 region takes under the admission rules (Chebyshev >= 2,
+    nearest to the player, at most `slots` windows in flight) when every window takes `forwards` steps: the step count
+    that bounds several GPUs before any host or exchange cost (`slots` = GPUs x slots per GPU). Host-only; returns
+    the driver's statistics (`forwards` = steps, `blocked_admissions` = slot-rounds left empty)."""
+    committed, region, biomes, player = start_region(seed, side0, side1, spec)
+    exp = Expansion(committed, biomes, spec, player, region, ranks=1, slots=slots)
+    exp.item = lambda cell: None   # the stand-in engine takes no conditions
+    return run(_StandInEngine(slots, forwards, (spec.height, spec.tile, spec.tile)), exp, 0)
+
+
 def main():
     """python -m streamvoxel_b200.stream.expand [--side0 8 --side1 16] (torchrun for several GPUs): one expansion
-    through the real engine; prints one JSON line with committed voxels/s and the admission statistics."""
+    through the real engine; prints one JSON line with committed voxels/s and the admission statistics.
+    With `--simulate`: the step counts of the admission alone at 1, 2, 4 and 8 times `--slots` (no GPU)."""
     import os
 
     import torch
@@ -380,7 +430,18 @@ def main():
     parser.add_argument('--side1', type=int, default=16)
     parser.add_argument('--slots', type=int, default=8)
     parser.add_argument('--small', action='store_true', help='the small test model instead of DiT-B/4 + ControlNet')
+    parser.add_argument('--simulate', action='store_true', help='admission step counts only (host, no GPU)')
     args = parser.parse_args()
+    if args.simulate:
+        spec = ModelSpec.of(sm.small_test_config() if args.small else sm.dit_b4_control())
+        base = None
+        for gpus in (1, 2, 4, 8):
+            st = simulate(args.side0, args.side1, spec, gpus * args.slots)
+            base = base or st['forwards']
+            print(json.dumps(dict(gpus=gpus, slots=gpus * args.slots, windows=st['windows'], steps=st['forwards'],
+                                  empty_slot_rounds=st['blocked_admissions'],
+                                  step_bound_speedup=round(base / st['forwards'], 3))))
+        return
     world_size = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))

@@ -186,3 +186,15 @@ def test_device_exchange_two_gloo_ranks():
     same host logic the NCCL group runs on GPUs."""
     from exchange_worker import check_rounds, run_two_ranks
     check_rounds(run_two_ranks('gloo'))
+
+
+def test_simulated_admission_bounds_the_step_count():
+    """`expand.simulate`: the admission alone, every window taking a fixed number of steps -- every window admitted
+    once, never fewer steps than the work needs, and more slots never taking more steps."""
+    steps = []
+    for slots in (2, 4, 8):
+        st = expand.simulate(4, 10, SPEC, slots, forwards=5, seed=5)
+        assert st['windows'] == 100 - 16
+        assert st['forwards'] >= (100 - 16) * 5 / slots
+        steps.append(st['forwards'])
+    assert steps[0] >= steps[1] >= steps[2]
