@@ -16,7 +16,49 @@ import time
 
 import numpy as np
 
-from .scheduler import fast_item, member_shares, separated, window_seed
+from .scheduler import fast_item, member_shares, window_seed
+
+
+class _InFlight(dict):
+    """The in-flight windows (cell -> owning rank) with, per cell, how many of them it lies too close to. `separated`
+    admits a cell when it keeps Chebyshev distance >= 2 from every in-flight window (Manhattan >= 2 with `diagonal`),
+    i.e. when no window lies in its 3x3 block (its 4-neighbour cross with `diagonal`); the blocks are symmetric, so
+    a cell is admissible exactly when it is not a key of `near`."""
+
+    def __init__(self, diagonal=False):
+        super().__init__()
+        self.reach = [(a, b) for a in (-1, 0, 1) for b in (-1, 0, 1) if not diagonal or abs(a) + abs(b) <= 1]
+        self.near = {}
+
+    def _count(self, cell, step):
+        z, x = cell
+        near = self.near
+        for a, b in self.reach:
+            key = (z + a, x + b)
+            count = near.get(key, 0) + step
+            if count:
+                near[key] = count
+            else:
+                del near[key]
+
+    def __setitem__(self, cell, rank):
+        if cell not in self:
+            self._count(cell, 1)
+        super().__setitem__(cell, rank)
+
+    def __delitem__(self, cell):
+        super().__delitem__(cell)
+        self._count(cell, -1)
+
+    def pop(self, cell, *default):
+        if cell in self:
+            self._count(cell, -1)
+        return super().pop(cell, *default)
+
+    def _unsupported(self, *args, **kwargs):
+        raise TypeError('in-flight windows change only by item assignment, del and pop')
+
+    update = setdefault = popitem = clear = _unsupported
 
 
 class Expansion:
@@ -31,33 +73,35 @@ class Expansion:
         self.cell_size, self.diagonal = cell_size, diagonal
         total = self.ranks * int(slots) if batch is None else int(batch)
         self.share = member_shares(total, [(r, int(slots), 1) for r in range(self.ranks)])
-        self.inflight = {}          # cell -> owning rank
-        self.ready = set()          # uncommitted cells with a committed 8-neighbour, inside the region
+        self.inflight = _InFlight(diagonal)  # cell -> owning rank
+        self.ready = {}             # uncommitted cells with a committed 8-neighbour, inside the region -> pick key
+        self.open = self.region - self.committed.keys()   # region cells still to commit
         for c in self.committed:
             self._touch(c)
         self.blocked_admissions = 0  # free slots left empty because no admissible cell existed
 
     def _touch(self, cell):
         z, x = cell
+        pz, px, size = self.player[0], self.player[1], self.cell_size
         for a in (z - 1, z, z + 1):
             for b in (x - 1, x, x + 1):
-                if (a, b) not in self.committed and (a, b) in self.region:
-                    self.ready.add((a, b))
-        self.ready.discard(cell)
+                if (a, b) not in self.committed and (a, b) in self.region and (a, b) not in self.ready:
+                    self.ready[(a, b)] = (((a + .5) * size - pz) ** 2 + ((b + .5) * size - px) ** 2, a, b)
+        self.ready.pop(cell, None)
 
     @property
     def done(self):
-        return self.region.issubset(self.committed.keys())
+        return not self.open
 
     def pick(self):
-        """`pick_window` restricted to the region, over the incrementally kept ready set (same key and rule)."""
-        pz, px = self.player
+        """`pick_window` restricted to the region, over the incrementally kept ready set (same key and rule): the
+        nearest ready cell that no in-flight window blocks. `_InFlight.near` answers `separated` per cell in O(1)
+        and `ready` maps each cell to its key (the player is fixed), so a pick costs one pass over the frontier."""
+        near = self.inflight.near
         best_key, best = None, None
-        for cell in self.ready:
-            if cell in self.inflight or not separated(cell, self.inflight, diagonal=self.diagonal):
+        for cell, key in self.ready.items():
+            if cell in near:
                 continue
-            z, x = cell
-            key = (((z + .5) * self.cell_size - pz) ** 2 + ((x + .5) * self.cell_size - px) ** 2, z, x)
             if best_key is None or key < best_key:
                 best_key, best = key, cell
         return best
@@ -67,6 +111,7 @@ class Expansion:
         for cell, tokens in commits:
             cell = tuple(cell)
             self.committed[cell] = np.asarray(tokens, np.int16)
+            self.open.discard(cell)
             self.inflight.pop(cell, None)
             self._touch(cell)
 

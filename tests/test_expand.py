@@ -112,6 +112,39 @@ def test_incremental_pick_equals_pick_window():
             exp.apply([(done, np.zeros((64, 16, 16), np.int16))])
 
 
+def test_block_counts_agree_with_separated():
+    """The in-flight block counts admit exactly the cells `separated` admits (both rules), through assignment, pop
+    and del, and `pick` stays the nearest such ready cell."""
+    rng = np.random.default_rng(3)
+    for diagonal in (False, True):
+        committed, region, biomes, player = expand.start_region(5, 4, 10, SPEC, classes=32)
+        exp = expand.Expansion(committed, biomes, SPEC, player, region, slots=8, diagonal=diagonal)
+        cells = [(z, x) for z in range(-2, 13) for x in range(-2, 13)]
+        for _ in range(60):
+            cell = cells[int(rng.integers(0, len(cells)))]
+            if cell in exp.inflight:
+                if rng.random() < 0.5:
+                    exp.inflight.pop(cell)
+                else:
+                    del exp.inflight[cell]
+            else:
+                exp.inflight[cell] = int(rng.integers(0, 2))
+            for c in cells:
+                assert (c not in exp.inflight.near) == sch.separated(c, exp.inflight, diagonal=diagonal)
+            free = [c for c in exp.ready if sch.separated(c, exp.inflight, diagonal=diagonal)]
+            want = min(free, key=lambda c: exp.ready[c]) if free else None
+            assert exp.pick() == want
+        for cell in list(exp.inflight):
+            exp.inflight.pop(cell)
+        assert not exp.inflight.near
+        try:
+            exp.inflight.update({(0, 0): 0})
+        except TypeError:
+            pass
+        else:
+            raise AssertionError('update bypasses the block counts')
+
+
 def _run(ranks, slots, rank=0, group=None):
     exp = _setup(ranks, slots)
     engine = FakeEngine(slots)
