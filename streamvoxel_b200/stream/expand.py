@@ -245,7 +245,11 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
 
     Pipelined (the default for an engine with `launch`/`collect`): the windows admitted after a step are built and
     armed while the next step runs on the GPU (their condition encode joins before the step after), so the host's
-    admission work overlaps the device; a slot whose window finished sits out one step."""
+    admission work overlaps the device; a slot whose window finished sits out one step.
+
+    Host timers in the statistics: `exchange_seconds` reading finished columns and the all-gather,
+    `admission_seconds` applying commits and `admit`, `item_seconds` / `arm_seconds` building and arming windows,
+    `collect_wait_seconds` (pipelined) waiting for a step."""
     if pipelined is None:
         pipelined = hasattr(engine, 'launch') and hasattr(engine, 'collect')
     if exchange is None:
@@ -273,13 +277,15 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
                     stats['windows'] += 1
                     stats['committed_voxels'] += int(tokens.size)
                     slot_cell[i] = None
-        t0 = clock()
+        t0_exchange = clock()
         free_slots = [i for i, c in enumerate(slot_cell) if c is None]
         gathered = exchange((finished, len(free_slots)))
-        stats['exchange_seconds'] += clock() - t0
+        t0 = clock()
+        stats['exchange_seconds'] += t0 - t0_exchange
         for commits, _ in gathered:
             expansion.apply(commits)
         picks = expansion.admit([n for _, n in gathered])
+        stats['admission_seconds'] += clock() - t0
         for cell in picks[rank]:
             i = free_slots.pop(0)
             t = clock()
@@ -289,7 +295,6 @@ def run(engine, expansion, rank, *, group=None, max_rounds=1_000_000, publisher=
             stats['item_seconds'] += t1 - t
             stats['arm_seconds'] += clock() - t1
             slot_cell[i] = cell
-        stats['admission_seconds'] += clock() - t0
         stats['rounds'] += 1
         if expansion.done:
             break
@@ -340,7 +345,8 @@ def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, 
         pending = []
         free_slots = [i for i, c in enumerate(slot_cell) if c is None]
         gathered = exchange((finished, len(free_slots)))
-        stats['exchange_seconds'] += clock() - t0
+        t0_admission = clock()
+        stats['exchange_seconds'] += t0_admission - t0
         for commits, _ in gathered:
             expansion.apply(commits)
         picks = expansion.admit([n for _, n in gathered])
@@ -348,7 +354,7 @@ def _run_pipelined(engine, expansion, rank, *, exchange, max_rounds, publisher, 
             i = free_slots.pop(0)
             slot_cell[i] = cell
             to_arm.append((i, cell))
-        stats['admission_seconds'] += clock() - t0
+        stats['admission_seconds'] += clock() - t0_admission
         # Arm while the step still runs (at least one per step; all of them when nothing runs), so a burst of finishing
         # windows does not idle the device.
         armed = 0
