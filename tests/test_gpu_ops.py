@@ -358,6 +358,30 @@ def test_attention_odd_query_tiles_ties_and_empty_slots(ops):
         torch.testing.assert_close(got[s * n:(s + 1) * n], want.transpose(0, 1).reshape(n, d), atol=2e-2, rtol=2e-2)
 
 
+def test_attention_key_length_edges(ops):
+    """Cross-attention at the engine's key capacity (9600 = 100 key tiles of 96) with a single key, exactly one tile,
+    one key into a second tile, one key short of the capacity and the whole capacity."""
+    torch.manual_seed(21)
+    heads, n, d, cap = 2, 256, 192, 9600
+    lengths_list = [1, 96, 97, 9599, 9600]
+    slots = len(lengths_list)
+    kc = (torch.randn((slots, heads, cap, 96), device='cuda') * 1.5).bfloat16()
+    vc = torch.randn((slots, heads, cap, 96), device='cuda').bfloat16()
+    lengths = torch.tensor(lengths_list, dtype=torch.int32, device='cuda')
+    qx = (torch.randn((slots * n, d), device='cuda') * 1.5).bfloat16()
+    got = ops.attention(qx, kc, vc, slots, heads, n, cap, q_row_stride=d, kv_slot_stride=heads * cap * 96,
+                        kv_head_stride=cap * 96, kv_row_stride=96, lengths=lengths).float()
+    for s, L in enumerate(lengths_list):
+        qs = qx[s * n:(s + 1) * n].float().reshape(n, heads, 96).transpose(0, 1)
+        want = torch.nn.functional.scaled_dot_product_attention(qs, kc[s, :, :L].float(), vc[s, :, :L].float())
+        torch.testing.assert_close(got[s * n:(s + 1) * n], want.transpose(0, 1).reshape(n, d), atol=2e-2, rtol=2e-2)
+    # One key: every query's output is that key's value row, to within one bf16 ulp (measured: about one row in seven
+    # comes out scaled by a factor within 2^-8 of 1, so some of its elements round to the neighbouring bf16 value).
+    single = vc[0, :, 0].float()
+    torch.testing.assert_close(got[:n].reshape(n, heads, 96), single[None].expand(n, heads, 96), atol=0,
+                               rtol=2 ** -7 + 1e-6)
+
+
 def test_layernorm_modulate(ops):
     torch.manual_seed(5)
     for d in (192, 768):

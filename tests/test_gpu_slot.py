@@ -157,6 +157,73 @@ def test_fast_slot_full_size_config3_windows_equal_reference_slot():
         assert np.array_equal(tokens[i].cpu().numpy(), ref_tokens[i])
 
 
+def _edge_air_boost(shape, seed=9):
+    """Per-slot masks of voxels whose air logit is raised far above the rest (p(air) > 1 - 1e-6), chosen so the
+    marking defers: every voxel (no solid step, the window ends at its marking); the upper half of every column;
+    all but 8 voxels (one solid step of 8, most 4^3 blocks with no legal voxel); nothing, although a third of the voxels
+    are air-certain (each column's top voxel is not, and the deferred run must reach the top)."""
+    y, z, x = shape
+    rng = np.random.default_rng(seed)
+    everything = np.ones(shape, bool)
+    upper = np.zeros(shape, bool)
+    upper[y // 2:] = True
+    but_eight = np.ones(shape, bool)
+    but_eight[:5, 0, 0] = False
+    but_eight[:3, 3, 4] = False
+    scattered = rng.random(shape) < 0.35
+    scattered[-1] = False
+    return [everything, upper, but_eight, scattered]
+
+
+def test_fast_slot_edge_windows_equal_reference_slot():
+    """Windows whose marking defers all, half, all but 8, or none of the voxels (fresh N(0, 1) logits every forward
+    plus the air boost of `_edge_air_boost`), through `consume_batch` + `SelectGraphs` on the slots' own generators,
+    against the reference slot on the same logits, seeds and block orders: every commit, the tokens and the records
+    bit-equal, including the window that ends at its marking and the steps whose quota lies in a few blocks."""
+    from streamvoxel_b200.stream.fast_ops import FastLowEntropyLastSlot, SelectGraphs, consume_batch
+    from reference_slot import ReferenceSlot
+    shape, classes, cap = (32, 8, 8), 6, 8
+    boosts = [torch.from_numpy(b).cuda() for b in _edge_air_boost(shape)]
+    slots_n = len(boosts)
+    logits = torch.zeros((slots_n, classes, *shape), dtype=torch.float32, device='cuda')
+    tokens = torch.full((slots_n, *shape), classes, dtype=torch.int16, device='cuda')
+    slots = [FastLowEntropyLastSlot(shape, classes, air_ids=(0,), air_token=0, last_eps=1e-4, block_size=4,
+                                    device='cuda', sampling='parity') for _ in range(slots_n)]
+    graphs = SelectGraphs(_Outputs(logits, tokens), slots)
+    refs = [ReferenceSlot(shape, classes, last_eps=1e-4) for _ in range(slots_n)]
+    ref_tokens = [np.full(shape, classes, np.int64) for _ in range(slots_n)]
+    for i in range(slots_n):
+        slots[i].arm(2000 + i, cap, (i, 0))
+        refs[i].arm(2000 + i, cap, (i, 0), slots[i].order.cpu().numpy())
+    generator = torch.Generator(device='cuda').manual_seed(13)
+    records, step = {}, 0
+    while len(records) < slots_n:
+        logits.copy_(torch.randn(logits.shape, generator=generator, device='cuda'))
+        for i in range(slots_n):
+            logits[i, 0].masked_fill_(boosts[i], 20.0)
+        results = consume_batch(slots, logits, tokens, slots_n, graphs)
+        for i, (record, commit) in results.items():
+            scores = slots[i].scores[0].cpu().numpy()
+            ref_record, ref_commit = refs[i].consume(logits[i], ref_tokens[i], scores)
+            assert (commit is None) == (ref_commit is None), (i, step)
+            if commit is not None:
+                assert np.array_equal(commit['positions'], ref_commit['positions']), (i, step)
+                assert np.array_equal(commit['values'], ref_commit['values']), (i, step)
+                assert commit['step'] == ref_commit['step']
+            assert (record is None) == (ref_record is None), (i, step)
+            if record is not None:
+                _record_equal(record, ref_record)
+                records[i] = record
+        step += 1
+        assert step <= cap + 2
+    total = int(np.prod(shape))
+    assert [records[i]['last_count'] for i in range(slots_n)][:3] == [total, total // 2, total - 8]
+    assert records[0]['nfe'] == 1 and records[0]['actual'] == 0 and records[2]['actual'] == 1
+    assert records[3]['last_count'] == 0 and records[3]['actual'] == cap
+    for i in range(slots_n):
+        assert np.array_equal(tokens[i].cpu().numpy(), ref_tokens[i])
+
+
 def _small_batch(sampling, slots=4):
     from streamvoxel_b200 import model as sm, synth
     from streamvoxel_b200.stream.batch import SlotBatch
